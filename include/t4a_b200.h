@@ -1,0 +1,157 @@
+/*
+ * t4a_b200: B200-native (sm_100a) implementation of the t4a-cuda-kernels hot path.
+ *
+ * C ABI of the host library libt4a_b200.so.  It replaces two reference interfaces:
+ *
+ *  1. The Rust planner `t4a_cuda_kernels::plan_*` (reference src/lib.rs), restated
+ *     here as `t4a_plan_*`: the same inputs, the same validation and the same
+ *     error codes (the order of the Rust `Error` enum, src/lib.rs:219-280, plus one),
+ *     returning the launch geometry of this library's kernels.
+ *  2. The caller's `cuLaunchKernel` on a module symbol (reference
+ *     tests/gpu/mod.rs:297-331): `t4a_launch_*` takes the planned `t4a_launch`, the
+ *     caller's stream and exactly the argument list of the kernel symbol it stands
+ *     for (docs/abi/c-kernel-abi.md entry tables), and launches it.
+ *
+ * The modules lib/{reduce,movement,gather_scatter,rrqr}.cubin built beside the
+ * library export the same
+ * `extern "C" __global__` symbols as the reference (t4a_cuda_reduce, ...), for
+ * callers that load kernels by name.
+ *
+ * Ownership is the reference's: the caller owns streams, device buffers and
+ * workspace; nothing here allocates device memory, frees it or synchronizes
+ * (t4a_reduce's workspace is caller-provided too).  Every function returns a
+ * t4a_status code.  `stream` is a cudaStream_t (NULL = legacy default stream).
+ */
+#ifndef T4A_B200_H_
+#define T4A_B200_H_
+
+#include <stddef.h>
+
+#include "t4a_b200/abi.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes: 0 = success; 1..25 = the reference planner's Error variants in
+ * declaration order (src/lib.rs:219-270, the fusion-only variants excluded);
+ * 64.. = runtime conditions of this library. */
+typedef enum {
+  T4A_OK = 0,
+  T4A_ERR_RANK_OUT_OF_RANGE = 1,
+  T4A_ERR_RANK_LENGTH = 2,
+  T4A_ERR_NEGATIVE_EXTENT = 3,
+  T4A_ERR_NEGATIVE_COUNT = 4,
+  T4A_ERR_OVERFLOW = 5,
+  T4A_ERR_COUNT_MISMATCH = 6,
+  T4A_ERR_OFFSET_OUT_OF_SPAN = 7,
+  T4A_ERR_BROADCAST_DESTINATION = 8,
+  T4A_ERR_UNSUPPORTED_DTYPE = 9,
+  T4A_ERR_NOT_ELEMENTWISE = 10,
+  T4A_ERR_LAUNCH_LIMIT = 11,
+  T4A_ERR_INVALID_TRANSPOSE_CONFIG = 12,
+  T4A_ERR_INVALID_AXIS = 13,
+  T4A_ERR_DUPLICATE_AXIS = 14,
+  T4A_ERR_NOT_COMPACT = 15,
+  T4A_ERR_SHAPE_MISMATCH = 16,
+  T4A_ERR_INVALID_STEP = 17,
+  T4A_ERR_INVALID_PADDING = 18,
+  T4A_ERR_DOMAIN_TOO_LARGE = 19,
+  T4A_ERR_INVALID_STRIDE = 20,
+  T4A_ERR_STRATEGY_MISMATCH = 21,
+  T4A_ERR_INVALID_PLANE_WIDTH = 22,
+  T4A_ERR_INVALID_SPLIT = 23,
+  T4A_ERR_INDEX_VECTOR_MISMATCH = 24,
+  T4A_ERR_UNSUPPORTED_OP = 25,
+  T4A_ERR_CUDA = 64,          /* a CUDA runtime call failed (launch or copy) */
+  T4A_ERR_WORKSPACE = 65,     /* caller workspace missing or too small */
+  T4A_ERR_NULL_ARGUMENT = 66  /* a required pointer argument is NULL */
+} t4a_status;
+
+/* Launch geometry of one kernel invocation (reference `Launch`, src/lib.rs:842-848).
+ * `variant` names the kernel path this library chose; a grid with a zero
+ * dimension means "no work" and the launchers skip it. */
+typedef struct {
+  unsigned grid[3];
+  unsigned block[3];
+  unsigned shared_bytes;
+  int variant;
+} t4a_launch;
+
+const char* t4a_status_string(int status);
+int t4a_abi_revision(void);
+/* Last CUDA error seen by a launcher of this thread (cudaError_t), 0 if none. */
+int t4a_last_cuda_error(void);
+
+/* ------------------------------------------------------------------------- */
+/* Single-axis reductions (reference src/lib.rs:3033-3557, reduce.cu:765-852)  */
+/* ------------------------------------------------------------------------- */
+
+typedef struct {
+  long long splits;
+  long long chunk_len;
+} t4a_split;
+
+/* Reference ReductionPlan (src/lib.rs:3170-3182): a direct pass, or pass 1 over
+ * `split` chunks plus a combine pass with `combine_op`. */
+typedef struct {
+  int is_split;
+  int strategy;
+  t4a_launch launch;
+  t4a_split split;
+  t4a_launch pass1;
+  int combine_strategy;
+  int combine_op;
+  t4a_launch pass2;
+} t4a_reduction_plan;
+
+/* split_policy (src/lib.rs:3152): splits = clamp(len / (W*8), 1, 4096), floor
+ * chunk; *has_split = 0 means one direct pass. */
+int t4a_split_policy(long long reduce_len, unsigned plane_width, int* has_split, t4a_split* split);
+
+/* plan_reduce (src/lib.rs:3318). */
+int t4a_plan_reduce(int dtype, int op, int strategy, const t4a_cuda_layout* out, long long out_len,
+                    const t4a_cuda_layout* in, long long in_len, unsigned axis, unsigned plane_width,
+                    t4a_launch* launch);
+
+/* plan_reduce_partials (src/lib.rs:3342). */
+int t4a_plan_reduce_partials(int dtype, int op, const t4a_cuda_layout* partials, long long partials_len,
+                             const t4a_cuda_layout* in, long long in_len, unsigned axis,
+                             t4a_split split, unsigned plane_width, t4a_launch* launch);
+
+/* plan_reduction (src/lib.rs:3457): the whole Auto policy. */
+int t4a_plan_reduction(int dtype, int op, const t4a_cuda_layout* out, long long out_len,
+                       const t4a_cuda_layout* in, long long in_len, unsigned axis,
+                       unsigned plane_width, t4a_reduction_plan* plan);
+
+/* reduction_partials_layout (src/lib.rs:3535): the input extents with the axis set
+ * to `splits`, compact. */
+int t4a_reduction_partials_layout(const t4a_cuda_layout* in, unsigned axis, long long splits,
+                                  t4a_cuda_layout* partials);
+
+/* Launch t4a_cuda_reduce (reduce.cu:765) / t4a_cuda_reduce_partials (reduce.cu:813)
+ * with a planned geometry on `stream`. */
+int t4a_launch_reduce(const t4a_launch* launch, void* stream, void* out, const void* in, int dtype,
+                      int op, int strategy, t4a_cuda_layout out_layout, t4a_cuda_layout in_layout,
+                      int axis, long long output_len);
+int t4a_launch_reduce_partials(const t4a_launch* launch, void* stream, void* partials, const void* in,
+                               int dtype, int op, t4a_cuda_layout partials_layout,
+                               t4a_cuda_layout in_layout, int axis, long long output_len,
+                               long long splits, long long chunk_len);
+
+/* Workspace bytes of t4a_reduce (the pass-1 partials; 0 for a direct pass). */
+int t4a_reduce_workspace_bytes(int dtype, int op, const t4a_cuda_layout* out, long long out_len,
+                               const t4a_cuda_layout* in, long long in_len, unsigned axis,
+                               unsigned plane_width, size_t* bytes);
+
+/* One call for a whole reduction: plans, then launches pass 1 and the combine pass
+ * (or the direct pass) on `stream`, partials in the caller's `workspace`. */
+int t4a_reduce(void* stream, int dtype, int op, void* out, const t4a_cuda_layout* out_layout,
+               long long out_len, const void* in, const t4a_cuda_layout* in_layout, long long in_len,
+               unsigned axis, unsigned plane_width, void* workspace, size_t workspace_bytes);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* T4A_B200_H_ */

@@ -1,0 +1,91 @@
+"""Build libt4a_b200.so and the kernel modules for sm_100a.
+
+    python t4a-cuda-kernels_b200/build.py [--jobs N] [--force]
+
+Objects go to <repo>/_build/; the library and the modules to
+t4a-cuda-kernels_b200/t4a_b200/lib/.  The modules are one cubin per kernel family
+(reduce, movement, gather_scatter, rrqr), like the reference's per-file modules,
+exporting the reference's `extern "C" __global__` symbols.  A source is rebuilt when it, or any header
+of csrc/ or include/, is newer than its object.
+"""
+import argparse
+import concurrent.futures
+import glob
+import os
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+CSRC = os.path.join(HERE, "csrc")
+BUILD = os.path.join(ROOT, "_build")
+LIBDIR = os.path.join(HERE, "t4a_b200", "lib")
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC = os.environ.get("NVCC", "nvcc")
+COMMON = ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC", "-I", os.path.join(ROOT, "include")]
+# Translation units that export the reference's __global__ symbols (the module).
+MODULE_TUS = ["reduce_abi.cu", "movement_abi.cu", "gather_scatter_abi.cu", "rrqr_abi.cu"]
+
+
+def headers():
+    return glob.glob(os.path.join(CSRC, "*.h")) + glob.glob(os.path.join(CSRC, "*.cuh")) + \
+        glob.glob(os.path.join(ROOT, "include", "**", "*.h"), recursive=True)
+
+
+def stale(target, sources):
+    if not os.path.exists(target):
+        return True
+    t = os.path.getmtime(target)
+    return any(os.path.getmtime(s) > t for s in sources)
+
+
+def run(cmd):
+    proc = subprocess.run(cmd, capture_output=True, text=True)
+    if proc.returncode != 0:
+        sys.stderr.write(" ".join(cmd) + "\n" + proc.stdout + proc.stderr)
+        raise SystemExit(f"build failed: {os.path.basename(cmd[-1])}")
+    return proc
+
+
+def compile_one(src, force):
+    name = os.path.basename(src)
+    obj = os.path.join(BUILD, name + ".o")
+    if force or stale(obj, [src] + headers()):
+        run([NVCC] + COMMON + ARCH + ["-c", src, "-o", obj])
+    return obj
+
+
+def module_one(src, force):
+    name = os.path.basename(src)
+    cubin = os.path.join(LIBDIR, name.replace("_abi.cu", ".cubin"))
+    if force or stale(cubin, [src] + headers()):
+        run([NVCC, "-std=c++17", "-O3", "-lineinfo", "-I", os.path.join(ROOT, "include"), "-cubin",
+             "-gencode", "arch=compute_100a,code=sm_100a", src, "-o", cubin])
+    return cubin
+
+
+def build(jobs=8, force=False):
+    os.makedirs(BUILD, exist_ok=True)
+    os.makedirs(LIBDIR, exist_ok=True)
+    sources = sorted(glob.glob(os.path.join(CSRC, "*.cu")) + glob.glob(os.path.join(CSRC, "*.cpp")))
+    module_sources = [os.path.join(CSRC, n) for n in MODULE_TUS if os.path.exists(os.path.join(CSRC, n))]
+    lib_sources = [s for s in sources if os.path.basename(s) not in MODULE_TUS]
+    with concurrent.futures.ThreadPoolExecutor(max_workers=jobs) as pool:
+        objs = list(pool.map(lambda s: compile_one(s, force), lib_sources))
+        cubins = list(pool.map(lambda s: module_one(s, force), module_sources))
+    lib = os.path.join(LIBDIR, "libt4a_b200.so")
+    if force or stale(lib, objs):
+        run([NVCC, "-shared"] + ARCH + ["-o", lib] + objs + ["-lcudart"])
+    return lib
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--jobs", type=int, default=os.cpu_count() or 4)
+    ap.add_argument("--force", action="store_true")
+    args = ap.parse_args()
+    print(build(args.jobs, args.force))
+
+
+if __name__ == "__main__":
+    main()

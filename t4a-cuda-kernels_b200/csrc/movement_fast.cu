@@ -1,0 +1,403 @@
+// Movement planning (reference src/lib.rs:1465-1737, :1498-1535) and the host
+// launchers of the movement entries.  The launchers rebuild the permutation plan on
+// the host and launch one kernel per path, compiled for that path alone.
+#include <cuda_runtime.h>
+
+#include "movement_core.cuh"
+#include "plan_common.h"
+#include "runtime.h"
+
+namespace t4a {
+namespace {
+
+template <int B, int V>
+__global__ void __launch_bounds__(256) k_rows(PermPlan p, void* dst, const void* src) {
+  using E = typename Elem<B>::T;
+  perm_rows<E, V>(p, static_cast<E*>(dst), static_cast<const E*>(src));
+}
+
+template <int B, int VS, int VD>
+__global__ void __launch_bounds__(256) k_tiles(PermPlan p, void* dst, const void* src) {
+  using E = typename Elem<B>::T;
+  constexpr int EDGE = B >= 16 ? 32 : 64;
+  perm_tiles<E, VS, VD, EDGE>(p, static_cast<E*>(dst), static_cast<const E*>(src));
+}
+
+template <int B>
+__global__ void __launch_bounds__(256) k_generic(PermPlan p, void* dst, const void* src) {
+  using E = typename Elem<B>::T;
+  perm_generic<E>(p, static_cast<E*>(dst), static_cast<const E*>(src));
+}
+
+template <int B>
+__global__ void __launch_bounds__(256) k_zero(void* out, t4a_cuda_layout l, long long len, bool view) {
+  using E = typename Elem<B>::T;
+  E* o = static_cast<E*>(out);
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long f = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; f < len; f += stride) {
+    E z;
+    memset(&z, 0, sizeof(E));
+    o[view ? decode_offset(f, l, l.strides, l.offset) : f] = z;
+  }
+}
+
+int host_esize(int dtype) { return plan::dtype_size(dtype); }
+
+constexpr int kMoveVariant = 32;  // t4a_launch.variant = kMoveVariant + PermKind
+
+// Geometry of a plan's path.
+int perm_geometry(const PermPlan& p, t4a_launch* launch) {
+  using namespace plan;
+  if (p.kind == kPermEmpty) {
+    *launch = empty_launch();
+    return T4A_OK;
+  }
+  unsigned long long units = 0;
+  if (p.kind == kPermRows) {
+    const long long seg = p.run.len < kPermRowsBytes / p.esize ? p.run.len : kPermRowsBytes / p.esize;
+    const long long rows = kPermRowsBytes / p.esize / seg;
+    units = ceil_div(p.rest.len, rows) * ceil_div(p.run.len, seg);
+  } else if (p.kind == kPermTiles) {
+    const long long edge = perm_tile_edge(p.esize);
+    units = static_cast<unsigned long long>(p.rest.len) * ceil_div(p.run.len, edge) * ceil_div(p.srun.len, edge);
+  } else {
+    units = ceil_div(p.len, kPermThreads);
+  }
+  if (units > kMaxGridX) units = kMaxGridX;  // every path is grid-stride
+  *launch = make_launch(units, kPermThreads, 1, perm_smem_bytes(p), kMoveVariant + p.kind);
+  return T4A_OK;
+}
+
+template <int B>
+int launch_plan_sized(const PermPlan& p, void* dst, const void* src, dim3 grid, unsigned smem, cudaStream_t s) {
+  constexpr int VV = B >= 16 ? 1 : 16 / B;
+  const bool src_al = (reinterpret_cast<unsigned long long>(src) & 15ull) == 0;
+  const bool dst_al = (reinterpret_cast<unsigned long long>(dst) & 15ull) == 0;
+  const dim3 block(kPermThreads);
+  if (p.kind == kPermRows) {
+    if constexpr (VV > 1) {
+      if (src_al && dst_al && perm_vec(p, 0) == VV && perm_vec(p, 1) == VV) {
+        k_rows<B, VV><<<grid, block, smem, s>>>(p, dst, src);
+        return runtime::check_launch();
+      }
+    }
+    k_rows<B, 1><<<grid, block, smem, s>>>(p, dst, src);
+  } else if (p.kind == kPermTiles) {
+    const bool vs = VV > 1 && src_al && perm_vec(p, 0) == VV;
+    const bool vd = VV > 1 && dst_al && perm_vec(p, 1) == VV;
+    if constexpr (VV > 1) {
+      if (vs && vd) {
+        k_tiles<B, VV, VV><<<grid, block, smem, s>>>(p, dst, src);
+      } else if (vs) {
+        k_tiles<B, VV, 1><<<grid, block, smem, s>>>(p, dst, src);
+      } else if (vd) {
+        k_tiles<B, 1, VV><<<grid, block, smem, s>>>(p, dst, src);
+      } else {
+        k_tiles<B, 1, 1><<<grid, block, smem, s>>>(p, dst, src);
+      }
+    } else {
+      k_tiles<B, 1, 1><<<grid, block, smem, s>>>(p, dst, src);
+    }
+  } else if (p.kind == kPermGeneric) {
+    k_generic<B><<<grid, block, 0, s>>>(p, dst, src);
+  }
+  return runtime::check_launch();
+}
+
+int launch_plan(const PermPlan& p, void* dst, const void* src, void* stream) {
+  if (p.kind == kPermEmpty) return T4A_OK;
+  t4a_launch l;
+  perm_geometry(p, &l);
+  const dim3 grid(l.grid[0]);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (p.esize) {
+    case 1: return launch_plan_sized<1>(p, dst, src, grid, l.shared_bytes, s);
+    case 4: return launch_plan_sized<4>(p, dst, src, grid, l.shared_bytes, s);
+    case 8: return launch_plan_sized<8>(p, dst, src, grid, l.shared_bytes, s);
+    case 16: return launch_plan_sized<16>(p, dst, src, grid, l.shared_bytes, s);
+    default: return T4A_ERR_UNSUPPORTED_DTYPE;
+  }
+}
+
+void compact_strides_host(const t4a_cuda_layout& l, long long* st) {
+  long long s = 1;
+  for (int d = 0; d < T4A_CUDA_MAX_RANK; ++d) {
+    st[d] = s;
+    if (d < l.rank) s *= l.extents[d];
+  }
+}
+
+PermPlan materialize_plan(int dtype, const t4a_cuda_layout& src) {
+  long long ds[T4A_CUDA_MAX_RANK];
+  compact_strides_host(src, ds);
+  return make_perm_plan(src.rank, src.extents, src.strides, ds, src.offset, 0, host_esize(dtype));
+}
+
+PermPlan view_plan(int dtype, const t4a_cuda_layout& dst) {
+  long long ss[T4A_CUDA_MAX_RANK];
+  compact_strides_host(dst, ss);
+  return make_perm_plan(dst.rank, dst.extents, ss, dst.strides, 0, dst.offset, host_esize(dtype));
+}
+
+PermPlan strided_plan(int dtype, const t4a_cuda_layout& src, const t4a_cuda_layout& dst) {
+  return make_perm_plan(src.rank, src.extents, src.strides, dst.strides, src.offset, dst.offset, host_esize(dtype));
+}
+
+PermPlan transpose_plan(int dtype, long long src_offset, long long batch_stride, long long m, long long n,
+                        long long batches) {
+  const long long ext[3] = {m, n, batches};
+  const long long ss[3] = {n, 1, batch_stride};
+  const long long ds[3] = {1, m, batch_stride};
+  return make_perm_plan(3, ext, ss, ds, src_offset, 0, host_esize(dtype));
+}
+
+PermPlan broadcast_plan(int dtype, const t4a_cuda_layout& out, const t4a_cuda_layout& in, const long long* dims,
+                        int ndims) {
+  long long ss[T4A_CUDA_MAX_RANK] = {0}, ds[T4A_CUDA_MAX_RANK];
+  compact_strides_host(out, ds);
+  for (int s = 0; s < ndims; ++s)
+    if (in.extents[s] != 1) ss[dims[s]] += in.strides[s];
+  return make_perm_plan(out.rank, out.extents, ss, ds, in.offset, 0, host_esize(dtype));
+}
+
+int check_dtype_move(int dtype) { return host_esize(dtype) ? T4A_OK : T4A_ERR_UNSUPPORTED_DTYPE; }
+
+}  // namespace
+}  // namespace t4a
+
+using namespace t4a;
+using namespace t4a::plan;
+
+extern "C" {
+
+// plan_materialize_strided (src/lib.rs:1630).
+int t4a_plan_materialize_strided(int dtype, const t4a_cuda_layout* src, long long src_len, t4a_launch* launch) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  T4A_TRY(check_dtype_move(dtype));
+  T4A_TRY(check_layout(src));
+  long long len;
+  T4A_TRY(element_count(*src, &len));
+  T4A_TRY(check_span(*src, src_len, host_esize(dtype)));
+  return perm_geometry(materialize_plan(dtype, *src), launch);
+}
+
+// plan_contiguous_to_view (src/lib.rs:1645).
+int t4a_plan_contiguous_to_view(int dtype, const t4a_cuda_layout* dst, long long dst_len, t4a_launch* launch) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  T4A_TRY(check_dtype_move(dtype));
+  T4A_TRY(check_layout(dst));
+  long long len;
+  T4A_TRY(element_count(*dst, &len));
+  T4A_TRY(require_destination(*dst));
+  T4A_TRY(check_span(*dst, dst_len, host_esize(dtype)));
+  return perm_geometry(view_plan(dtype, *dst), launch);
+}
+
+// plan_strided_to_strided (src/lib.rs:1660).
+int t4a_plan_strided_to_strided(int dtype, const t4a_cuda_layout* src, long long src_len,
+                                const t4a_cuda_layout* dst, long long dst_len, t4a_launch* launch) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  T4A_TRY(check_dtype_move(dtype));
+  T4A_TRY(check_layout(src));
+  T4A_TRY(check_layout(dst));
+  if (src->rank != dst->rank) return T4A_ERR_COUNT_MISMATCH;
+  for (int d = 0; d < src->rank; ++d)
+    if (src->extents[d] != dst->extents[d]) return T4A_ERR_COUNT_MISMATCH;
+  long long len;
+  T4A_TRY(element_count(*src, &len));
+  T4A_TRY(require_destination(*dst));
+  T4A_TRY(check_span(*src, src_len, host_esize(dtype)));
+  T4A_TRY(check_span(*dst, dst_len, host_esize(dtype)));
+  return perm_geometry(strided_plan(dtype, *src, *dst), launch);
+}
+
+// plan_copy_exact (src/lib.rs:1624).
+int t4a_plan_copy_exact(int dtype, long long len, t4a_launch* launch) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  T4A_TRY(check_dtype_move(dtype));
+  if (len < 0) return T4A_ERR_NEGATIVE_COUNT;
+  const long long one = 1;
+  return perm_geometry(make_perm_plan(1, &len, &one, &one, 0, 0, host_esize(dtype)), launch);
+}
+
+// plan_fill_zero (src/lib.rs:1601) / plan_fill_zero_view (:1609).
+int t4a_plan_fill_zero(int dtype, long long len, t4a_launch* launch) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  T4A_TRY(check_dtype_move(dtype));
+  if (len < 0) return T4A_ERR_NEGATIVE_COUNT;
+  if (len == 0) {
+    *launch = empty_launch();
+    return T4A_OK;
+  }
+  unsigned long long grid;
+  T4A_TRY(grid_of(len, kFlatBlock, &grid));
+  *launch = make_launch(grid, kFlatBlock, 1, 0, 0);
+  return T4A_OK;
+}
+
+int t4a_plan_fill_zero_view(int dtype, const t4a_cuda_layout* dst, long long dst_len, t4a_launch* launch) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  T4A_TRY(check_dtype_move(dtype));
+  T4A_TRY(check_layout(dst));
+  long long len;
+  T4A_TRY(element_count(*dst, &len));
+  T4A_TRY(require_destination(*dst));
+  T4A_TRY(check_span(*dst, dst_len, host_esize(dtype)));
+  return t4a_plan_fill_zero(dtype, len, launch);
+}
+
+// plan_tiled_transpose (src/lib.rs:1685): the grid's z dimension is the batch count.
+int t4a_plan_tiled_transpose(int dtype, t4a_cuda_transpose_config config, long long src_offset,
+                             long long batch_stride, long long dst_fast_extent, long long src_fast_extent,
+                             long long batches, long long src_len, long long dst_len, t4a_launch* launch) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  T4A_TRY(check_dtype_move(dtype));
+  const int t = config.tile, r = config.block_rows, pad = config.padding, v = config.vector_width;
+  if (!(t == 8 || t == 16 || t == 32) || !(r == 4 || r == 8 || r == 16) || pad < 0 || pad > 1 ||
+      !(v == 1 || v == 2 || v == 4) || t % v != 0)
+    return T4A_ERR_INVALID_TRANSPOSE_CONFIG;
+  if (dst_fast_extent < 0 || src_fast_extent < 0 || batches < 0 || src_offset < 0) return T4A_ERR_NEGATIVE_COUNT;
+  long long matrix, span, end;
+  if (mul_overflows(dst_fast_extent, src_fast_extent, &matrix)) return T4A_ERR_OVERFLOW;
+  if (batch_stride != matrix) return T4A_ERR_INVALID_TRANSPOSE_CONFIG;
+  if (mul_overflows(matrix, batches, &span)) return T4A_ERR_OVERFLOW;
+  if (add_overflows(src_offset, span, &end)) return T4A_ERR_OVERFLOW;
+  if (end > src_len || span > dst_len) return T4A_ERR_OFFSET_OUT_OF_SPAN;
+  if (static_cast<long long>(t) * (t + pad) * host_esize(dtype) > 48 * 1024) return T4A_ERR_LAUNCH_LIMIT;
+  if (ceil_div(dst_fast_extent, t) > kMaxGridX || ceil_div(src_fast_extent, t) > kMaxGridYZ ||
+      static_cast<unsigned long long>(batches) > kMaxGridYZ)
+    return T4A_ERR_LAUNCH_LIMIT;
+  if (matrix == 0 || batches == 0) {
+    *launch = empty_launch();
+    return T4A_OK;
+  }
+  const PermPlan p = transpose_plan(dtype, src_offset, batch_stride, dst_fast_extent, src_fast_extent, 1);
+  T4A_TRY(perm_geometry(p, launch));
+  launch->grid[2] = static_cast<unsigned>(batches);
+  return T4A_OK;
+}
+
+// plan_broadcast_in_dim (src/lib.rs:1498).
+int t4a_plan_broadcast_in_dim(int dtype, const t4a_cuda_layout* out, long long out_len, const t4a_cuda_layout* in,
+                              long long in_len, const long long* dims, int ndims, t4a_launch* launch) {
+  if (launch == nullptr || (ndims > 0 && dims == nullptr)) return T4A_ERR_NULL_ARGUMENT;
+  T4A_TRY(check_dtype_move(dtype));
+  T4A_TRY(check_layout(out));
+  T4A_TRY(check_layout(in));
+  T4A_TRY(require_compact(*out));
+  T4A_TRY(require_destination(*out));
+  if (ndims != in->rank) return T4A_ERR_RANK_LENGTH;
+  bool seen[T4A_CUDA_MAX_RANK] = {false};
+  for (int s = 0; s < ndims; ++s) {
+    if (dims[s] < 0 || dims[s] >= out->rank) return T4A_ERR_INVALID_AXIS;
+    if (seen[dims[s]]) return T4A_ERR_DUPLICATE_AXIS;
+    seen[dims[s]] = true;
+    if (in->extents[s] != out->extents[dims[s]] && in->extents[s] != 1) return T4A_ERR_SHAPE_MISMATCH;
+  }
+  long long len;
+  T4A_TRY(element_count(*out, &len));
+  T4A_TRY(check_span(*in, in_len, host_esize(dtype)));
+  T4A_TRY(check_span(*out, out_len, host_esize(dtype)));
+  return perm_geometry(broadcast_plan(dtype, *out, *in, dims, ndims), launch);
+}
+
+// ---- launchers: the argument lists of the kernel symbols ----------------------
+
+int t4a_launch_materialize_strided(const t4a_launch* launch, void* stream, void* dst, const void* src, int dtype,
+                                   t4a_cuda_layout src_layout, long long len) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  (void)len;
+  T4A_TRY(check_dtype_move(dtype));
+  return launch_plan(materialize_plan(dtype, src_layout), dst, src, stream);
+}
+
+int t4a_launch_contiguous_to_view(const t4a_launch* launch, void* stream, void* dst, const void* src, int dtype,
+                                  t4a_cuda_layout dst_layout, long long len) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  (void)len;
+  T4A_TRY(check_dtype_move(dtype));
+  return launch_plan(view_plan(dtype, dst_layout), dst, src, stream);
+}
+
+int t4a_launch_strided_to_strided(const t4a_launch* launch, void* stream, void* dst, const void* src, int dtype,
+                                  t4a_cuda_layout src_layout, t4a_cuda_layout dst_layout, long long len) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  (void)len;
+  T4A_TRY(check_dtype_move(dtype));
+  return launch_plan(strided_plan(dtype, src_layout, dst_layout), dst, src, stream);
+}
+
+int t4a_launch_copy_exact(const t4a_launch* launch, void* stream, void* dst, const void* src, int dtype,
+                          long long len) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  T4A_TRY(check_dtype_move(dtype));
+  const long long one = 1;
+  return launch_plan(make_perm_plan(1, &len, &one, &one, 0, 0, host_esize(dtype)), dst, src, stream);
+}
+
+int t4a_launch_tiled_transpose(const t4a_launch* launch, void* stream, void* dst, const void* src, int dtype,
+                               long long src_offset, long long batch_stride, long long dst_fast_extent,
+                               long long src_fast_extent, t4a_cuda_transpose_config config) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  (void)config;
+  T4A_TRY(check_dtype_move(dtype));
+  if (launch->grid[0] == 0 || launch->grid[2] == 0) return T4A_OK;
+  const long long batches = launch->grid[2];
+  return launch_plan(transpose_plan(dtype, src_offset, batch_stride, dst_fast_extent, src_fast_extent, batches),
+                     dst, src, stream);
+}
+
+int t4a_launch_broadcast_in_dim(const t4a_launch* launch, void* stream, void* out, const void* in, int dtype,
+                                t4a_cuda_layout out_layout, t4a_cuda_layout in_layout, t4a_cuda_axis_values dims,
+                                long long out_len) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  (void)out_len;
+  T4A_TRY(check_dtype_move(dtype));
+  return launch_plan(broadcast_plan(dtype, out_layout, in_layout, dims.values, dims.rank), out, in, stream);
+}
+
+int t4a_launch_fill_zero(const t4a_launch* launch, void* stream, void* out, int dtype, long long len) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  if (launch->grid[0] == 0) return T4A_OK;
+  t4a_cuda_layout none;
+  std::memset(&none, 0, sizeof(none));
+  const dim3 grid(launch->grid[0]), block(launch->block[0]);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (host_esize(dtype)) {
+    case 1: k_zero<1><<<grid, block, 0, s>>>(out, none, len, false); break;
+    case 4: k_zero<4><<<grid, block, 0, s>>>(out, none, len, false); break;
+    case 8: k_zero<8><<<grid, block, 0, s>>>(out, none, len, false); break;
+    case 16: k_zero<16><<<grid, block, 0, s>>>(out, none, len, false); break;
+    default: return T4A_ERR_UNSUPPORTED_DTYPE;
+  }
+  return runtime::check_launch();
+}
+
+int t4a_launch_fill_zero_view(const t4a_launch* launch, void* stream, void* out, int dtype, t4a_cuda_layout layout,
+                              long long len) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  if (launch->grid[0] == 0) return T4A_OK;
+  const dim3 grid(launch->grid[0]), block(launch->block[0]);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (host_esize(dtype)) {
+    case 1: k_zero<1><<<grid, block, 0, s>>>(out, layout, len, true); break;
+    case 4: k_zero<4><<<grid, block, 0, s>>>(out, layout, len, true); break;
+    case 8: k_zero<8><<<grid, block, 0, s>>>(out, layout, len, true); break;
+    case 16: k_zero<16><<<grid, block, 0, s>>>(out, layout, len, true); break;
+    default: return T4A_ERR_UNSUPPORTED_DTYPE;
+  }
+  return runtime::check_launch();
+}
+
+// One call: validate and copy between two layouts of the same extents.
+int t4a_copy_strided(void* stream, int dtype, void* dst, const t4a_cuda_layout* dst_layout, long long dst_len,
+                     const void* src, const t4a_cuda_layout* src_layout, long long src_len) {
+  if (dst == nullptr || src == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  t4a_launch launch;
+  T4A_TRY(t4a_plan_strided_to_strided(dtype, src_layout, src_len, dst_layout, dst_len, &launch));
+  long long len;
+  T4A_TRY(element_count(*src_layout, &len));
+  return t4a_launch_strided_to_strided(&launch, stream, dst, src, dtype, *src_layout, *dst_layout, len);
+}
+
+}  // extern "C"

@@ -1,0 +1,188 @@
+// Per-path reduction kernels and the host launchers of the reduction entries.
+//
+// The exported symbols (reduce_abi.cu) choose their path at run time, so one register
+// allocation serves every path.  The launchers here launch one kernel per path
+// instead (t4a_launch.variant, chosen by the planner), each compiled for its own
+// register budget.  All of them fold with the same device bodies (reduce_core.cuh),
+// so both routes produce the same bits.
+#include <cuda_runtime.h>
+
+#include "plan_common.h"
+#include "reduce_core.cuh"
+#include "runtime.h"
+
+namespace t4a {
+namespace {
+
+template <typename Op, typename T>
+__global__ void __launch_bounds__(256) k_strided(T* dst, const T* in, t4a_cuda_layout dst_l,
+                                                 t4a_cuda_layout in_l, int axis, long long splits,
+                                                 long long chunk, bool partials) {
+  constexpr int V = VecOf<T>::kLanes;
+  strided_tiles<Op, T, V, 4>(in, dst, in_l, dst_l, strided_ctx(in_l, axis, splits, chunk, V, partials), Op());
+}
+
+template <typename Op, typename T>
+__global__ void __launch_bounds__(256) k_cubes(T* dst, const T* in, t4a_cuda_layout dst_l, t4a_cuda_layout in_l,
+                                               int axis, long long outputs, long long splits, long long chunk,
+                                               bool partials) {
+  plane_cubes<Op, T>(in, dst, in_l, dst_l, axis, outputs, splits, chunk, blockDim.x, partials, partials, Op());
+}
+
+template <typename Op, typename T>
+__global__ void __launch_bounds__(256) k_unit_rows(T* out, const T* in, t4a_cuda_layout out_l, t4a_cuda_layout in_l,
+                                                   long long outputs, int rows) {
+  unit_rows<Op, T>(in, out, out_l, in_l, outputs, rows, Op());
+}
+
+template <typename Op, typename T>
+__global__ void __launch_bounds__(256) k_unit(T* out, const T* in, t4a_cuda_layout out_l, t4a_cuda_layout in_l,
+                                              int axis, long long outputs) {
+  unit_generic<Op, T>(in, out, out_l, in_l, axis, outputs, Op());
+}
+
+template <typename Op, typename T>
+__global__ void __launch_bounds__(512) k_wide(T* out, const T* in, t4a_cuda_layout out_l, t4a_cuda_layout in_l,
+                                              int axis, long long outputs) {
+  wide_plane<Op, T>(in, out, out_l, in_l, axis, outputs, Op());
+}
+
+struct PassArgs {
+  void* dst;
+  const void* in;
+  t4a_cuda_layout dst_l;
+  t4a_cuda_layout in_l;
+  int axis;
+  long long outputs;
+  long long splits;
+  long long chunk;
+  bool partials;
+};
+
+template <typename Op, typename T>
+void launch_path(int path, dim3 grid, dim3 block, unsigned smem, cudaStream_t stream, const PassArgs& a) {
+  T* dst = static_cast<T*>(a.dst);
+  const T* in = static_cast<const T*>(a.in);
+  switch (path) {
+    case kPathStrided:
+      k_strided<Op, T><<<grid, block, smem, stream>>>(dst, in, a.dst_l, a.in_l, a.axis, a.splits, a.chunk, a.partials);
+      break;
+    case kPathUnitRows: {
+      const int rows = unit_rows_per_tile(a.in_l, a.axis, sizeof(T));
+      k_unit_rows<Op, T><<<grid, block, smem, stream>>>(dst, in, a.dst_l, a.in_l, a.outputs, rows);
+      break;
+    }
+    case kPathUnit:
+      k_unit<Op, T><<<grid, block, smem, stream>>>(dst, in, a.dst_l, a.in_l, a.axis, a.outputs);
+      break;
+    case kPathWide:
+      k_wide<Op, T><<<grid, block, smem, stream>>>(dst, in, a.dst_l, a.in_l, a.axis, a.outputs);
+      break;
+    default:
+      k_cubes<Op, T><<<grid, block, smem, stream>>>(dst, in, a.dst_l, a.in_l, a.axis, a.outputs, a.splits,
+                                                    a.chunk, a.partials);
+      break;
+  }
+}
+
+// A 16-byte-vector path needs a 16-byte-aligned base; otherwise the same pass runs on
+// the per-cube path, whose geometry is recomputed here.
+bool fix_alignment(int dtype, const void* in, int* path, dim3* grid, dim3* block, unsigned* smem,
+                   const PassArgs& a) {
+  if (*path != kPathStrided || strided_vec_lanes(dtype) == 1) return true;
+  const int esize = plan::dtype_size(dtype);
+  if (((reinterpret_cast<unsigned long long>(in) + a.in_l.offset * esize) & 15ull) == 0 &&
+      (reinterpret_cast<unsigned long long>(in) & 15ull) == 0)
+    return true;
+  const unsigned w = 32;
+  *path = kPathCubes;
+  *block = dim3(w, kTileThreads / w, 1);
+  *smem = 0;
+  const unsigned long long grid_x = plan::ceil_div(static_cast<unsigned long long>(a.outputs) * a.splits, kTileThreads / w);
+  if (grid_x > plan::kMaxGridX) return false;
+  *grid = dim3(static_cast<unsigned>(grid_x), 1, 1);
+  return true;
+}
+
+int run_pass(const t4a_launch* launch, void* stream, int dtype, int op, PassArgs a) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  if (launch->grid[0] == 0 || launch->grid[1] == 0 || launch->grid[2] == 0) return T4A_OK;
+  int path = launch->variant;
+  dim3 grid(launch->grid[0], launch->grid[1], launch->grid[2]);
+  dim3 block(launch->block[0], launch->block[1], launch->block[2]);
+  unsigned smem = launch->shared_bytes;
+  if (!fix_alignment(dtype, a.in, &path, &grid, &block, &smem, a)) return T4A_ERR_LAUNCH_LIMIT;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (smem > 48 * 1024) {
+    // Not reached by the planner's geometry (at most 32 KiB); kept explicit.
+    return T4A_ERR_LAUNCH_LIMIT;
+  }
+#define T4A_CALL(OP, T) launch_path<OP, T>(path, grid, block, smem, s, a)
+  T4A_REDUCE_SWITCH(op, dtype, T4A_CALL)
+#undef T4A_CALL
+  return runtime::check_launch();
+}
+
+}  // namespace
+}  // namespace t4a
+
+using namespace t4a;
+
+extern "C" {
+
+int t4a_launch_reduce(const t4a_launch* launch, void* stream, void* out, const void* in, int dtype, int op,
+                      int strategy, t4a_cuda_layout out_layout, t4a_cuda_layout in_layout, int axis,
+                      long long output_len) {
+  (void)strategy;  // carried by the launch's path
+  PassArgs a{out, in, out_layout, in_layout, axis, output_len, 1, in_layout.extents[axis], false};
+  return run_pass(launch, stream, dtype, op, a);
+}
+
+int t4a_launch_reduce_partials(const t4a_launch* launch, void* stream, void* partials, const void* in,
+                               int dtype, int op, t4a_cuda_layout partials_layout, t4a_cuda_layout in_layout,
+                               int axis, long long output_len, long long splits, long long chunk_len) {
+  PassArgs a{partials, in, partials_layout, in_layout, axis, output_len, splits, chunk_len, true};
+  return run_pass(launch, stream, dtype, op, a);
+}
+
+int t4a_reduce_workspace_bytes(int dtype, int op, const t4a_cuda_layout* out, long long out_len,
+                               const t4a_cuda_layout* in, long long in_len, unsigned axis, unsigned w,
+                               size_t* bytes) {
+  if (bytes == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  t4a_reduction_plan plan;
+  T4A_TRY(t4a_plan_reduction(dtype, op, out, out_len, in, in_len, axis, w, &plan));
+  *bytes = 0;
+  if (!plan.is_split) return T4A_OK;
+  t4a_cuda_layout partials;
+  T4A_TRY(t4a_reduction_partials_layout(in, axis, plan.split.splits, &partials));
+  long long count;
+  T4A_TRY(plan::element_count(partials, &count));
+  *bytes = static_cast<size_t>(count) * plan::dtype_size(dtype);
+  return T4A_OK;
+}
+
+int t4a_reduce(void* stream, int dtype, int op, void* out, const t4a_cuda_layout* out_layout, long long out_len,
+               const void* in, const t4a_cuda_layout* in_layout, long long in_len, unsigned axis, unsigned w,
+               void* workspace, size_t workspace_bytes) {
+  if (out == nullptr || in == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  t4a_reduction_plan plan;
+  T4A_TRY(t4a_plan_reduction(dtype, op, out_layout, out_len, in_layout, in_len, axis, w, &plan));
+  long long outputs;
+  T4A_TRY(plan::element_count(*out_layout, &outputs));
+  if (!plan.is_split) {
+    return t4a_launch_reduce(&plan.launch, stream, out, in, dtype, op, plan.strategy, *out_layout, *in_layout,
+                             static_cast<int>(axis), outputs);
+  }
+  t4a_cuda_layout partials;
+  T4A_TRY(t4a_reduction_partials_layout(in_layout, axis, plan.split.splits, &partials));
+  long long count;
+  T4A_TRY(plan::element_count(partials, &count));
+  const size_t need = static_cast<size_t>(count) * plan::dtype_size(dtype);
+  if (workspace == nullptr || workspace_bytes < need) return T4A_ERR_WORKSPACE;
+  T4A_TRY(t4a_launch_reduce_partials(&plan.pass1, stream, workspace, in, dtype, op, partials, *in_layout,
+                                     static_cast<int>(axis), outputs, plan.split.splits, plan.split.chunk_len));
+  return t4a_launch_reduce(&plan.pass2, stream, out, workspace, dtype, plan.combine_op, plan.combine_strategy,
+                           *out_layout, partials, static_cast<int>(axis), outputs);
+}
+
+}  // extern "C"

@@ -1,0 +1,197 @@
+"""Python mirror of the t4a_b200 C ABI (include/t4a_b200.h).
+
+Host-side counterpart of the reference's Rust facade (`t4a_cuda_kernels::plan_*`,
+reference src/lib.rs): planners that validate metadata and return launch geometry,
+launchers that run this library's sm_100a kernels on the caller's stream, and
+one-call helpers over torch tensors.  Every call goes through libt4a_b200.so; there
+is no CPU or PyTorch fallback, and a missing library raises at import of `lib()`.
+"""
+import ctypes
+import os
+
+from . import abi
+from .abi import (F32, F64, I32, I64, BOOL, C32, C64, SUM, PROD, SUM_SQUARES, MAX, MIN, UNIT, PLANE,
+                  Layout, layout, numpy_layout)
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "lib", "libt4a_b200.so")
+MODULE_DIR = os.path.join(HERE, "lib")
+
+_LIB = None
+
+
+class T4AError(RuntimeError):
+    """A planner refusal or launch failure; `status` is the t4a_status code."""
+
+    def __init__(self, status, where=""):
+        self.status = status
+        msg = status_string(status) if _LIB is not None else str(status)
+        super().__init__(f"{where}: {msg} (status {status})" if where else f"{msg} (status {status})")
+
+
+class Launch(ctypes.Structure):
+    _fields_ = [("grid", ctypes.c_uint * 3), ("block", ctypes.c_uint * 3),
+                ("shared_bytes", ctypes.c_uint), ("variant", ctypes.c_int)]
+
+    def is_empty(self):
+        return 0 in tuple(self.grid)
+
+    def __repr__(self):
+        return (f"Launch(grid={tuple(self.grid)}, block={tuple(self.block)}, "
+                f"shared_bytes={self.shared_bytes}, variant={self.variant})")
+
+
+class Split(ctypes.Structure):
+    _fields_ = [("splits", ctypes.c_longlong), ("chunk_len", ctypes.c_longlong)]
+
+
+class ReductionPlan(ctypes.Structure):
+    _fields_ = [("is_split", ctypes.c_int), ("strategy", ctypes.c_int), ("launch", Launch),
+                ("split", Split), ("pass1", Launch), ("combine_strategy", ctypes.c_int),
+                ("combine_op", ctypes.c_int), ("pass2", Launch)]
+
+
+def lib():
+    """The loaded libt4a_b200.so.  Raises when it has not been built."""
+    global _LIB
+    if _LIB is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"libt4a_b200.so is not built ({LIB_PATH}); run t4a-cuda-kernels_b200/build.py")
+        _LIB = ctypes.CDLL(LIB_PATH)
+        _declare(_LIB)
+    return _LIB
+
+
+def _declare(l):
+    P, I, U, LL, SZ = ctypes.c_void_p, ctypes.c_int, ctypes.c_uint, ctypes.c_longlong, ctypes.c_size_t
+    LP = ctypes.POINTER(Layout)
+    LB = Layout  # by value
+    sig = {
+        "t4a_status_string": (ctypes.c_char_p, [I]),
+        "t4a_abi_revision": (I, []),
+        "t4a_last_cuda_error": (I, []),
+        "t4a_split_policy": (I, [LL, U, ctypes.POINTER(I), ctypes.POINTER(Split)]),
+        "t4a_plan_reduce": (I, [I, I, I, LP, LL, LP, LL, U, U, ctypes.POINTER(Launch)]),
+        "t4a_plan_reduce_partials": (I, [I, I, LP, LL, LP, LL, U, Split, U, ctypes.POINTER(Launch)]),
+        "t4a_plan_reduction": (I, [I, I, LP, LL, LP, LL, U, U, ctypes.POINTER(ReductionPlan)]),
+        "t4a_reduction_partials_layout": (I, [LP, U, LL, LP]),
+        "t4a_launch_reduce": (I, [ctypes.POINTER(Launch), P, P, P, I, I, I, LB, LB, I, LL]),
+        "t4a_launch_reduce_partials": (I, [ctypes.POINTER(Launch), P, P, P, I, I, LB, LB, I, LL, LL, LL]),
+        "t4a_reduce_workspace_bytes": (I, [I, I, LP, LL, LP, LL, U, U, ctypes.POINTER(SZ)]),
+        "t4a_reduce": (I, [P, I, I, P, LP, LL, P, LP, LL, U, U, P, SZ]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(l, name, None)
+        if fn is None:
+            continue
+        fn.restype = res
+        fn.argtypes = args
+    _declare_more(l)
+
+
+_EXTRA_DECLS = []
+
+
+def _declare_more(l):
+    for decl in _EXTRA_DECLS:
+        decl(l)
+
+
+def status_string(status):
+    return lib().t4a_status_string(status).decode()
+
+
+def check(status, where=""):
+    if status != 0:
+        raise T4AError(status, where)
+
+
+# ---- torch interop ------------------------------------------------------------
+
+def torch_dtype_tag(t):
+    import torch
+    return {torch.float32: F32, torch.float64: F64, torch.int32: I32, torch.int64: I64,
+            torch.bool: BOOL, torch.uint8: BOOL, torch.complex64: C32, torch.complex128: C64}[t.dtype]
+
+
+def tensor_layout(t):
+    """Layout of a torch tensor relative to its data_ptr (NumPy axes reversed)."""
+    return numpy_layout(list(t.shape), list(t.stride()), 0)
+
+
+def span(t):
+    """Elements reachable from data_ptr for a non-negative-stride tensor (the span length)."""
+    if t.numel() == 0:
+        return 0
+    return 1 + sum((e - 1) * s for e, s in zip(t.shape, t.stride()))
+
+
+def stream_handle(stream=None):
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+# ---- reductions (reference src/lib.rs:3033-3557) ----------------------------------
+
+def split_policy(reduce_len, plane_width=32):
+    has = ctypes.c_int()
+    sp = Split()
+    check(lib().t4a_split_policy(reduce_len, plane_width, ctypes.byref(has), ctypes.byref(sp)), "split_policy")
+    return sp if has.value else None
+
+
+def plan_reduction(dtype, op, out_layout, out_len, in_layout, in_len, axis, plane_width=32):
+    plan = ReductionPlan()
+    check(lib().t4a_plan_reduction(dtype, op, ctypes.byref(out_layout), out_len, ctypes.byref(in_layout),
+                                   in_len, axis, plane_width, ctypes.byref(plan)), "plan_reduction")
+    return plan
+
+
+def plan_reduce(dtype, op, strategy, out_layout, out_len, in_layout, in_len, axis, plane_width=32):
+    launch = Launch()
+    check(lib().t4a_plan_reduce(dtype, op, strategy, ctypes.byref(out_layout), out_len, ctypes.byref(in_layout),
+                                in_len, axis, plane_width, ctypes.byref(launch)), "plan_reduce")
+    return launch
+
+
+def reduction_partials_layout(in_layout, axis, splits):
+    out = Layout()
+    check(lib().t4a_reduction_partials_layout(ctypes.byref(in_layout), axis, splits, ctypes.byref(out)),
+          "reduction_partials_layout")
+    return out
+
+
+def reduce_workspace_bytes(dtype, op, out_layout, out_len, in_layout, in_len, axis, plane_width=32):
+    n = ctypes.c_size_t()
+    check(lib().t4a_reduce_workspace_bytes(dtype, op, ctypes.byref(out_layout), out_len, ctypes.byref(in_layout),
+                                           in_len, axis, plane_width, ctypes.byref(n)), "reduce_workspace_bytes")
+    return n.value
+
+
+def reduce_raw(stream, dtype, op, out_ptr, out_layout, out_len, in_ptr, in_layout, in_len, axis, plane_width=32,
+               workspace_ptr=None, workspace_bytes=0):
+    check(lib().t4a_reduce(stream, dtype, op, out_ptr, ctypes.byref(out_layout), out_len, in_ptr,
+                           ctypes.byref(in_layout), in_len, axis, plane_width, workspace_ptr, workspace_bytes),
+          "reduce")
+
+
+def reduce(inp, axis, op=SUM, plane_width=32, out=None, workspace=None, stream=None):
+    """Keepdims reduction of a CUDA tensor along NumPy axis `axis`."""
+    import torch
+    nd = inp.dim()
+    ref_axis = nd - 1 - axis
+    if out is None:
+        shape = list(inp.shape)
+        shape[axis] = 1
+        out = torch.empty(shape, dtype=inp.dtype, device=inp.device)
+    dtype = torch_dtype_tag(inp)
+    il, ol = tensor_layout(inp), tensor_layout(out)
+    n_in, n_out = span(inp), span(out)
+    need = reduce_workspace_bytes(dtype, op, ol, n_out, il, n_in, ref_axis, plane_width)
+    if need and (workspace is None or workspace.numel() * workspace.element_size() < need):
+        workspace = torch.empty(need, dtype=torch.uint8, device=inp.device)
+    reduce_raw(stream_handle(stream), dtype, op, ctypes.c_void_p(out.data_ptr()), ol, n_out,
+               ctypes.c_void_p(inp.data_ptr()), il, n_in, ref_axis, plane_width,
+               ctypes.c_void_p(workspace.data_ptr()) if need else None, need)
+    return out

@@ -1,0 +1,163 @@
+"""Device-free tests of the C++ planner behind the C ABI (libt4a_b200.so).
+
+The validation rules and the numerical-topology choices are the reference
+planner's; these cases restate the reference's own planning tests
+(tests/planning.rs:698-1100).  Launch geometry is this library's and is checked
+for consistency (non-empty, within limits), not against the reference's numbers.
+"""
+import ctypes
+import glob
+import os
+import re
+
+import pytest
+
+import t4a_b200 as t4
+from t4a_b200 import abi
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    names = set()
+    for path in glob.glob(os.path.join(ROOT, "include", "**", "*.h"), recursive=True):
+        text = open(path).read()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        for m in re.finditer(r"^[A-Za-z_][\w \*]*?\b(t4a_\w+)\s*\(", text, flags=re.M):
+            names.add(m.group(1))
+    return names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = t4.lib()
+    names = declared_symbols()
+    assert len(names) >= 12
+    missing = [n for n in sorted(names) if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_abi_revision_and_status_strings():
+    assert t4.lib().t4a_abi_revision() == 14
+    assert t4.status_string(0) == "ok"
+    assert "plane width" in t4.status_string(22)
+
+
+def reduced(extents, axis):
+    out = list(extents)
+    out[axis] = 1
+    return abi.layout(extents), abi.layout(out)
+
+
+def status_of(fn, *args):
+    try:
+        fn(*args)
+    except t4.T4AError as e:
+        return e.status
+    return 0
+
+
+def test_split_policy_matches_the_reference_table():
+    sp = t4.split_policy
+    assert sp(255) is None and sp(256) is None
+    assert (sp(512).splits, sp(512).chunk_len) == (2, 256)
+    assert (sp(513).splits, sp(513).chunk_len) == (2, 256)
+    assert (sp(1000).splits, sp(1000).chunk_len) == (3, 333)
+    assert (sp(8448).splits, sp(8448).chunk_len) == (33, 256)
+    capped = sp(10_000_000)
+    assert (capped.splits, capped.chunk_len) == (4096, 10_000_000 // 4096)
+    assert (sp(256, 16).splits, sp(256, 16).chunk_len) == (2, 128)
+    assert (sp(255, 8).splits, sp(255, 8).chunk_len) == (3, 85)
+    assert sp(0) is None
+    assert status_of(sp, 512, 0) == 22
+
+
+def test_strategy_boundary_is_the_plane_width():
+    inp, out = reduced([32, 3], 0)
+    assert status_of(t4.plan_reduce, abi.F32, abi.SUM, abi.UNIT, out, 3, inp, 96, 0, 32) == 0
+    assert status_of(t4.plan_reduce, abi.F32, abi.SUM, abi.PLANE, out, 3, inp, 96, 0, 32) == 0
+    inp, out = reduced([31, 3], 0)
+    assert status_of(t4.plan_reduce, abi.F32, abi.SUM, abi.PLANE, out, 3, inp, 93, 0, 32) == 21
+    inp, out = reduced([33, 3], 0)
+    assert status_of(t4.plan_reduce, abi.F32, abi.SUM, abi.UNIT, out, 3, inp, 99, 0, 32) == 21
+    assert status_of(t4.plan_reduce, abi.F32, abi.SUM, abi.PLANE, out, 3, inp, 99, 0, 32) == 0
+    assert status_of(t4.plan_reduce, abi.F32, abi.SUM, abi.PLANE, out, 3, inp, 99, 0, 24) == 22
+
+
+def test_reduction_shapes_are_validated():
+    inp, _ = reduced([4, 64], 1)
+    assert status_of(t4.plan_reduce, abi.F32, abi.SUM, abi.PLANE, abi.layout([4]), 4, inp, 256, 1, 32) == 2
+    assert status_of(t4.plan_reduce, abi.F32, abi.SUM, abi.PLANE, abi.layout([5, 1]), 5, inp, 256, 1, 32) == 16
+    zin, zout = reduced([4, 0], 1)
+    assert status_of(t4.plan_reduce, abi.F32, abi.SUM, abi.UNIT, zout, 4, zin, 0, 1, 32) == 4
+    ein, eout = reduced([0, 64], 1)
+    assert t4.plan_reduce(abi.F32, abi.SUM, abi.PLANE, eout, 0, ein, 0, 1, 32).is_empty()
+    # Spans: an input allocation one element short is refused.
+    inp, out = reduced([64, 4], 0)
+    assert status_of(t4.plan_reduce, abi.F32, abi.SUM, abi.PLANE, out, 4, inp, 255, 0, 32) == 7
+    # A broadcast destination axis is refused.
+    bad_out = abi.layout([1, 4], [1, 0])
+    assert status_of(t4.plan_reduce, abi.F32, abi.SUM, abi.PLANE, bad_out, 4, inp, 256, 0, 32) == 8
+    assert status_of(t4.plan_reduce, abi.F32, abi.SUM, abi.PLANE, out, 4, inp, 256, 2, 32) == 13
+
+
+def test_dtype_gates_follow_the_operation():
+    inp, out = reduced([64, 2], 0)
+    assert status_of(t4.plan_reduce, abi.C64, abi.MAX, abi.PLANE, out, 2, inp, 128, 0, 32) == 9
+    assert status_of(t4.plan_reduce, abi.I32, abi.SUM_SQUARES, abi.PLANE, out, 2, inp, 128, 0, 32) == 9
+    assert status_of(t4.plan_reduce, abi.C64, abi.PROD, abi.PLANE, out, 2, inp, 128, 0, 32) == 0
+    assert status_of(t4.plan_reduce, abi.BOOL, abi.SUM, abi.PLANE, out, 2, inp, 128, 0, 32) == 9
+
+
+def test_auto_policy():
+    inp, out = reduced([64, 4], 0)
+    plan = t4.plan_reduction(abi.F64, abi.SUM, out, 4, inp, 256, 0)
+    assert plan.is_split == 0 and plan.strategy == abi.PLANE and not plan.launch.is_empty()
+    inp, out = reduced([512, 4], 0)
+    plan = t4.plan_reduction(abi.F64, abi.SUM, out, 4, inp, 2048, 0)
+    assert plan.is_split == 1 and (plan.split.splits, plan.split.chunk_len) == (2, 256)
+    assert plan.combine_strategy == abi.UNIT and plan.combine_op == abi.SUM
+    inp, out = reduced([8448, 2], 0)
+    plan = t4.plan_reduction(abi.F32, abi.SUM_SQUARES, out, 2, inp, 16896, 0)
+    assert plan.split.splits == 33 and plan.combine_strategy == abi.PLANE and plan.combine_op == abi.SUM
+    # Many partials widen the combine block unless the op is PROD.
+    inp, out = reduced([65536 * 8, 1], 0)
+    plan = t4.plan_reduction(abi.F32, abi.SUM, out, 1, inp, 65536 * 8, 0)
+    assert plan.split.splits == 2048 and plan.pass2.block[0] == 256
+    plan = t4.plan_reduction(abi.F32, abi.PROD, out, 1, inp, 65536 * 8, 0)
+    assert plan.pass2.block[0] == 32
+
+
+def test_partials_plans_enforce_the_floor_split():
+    inp, _ = reduced([512, 4], 0)
+    partials = abi.layout([2, 4])
+
+    def plan(splits, chunk):
+        launch = t4.Launch()
+        return t4.lib().t4a_plan_reduce_partials(abi.F32, abi.SUM, ctypes.byref(partials), 8, ctypes.byref(inp),
+                                                 2048, 0, t4.Split(splits, chunk), 32, ctypes.byref(launch))
+
+    assert plan(2, 256) == 0
+    assert plan(64, 1) == 23
+    assert plan(2, 255) == 23
+    assert plan(1, 512) == 23
+
+
+def test_partials_layout_is_compact_with_the_split_axis():
+    inp = abi.layout([4096, 4096, 32][::-1])
+    p = t4.reduction_partials_layout(inp, 2, 16)
+    assert p.extents_list() == [32, 4096, 16] and p.strides_list() == [1, 32, 131072]
+
+
+@pytest.mark.parametrize("numpy_axis", [0, 1, 2])
+def test_config3_reductions_plan_the_coalesced_paths(numpy_axis):
+    shape = [4096, 4096, 32]
+    inp = abi.numpy_layout(shape)
+    out_shape = list(shape)
+    out_shape[numpy_axis] = 1
+    out = abi.numpy_layout(out_shape)
+    axis = 2 - numpy_axis
+    plan = t4.plan_reduction(abi.F32, abi.SUM, out, out.count(), inp, inp.count(), axis)
+    if numpy_axis == 2:
+        assert plan.is_split == 0 and plan.strategy == abi.UNIT and plan.launch.variant == 18
+    else:
+        assert plan.is_split == 1 and plan.split.splits == 16 and plan.pass1.variant == 17
