@@ -150,6 +150,58 @@ int t4a_reduce(void* stream, int dtype, int op, void* out, const t4a_cuda_layout
                long long out_len, const void* in, const t4a_cuda_layout* in_layout, long long in_len,
                unsigned axis, unsigned plane_width, void* workspace, size_t workspace_bytes);
 
+
+/* ------------------------------------------------------------------------- */
+/* Strided movement (reference src/lib.rs:1465-1737, movement.cu:514-656)      */
+/* Every planner validates like its reference counterpart; the launch carries  */
+/* this library's path (variant 32 + kind) and geometry.                        */
+/* ------------------------------------------------------------------------- */
+
+/* plan_materialize_strided (src/lib.rs:1630): compact dst <- strided src. */
+int t4a_plan_materialize_strided(int dtype, const t4a_cuda_layout* src, long long src_len, t4a_launch* launch);
+/* plan_contiguous_to_view (src/lib.rs:1645): strided dst <- compact src. */
+int t4a_plan_contiguous_to_view(int dtype, const t4a_cuda_layout* dst, long long dst_len, t4a_launch* launch);
+/* plan_strided_to_strided (src/lib.rs:1660): both layouts share the extents. */
+int t4a_plan_strided_to_strided(int dtype, const t4a_cuda_layout* src, long long src_len,
+                                const t4a_cuda_layout* dst, long long dst_len, t4a_launch* launch);
+/* plan_copy_exact (src/lib.rs:1624), plan_fill_zero (:1601), plan_fill_zero_view (:1609). */
+int t4a_plan_copy_exact(int dtype, long long len, t4a_launch* launch);
+int t4a_plan_fill_zero(int dtype, long long len, t4a_launch* launch);
+int t4a_plan_fill_zero_view(int dtype, const t4a_cuda_layout* dst, long long dst_len, t4a_launch* launch);
+/* plan_tiled_transpose (src/lib.rs:1685): dst[b*S + i + j*M] = src[src_offset + b*S + i*N + j],
+ * M = dst_fast_extent, N = src_fast_extent; grid[2] is the batch count. */
+int t4a_plan_tiled_transpose(int dtype, t4a_cuda_transpose_config config, long long src_offset,
+                             long long batch_stride, long long dst_fast_extent, long long src_fast_extent,
+                             long long batches, long long src_len, long long dst_len, t4a_launch* launch);
+/* plan_broadcast_in_dim (src/lib.rs:1498): dims[s] is the destination axis of input axis s. */
+int t4a_plan_broadcast_in_dim(int dtype, const t4a_cuda_layout* out, long long out_len,
+                              const t4a_cuda_layout* in, long long in_len, const long long* dims, int ndims,
+                              t4a_launch* launch);
+
+/* Launchers with the argument lists of movement.cu:535, :544, :553, :528, :571, :648, :514 and
+ * fill_zero_view (:519). */
+int t4a_launch_materialize_strided(const t4a_launch* launch, void* stream, void* dst, const void* src, int dtype,
+                                   t4a_cuda_layout src_layout, long long len);
+int t4a_launch_contiguous_to_view(const t4a_launch* launch, void* stream, void* dst, const void* src, int dtype,
+                                  t4a_cuda_layout dst_layout, long long len);
+int t4a_launch_strided_to_strided(const t4a_launch* launch, void* stream, void* dst, const void* src, int dtype,
+                                  t4a_cuda_layout src_layout, t4a_cuda_layout dst_layout, long long len);
+int t4a_launch_copy_exact(const t4a_launch* launch, void* stream, void* dst, const void* src, int dtype,
+                          long long len);
+int t4a_launch_tiled_transpose(const t4a_launch* launch, void* stream, void* dst, const void* src, int dtype,
+                               long long src_offset, long long batch_stride, long long dst_fast_extent,
+                               long long src_fast_extent, t4a_cuda_transpose_config config);
+int t4a_launch_broadcast_in_dim(const t4a_launch* launch, void* stream, void* out, const void* in, int dtype,
+                                t4a_cuda_layout out_layout, t4a_cuda_layout in_layout, t4a_cuda_axis_values dims,
+                                long long out_len);
+int t4a_launch_fill_zero(const t4a_launch* launch, void* stream, void* out, int dtype, long long len);
+int t4a_launch_fill_zero_view(const t4a_launch* launch, void* stream, void* out, int dtype, t4a_cuda_layout layout,
+                              long long len);
+
+/* One call: validate (as t4a_plan_strided_to_strided) and copy. */
+int t4a_copy_strided(void* stream, int dtype, void* dst, const t4a_cuda_layout* dst_layout, long long dst_len,
+                     const void* src, const t4a_cuda_layout* src_layout, long long src_len);
+
 #ifdef __cplusplus
 }
 #endif

@@ -27,9 +27,26 @@ COMMON = ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC", "-I", os.path
 MODULE_TUS = ["reduce_abi.cu", "movement_abi.cu", "gather_scatter_abi.cu", "rrqr_abi.cu"]
 
 
-def headers():
-    return glob.glob(os.path.join(CSRC, "*.h")) + glob.glob(os.path.join(CSRC, "*.cuh")) + \
-        glob.glob(os.path.join(ROOT, "include", "**", "*.h"), recursive=True)
+def headers(src=None):
+    """Headers `src` includes, transitively (quoted includes only); all when src is None."""
+    if src is None:
+        return glob.glob(os.path.join(CSRC, "*.h")) + glob.glob(os.path.join(CSRC, "*.cuh")) + \
+            glob.glob(os.path.join(ROOT, "include", "**", "*.h"), recursive=True)
+    seen, todo = set(), [src]
+    while todo:
+        path = todo.pop()
+        try:
+            text = open(path).read()
+        except OSError:
+            continue
+        for line in text.splitlines():
+            line = line.strip()
+            if line.startswith("#include \""):
+                dep = os.path.normpath(os.path.join(os.path.dirname(path), line.split('"')[1]))
+                if dep not in seen:
+                    seen.add(dep)
+                    todo.append(dep)
+    return sorted(seen)
 
 
 def stale(target, sources):
@@ -50,7 +67,7 @@ def run(cmd):
 def compile_one(src, force):
     name = os.path.basename(src)
     obj = os.path.join(BUILD, name + ".o")
-    if force or stale(obj, [src] + headers()):
+    if force or stale(obj, [src] + headers(src)):
         run([NVCC] + COMMON + ARCH + ["-c", src, "-o", obj])
     return obj
 
@@ -58,7 +75,7 @@ def compile_one(src, force):
 def module_one(src, force):
     name = os.path.basename(src)
     cubin = os.path.join(LIBDIR, name.replace("_abi.cu", ".cubin"))
-    if force or stale(cubin, [src] + headers()):
+    if force or stale(cubin, [src] + headers(src)):
         run([NVCC, "-std=c++17", "-O3", "-lineinfo", "-I", os.path.join(ROOT, "include"), "-cubin",
              "-gencode", "arch=compute_100a,code=sm_100a", src, "-o", cubin])
     return cubin
@@ -71,8 +88,10 @@ def build(jobs=8, force=False):
     module_sources = [os.path.join(CSRC, n) for n in MODULE_TUS if os.path.exists(os.path.join(CSRC, n))]
     lib_sources = [s for s in sources if os.path.basename(s) not in MODULE_TUS]
     with concurrent.futures.ThreadPoolExecutor(max_workers=jobs) as pool:
-        objs = list(pool.map(lambda s: compile_one(s, force), lib_sources))
-        cubins = list(pool.map(lambda s: module_one(s, force), module_sources))
+        obj_futures = [pool.submit(compile_one, s, force) for s in lib_sources]
+        cubin_futures = [pool.submit(module_one, s, force) for s in module_sources]
+        objs = [f.result() for f in obj_futures]
+        [f.result() for f in cubin_futures]
     lib = os.path.join(LIBDIR, "libt4a_b200.so")
     if force or stale(lib, objs):
         run([NVCC, "-shared"] + ARCH + ["-o", lib] + objs + ["-lcudart"])

@@ -107,31 +107,44 @@ T4A_HD PermPlan make_perm_plan(int rank, const long long* ext_in, const long lon
     p.kind = kPermEmpty;
     return p;
   }
-  // 2. The destination-contiguous chain (D) and the source-contiguous chain (S).
+  // 2. The source-contiguous chain (S) and the destination-contiguous chain (D).
+  //    When the fastest axes differ, the two runs of a tile must stay disjoint.
   bool in_d[T4A_CUDA_MAX_RANK] = {false, false, false, false, false, false, false, false};
   bool in_s[T4A_CUDA_MAX_RANK] = {false, false, false, false, false, false, false, false};
   int dchain[T4A_CUDA_MAX_RANK], schain[T4A_CUDA_MAX_RANK];
   int nd = 0, ns = 0;
   long long want = 1;
-  for (bool grew = true; grew && nd < n;) {
-    grew = false;
-    for (int i = 0; i < n; ++i) {
-      if (!in_d[i] && d[i] == want) {
-        in_d[i] = true;
-        dchain[nd++] = i;
-        want *= e[i];
-        grew = true;
-        break;
-      }
-    }
-  }
-  want = 1;
   for (bool grew = true; grew && ns < n;) {
     grew = false;
     for (int i = 0; i < n; ++i) {
       if (!in_s[i] && s[i] == want) {
         in_s[i] = true;
         schain[ns++] = i;
+        want *= e[i];
+        grew = true;
+        break;
+      }
+    }
+  }
+  // The shortest prefix of the S chain that fills a tile edge is reserved for the S
+  // run; the D chain stops at any reserved axis.
+  const long long edge = esize >= 16 ? 32 : 64;
+  bool reserved[T4A_CUDA_MAX_RANK] = {false, false, false, false, false, false, false, false};
+  {
+    long long filled = 1;
+    for (int k = 0; k < ns && filled < edge; ++k) {
+      reserved[schain[k]] = true;
+      filled *= e[schain[k]];
+    }
+  }
+  want = 1;
+  for (bool grew = true; grew && nd < n;) {
+    grew = false;
+    for (int i = 0; i < n; ++i) {
+      if (!in_d[i] && d[i] == want) {
+        if (nd > 0 && reserved[i]) break;
+        in_d[i] = true;
+        dchain[nd++] = i;
         want *= e[i];
         grew = true;
         break;

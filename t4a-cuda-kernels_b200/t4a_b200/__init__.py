@@ -79,6 +79,23 @@ def _declare(l):
         "t4a_launch_reduce_partials": (I, [ctypes.POINTER(Launch), P, P, P, I, I, LB, LB, I, LL, LL, LL]),
         "t4a_reduce_workspace_bytes": (I, [I, I, LP, LL, LP, LL, U, U, ctypes.POINTER(SZ)]),
         "t4a_reduce": (I, [P, I, I, P, LP, LL, P, LP, LL, U, U, P, SZ]),
+        "t4a_plan_materialize_strided": (I, [I, LP, LL, ctypes.POINTER(Launch)]),
+        "t4a_plan_contiguous_to_view": (I, [I, LP, LL, ctypes.POINTER(Launch)]),
+        "t4a_plan_strided_to_strided": (I, [I, LP, LL, LP, LL, ctypes.POINTER(Launch)]),
+        "t4a_plan_copy_exact": (I, [I, LL, ctypes.POINTER(Launch)]),
+        "t4a_plan_fill_zero": (I, [I, LL, ctypes.POINTER(Launch)]),
+        "t4a_plan_fill_zero_view": (I, [I, LP, LL, ctypes.POINTER(Launch)]),
+        "t4a_plan_tiled_transpose": (I, [I, abi.TransposeConfig, LL, LL, LL, LL, LL, LL, LL, ctypes.POINTER(Launch)]),
+        "t4a_plan_broadcast_in_dim": (I, [I, LP, LL, LP, LL, ctypes.POINTER(LL), I, ctypes.POINTER(Launch)]),
+        "t4a_launch_materialize_strided": (I, [ctypes.POINTER(Launch), P, P, P, I, LB, LL]),
+        "t4a_launch_contiguous_to_view": (I, [ctypes.POINTER(Launch), P, P, P, I, LB, LL]),
+        "t4a_launch_strided_to_strided": (I, [ctypes.POINTER(Launch), P, P, P, I, LB, LB, LL]),
+        "t4a_launch_copy_exact": (I, [ctypes.POINTER(Launch), P, P, P, I, LL]),
+        "t4a_launch_tiled_transpose": (I, [ctypes.POINTER(Launch), P, P, P, I, LL, LL, LL, LL, abi.TransposeConfig]),
+        "t4a_launch_broadcast_in_dim": (I, [ctypes.POINTER(Launch), P, P, P, I, LB, LB, abi.AxisValues, LL]),
+        "t4a_launch_fill_zero": (I, [ctypes.POINTER(Launch), P, P, I, LL]),
+        "t4a_launch_fill_zero_view": (I, [ctypes.POINTER(Launch), P, P, I, LB, LL]),
+        "t4a_copy_strided": (I, [P, I, P, LP, LL, P, LP, LL]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(l, name, None)
@@ -194,4 +211,56 @@ def reduce(inp, axis, op=SUM, plane_width=32, out=None, workspace=None, stream=N
     reduce_raw(stream_handle(stream), dtype, op, ctypes.c_void_p(out.data_ptr()), ol, n_out,
                ctypes.c_void_p(inp.data_ptr()), il, n_in, ref_axis, plane_width,
                ctypes.c_void_p(workspace.data_ptr()) if need else None, need)
+    return out
+
+
+# ---- strided movement (reference src/lib.rs:1465-1737) -----------------------------
+
+def _plan(fn, *args):
+    launch = Launch()
+    check(getattr(lib(), fn)(*args, ctypes.byref(launch)), fn)
+    return launch
+
+
+def plan_materialize_strided(dtype, src_layout, src_len):
+    return _plan("t4a_plan_materialize_strided", dtype, ctypes.byref(src_layout), src_len)
+
+
+def plan_strided_to_strided(dtype, src_layout, src_len, dst_layout, dst_len):
+    return _plan("t4a_plan_strided_to_strided", dtype, ctypes.byref(src_layout), src_len, ctypes.byref(dst_layout),
+                 dst_len)
+
+
+def plan_contiguous_to_view(dtype, dst_layout, dst_len):
+    return _plan("t4a_plan_contiguous_to_view", dtype, ctypes.byref(dst_layout), dst_len)
+
+
+def plan_tiled_transpose(dtype, config, src_offset, batch_stride, dst_fast_extent, src_fast_extent, batches,
+                         src_len, dst_len):
+    return _plan("t4a_plan_tiled_transpose", dtype, config, src_offset, batch_stride, dst_fast_extent,
+                 src_fast_extent, batches, src_len, dst_len)
+
+
+def plan_broadcast_in_dim(dtype, out_layout, out_len, in_layout, in_len, dims):
+    arr = (ctypes.c_longlong * max(1, len(dims)))(*dims)
+    return _plan("t4a_plan_broadcast_in_dim", dtype, ctypes.byref(out_layout), out_len, ctypes.byref(in_layout),
+                 in_len, arr, len(dims))
+
+
+def copy_strided_raw(stream, dtype, dst_ptr, dst_layout, dst_len, src_ptr, src_layout, src_len):
+    check(lib().t4a_copy_strided(stream, dtype, dst_ptr, ctypes.byref(dst_layout), dst_len, src_ptr,
+                                 ctypes.byref(src_layout), src_len), "copy_strided")
+
+
+def materialize(view, out=None, stream=None):
+    """Compact copy of a (permuted, sliced, expanded) CUDA tensor view."""
+    import torch
+    if out is None:
+        out = torch.empty(view.shape, dtype=view.dtype, device=view.device)
+    dtype = torch_dtype_tag(view)
+    base = view.storage_offset()
+    src_l = numpy_layout(list(view.shape), list(view.stride()), 0)
+    src_len = view.untyped_storage().nbytes() // view.element_size() - base
+    copy_strided_raw(stream_handle(stream), dtype, ctypes.c_void_p(out.data_ptr()), tensor_layout(out), span(out),
+                     ctypes.c_void_p(view.data_ptr()), src_l, src_len)
     return out
