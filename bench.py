@@ -11,8 +11,8 @@ plan).  Inputs are seeded normal(0,1) values (synthetic; no dataset is involved)
 `value` is the algorithmic HBM traffic (each element read once and written once)
 per second of kernel time, summed over all ranks; each rank copies its own full
 workload (weak scaling, no collective: the movement ops shard by independent
-tensors).  L2 is flushed between steps (a 256 MiB write, outside the timed events),
-so every step streams from HBM.
+tensors).  L2 is flushed before every op (a 256 MiB read, outside the timed events),
+so every kernel streams from HBM and starts without another kernel's dirty lines.
 
 `--op` selects another BASELINE config as the workload (reduce, gather, scatter,
 rrqr) for the secondary lines; the driver's runs use the default.
@@ -205,8 +205,15 @@ class MovementWorkload:
 WORKLOADS = {"movement": MovementWorkload}
 
 
+def torch_int64():
+    import torch
+    return torch.int64
+
+
 def flush_l2(buf):
-    buf.zero_()
+    """Evict the working set from L2 by reading a buffer larger than L2 (clean lines, so
+    nothing is written back during the next timed op)."""
+    buf.sum(dtype=torch_int64())
 
 
 def run_ours(args, rank, world, local_rank):
@@ -214,10 +221,13 @@ def run_ours(args, rank, world, local_rank):
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     wl = WORKLOADS[args.op](device)
+    if args.only:
+        keep = set(args.only.split(","))
+        wl.ops = [op for op in wl.ops if op["tag"] in keep]
     t4 = wl.t4
     stream = torch.cuda.current_stream()
     sh = ctypes.c_void_p(stream.cuda_stream)
-    flush = torch.empty(256 * MIB, dtype=torch.uint8, device=device)
+    flush = torch.ones(256 * MIB, dtype=torch.uint8, device=device)
     dist = world > 1
 
     def barrier():
@@ -238,12 +248,15 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     wall0 = time.perf_counter()
     with sampler:
+        # Hold the stream with a bounded sleep kernel while the timed steps are enqueued,
+        # so each event pair brackets GPU work only, not the host's launch latency.
+        torch.cuda._sleep(int(2e8))
         for k in range(args.steps):
             for j, op in enumerate(wl.ops):
+                flush_l2(flush)
                 events[k][j][0].record(stream)
                 wl.run_op(op, sh)
                 events[k][j][1].record(stream)
-            flush_l2(flush)
         torch.cuda.synchronize()
     barrier()
     wall = time.perf_counter() - wall0
@@ -259,8 +272,8 @@ def run_ours(args, rank, world, local_rank):
 
     # End to end through the public API: pinned host inputs -> device -> op -> host.
     e2e_ms = None
-    h2d = sum(h.numel() * h.element_size() for h in wl.host_in)
-    d2h = sum(h.numel() * h.element_size() for h in wl.host_out)
+    h2d = sum(wl.host_in[op["i"]].numel() * wl.host_in[op["i"]].element_size() for op in wl.ops)
+    d2h = sum(wl.host_out[op["i"]].numel() * wl.host_out[op["i"]].element_size() for op in wl.ops)
     barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -308,7 +321,7 @@ def run_ours(args, rank, world, local_rank):
         "dtype": wl.dtype,
         "data": "synthetic (seeded normal(0,1), SplitMix64 Box-Muller)",
         "config": {"workload": wl.name, "ops": [op["tag"] for op in wl.ops],
-                   "bytes_per_step_per_gpu": wl.units(), "l2": "flushed between steps (256 MiB write, untimed)",
+                   "bytes_per_step_per_gpu": wl.units(), "l2": "flushed before every op (256 MiB read, untimed)",
                    "parallelism": f"replicas x{world}" if world > 1 else "1 gpu",
                    "timing": "CUDA events per op on the launching stream, max over ranks"},
         "roofline": {"bound": "hbm", "kernel": dom_op["tag"], "achieved": round(achieved, 1), "peak": peak,
@@ -389,6 +402,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--op", default="movement", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only", default=None, help="comma-separated op tags of the workload to run (profiling)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
 

@@ -23,7 +23,7 @@ __device__ __forceinline__ int move_esize(int dtype) {
 }
 
 __device__ __forceinline__ void run_plan(const PermPlan& p, void* dst, const void* src) {
-  const bool smem_ok = move_dynamic_smem() >= static_cast<unsigned>(perm_smem_bytes(p));
+  const bool smem_ok = move_dynamic_smem() >= static_cast<unsigned>(perm_smem_bytes(p, block_threads()));
   switch (p.esize) {
     case 1: perm_run<1>(p, dst, src, smem_ok); break;
     case 4: perm_run<4>(p, dst, src, smem_ok); break;

@@ -10,17 +10,37 @@
 namespace t4a {
 namespace {
 
-template <int B, int V>
+template <int B, int V, bool A16, bool AFF>
 __global__ void __launch_bounds__(256) k_rows(PermPlan p, void* dst, const void* src) {
   using E = typename Elem<B>::T;
-  perm_rows<E, V>(p, static_cast<E*>(dst), static_cast<const E*>(src));
+  perm_rows<E, V, A16, AFF>(p, static_cast<E*>(dst), static_cast<const E*>(src));
 }
 
-template <int B, int VS, int VD>
-__global__ void __launch_bounds__(256) k_tiles(PermPlan p, void* dst, const void* src) {
+template <int B, bool VS, bool VD, bool AFF>
+__global__ void __launch_bounds__(256, 4) k_tiles(PermPlan p, void* dst, const void* src) {
   using E = typename Elem<B>::T;
-  constexpr int EDGE = B >= 16 ? 32 : 64;
-  perm_tiles<E, VS, VD, EDGE>(p, static_cast<E*>(dst), static_cast<const E*>(src));
+  perm_tiles<E, VS, VD, AFF>(p, static_cast<E*>(dst), static_cast<const E*>(src));
+}
+
+// Launch a rows/tiles kernel variant with the plan's affine choice.
+template <int B, int V, bool A16>
+void launch_rows(bool aff, dim3 grid, dim3 block, unsigned smem, cudaStream_t s, const PermPlan& p, void* dst,
+                 const void* src) {
+  if (aff) {
+    k_rows<B, V, A16, true><<<grid, block, smem, s>>>(p, dst, src);
+  } else {
+    k_rows<B, V, A16, false><<<grid, block, smem, s>>>(p, dst, src);
+  }
+}
+
+template <int B, bool VS, bool VD>
+void launch_tiles(bool aff, dim3 grid, dim3 block, unsigned smem, cudaStream_t s, const PermPlan& p, void* dst,
+                  const void* src) {
+  if (aff) {
+    k_tiles<B, VS, VD, true><<<grid, block, smem, s>>>(p, dst, src);
+  } else {
+    k_tiles<B, VS, VD, false><<<grid, block, smem, s>>>(p, dst, src);
+  }
 }
 
 template <int B>
@@ -52,14 +72,16 @@ int perm_geometry(const PermPlan& p, t4a_launch* launch) {
     *launch = empty_launch();
     return T4A_OK;
   }
+  // Rows and tiles are per-warp units (8 warps per block); generic is per thread.
   unsigned long long units = 0;
+  constexpr unsigned long long kWarpsPerBlock = kPermThreads / 32;
   if (p.kind == kPermRows) {
-    const long long seg = p.run.len < kPermRowsBytes / p.esize ? p.run.len : kPermRowsBytes / p.esize;
-    const long long rows = kPermRowsBytes / p.esize / seg;
-    units = ceil_div(p.rest.len, rows) * ceil_div(p.run.len, seg);
+    const PermRowsShape shape = perm_rows_shape(p, perm_rows_vec(p));
+    units = ceil_div(ceil_div(p.rest.len, shape.rows) * ceil_div(p.run.len, shape.seg), kWarpsPerBlock);
   } else if (p.kind == kPermTiles) {
-    const long long edge = perm_tile_edge(p.esize);
-    units = static_cast<unsigned long long>(p.rest.len) * ceil_div(p.run.len, edge) * ceil_div(p.srun.len, edge);
+    units = ceil_div(static_cast<unsigned long long>(p.rest.len) * ceil_div(p.run.len, warp_tile_d(p.esize)) *
+                         ceil_div(p.srun.len, warp_tile_s(p.esize)),
+                     kWarpsPerBlock);
   } else {
     units = ceil_div(p.len, kPermThreads);
   }
@@ -74,29 +96,31 @@ int launch_plan_sized(const PermPlan& p, void* dst, const void* src, dim3 grid, 
   const bool src_al = (reinterpret_cast<unsigned long long>(src) & 15ull) == 0;
   const bool dst_al = (reinterpret_cast<unsigned long long>(dst) & 15ull) == 0;
   const dim3 block(kPermThreads);
+  const bool rows_vec = VV > 1 && src_al && dst_al && perm_vec(p, 0) == VV && perm_vec(p, 1) == VV;
+  const bool aff = perm_affine(p, rows_vec ? VV : 1);
   if (p.kind == kPermRows) {
     if constexpr (VV > 1) {
-      if (src_al && dst_al && perm_vec(p, 0) == VV && perm_vec(p, 1) == VV) {
-        k_rows<B, VV><<<grid, block, smem, s>>>(p, dst, src);
+      if (rows_vec) {
+        launch_rows<B, VV, true>(aff, grid, block, smem, s, p, dst, src);
         return runtime::check_launch();
       }
     }
-    k_rows<B, 1><<<grid, block, smem, s>>>(p, dst, src);
-  } else if (p.kind == kPermTiles) {
-    const bool vs = VV > 1 && src_al && perm_vec(p, 0) == VV;
-    const bool vd = VV > 1 && dst_al && perm_vec(p, 1) == VV;
-    if constexpr (VV > 1) {
-      if (vs && vd) {
-        k_tiles<B, VV, VV><<<grid, block, smem, s>>>(p, dst, src);
-      } else if (vs) {
-        k_tiles<B, VV, 1><<<grid, block, smem, s>>>(p, dst, src);
-      } else if (vd) {
-        k_tiles<B, 1, VV><<<grid, block, smem, s>>>(p, dst, src);
-      } else {
-        k_tiles<B, 1, 1><<<grid, block, smem, s>>>(p, dst, src);
-      }
+    if (B == 16 && src_al && dst_al) {
+      launch_rows<B, 1, true>(aff, grid, block, smem, s, p, dst, src);
     } else {
-      k_tiles<B, 1, 1><<<grid, block, smem, s>>>(p, dst, src);
+      launch_rows<B, 1, false>(aff, grid, block, smem, s, p, dst, src);
+    }
+  } else if (p.kind == kPermTiles) {
+    const bool vs = src_al && (VV == 1 || perm_vec(p, 0) == VV);
+    const bool vd = dst_al && (VV == 1 || perm_vec(p, 1) == VV);
+    if (vs && vd) {
+      launch_tiles<B, true, true>(aff, grid, block, smem, s, p, dst, src);
+    } else if (vs) {
+      launch_tiles<B, true, false>(aff, grid, block, smem, s, p, dst, src);
+    } else if (vd) {
+      launch_tiles<B, false, true>(aff, grid, block, smem, s, p, dst, src);
+    } else {
+      launch_tiles<B, false, false>(aff, grid, block, smem, s, p, dst, src);
     }
   } else if (p.kind == kPermGeneric) {
     k_generic<B><<<grid, block, 0, s>>>(p, dst, src);

@@ -222,10 +222,66 @@ T4A_HD int perm_vec(const PermPlan& p, int side) {
   return 1;
 }
 
-// Tile shape of kPermTiles: kTileD positions of the D run x kTileS of the S run.
-T4A_HD int perm_tile_edge(int esize) { return esize >= 16 ? 32 : 64; }
+// Warp-tile shape of kPermTiles (4 KiB per warp): S positions per tile and D positions
+// per tile for an element size.
+T4A_HD int warp_tile_s(int esize) { return esize == 1 ? 64 : (esize >= 16 ? 16 : 32); }
+T4A_HD int warp_tile_d(int esize) { return 4096 / esize / warp_tile_s(esize); }
 
 constexpr int kPermThreads = 256;
-constexpr int kPermRowsBytes = 16384;  // bytes per block tile of the rows path
+constexpr int kPermRowsBytes = 4096;   // bytes per (warp) work unit of the rows path
+constexpr int kPermRowsMax = 32;       // rows per unit: one per lane
 
+struct PermRowsShape {
+  long long seg;  // run elements per unit: chunks * V, chunks a power of two
+  int lv;         // log2 of the chunks per unit row
+  int rows;       // rows per unit, a power of two
+};
+
+// Unit shape of the rows path for chunks of `v` elements (v divides the run when v > 1):
+// a power-of-two number of chunks per row segment and of rows, about 4 KiB in all.
+T4A_HD PermRowsShape perm_rows_shape(const PermPlan& p, int v) {
+  PermRowsShape s;
+  const long long run_chunks = p.run.len / v;
+  long long cap = kPermRowsBytes / (v * p.esize);  // chunks per unit
+  if (cap < 1) cap = 1;
+  const long long want = run_chunks < cap ? run_chunks : cap;
+  int lv = 0;
+  while ((2LL << lv) <= want) ++lv;
+  s.lv = lv;
+  s.seg = (1LL << lv) * v;
+  long long rows = cap >> lv;
+  if (rows > kPermRowsMax) rows = kPermRowsMax;
+  int r = 1;
+  while (2 * r <= rows) r *= 2;
+  s.rows = r;
+  return s;
+}
+
+// Vector width (elements) of the rows path for 16-byte-aligned pointers.
+T4A_HD int perm_rows_vec(const PermPlan& p);
+
+// Offsets of T consecutive flat indices f0 + i (f0 a multiple of T) of a group on one
+// side are linear, i * s0, when axis 0 alone holds the span (e0 a multiple of T) or
+// the group is empty.  `ok` is false otherwise (decode every index).
+struct AffineSpan {
+  bool ok;
+  long long s0;
+};
+
+T4A_HD AffineSpan affine_span(const PermGroup& g, int side, long long t) {
+  AffineSpan a;
+  a.ok = g.n == 0 || g.ext[0] % t == 0;
+  a.s0 = g.n == 0 ? 0 : (side == 0 ? g.ss[0] : g.ds[0]);
+  return a;
+}
+
+T4A_HD long long affine_at(const AffineSpan& a, int i) { return i * a.s0; }
+
+}  // namespace t4a
+
+namespace t4a {
+T4A_HD int perm_rows_vec(const PermPlan& p) {
+  const int v = p.esize >= 16 ? 1 : 16 / p.esize;
+  return (v > 1 && perm_vec(p, 0) == v && perm_vec(p, 1) == v) ? v : 1;
+}
 }  // namespace t4a
