@@ -150,6 +150,20 @@ int t4a_reduce(void* stream, int dtype, int op, void* out, const t4a_cuda_layout
                long long out_len, const void* in, const t4a_cuda_layout* in_layout, long long in_len,
                unsigned axis, unsigned plane_width, void* workspace, size_t workspace_bytes);
 
+/* Bytes of device memory the library keeps per GPU for t4a_reduce_noalloc. */
+#define T4A_REDUCE_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+/* No counterpart in the reference.  t4a_reduce for callers that cannot allocate
+ * device memory or hand over a workspace: the pass-1 partials go to an array of
+ * T4A_REDUCE_NOALLOC_SCRATCH_BYTES that the library's module holds on every GPU that
+ * loads it.  Allocates nothing.  Returns T4A_ERR_WORKSPACE when the partials would
+ * not fit that array.  The first call on a device looks the array up (make it before
+ * any stream capture); all calls on a device share the array, so calls that may
+ * overlap on the GPU race on it. */
+int t4a_reduce_noalloc(void* stream, int dtype, int op, void* out, const t4a_cuda_layout* out_layout,
+                       long long out_len, const void* in, const t4a_cuda_layout* in_layout, long long in_len,
+                       unsigned axis, unsigned plane_width);
+
 
 /* ------------------------------------------------------------------------- */
 /* Strided movement (reference src/lib.rs:1465-1737, movement.cu:514-656)      */
