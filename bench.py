@@ -125,21 +125,106 @@ class ClockSampler:
 # (tag, algorithmic bytes, launch(stream), host_inputs, device_inputs, device_outputs).
 # ---------------------------------------------------------------------------
 
-def splitmix_normal(seed, count, dtype):
-    """Seeded normal(0,1) values (Box-Muller over a counter-based SplitMix64 stream)."""
+def gen_device():
+    """A GPU to generate inputs on when one is visible (the reference arm times only host
+    work), else None."""
+    import torch
+    return torch.device("cuda", 0) if torch.cuda.is_available() else None
+
+
+def _splitmix_bits(seed, start, count):
+    """Draws start+1 .. start+count of a SplitMix64 stream from state `seed` (counter-based)."""
     import numpy as np
     with np.errstate(over="ignore"):
-        k = np.arange(1, 2 * count + 1, dtype=np.uint64)
+        k = np.arange(start + 1, start + count + 1, dtype=np.uint64)
         z = np.uint64(seed) + k * np.uint64(0x9E3779B97F4A7C15)
         z = (z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
         z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
-        z = z ^ (z >> np.uint64(31))
-    u = ((z >> np.uint64(11)).astype(np.float64) + 0.5) * (1.0 / (1 << 53))
-    u1, u2 = u[0::2], u[1::2]
-    return (np.sqrt(-2.0 * np.log(u1)) * np.cos(2 * np.pi * u2)).astype(dtype)
+        return z ^ (z >> np.uint64(31))
 
 
-class MovementWorkload:
+def _srl(z, n):
+    """Logical right shift of an int64 tensor holding uint64 bits."""
+    return (z >> n) & ((1 << (64 - n)) - 1)
+
+
+def _i64(x):
+    return x - (1 << 64) if x >= 1 << 63 else x
+
+
+def _splitmix_bits_torch(seed, start, count, device):
+    import torch
+    k = torch.arange(start + 1, start + count + 1, dtype=torch.int64, device=device)
+    z = _i64(seed) + k * _i64(0x9E3779B97F4A7C15)
+    z = (z ^ _srl(z, 30)) * _i64(0xBF58476D1CE4E5B9)
+    z = (z ^ _srl(z, 27)) * _i64(0x94D049BB133111EB)
+    return z ^ _srl(z, 31)
+
+
+def gen_normal(seed, count, np_dtype, device=None, chunk=1 << 24):
+    """Seeded normal(0,1) values: Box-Muller over a SplitMix64 stream (draws 2i, 2i+1
+    make value i).  On `device` when given (torch int64 arithmetic wraps like uint64),
+    else with NumPy; both produce the same values.  Returns a CPU torch tensor."""
+    import numpy as np
+    import torch
+    if device is None or not torch.cuda.is_available():
+        out = np.empty(count, dtype=np_dtype)
+        for lo in range(0, count, chunk):
+            n = min(chunk, count - lo)
+            z = _splitmix_bits(seed, 2 * lo, 2 * n)
+            u = ((z >> np.uint64(11)).astype(np.float64) + 0.5) * (1.0 / (1 << 53))
+            out[lo:lo + n] = np.sqrt(-2.0 * np.log(u[0::2])) * np.cos(2 * np.pi * u[1::2])
+        return torch.from_numpy(out)
+    tdt = {np.float32: torch.float32, np.float64: torch.float64}[np_dtype]
+    out = torch.empty(count, dtype=tdt)
+    for lo in range(0, count, chunk):
+        n = min(chunk, count - lo)
+        z = _splitmix_bits_torch(seed, 2 * lo, 2 * n, device)
+        u = (_srl(z, 11).double() + 0.5) * (1.0 / (1 << 53))
+        v = torch.sqrt(-2.0 * torch.log(u[0::2])) * torch.cos(2 * np.pi * u[1::2])
+        out[lo:lo + n] = v.to(tdt).cpu()
+    return out
+
+
+def gen_uniform(seed, count, np_dtype, device=None, chunk=1 << 24):
+    """Seeded uniform(-1,1) values on a 2^-52 grid: (next >> 11) * 2^-52 - 1."""
+    import numpy as np
+    import torch
+    if device is None or not torch.cuda.is_available():
+        out = np.empty(count, dtype=np_dtype)
+        for lo in range(0, count, chunk):
+            n = min(chunk, count - lo)
+            z = _splitmix_bits(seed, lo, n)
+            out[lo:lo + n] = (z >> np.uint64(11)).astype(np.float64) * (1.0 / (1 << 52)) - 1.0
+        return torch.from_numpy(out)
+    tdt = {np.float32: torch.float32, np.float64: torch.float64}[np_dtype]
+    out = torch.empty(count, dtype=tdt)
+    for lo in range(0, count, chunk):
+        n = min(chunk, count - lo)
+        z = _splitmix_bits_torch(seed, lo, n, device)
+        out[lo:lo + n] = (_srl(z, 11).double() * (1.0 / (1 << 52)) - 1.0).to(tdt).cpu()
+    return out
+
+
+class Workload:
+    """Shared defaults: one input tensor (host_in[i] -> dev_in[i]) and one output
+    (dev_out[j] -> host_out[j]) per op; the CPU leg runs the whole step."""
+
+    def e2e_inputs(self, op):
+        return [(self.host_in[op["i"]], self.dev_in[op["i"]])]
+
+    def e2e_outputs(self, op):
+        j = op.get("j", op["i"])
+        return [(self.dev_out[j], self.host_out[j])]
+
+    def cpu_units(self):
+        return self.units()
+
+    def cpu_sample(self):
+        return f"the full {self.name} step"
+
+
+class MovementWorkload(Workload):
     name = "config2-permutation-movement"
     dtype = "f32,c64"
 
@@ -150,14 +235,13 @@ class MovementWorkload:
         from t4a_b200 import abi
         self.t4, self.abi = t4, abi
         self.device = device
-        a = splitmix_normal(2, 64 ** 4, np.float32)
-        re = splitmix_normal(3, 16 ** 6, np.float64)
-        im = splitmix_normal(3 + 1000, 16 ** 6, np.float64)
-        b = np.empty(16 ** 6, dtype=np.complex128)
-        b.real, b.imag = re, im
-        c = splitmix_normal(4, 64 ** 4, np.float32)
+        gdev = device if device is not None else gen_device()
+        a = gen_normal(2, 64 ** 4, np.float32, gdev)
+        b = torch.stack([gen_normal(3, 16 ** 6, np.float64, gdev), gen_normal(3 + 1000, 16 ** 6, np.float64, gdev)],
+                        dim=1).reshape(-1)  # interleaved (re, im)
+        c = gen_normal(4, 64 ** 4, np.float32, gdev)
         pin = device is not None
-        host = [torch.from_numpy(a), torch.from_numpy(b.view(np.float64)), torch.from_numpy(c)]
+        host = [a, b, c]
         self.host_in = [h.pin_memory() for h in host] if pin else host
         self.host_out = [torch.empty_like(h).pin_memory() if pin else torch.empty_like(h) for h in host]
         if device is not None:
@@ -191,8 +275,9 @@ class MovementWorkload:
         self.t4.copy_strided_raw(stream_handle, op["dtype"], ctypes.c_void_p(dst.data_ptr()), op["dst_l"], op["n"],
                                  ctypes.c_void_p(src.data_ptr()), op["src_l"], op["n"])
 
-    def cpu_op(self, op, threads, host_src, host_dst):
+    def cpu_op(self, op, threads, srcs, dsts):
         oracle = _oracle()
+        host_src, host_dst = srcs[op["i"]], dsts[op["i"]]
         rc = oracle.lib().t4a_oracle_strided_to_strided(op["dtype"], oracle.ptr(host_dst), oracle.ptr(host_src),
                                                         ctypes.byref(op["src_l"]), ctypes.byref(op["dst_l"]), threads)
         assert rc == 0
@@ -202,7 +287,215 @@ class MovementWorkload:
 
 
 
-WORKLOADS = {"movement": MovementWorkload}
+class ReduceWorkload(Workload):
+    """BASELINE configs[2] (and configs[0]): single-axis reductions.
+
+    F32 [4096,4096,32] normal(0,1): sum, sum_squares and max over each NumPy axis; C64
+    [8192,8192] sum over axis 1; F64 [256,1024,64] uniform(-1,1) sum and max over axis 1.
+    Each op is one whole reduction (t4a_reduce: pass 1 + combine, or a direct pass)."""
+
+    name = "config3-reduction-sweep+config1"
+    dtype = "f32,f64,c64"
+
+    def __init__(self, device=None):
+        import numpy as np
+        import torch
+        import t4a_b200 as t4
+        from t4a_b200 import abi
+        self.t4, self.abi = t4, abi
+        self.device = device
+        gdev = device if device is not None else gen_device()
+        big = gen_normal(4, 4096 * 4096 * 32, np.float32, gdev).reshape(4096, 4096, 32)
+        c = torch.complex(gen_normal(5, 8192 * 8192, np.float64, gdev),
+                          gen_normal(5 + 1000, 8192 * 8192, np.float64, gdev)).reshape(8192, 8192)
+        u = gen_uniform(0, 256 * 1024 * 64, np.float64, gdev).reshape(256, 1024, 64)
+        self.host_in = [big, c, u]
+        if device is not None:
+            self.host_in = [h.pin_memory() for h in self.host_in]
+            self.dev_in = [h.to(device) for h in self.host_in]
+        specs = []
+        for ax in (0, 1, 2):
+            for op, tag in ((abi.SUM, "sum"), (abi.SUM_SQUARES, "sumsq"), (abi.MAX, "max")):
+                specs.append((f"{tag}-f32-4096x4096x32-axis{ax}", 0, ax, op))
+        specs.append(("sum-c64-8192x8192-axis1", 1, 1, abi.SUM))
+        specs.append(("sum-f64-256x1024x64-axis1", 2, 1, abi.SUM))
+        specs.append(("max-f64-256x1024x64-axis1", 2, 1, abi.MAX))
+        self.ops = []
+        self.dev_out, self.host_out, self.workspace = [], [], None
+        need_ws = 0
+        for j, (tag, i, ax, op) in enumerate(specs):
+            x = self.host_in[i]
+            shape = list(x.shape)
+            oshape = list(shape)
+            oshape[ax] = 1
+            dt = t4.torch_dtype_tag(x)
+            in_l = abi.numpy_layout(shape)
+            out_l = abi.numpy_layout(oshape)
+            n_out = int(np.prod(oshape))
+            ws = t4.reduce_workspace_bytes(dt, op, out_l, n_out, in_l, x.numel(), len(shape) - 1 - ax)
+            need_ws = max(need_ws, ws)
+            esize = x.element_size()
+            self.ops.append(dict(tag=tag, i=i, j=j, op=op, dtype=dt, in_l=in_l, out_l=out_l, n_in=x.numel(),
+                                 n_out=n_out, axis=len(shape) - 1 - ax, ws=ws, np_axis=ax,
+                                 bytes=(x.numel() + n_out) * esize, launches=2 if ws else 1))
+            self.host_out.append(torch.empty(oshape, dtype=x.dtype).pin_memory() if device is not None
+                                 else torch.empty(oshape, dtype=x.dtype))
+            if device is not None:
+                self.dev_out.append(torch.empty(oshape, dtype=x.dtype, device=device))
+        if device is not None:
+            self.workspace = torch.empty(max(need_ws, 16), dtype=torch.uint8, device=device)
+
+    def units(self):
+        return sum(op["bytes"] for op in self.ops)
+
+    def run_op(self, op, stream_handle, dev_in=None, dev_out=None):
+        src = (dev_in or self.dev_in)[op["i"]]
+        dst = (dev_out or self.dev_out)[op["j"]]
+        self.t4.reduce_raw(stream_handle, op["dtype"], op["op"], ctypes.c_void_p(dst.data_ptr()), op["out_l"],
+                           op["n_out"], ctypes.c_void_p(src.data_ptr()), op["in_l"], op["n_in"], op["axis"], 32,
+                           ctypes.c_void_p(self.workspace.data_ptr()), op["ws"])
+
+    def cpu_op(self, op, threads, srcs, dsts):
+        oracle = _oracle()
+        host_src, host_dst = srcs[op["i"]], dsts[op["j"]]
+        rc = oracle.lib().t4a_oracle_reduce_threaded(op["dtype"], op["op"], oracle.ptr(host_dst),
+                                                     ctypes.byref(op["out_l"]), oracle.ptr(host_src),
+                                                     ctypes.byref(op["in_l"]), op["axis"], 32, threads)
+        assert rc == 0
+
+    def host_arrays(self):
+        srcs = [h.numpy() for h in self.host_in]
+        outs = [h.numpy() for h in self.host_out]
+        return srcs, outs
+
+
+class GatherScatterWorkload(Workload):
+    """XLA gather of 4,194,304 rows from an F32 table
+    [1,048,576,128] with I64 indices uniform in [0, 1048576) (seeds 6, 7), and
+    scatter_add of F64 updates [4,194,304,128] normal(0,1) (seed 8) into a
+    [1,048,576,128] destination with Zipf(s=1.1) row indices (seed 9; inverse CDF over
+    ranks 1..1048576, row = rank - 1).  Algorithmic bytes: gather = output + gathered
+    rows + indices; scatter = updates + indices + destination read and write.  The
+    destination is zeroed once; the caller's operand copy (copy_exact) is not part of
+    the timed scatter op.  The CPU leg runs the oracle on the first 262,144 index rows
+    of each op."""
+
+    name = "config4-gather-scatter"
+    dtype = "f32 (gather), f64 (scatter); i64 indices"
+    ROWS, COLS, N, SAMPLE = 1 << 20, 128, 1 << 22, 1 << 18
+
+    def __init__(self, device=None):
+        import numpy as np
+        import torch
+        import t4a_b200 as t4
+        from t4a_b200 import abi
+        self.t4, self.abi = t4, abi
+        self.device = device
+        gdev = device if device is not None else gen_device()
+        R, C, N = self.ROWS, self.COLS, self.N
+        table = gen_normal(6, R * C, np.float32, gdev).reshape(R, C)
+        gidx = self._uniform_rows(7, N, R, gdev)
+        upd = gen_normal(8, N * C, np.float64, gdev).reshape(N, C)
+        sidx = self._zipf_rows(9, N, R, 1.1, gdev)
+        dest0 = torch.zeros((R, C), dtype=torch.float64)
+        pin = device is not None
+        self.host = {"table": table, "gidx": gidx, "upd": upd, "sidx": sidx, "dest": dest0,
+                     "gout": torch.empty((N, C), dtype=torch.float32)}
+        if pin:
+            self.host = {k: v.pin_memory() for k, v in self.host.items()}
+            self.dev = {k: v.to(device) for k, v in self.host.items()}
+        self.gplan = abi.gather_plan([0], [0], [1], [C, 1], 1, 2)
+        self.splan = abi.scatter_plan([0], [0], [1], 1, 2, 2)
+        self.ops = [
+            dict(tag="gather-f32-4Mx128-of-1Mx128", kind="gather", i=0,
+                 bytes=N * C * 4 * 2 + N * 8),
+            dict(tag="scatter-add-f64-4Mx128-zipf-into-1Mx128", kind="scatter", i=1,
+                 bytes=N * C * 8 + N * 8 + 2 * R * C * 8),
+        ]
+
+    @staticmethod
+    def _uniform_rows(seed, n, rows, gdev):
+        import numpy as np
+        import torch
+        if gdev is None:
+            z = _splitmix_bits(seed, 0, n)
+            u = (z >> np.uint64(11)).astype(np.float64) * (1.0 / (1 << 53))
+            return torch.from_numpy((u * rows).astype(np.int64))
+        z = _splitmix_bits_torch(seed, 0, n, gdev)
+        u = _srl(z, 11).double() * (1.0 / (1 << 53))
+        return (u * rows).to(torch.int64).cpu()
+
+    @staticmethod
+    def _zipf_rows(seed, n, rows, s, gdev):
+        import numpy as np
+        import torch
+        w = np.arange(1, rows + 1, dtype=np.float64) ** -s
+        cdf = np.cumsum(w)
+        cdf /= cdf[-1]
+        if gdev is None:
+            z = _splitmix_bits(seed, 0, n)
+            u = (z >> np.uint64(11)).astype(np.float64) * (1.0 / (1 << 53))
+            return torch.from_numpy(np.minimum(np.searchsorted(cdf, u, side="right"), rows - 1).astype(np.int64))
+        z = _splitmix_bits_torch(seed, 0, n, gdev)
+        u = _srl(z, 11).double() * (1.0 / (1 << 53))
+        r = torch.searchsorted(torch.from_numpy(cdf).to(gdev), u, right=True)
+        return torch.clamp(r, max=rows - 1).to(torch.int64).cpu()
+
+    def units(self):
+        return sum(op["bytes"] for op in self.ops)
+
+    def run_op(self, op, stream_handle, dev_in=None, dev_out=None):
+        t4, abi, d = self.t4, self.abi, self.dev
+        R, C, N = self.ROWS, self.COLS, self.N
+        vp = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+        if op["kind"] == "gather":
+            t4.gather_raw(stream_handle, abi.F32, abi.I64, vp(d["gout"]), abi.numpy_layout([N, C]), N * C,
+                          vp(d["table"]), abi.numpy_layout([R, C]), R * C, vp(d["gidx"]), abi.layout([N, 1]), N,
+                          self.gplan)
+        else:
+            t4.scatter_add_raw(stream_handle, abi.F64, abi.I64, vp(d["dest"]), abi.numpy_layout([R, C]), R * C,
+                               vp(d["sidx"]), abi.layout([N, 1]), N, vp(d["upd"]), abi.numpy_layout([N, C]), N * C,
+                               self.splan)
+
+    def e2e_inputs(self, op):
+        keys = ["table", "gidx"] if op["kind"] == "gather" else ["dest", "sidx", "upd"]
+        return [(self.host[k], self.dev[k]) for k in keys]
+
+    def e2e_outputs(self, op):
+        k = "gout" if op["kind"] == "gather" else "dest"
+        return [(self.dev[k], self.host[k])]
+
+    def host_arrays(self):
+        return self.host, None
+
+    def cpu_units(self):
+        return sum(op["bytes"] for op in self.ops) * self.SAMPLE // self.N
+
+    def cpu_sample(self):
+        return f"the first {self.SAMPLE} of {self.N} index rows of each {self.name} op"
+
+    def cpu_op(self, op, threads, srcs, dsts):
+        oracle = _oracle()
+        abi = self.abi
+        R, C, S = self.ROWS, self.COLS, self.SAMPLE
+        h = srcs
+        if op["kind"] == "gather":
+            rc = oracle.lib().t4a_oracle_gather(abi.F32, abi.I64, oracle.ptr(h["gout"].numpy()),
+                                                oracle.ptr(h["table"].numpy()), oracle.ptr(h["gidx"].numpy()),
+                                                ctypes.byref(abi.numpy_layout([S, C])),
+                                                ctypes.byref(abi.numpy_layout([R, C])),
+                                                ctypes.byref(abi.layout([S, 1])), ctypes.byref(self.gplan), threads)
+        else:
+            rc = oracle.lib().t4a_oracle_scatter_add(abi.F64, abi.I64, oracle.ptr(h["dest"].numpy()),
+                                                     oracle.ptr(h["sidx"].numpy()), oracle.ptr(h["upd"].numpy()),
+                                                     ctypes.byref(abi.numpy_layout([R, C])),
+                                                     ctypes.byref(abi.layout([S, 1])),
+                                                     ctypes.byref(abi.numpy_layout([S, C])),
+                                                     ctypes.byref(self.splan), threads)
+        assert rc == 0
+
+
+WORKLOADS = {"movement": MovementWorkload, "reduce": ReduceWorkload, "gather": GatherScatterWorkload}
 
 
 def torch_int64():
@@ -272,18 +565,19 @@ def run_ours(args, rank, world, local_rank):
 
     # End to end through the public API: pinned host inputs -> device -> op -> host.
     e2e_ms = None
-    h2d = sum(wl.host_in[op["i"]].numel() * wl.host_in[op["i"]].element_size() for op in wl.ops)
-    d2h = sum(wl.host_out[op["i"]].numel() * wl.host_out[op["i"]].element_size() for op in wl.ops)
+    h2d = sum(h.numel() * h.element_size() for op in wl.ops for h, _ in wl.e2e_inputs(op))
+    d2h = sum(h.numel() * h.element_size() for op in wl.ops for _, h in wl.e2e_outputs(op))
     barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(args.steps):
         for op in wl.ops:
-            i = op["i"]
-            wl.dev_in[i].copy_(wl.host_in[i], non_blocking=True)
+            for h, d in wl.e2e_inputs(op):
+                d.copy_(h, non_blocking=True)
             wl.run_op(op, sh)
-            wl.host_out[i].copy_(wl.dev_out[i], non_blocking=True)
+            for d, h in wl.e2e_outputs(op):
+                h.copy_(d, non_blocking=True)
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
@@ -330,7 +624,7 @@ def run_ours(args, rank, world, local_rank):
         "ops": ops_detail,
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": round(e2e_ms / args.steps, 3)},
-        "gpu_launches": len(wl.ops) * args.steps,
+        "gpu_launches": sum(op.get("launches", 1) for op in wl.ops) * args.steps,
         "clocks": sampler.summary(),
         "wall_s_timed_region": round(wall, 3),
     }
@@ -355,13 +649,13 @@ def cpu_baseline(wl, args, repeats=1):
     n = 0
     while True:
         for op in wl.ops:
-            wl.cpu_op(op, threads, srcs[op["i"]], dsts[op["i"]])
+            wl.cpu_op(op, threads, srcs, dsts)
         n += 1
         if time.perf_counter() - t0 > 2.0 or n >= repeats:
             break
     dt = time.perf_counter() - t0
-    return {"value": round(wl.units() * n / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"{n} full step(s) of {wl.name} ({wl.units() / MIB:.0f} MiB algorithmic), {dt:.2f} s"}
+    return {"value": round(wl.cpu_units() * n / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{n} step(s) of {wl.cpu_sample()} ({wl.cpu_units() / MIB:.0f} MiB algorithmic), {dt:.2f} s"}
 
 
 def run_reference(args, rank, world):
@@ -374,13 +668,13 @@ def run_reference(args, rank, world):
     srcs, dsts = wl.host_arrays()
     for _ in range(max(0, min(args.warmup, 1))):
         for op in wl.ops:
-            wl.cpu_op(op, threads, srcs[op["i"]], dsts[op["i"]])
+            wl.cpu_op(op, threads, srcs, dsts)
     t0 = time.perf_counter()
     for _ in range(args.steps):
         for op in wl.ops:
-            wl.cpu_op(op, threads, srcs[op["i"]], dsts[op["i"]])
+            wl.cpu_op(op, threads, srcs, dsts)
     dt = time.perf_counter() - t0
-    value = wl.units() * args.steps / dt / 1e9
+    value = wl.cpu_units() * args.steps / dt / 1e9
     return {
         "impl": "reference",
         "metric": "achieved HBM GB/s (% of B200 peak) per op at 1/2/4/8 GPUs vs CPU baseline",
@@ -389,7 +683,7 @@ def run_reference(args, rank, world):
         "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic (seeded normal(0,1))",
         "config": {"workload": wl.name, "ops": [op["tag"] for op in wl.ops], "bytes_per_step": wl.units()},
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": f"{args.steps} full steps of {wl.name} on the host cores"},
+                         "sample": f"{args.steps} steps of {wl.cpu_sample()} on the host cores"},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 

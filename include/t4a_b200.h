@@ -216,6 +216,47 @@ int t4a_launch_fill_zero_view(const t4a_launch* launch, void* stream, void* out,
 int t4a_copy_strided(void* stream, int dtype, void* dst, const t4a_cuda_layout* dst_layout, long long dst_len,
                      const void* src, const t4a_cuda_layout* src_layout, long long src_len);
 
+/* ------------------------------------------------------------------------- */
+/* Gather and additive scatter (reference src/lib.rs:2779-3029,               */
+/* gather_scatter.cu:454-492).  The plans are the by-value mirrors             */
+/* (CGatherPlan / CScatterPlan, src/lib.rs:4192-4303).                         */
+/* ------------------------------------------------------------------------- */
+
+/* plan_gather (src/lib.rs:2867): validates the maps and the derived output extents;
+ * *output_len receives the output element count the launch expects. */
+int t4a_plan_gather(int dtype, int index_dtype, const t4a_cuda_layout* out, long long out_len,
+                    const t4a_cuda_layout* operand, long long operand_len, const t4a_cuda_layout* indices,
+                    long long indices_len, const t4a_cuda_gather_plan* plan, t4a_launch* launch,
+                    long long* output_len);
+/* plan_scatter_add (src/lib.rs:2970): `out` already holds the operand (copy_exact first).
+ * Updates whose window does not fit the destination are skipped, as in the reference. */
+int t4a_plan_scatter_add(int dtype, int index_dtype, const t4a_cuda_layout* out, long long out_len,
+                         const t4a_cuda_layout* indices, long long indices_len, const t4a_cuda_layout* updates,
+                         long long updates_len, const t4a_cuda_scatter_plan* plan, t4a_launch* launch);
+
+/* Launchers with the argument lists of gather_scatter.cu:454 and :486 (layouts by pointer). */
+int t4a_launch_gather(const t4a_launch* launch, void* stream, void* out, const void* operand, const void* indices,
+                      int dtype, int index_dtype, const t4a_cuda_layout* out_layout,
+                      const t4a_cuda_layout* operand_layout, const t4a_cuda_layout* indices_layout,
+                      const t4a_cuda_gather_plan* plan, long long output_len);
+/* Collisions are summed in update order inside each chunk of 2048 updates and
+ * atomically across chunks, so the floating result depends on the schedule (the
+ * reference's atomics are order-free as well). */
+int t4a_launch_scatter_add(const t4a_launch* launch, void* stream, void* out, const void* indices,
+                           const void* updates, int dtype, int index_dtype, const t4a_cuda_layout* out_layout,
+                           const t4a_cuda_layout* indices_layout, const t4a_cuda_layout* updates_layout,
+                           const t4a_cuda_scatter_plan* plan, long long update_len);
+
+/* One call each: plan and launch. */
+int t4a_gather(void* stream, int dtype, int index_dtype, void* out, const t4a_cuda_layout* out_layout,
+               long long out_len, const void* operand, const t4a_cuda_layout* operand_layout, long long operand_len,
+               const void* indices, const t4a_cuda_layout* indices_layout, long long indices_len,
+               const t4a_cuda_gather_plan* plan);
+int t4a_scatter_add(void* stream, int dtype, int index_dtype, void* out, const t4a_cuda_layout* out_layout,
+                    long long out_len, const void* indices, const t4a_cuda_layout* indices_layout,
+                    long long indices_len, const void* updates, const t4a_cuda_layout* updates_layout,
+                    long long updates_len, const t4a_cuda_scatter_plan* plan);
+
 #ifdef __cplusplus
 }
 #endif

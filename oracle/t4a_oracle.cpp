@@ -595,6 +595,9 @@ template <typename I>
 long long clamp_start(I start, long long dim, long long window) {
   const long long max_start = dim > window ? dim - window : 0;
   if (!(start > static_cast<I>(0))) return 0;
+  // A float start at or above 2^64 (+inf included) converts to the largest u64 on
+  // the device (cvt.rzi saturates); C++ leaves that conversion undefined.
+  if (static_cast<double>(start) >= 18446744073709551616.0) return max_start;
   const unsigned long long raw = static_cast<unsigned long long>(start);
   return raw < static_cast<unsigned long long>(max_start) ? static_cast<long long>(raw) : max_start;
 }

@@ -1,0 +1,376 @@
+// Gather / scatter_add planning (reference src/lib.rs:2779-3029, CGatherPlan and
+// CScatterPlan at :4192-4303) and the host launchers.  The launchers rebuild the
+// window plan on the host, pick the vector width from the plan and the pointers,
+// and launch a kernel compiled for that width and index type.
+#include <cuda_runtime.h>
+
+#include "gather_scatter_core.cuh"
+#include "plan_common.h"
+#include "runtime.h"
+
+namespace t4a {
+namespace {
+
+template <typename I, int V>
+__global__ void __launch_bounds__(kGatherThreads) k_gather(WindowPlan p, void* out, const void* operand,
+                                                           const void* indices, long long units, long long nvec,
+                                                           Pieces pc, int lshift) {
+  __shared__ GatherSlot slots[kGatherThreads];
+  gather_units<I, V>(p, static_cast<unsigned char*>(out), static_cast<const unsigned char*>(operand),
+                     static_cast<const I*>(indices), units, nvec, pc, lshift, slots);
+}
+
+template <typename F, typename I, int V, int JB>
+__global__ void __launch_bounds__(kScatterThreads) k_scatter(WindowPlan p, void* out, const void* indices,
+                                                             const void* updates, long long units, long long nvec) {
+  __shared__ ScatterSmem sm;
+  scatter_units<F, I, V, JB>(p, static_cast<unsigned char*>(out), static_cast<const unsigned char*>(updates),
+                             static_cast<const I*>(indices), units, nvec, sm);
+}
+
+constexpr int kGatherVariant = 48;
+constexpr int kScatterVariant = 49;
+constexpr unsigned long long kResidentBlocks = 148ull * 8;  // grid cap: a few waves of resident blocks
+
+int index_size(int index_dtype) {
+  switch (index_dtype) {
+    case T4A_CUDA_F32:
+    case T4A_CUDA_I32: return 4;
+    case T4A_CUDA_F64:
+    case T4A_CUDA_I64: return 8;
+    default: return 0;
+  }
+}
+
+int require_index_dtype(int index_dtype) { return index_size(index_dtype) ? T4A_OK : T4A_ERR_UNSUPPORTED_DTYPE; }
+
+// require_unique_axes (src/lib.rs:2815).
+int require_unique_axes(const long long* axes, int n, long long rank) {
+  for (int i = 0; i < n; ++i) {
+    if (axes[i] < 0 || axes[i] >= rank) return T4A_ERR_INVALID_AXIS;
+    for (int j = 0; j < i; ++j)
+      if (axes[j] == axes[i]) return T4A_ERR_DUPLICATE_AXIS;
+  }
+  return T4A_OK;
+}
+
+// index_vector_size (src/lib.rs:2838): the vector axis' extent, 1 when absent.
+int index_vector_size(const t4a_cuda_layout& indices, int index_vector_dim, long long* size) {
+  if (index_vector_dim < 0 || index_vector_dim > indices.rank) return T4A_ERR_INVALID_AXIS;
+  *size = index_vector_dim == indices.rank ? 1 : indices.extents[index_vector_dim];
+  return T4A_OK;
+}
+
+// Index batch extents: the index extents without the vector axis.
+int index_batch_extents(const t4a_cuda_layout& indices, int index_vector_dim, long long* out) {
+  int n = 0;
+  for (int ax = 0; ax < indices.rank; ++ax)
+    if (ax != index_vector_dim) out[n++] = indices.extents[ax];
+  return n;
+}
+
+// The by-value mirror's counts are within the ABI's fixed arrays (CGatherPlan::new,
+// CScatterPlan::new, src/lib.rs:4208, :4274).
+int check_counts(int a, int b, int c) {
+  if (a < 0 || b < 0 || c < 0) return T4A_ERR_RANK_OUT_OF_RANGE;
+  if (a > T4A_CUDA_MAX_RANK || b > T4A_CUDA_MAX_RANK || c > T4A_CUDA_MAX_RANK) return T4A_ERR_RANK_OUT_OF_RANGE;
+  return T4A_OK;
+}
+
+// plan_gather validation (src/lib.rs:2867-2965).
+int validate_gather(int dtype, int index_dtype, const t4a_cuda_layout& out, long long out_len,
+                    const t4a_cuda_layout& operand, long long operand_len, const t4a_cuda_layout& indices,
+                    long long indices_len, const t4a_cuda_gather_plan& g) {
+  using namespace plan;
+  if (dtype_size(dtype) == 0) return T4A_ERR_UNSUPPORTED_DTYPE;
+  T4A_TRY(require_index_dtype(index_dtype));
+  T4A_TRY(require_compact(indices));
+  T4A_TRY(check_counts(g.operand_rank, g.window_rank, g.start_map_len));
+  const int operand_rank = operand.rank;
+  if (g.operand_rank != operand_rank) return T4A_ERR_RANK_LENGTH;
+  for (int ax = 0; ax < operand_rank; ++ax)
+    if (g.slice_sizes[ax] < 0) return T4A_ERR_NEGATIVE_EXTENT;
+  T4A_TRY(require_unique_axes(g.start_index_map, g.start_map_len, operand_rank));
+  T4A_TRY(require_unique_axes(g.window_dims, g.window_rank, operand_rank));
+  long long vsize = 0;
+  T4A_TRY(index_vector_size(indices, g.index_vector_dim, &vsize));
+  if (vsize != g.start_map_len) return T4A_ERR_INDEX_VECTOR_MISMATCH;
+  for (int ax = 0; ax < operand_rank; ++ax) {
+    bool window = false;
+    for (int q = 0; q < g.window_rank; ++q)
+      if (g.window_dims[q] == ax) window = true;
+    if (window) {
+      if (g.slice_sizes[ax] > operand.extents[ax]) return T4A_ERR_SHAPE_MISMATCH;
+    } else if (g.slice_sizes[ax] != 1) {
+      return T4A_ERR_SHAPE_MISMATCH;
+    }
+  }
+  long long batch[T4A_CUDA_MAX_RANK];
+  const int nbatch = index_batch_extents(indices, g.index_vector_dim, batch);
+  const int out_rank = nbatch + g.window_rank;
+  for (int q = 0; q < g.window_rank; ++q)
+    if (g.offset_dims[q] < 0 || g.offset_dims[q] >= out_rank) return T4A_ERR_INVALID_AXIS;
+  T4A_TRY(require_unique_axes(g.offset_dims, g.window_rank, out_rank));
+  if (out_rank > T4A_CUDA_MAX_RANK) return T4A_ERR_SHAPE_MISMATCH;
+  long long derived[T4A_CUDA_MAX_RANK] = {0};
+  bool filled[T4A_CUDA_MAX_RANK] = {false};
+  for (int q = 0; q < g.window_rank; ++q) {
+    derived[g.offset_dims[q]] = g.slice_sizes[g.window_dims[q]];
+    filled[g.offset_dims[q]] = true;
+  }
+  int b = 0;
+  for (int ax = 0; ax < out_rank; ++ax) {
+    if (!filled[ax]) {
+      if (b >= nbatch) return T4A_ERR_SHAPE_MISMATCH;
+      derived[ax] = batch[b++];
+    }
+  }
+  if (b != nbatch) return T4A_ERR_SHAPE_MISMATCH;
+  if (out.rank != out_rank) return T4A_ERR_SHAPE_MISMATCH;
+  for (int ax = 0; ax < out_rank; ++ax)
+    if (out.extents[ax] != derived[ax]) return T4A_ERR_SHAPE_MISMATCH;
+  T4A_TRY(require_destination(out));
+  T4A_TRY(check_span(operand, operand_len, dtype_size(dtype)));
+  T4A_TRY(check_span(indices, indices_len, index_size(index_dtype)));
+  T4A_TRY(check_span(out, out_len, dtype_size(dtype)));
+  return T4A_OK;
+}
+
+// plan_scatter_add validation (src/lib.rs:2970-3029).
+int validate_scatter(int dtype, int index_dtype, const t4a_cuda_layout& out, long long out_len,
+                     const t4a_cuda_layout& indices, long long indices_len, const t4a_cuda_layout& updates,
+                     long long updates_len, const t4a_cuda_scatter_plan& g) {
+  using namespace plan;
+  if (dtype != T4A_CUDA_F32 && dtype != T4A_CUDA_F64 && dtype != T4A_CUDA_C32 && dtype != T4A_CUDA_C64)
+    return T4A_ERR_UNSUPPORTED_DTYPE;
+  T4A_TRY(require_index_dtype(index_dtype));
+  T4A_TRY(require_compact(indices));
+  T4A_TRY(check_counts(g.window_rank, g.window_rank, g.scatter_map_len));
+  T4A_TRY(require_unique_axes(g.scatter_dims, g.scatter_map_len, out.rank));
+  T4A_TRY(require_unique_axes(g.window_dims, g.window_rank, out.rank));
+  T4A_TRY(require_unique_axes(g.update_window_dims, g.window_rank, updates.rank));
+  long long vsize = 0;
+  T4A_TRY(index_vector_size(indices, g.index_vector_dim, &vsize));
+  if (vsize != g.scatter_map_len) return T4A_ERR_INDEX_VECTOR_MISMATCH;
+  long long from_updates[T4A_CUDA_MAX_RANK], from_indices[T4A_CUDA_MAX_RANK];
+  int nu = 0;
+  for (int ax = 0; ax < updates.rank; ++ax) {
+    bool window = false;
+    for (int q = 0; q < g.window_rank; ++q)
+      if (g.update_window_dims[q] == ax) window = true;
+    if (!window) from_updates[nu++] = updates.extents[ax];
+  }
+  const int ni = index_batch_extents(indices, g.index_vector_dim, from_indices);
+  if (nu != ni) return T4A_ERR_SHAPE_MISMATCH;
+  for (int i = 0; i < nu; ++i)
+    if (from_updates[i] != from_indices[i]) return T4A_ERR_SHAPE_MISMATCH;
+  long long count = 0;
+  T4A_TRY(element_count(updates, &count));
+  T4A_TRY(require_destination(out));
+  T4A_TRY(check_span(out, out_len, dtype_size(dtype)));
+  T4A_TRY(check_span(indices, indices_len, index_size(index_dtype)));
+  T4A_TRY(check_span(updates, updates_len, dtype_size(dtype)));
+  return T4A_OK;
+}
+
+t4a_launch gather_geometry(const WindowPlan& p) {
+  using namespace plan;
+  const long long units = p.batch.len * p.wrest.len;
+  if (units <= 0 || p.run <= 0) return empty_launch();
+  const long long nvec = p.run;  // vector count at the narrowest width bounds the piece count
+  const Pieces pc = make_pieces(nvec, kGatherPieceVecs);
+  const unsigned long long batches = ceil_div(static_cast<unsigned long long>(units * pc.count), 32);
+  unsigned long long grid = ceil_div(batches, kGatherThreads / 32);
+  if (grid > kResidentBlocks * 4) grid = kResidentBlocks * 4;  // warps are grid-stride
+  return make_launch(grid, kGatherThreads, 1, 0, kGatherVariant);
+}
+
+t4a_launch scatter_geometry(const WindowPlan& p) {
+  using namespace plan;
+  const long long units = p.batch.len * p.wrest.len;
+  if (units <= 0 || p.run <= 0 || !scatter_windows_fit(p)) return empty_launch();
+  const Pieces pc = make_pieces(p.run, 32ll * 2);
+  const unsigned long long chunks = ceil_div(static_cast<unsigned long long>(units * pc.count), kScatterChunk);
+  unsigned long long grid = chunks;
+  if (grid > kResidentBlocks) grid = kResidentBlocks;  // blocks are grid-stride over chunks
+  return make_launch(grid, kScatterThreads, 1, 0, kScatterVariant);
+}
+
+template <typename I>
+int launch_gather_typed(const WindowPlan& p, dim3 grid, cudaStream_t s, void* out, const void* operand,
+                        const void* indices) {
+  const long long units = p.batch.len * p.wrest.len;
+  const int v = window_vec_bytes(p, reinterpret_cast<unsigned long long>(out),
+                                 reinterpret_cast<unsigned long long>(operand));
+  const long long nvec = p.run * p.esize / v;
+  const Pieces pc = make_pieces(nvec, kGatherPieceVecs);
+  const int ls = lane_shift_of(pc.vecs);
+  const dim3 block(kGatherThreads);
+  switch (v) {
+    case 16: k_gather<I, 16><<<grid, block, 0, s>>>(p, out, operand, indices, units, nvec, pc, ls); break;
+    case 8: k_gather<I, 8><<<grid, block, 0, s>>>(p, out, operand, indices, units, nvec, pc, ls); break;
+    case 4: k_gather<I, 4><<<grid, block, 0, s>>>(p, out, operand, indices, units, nvec, pc, ls); break;
+    case 2: k_gather<I, 2><<<grid, block, 0, s>>>(p, out, operand, indices, units, nvec, pc, ls); break;
+    default: k_gather<I, 1><<<grid, block, 0, s>>>(p, out, operand, indices, units, nvec, pc, ls); break;
+  }
+  return runtime::check_launch();
+}
+
+template <typename F, typename I, int V>
+void launch_scatter_width(const WindowPlan& p, dim3 grid, cudaStream_t s, void* out, const void* indices,
+                          const void* updates, long long units, long long nvec) {
+  const dim3 block(kScatterThreads);
+  if (nvec <= 32) {
+    k_scatter<F, I, V, 1><<<grid, block, 0, s>>>(p, out, indices, updates, units, nvec);
+  } else if (nvec <= 64) {
+    k_scatter<F, I, V, 2><<<grid, block, 0, s>>>(p, out, indices, updates, units, nvec);
+  } else {
+    k_scatter<F, I, V, 4><<<grid, block, 0, s>>>(p, out, indices, updates, units, nvec);
+  }
+}
+
+template <typename F, typename I>
+int launch_scatter_typed(const WindowPlan& p, dim3 grid, cudaStream_t s, void* out, const void* indices,
+                         const void* updates) {
+  const long long units = p.batch.len * p.wrest.len;
+  const int v = window_vec_bytes(p, reinterpret_cast<unsigned long long>(out),
+                                 reinterpret_cast<unsigned long long>(updates));
+  const long long nvec = p.run * p.esize / v;
+  if (v >= 16) {
+    launch_scatter_width<F, I, 16>(p, grid, s, out, indices, updates, units, nvec);
+  } else if (v == 8) {
+    launch_scatter_width<F, I, 8>(p, grid, s, out, indices, updates, units, nvec);
+  } else if constexpr (sizeof(F) == 4) {
+    launch_scatter_width<F, I, 4>(p, grid, s, out, indices, updates, units, nvec);
+  }
+  return runtime::check_launch();
+}
+
+template <typename F>
+int launch_scatter_index(int index_dtype, const WindowPlan& p, dim3 grid, cudaStream_t s, void* out,
+                         const void* indices, const void* updates) {
+  switch (index_dtype) {
+    case T4A_CUDA_F32: return launch_scatter_typed<F, float>(p, grid, s, out, indices, updates);
+    case T4A_CUDA_F64: return launch_scatter_typed<F, double>(p, grid, s, out, indices, updates);
+    case T4A_CUDA_I32: return launch_scatter_typed<F, int>(p, grid, s, out, indices, updates);
+    case T4A_CUDA_I64: return launch_scatter_typed<F, long long>(p, grid, s, out, indices, updates);
+    default: return T4A_ERR_UNSUPPORTED_DTYPE;
+  }
+}
+
+}  // namespace
+}  // namespace t4a
+
+using namespace t4a;
+using namespace t4a::plan;
+
+extern "C" {
+
+int t4a_plan_gather(int dtype, int index_dtype, const t4a_cuda_layout* out, long long out_len,
+                    const t4a_cuda_layout* operand, long long operand_len, const t4a_cuda_layout* indices,
+                    long long indices_len, const t4a_cuda_gather_plan* plan, t4a_launch* launch,
+                    long long* output_len) {
+  if (plan == nullptr || launch == nullptr || output_len == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  T4A_TRY(check_layout(out));
+  T4A_TRY(check_layout(operand));
+  T4A_TRY(check_layout(indices));
+  T4A_TRY(validate_gather(dtype, index_dtype, *out, out_len, *operand, operand_len, *indices, indices_len, *plan));
+  long long count = 0;
+  T4A_TRY(element_count(*out, &count));
+  *output_len = count;
+  *launch = gather_geometry(make_gather_plan(*out, *operand, *indices, *plan, dtype_size(dtype)));
+  return T4A_OK;
+}
+
+int t4a_plan_scatter_add(int dtype, int index_dtype, const t4a_cuda_layout* out, long long out_len,
+                         const t4a_cuda_layout* indices, long long indices_len, const t4a_cuda_layout* updates,
+                         long long updates_len, const t4a_cuda_scatter_plan* plan, t4a_launch* launch) {
+  if (plan == nullptr || launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  T4A_TRY(check_layout(out));
+  T4A_TRY(check_layout(indices));
+  T4A_TRY(check_layout(updates));
+  T4A_TRY(
+      validate_scatter(dtype, index_dtype, *out, out_len, *indices, indices_len, *updates, updates_len, *plan));
+  long long count = 0;
+  T4A_TRY(element_count(*out, &count));
+  if (count == 0) {
+    *launch = empty_launch();
+    return T4A_OK;
+  }
+  *launch = scatter_geometry(make_scatter_plan(*out, *indices, *updates, *plan, dtype_size(dtype)));
+  return T4A_OK;
+}
+
+int t4a_launch_gather(const t4a_launch* launch, void* stream, void* out, const void* operand, const void* indices,
+                      int dtype, int index_dtype, const t4a_cuda_layout* out_layout,
+                      const t4a_cuda_layout* operand_layout, const t4a_cuda_layout* indices_layout,
+                      const t4a_cuda_gather_plan* plan, long long output_len) {
+  if (launch == nullptr || out_layout == nullptr || operand_layout == nullptr || indices_layout == nullptr ||
+      plan == nullptr)
+    return T4A_ERR_NULL_ARGUMENT;
+  if (launch->grid[0] == 0 || output_len <= 0) return T4A_OK;
+  const int es = dtype_size(dtype);
+  if (es == 0) return T4A_ERR_UNSUPPORTED_DTYPE;
+  if (!gather_maps_ok(*out_layout, *operand_layout, *indices_layout, *plan)) return T4A_ERR_INVALID_AXIS;
+  const WindowPlan p = make_gather_plan(*out_layout, *operand_layout, *indices_layout, *plan, es);
+  if (p.run <= 0 || p.batch.len * p.wrest.len <= 0) return T4A_OK;
+  const dim3 grid(launch->grid[0]);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (index_dtype) {
+    case T4A_CUDA_F32: return launch_gather_typed<float>(p, grid, s, out, operand, indices);
+    case T4A_CUDA_F64: return launch_gather_typed<double>(p, grid, s, out, operand, indices);
+    case T4A_CUDA_I32: return launch_gather_typed<int>(p, grid, s, out, operand, indices);
+    case T4A_CUDA_I64: return launch_gather_typed<long long>(p, grid, s, out, operand, indices);
+    default: return T4A_ERR_UNSUPPORTED_DTYPE;
+  }
+}
+
+int t4a_launch_scatter_add(const t4a_launch* launch, void* stream, void* out, const void* indices,
+                           const void* updates, int dtype, int index_dtype, const t4a_cuda_layout* out_layout,
+                           const t4a_cuda_layout* indices_layout, const t4a_cuda_layout* updates_layout,
+                           const t4a_cuda_scatter_plan* plan, long long update_len) {
+  if (launch == nullptr || out_layout == nullptr || indices_layout == nullptr || updates_layout == nullptr ||
+      plan == nullptr)
+    return T4A_ERR_NULL_ARGUMENT;
+  if (launch->grid[0] == 0 || update_len <= 0) return T4A_OK;
+  const int es = dtype_size(dtype);
+  if (!scatter_maps_ok(*out_layout, *indices_layout, *updates_layout, *plan)) return T4A_ERR_INVALID_AXIS;
+  const WindowPlan p = make_scatter_plan(*out_layout, *indices_layout, *updates_layout, *plan, es);
+  if (p.run <= 0 || p.batch.len * p.wrest.len <= 0 || !scatter_windows_fit(p)) return T4A_OK;
+  const dim3 grid(launch->grid[0]);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case T4A_CUDA_F32:
+    case T4A_CUDA_C32: return launch_scatter_index<float>(index_dtype, p, grid, s, out, indices, updates);
+    case T4A_CUDA_F64:
+    case T4A_CUDA_C64: return launch_scatter_index<double>(index_dtype, p, grid, s, out, indices, updates);
+    default: return T4A_ERR_UNSUPPORTED_DTYPE;
+  }
+}
+
+int t4a_gather(void* stream, int dtype, int index_dtype, void* out, const t4a_cuda_layout* out_layout,
+               long long out_len, const void* operand, const t4a_cuda_layout* operand_layout, long long operand_len,
+               const void* indices, const t4a_cuda_layout* indices_layout, long long indices_len,
+               const t4a_cuda_gather_plan* plan) {
+  t4a_launch l;
+  long long output_len = 0;
+  T4A_TRY(t4a_plan_gather(dtype, index_dtype, out_layout, out_len, operand_layout, operand_len, indices_layout,
+                          indices_len, plan, &l, &output_len));
+  return t4a_launch_gather(&l, stream, out, operand, indices, dtype, index_dtype, out_layout, operand_layout,
+                           indices_layout, plan, output_len);
+}
+
+int t4a_scatter_add(void* stream, int dtype, int index_dtype, void* out, const t4a_cuda_layout* out_layout,
+                    long long out_len, const void* indices, const t4a_cuda_layout* indices_layout,
+                    long long indices_len, const void* updates, const t4a_cuda_layout* updates_layout,
+                    long long updates_len, const t4a_cuda_scatter_plan* plan) {
+  t4a_launch l;
+  T4A_TRY(t4a_plan_scatter_add(dtype, index_dtype, out_layout, out_len, indices_layout, indices_len, updates_layout,
+                               updates_len, plan, &l));
+  long long update_count = 0;
+  T4A_TRY(element_count(*updates_layout, &update_count));
+  return t4a_launch_scatter_add(&l, stream, out, indices, updates, dtype, index_dtype, out_layout, indices_layout,
+                                updates_layout, plan, update_count);
+}
+
+}  // extern "C"

@@ -96,6 +96,16 @@ def _declare(l):
         "t4a_launch_fill_zero": (I, [ctypes.POINTER(Launch), P, P, I, LL]),
         "t4a_launch_fill_zero_view": (I, [ctypes.POINTER(Launch), P, P, I, LB, LL]),
         "t4a_copy_strided": (I, [P, I, P, LP, LL, P, LP, LL]),
+        "t4a_plan_gather": (I, [I, I, LP, LL, LP, LL, LP, LL, ctypes.POINTER(abi.GatherPlan),
+                                ctypes.POINTER(Launch), ctypes.POINTER(LL)]),
+        "t4a_plan_scatter_add": (I, [I, I, LP, LL, LP, LL, LP, LL, ctypes.POINTER(abi.ScatterPlan),
+                                     ctypes.POINTER(Launch)]),
+        "t4a_launch_gather": (I, [ctypes.POINTER(Launch), P, P, P, P, I, I, LP, LP, LP,
+                                  ctypes.POINTER(abi.GatherPlan), LL]),
+        "t4a_launch_scatter_add": (I, [ctypes.POINTER(Launch), P, P, P, P, I, I, LP, LP, LP,
+                                       ctypes.POINTER(abi.ScatterPlan), LL]),
+        "t4a_gather": (I, [P, I, I, P, LP, LL, P, LP, LL, P, LP, LL, ctypes.POINTER(abi.GatherPlan)]),
+        "t4a_scatter_add": (I, [P, I, I, P, LP, LL, P, LP, LL, P, LP, LL, ctypes.POINTER(abi.ScatterPlan)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(l, name, None)
@@ -264,3 +274,68 @@ def materialize(view, out=None, stream=None):
     copy_strided_raw(stream_handle(stream), dtype, ctypes.c_void_p(out.data_ptr()), tensor_layout(out), span(out),
                      ctypes.c_void_p(view.data_ptr()), src_l, src_len)
     return out
+
+
+# ---- gather and additive scatter (reference src/lib.rs:2779-3029) ----------------
+
+def plan_gather(dtype, index_dtype, out_layout, out_len, operand_layout, operand_len, indices_layout, indices_len,
+                plan):
+    """plan_gather: returns (launch, output element count)."""
+    launch, count = Launch(), ctypes.c_longlong(0)
+    check(lib().t4a_plan_gather(dtype, index_dtype, ctypes.byref(out_layout), out_len, ctypes.byref(operand_layout),
+                                operand_len, ctypes.byref(indices_layout), indices_len, ctypes.byref(plan),
+                                ctypes.byref(launch), ctypes.byref(count)), "plan_gather")
+    return launch, count.value
+
+
+def plan_scatter_add(dtype, index_dtype, out_layout, out_len, indices_layout, indices_len, updates_layout,
+                     updates_len, plan):
+    launch = Launch()
+    check(lib().t4a_plan_scatter_add(dtype, index_dtype, ctypes.byref(out_layout), out_len,
+                                     ctypes.byref(indices_layout), indices_len, ctypes.byref(updates_layout),
+                                     updates_len, ctypes.byref(plan), ctypes.byref(launch)), "plan_scatter_add")
+    return launch
+
+
+def gather_raw(stream, dtype, index_dtype, out_ptr, out_layout, out_len, operand_ptr, operand_layout, operand_len,
+               indices_ptr, indices_layout, indices_len, plan):
+    check(lib().t4a_gather(stream, dtype, index_dtype, out_ptr, ctypes.byref(out_layout), out_len, operand_ptr,
+                           ctypes.byref(operand_layout), operand_len, indices_ptr, ctypes.byref(indices_layout),
+                           indices_len, ctypes.byref(plan)), "gather")
+
+
+def scatter_add_raw(stream, dtype, index_dtype, out_ptr, out_layout, out_len, indices_ptr, indices_layout,
+                    indices_len, updates_ptr, updates_layout, updates_len, plan):
+    check(lib().t4a_scatter_add(stream, dtype, index_dtype, out_ptr, ctypes.byref(out_layout), out_len,
+                                indices_ptr, ctypes.byref(indices_layout), indices_len, updates_ptr,
+                                ctypes.byref(updates_layout), updates_len, ctypes.byref(plan)), "scatter_add")
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def gather_rows(table, indices, out=None, stream=None):
+    """out[i, :] = table[clamp(indices[i]), :] for a row-major CUDA table [rows, cols]
+    (the XLA gather of whole rows; starts clamp as the reference's)."""
+    import torch
+    rows, cols = table.shape
+    n = indices.numel()
+    if out is None:
+        out = torch.empty((n, cols), dtype=table.dtype, device=table.device)
+    plan = abi.gather_plan([0], [0], [1], [cols, 1], 1, 2)
+    gather_raw(stream_handle(stream), torch_dtype_tag(table), torch_dtype_tag(indices), _ptr(out),
+               tensor_layout(out), span(out), _ptr(table), tensor_layout(table), span(table), _ptr(indices),
+               abi.layout([n, 1]), n, plan)
+    return out
+
+
+def scatter_add_rows(dest, indices, updates, stream=None):
+    """dest[clamp(indices[i]), :] += updates[i, :] in place, for a row-major CUDA
+    destination [rows, cols] (the XLA additive scatter of whole rows)."""
+    n, cols = updates.shape
+    plan = abi.scatter_plan([0], [0], [1], 1, 2, 2)
+    scatter_add_raw(stream_handle(stream), torch_dtype_tag(dest), torch_dtype_tag(indices), _ptr(dest),
+                    tensor_layout(dest), span(dest), _ptr(indices), abi.layout([n, 1]), n, _ptr(updates),
+                    tensor_layout(updates), span(updates), plan)
+    return dest

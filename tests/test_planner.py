@@ -161,3 +161,59 @@ def test_config3_reductions_plan_the_coalesced_paths(numpy_axis):
         assert plan.is_split == 0 and plan.strategy == abi.UNIT and plan.launch.variant == 18
     else:
         assert plan.is_split == 1 and plan.split.splits == 16 and plan.pass1.variant == 17
+
+
+# ---- gather / scatter_add planners (src/lib.rs:2867-3029) ------------------------
+
+def test_gather_planner_errors():
+    op_l, idx_l = abi.layout([4, 3]), abi.layout([2, 1])
+    plan = abi.gather_plan([1], [1], [0], [1, 3], 1, 2)
+    ok = t4.plan_gather(abi.F64, abi.I64, abi.layout([2, 3]), 6, op_l, 12, idx_l, 2, plan)
+    assert ok[1] == 6
+    cases = [
+        (abi.F64, abi.BOOL, abi.layout([2, 3]), plan, idx_l, 9),                        # index dtype
+        (abi.F64, abi.I64, abi.layout([2, 4]), plan, idx_l, 16),                        # derived extents
+        (abi.F64, abi.I64, abi.layout([2, 3]), abi.gather_plan([1], [1], [0], [1, 4], 1, 2), idx_l, 16),  # slice > extent
+        (abi.F64, abi.I64, abi.layout([2, 3]), abi.gather_plan([1], [1], [0], [2, 3], 1, 2), idx_l, 16),  # collapsed != 1
+        (abi.F64, abi.I64, abi.layout([2, 3]), abi.gather_plan([1], [1], [0, 1], [1, 3], 1, 2), idx_l, 24),  # vector size
+        (abi.F64, abi.I64, abi.layout([2, 3]), abi.gather_plan([1], [1], [0], [1, 3], 1, 2), abi.layout([2, 1], [2, 1]), 15),
+        (abi.F64, abi.I64, abi.layout([2, 3]), abi.gather_plan([1], [1], [5], [1, 3], 1, 2), idx_l, 13),  # invalid axis
+        (abi.F64, abi.I64, abi.layout([2, 3]), abi.gather_plan([1, 1], [1, 0], [0], [1, 3], 1, 2), idx_l, 14),  # duplicate
+    ]
+    for dtype, idt, out_l, p, il, code in cases:
+        with pytest.raises(t4.T4AError) as err:
+            t4.plan_gather(dtype, idt, out_l, out_l.count(), op_l, 12, il, 4, p)
+        assert err.value.status == code, (p, code)
+
+
+def test_gather_config4_plans_a_grid_stride_launch():
+    rows, cols, n = 1 << 20, 128, 1 << 22
+    plan = abi.gather_plan([0], [0], [1], [cols, 1], 1, 2)
+    launch, count = t4.plan_gather(abi.F32, abi.I64, abi.numpy_layout([n, cols]), n * cols,
+                                   abi.numpy_layout([rows, cols]), rows * cols, abi.layout([n, 1]), n, plan)
+    assert count == n * cols
+    assert 0 < launch.grid[0] <= 2 ** 31 - 1 and launch.block[0] == 256
+
+
+def test_scatter_planner_errors():
+    out_l, idx_l, upd_l = abi.layout([6]), abi.layout([4]), abi.layout([4, 2])
+    plan = abi.scatter_plan([0], [1], [0], 1, 1, 2)
+    t4.plan_scatter_add(abi.F64, abi.I64, out_l, 6, idx_l, 4, upd_l, 8, plan)
+    cases = [
+        (abi.I32, abi.I64, upd_l, plan, idx_l, 9),                       # data dtype
+        (abi.F64, abi.I64, abi.layout([5, 2]), plan, idx_l, 16),         # batch mismatch
+        (abi.F64, abi.I64, upd_l, abi.scatter_plan([0], [1], [0, 0], 1, 1, 2), abi.layout([4, 2]), 14),
+        (abi.F64, abi.I64, upd_l, abi.scatter_plan([0], [1], [0], 0, 1, 2), idx_l, 24),  # vector size
+        (abi.F64, abi.I64, upd_l, plan, abi.layout([4], [2]), 15),      # not compact
+    ]
+    for dtype, idt, ul, p, il, code in cases:
+        with pytest.raises(t4.T4AError) as err:
+            t4.plan_scatter_add(dtype, idt, out_l, 6, il, il.count() * 2, ul, ul.count(), p)
+        assert err.value.status == code, (p, code)
+
+
+def test_scatter_plans_nothing_when_no_window_fits():
+    plan = abi.scatter_plan([0], [1], [0], 1, 1, 2)
+    launch = t4.plan_scatter_add(abi.F64, abi.I64, abi.layout([6]), 6, abi.layout([2, 1]), 2,
+                                 abi.layout([2, 7]), 14, plan)
+    assert launch.grid[0] == 0
