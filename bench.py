@@ -406,10 +406,14 @@ class GatherScatterWorkload(Workload):
             self.dev = {k: v.to(device) for k, v in self.host.items()}
         self.gplan = abi.gather_plan([0], [0], [1], [C, 1], 1, 2)
         self.splan = abi.scatter_plan([0], [0], [1], 1, 2, 2)
+        self.ws_bytes = t4.scatter_add_workspace_bytes(abi.F64, abi.I64, abi.numpy_layout([R, C]),
+                                                       abi.layout([N, 1]), abi.numpy_layout([N, C]), self.splan)
+        if pin:
+            self.ws = torch.empty(self.ws_bytes, dtype=torch.uint8, device=device)
         self.ops = [
             dict(tag="gather-f32-4Mx128-of-1Mx128", kind="gather", i=0,
                  bytes=N * C * 4 * 2 + N * 8),
-            dict(tag="scatter-add-f64-4Mx128-zipf-into-1Mx128", kind="scatter", i=1,
+            dict(tag="scatter-add-f64-4Mx128-zipf-into-1Mx128", kind="scatter", i=1, launches=2,
                  bytes=N * C * 8 + N * 8 + 2 * R * C * 8),
         ]
 
@@ -455,7 +459,7 @@ class GatherScatterWorkload(Workload):
         else:
             t4.scatter_add_raw(stream_handle, abi.F64, abi.I64, vp(d["dest"]), abi.numpy_layout([R, C]), R * C,
                                vp(d["sidx"]), abi.layout([N, 1]), N, vp(d["upd"]), abi.numpy_layout([N, C]), N * C,
-                               self.splan)
+                               self.splan, vp(self.ws), self.ws_bytes)
 
     def e2e_inputs(self, op):
         keys = ["table", "gidx"] if op["kind"] == "gather" else ["dest", "sidx", "upd"]

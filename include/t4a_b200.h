@@ -239,23 +239,35 @@ int t4a_launch_gather(const t4a_launch* launch, void* stream, void* out, const v
                       int dtype, int index_dtype, const t4a_cuda_layout* out_layout,
                       const t4a_cuda_layout* operand_layout, const t4a_cuda_layout* indices_layout,
                       const t4a_cuda_gather_plan* plan, long long output_len);
-/* Collisions are summed in update order inside each chunk of 2048 updates and
- * atomically across chunks, so the floating result depends on the schedule (the
- * reference's atomics are order-free as well). */
+/* One-kernel scatter (the exported symbol's path): each block sorts a chunk of 2048
+ * update pieces by destination in shared memory and folds it.  Collisions are summed
+ * in update order inside a chunk and atomically across chunks, so the floating result
+ * depends on the schedule (the reference's atomics are order-free as well). */
 int t4a_launch_scatter_add(const t4a_launch* launch, void* stream, void* out, const void* indices,
                            const void* updates, int dtype, int index_dtype, const t4a_cuda_layout* out_layout,
                            const t4a_cuda_layout* indices_layout, const t4a_cuda_layout* updates_layout,
                            const t4a_cuda_scatter_plan* plan, long long update_len);
+/* Workspace of the two-kernel scatter (a grouping pass writes each chunk's sorted
+ * (destination, source) list, 16 bytes an update piece; a streaming pass folds it). */
+int t4a_scatter_add_workspace_bytes(int dtype, int index_dtype, const t4a_cuda_layout* out_layout,
+                                    const t4a_cuda_layout* indices_layout, const t4a_cuda_layout* updates_layout,
+                                    const t4a_cuda_scatter_plan* plan, size_t* bytes);
 
 /* One call each: plan and launch. */
 int t4a_gather(void* stream, int dtype, int index_dtype, void* out, const t4a_cuda_layout* out_layout,
                long long out_len, const void* operand, const t4a_cuda_layout* operand_layout, long long operand_len,
                const void* indices, const t4a_cuda_layout* indices_layout, long long indices_len,
                const t4a_cuda_gather_plan* plan);
+/* t4a_scatter_add: with a workspace of t4a_scatter_add_workspace_bytes (16-byte
+ * aligned) the two-kernel path, with NULL the one-kernel path; a smaller workspace
+ * is T4A_ERR_WORKSPACE.  The workspace's first int is a status word: the grouping
+ * pass sets it to 0, and the fold sets it to 1 when a bulk copy's completion wait
+ * ran out (the fold then stops); it is left untouched when there is no work. */
 int t4a_scatter_add(void* stream, int dtype, int index_dtype, void* out, const t4a_cuda_layout* out_layout,
                     long long out_len, const void* indices, const t4a_cuda_layout* indices_layout,
                     long long indices_len, const void* updates, const t4a_cuda_layout* updates_layout,
-                    long long updates_len, const t4a_cuda_scatter_plan* plan);
+                    long long updates_len, const t4a_cuda_scatter_plan* plan, void* workspace,
+                    size_t workspace_bytes);
 
 #ifdef __cplusplus
 }

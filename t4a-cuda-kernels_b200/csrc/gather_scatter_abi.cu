@@ -51,23 +51,25 @@ __device__ __forceinline__ void gather_dispatch(const WindowPlan& p, void* out, 
 
 template <typename F, typename I>
 __device__ __forceinline__ void scatter_dispatch(const WindowPlan& p, void* out, const void* indices,
-                                                 const void* updates, long long units, ScatterSmem& sm) {
+                                                 const void* updates, long long units, ScatterSmem& sm,
+                                                 long long max_dst_bytes) {
   auto* o = static_cast<unsigned char*>(out);
   const auto* u = static_cast<const unsigned char*>(updates);
   const I* idx = static_cast<const I*>(indices);
-  if (!whole_warps()) {
+  const int v = window_vec_bytes(p, reinterpret_cast<unsigned long long>(out),
+                                 reinterpret_cast<unsigned long long>(updates));
+  // The grouped path packs destination offsets / v beside the position bits.
+  if (!whole_warps() || max_dst_bytes / v >= kScatterMaxVecOffset) {
     scatter_elements<F, I>(p, o, u, idx, units);
     return;
   }
-  const int v = window_vec_bytes(p, reinterpret_cast<unsigned long long>(out),
-                                 reinterpret_cast<unsigned long long>(updates));
   const long long nvec = p.run * p.esize / v;
   if (v >= 16) {
-    scatter_units<F, I, 16, 2>(p, o, u, idx, units, nvec, sm);
+    scatter_units<F, I, 16>(p, o, u, idx, units, nvec, sm);
   } else if (v == 8) {
-    scatter_units<F, I, 8, 2>(p, o, u, idx, units, nvec, sm);
+    scatter_units<F, I, 8>(p, o, u, idx, units, nvec, sm);
   } else if constexpr (sizeof(F) == 4) {
-    scatter_units<F, I, 4, 2>(p, o, u, idx, units, nvec, sm);
+    scatter_units<F, I, 4>(p, o, u, idx, units, nvec, sm);
   }
 }
 
@@ -115,23 +117,24 @@ extern "C" __global__ void __launch_bounds__(512) t4a_cuda_scatter_add(
   __syncthreads();
   if (sp.run <= 0 || !scatter_windows_fit(sp)) return;
   const long long units = sp.batch.len * sp.wrest.len;
+  const long long max_dst = (layout_max_offset(out_layout) + 1) * es;
   const bool dbl = dtype == T4A_CUDA_F64 || dtype == T4A_CUDA_C64;  // component type
   switch (index_dtype) {
     case T4A_CUDA_F32:
-      if (dbl) scatter_dispatch<double, float>(sp, out, indices, updates, units, sm);
-      else scatter_dispatch<float, float>(sp, out, indices, updates, units, sm);
+      if (dbl) scatter_dispatch<double, float>(sp, out, indices, updates, units, sm, max_dst);
+      else scatter_dispatch<float, float>(sp, out, indices, updates, units, sm, max_dst);
       break;
     case T4A_CUDA_F64:
-      if (dbl) scatter_dispatch<double, double>(sp, out, indices, updates, units, sm);
-      else scatter_dispatch<float, double>(sp, out, indices, updates, units, sm);
+      if (dbl) scatter_dispatch<double, double>(sp, out, indices, updates, units, sm, max_dst);
+      else scatter_dispatch<float, double>(sp, out, indices, updates, units, sm, max_dst);
       break;
     case T4A_CUDA_I32:
-      if (dbl) scatter_dispatch<double, int>(sp, out, indices, updates, units, sm);
-      else scatter_dispatch<float, int>(sp, out, indices, updates, units, sm);
+      if (dbl) scatter_dispatch<double, int>(sp, out, indices, updates, units, sm, max_dst);
+      else scatter_dispatch<float, int>(sp, out, indices, updates, units, sm, max_dst);
       break;
     case T4A_CUDA_I64:
-      if (dbl) scatter_dispatch<double, long long>(sp, out, indices, updates, units, sm);
-      else scatter_dispatch<float, long long>(sp, out, indices, updates, units, sm);
+      if (dbl) scatter_dispatch<double, long long>(sp, out, indices, updates, units, sm, max_dst);
+      else scatter_dispatch<float, long long>(sp, out, indices, updates, units, sm, max_dst);
       break;
     default: break;
   }

@@ -9,13 +9,10 @@
 // clamped) into shared memory, then the warp copies the 32 runs with V-byte vectors,
 // kGatherDepth loads in flight per lane before their stores.
 //
-// Scatter: each block takes a chunk of kScatterChunk units, sorts it by destination
-// (bitonic, in shared memory), and each warp folds its share of the sorted chunk in
-// registers: consecutive units with the same destination are summed in update order
-// and reach memory as one vector of `red.global.add` per distinct destination.
-// Collisions on hot destinations (Zipf indices) therefore cost one atomic row per
-// chunk instead of one per update.  Results equal the reference's up to the order of
-// floating additions, which the reference leaves to its atomics as well.
+// Scatter: update rows are grouped by destination inside chunks (a counting sort
+// through a shared-memory hash table), and each group is summed in registers and
+// added to memory with one vector of `red.global.add` per lane; details at the
+// scatter section below.
 #pragma once
 
 #include "common.cuh"
@@ -26,8 +23,6 @@ namespace t4a {
 constexpr int kGatherThreads = 256;
 constexpr int kGatherDepth = 8;
 constexpr int kScatterThreads = 512;
-constexpr int kScatterChunk = 2048;
-constexpr long long kScatterSentinel = 0x7fffffffffffffffll;
 
 // ---- raw vectors of V bytes ---------------------------------------------------
 template <int V> struct Raw;
@@ -252,11 +247,27 @@ __device__ __forceinline__ void gather_elements(const WindowPlan& p, unsigned ch
 }
 
 // ---- scatter ------------------------------------------------------------------
-struct ScatterSmem {
-  long long dst[kScatterChunk];  // destination byte offset of the piece (sort key)
-  long long src[kScatterChunk];  // updates byte offset of the piece (second key)
-  int piece[kScatterChunk];      // piece of the run
-};
+// Work unit: a piece = up to 32 * kScatterVecs vectors of one update run.  Pieces are
+// grouped by destination inside chunks (a hash table in shared memory counts each
+// destination's pieces, a block scan turns the counts into group offsets: a counting
+// sort), then folded by sub-warps of L lanes (kScatterVecs vectors a lane):
+// consecutive pieces with one destination are summed in registers and reach memory
+// as one vector of `red.global.add` per lane.  Under Zipf indices a hot destination
+// therefore costs one atomic row per chunk instead of one per update.  Results equal
+// the reference's up to the order of floating additions, which the reference leaves
+// to its atomics as well.
+//
+// Two ways to run it:
+//  * two kernels (library launcher with a workspace): k_scatter_group writes each
+//    chunk's grouped (destination, source) list to the workspace; k_scatter_fold then
+//    streams the list with no block barrier, each lane keeping kFoldSlots pieces in
+//    flight through a cp.async ring in shared memory;
+//  * one kernel (the exported ABI symbol, or no workspace): each block groups a chunk
+//    in shared memory and folds it from there.
+constexpr int kScatterVecs = 4;  // vectors per lane and piece
+constexpr unsigned long long kEmptySlot = ~0ull;
+// Keys pack (destination / V) << 1 | short-piece flag.
+constexpr long long kScatterMaxVecOffset = 1ll << 62;
 
 // Reductions without a return value; V-byte vectors of F components.
 template <typename F, int V>
@@ -283,131 +294,639 @@ __device__ __forceinline__ void raw_to_f(typename Raw<V>::T r, F (&x)[V / sizeof
   memcpy(&x, &r, sizeof(x));
 }
 
-// Block-wide ascending sort of the chunk by (dst, src): bitonic network, every stage
-// ends with a block barrier.  `n` is a power of two.
-__device__ __forceinline__ void sort_chunk(ScatterSmem& sm, int n, int tid, int nthreads) {
-  for (int k = 2; k <= n; k <<= 1) {
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int i = tid; i < (n >> 1); i += nthreads) {
-        const int lo = ((i & ~(j - 1)) << 1) | (i & (j - 1));
-        const int hi = lo + j;
-        const bool up = (lo & k) == 0;
-        const long long dl = sm.dst[lo], dh = sm.dst[hi];
-        const long long sl = sm.src[lo], sh = sm.src[hi];
-        const bool greater = dl > dh || (dl == dh && sl > sh);
-        if (greater == up) {
-          sm.dst[lo] = dh;
-          sm.dst[hi] = dl;
-          sm.src[lo] = sh;
-          sm.src[hi] = sl;
-          const int pl = sm.piece[lo];
-          sm.piece[lo] = sm.piece[hi];
-          sm.piece[hi] = pl;
-        }
-      }
-      __syncthreads();
-    }
+// Geometry of a launch's pieces and sub-warps.
+struct ScatterShape {
+  Pieces piece;    // pieces of at most 32 * kScatterVecs vectors
+  long long last;  // vectors of a unit's last piece
+  int lshift;      // log2 lanes per piece
+};
+
+__host__ __device__ __forceinline__ ScatterShape scatter_shape(long long nvec) {
+  ScatterShape r;
+  r.piece = make_pieces(nvec, 32ll * kScatterVecs);
+  r.last = r.piece.count > 0 ? nvec - (r.piece.count - 1) * r.piece.vecs : 0;
+  const long long per_lane = (r.piece.vecs + kScatterVecs - 1) / kScatterVecs;
+  r.lshift = lane_shift_of(per_lane);
+  return r;
+}
+
+// Destination and updates byte offsets of piece w; the destination carries the
+// short-piece flag in bit 0 (destinations are multiples of V >= 4).
+template <typename I, int V>
+__device__ __forceinline__ void piece_offsets(const WindowPlan& p, const I* __restrict__ idx, long long w,
+                                              const ScatterShape& sh, long long* dflag, long long* s) {
+  long long u = w, pc = 0;
+  if (sh.piece.count > 1) {
+    u = w / sh.piece.count;
+    pc = w - u * sh.piece.count;
+  }
+  long long oa, ob;
+  unit_offsets<I>(p, idx, u, &oa, &ob);
+  const long long shift = pc * sh.piece.vecs * V;
+  const bool short_piece = pc == sh.piece.count - 1 && sh.last != sh.piece.vecs;
+  *dflag = (oa * p.esize + shift) | static_cast<long long>(short_piece);
+  *s = ob * p.esize + shift;
+}
+
+__device__ __forceinline__ unsigned long long key_of(long long dflag, int vbytes) {
+  return (static_cast<unsigned long long>((dflag & ~1ll) / vbytes) << 1) | static_cast<unsigned long long>(dflag & 1);
+}
+
+__device__ __forceinline__ long long dflag_of(unsigned long long key, int vbytes) {
+  return static_cast<long long>(key >> 1) * vbytes | static_cast<long long>(key & 1);
+}
+
+// Hash table of a chunk of C pieces: 3C/2 slots, so a free or matching slot exists.
+template <int C>
+struct GroupTable {
+  static constexpr int H = C + C / 2;
+  unsigned long long key[H];
+  unsigned count[H];  // pieces per slot, then the exclusive group offsets
+  unsigned warp_total[32];
+};
+
+template <int C>
+__device__ __forceinline__ void clear_table(GroupTable<C>& t, int tid, int nthreads) {
+  for (int q = tid; q < GroupTable<C>::H; q += nthreads) {
+    t.key[q] = kEmptySlot;
+    t.count[q] = 0;
   }
 }
 
-// Scatters `units` update runs of `nvec` V-byte vectors into `out`.  The block is
-// whole warps; JB = vectors per lane per piece (pieces are 32 * JB vectors).
-template <typename F, typename I, int V, int JB>
+// Slot of a key, inserting it.  At most C keys live in 3C/2 slots, so a free or
+// matching slot exists and the probe ends within H steps.
+template <int C>
+__device__ __forceinline__ unsigned find_slot(GroupTable<C>& t, unsigned long long key) {
+  constexpr unsigned H = GroupTable<C>::H;
+  unsigned h = __umulhi(static_cast<unsigned>((key * 0x9E3779B97F4A7C15ull) >> 32), H);
+  for (unsigned probe = 0; probe < H; ++probe) {
+    const unsigned long long prev = atomicCAS(&t.key[h], kEmptySlot, key);
+    if (prev == kEmptySlot || prev == key) break;
+    h = h + 1 == H ? 0 : h + 1;
+  }
+  return h;
+}
+
+// Warp-aggregated insert, called by all 32 lanes (`key` == kEmptySlot: no piece):
+// lanes holding the same key elect one leader that inserts it and reserves their
+// ranks with one atomic, so a hot destination costs one shared atomic per warp.
+template <int C>
+__device__ __forceinline__ unsigned insert_key(GroupTable<C>& t, unsigned long long key, unsigned* rank) {
+  const unsigned peers = __match_any_sync(0xffffffffu, key);
+  const int lane = threadIdx.x & 31;
+  const int leader = __ffs(peers) - 1;
+  unsigned slot = 0, base = 0;
+  if (lane == leader && key != kEmptySlot) {
+    slot = find_slot(t, key);
+    base = atomicAdd(&t.count[slot], static_cast<unsigned>(__popc(peers)));
+  }
+  slot = __shfl_sync(0xffffffffu, slot, leader);
+  base = __shfl_sync(0xffffffffu, base, leader);
+  *rank = base + static_cast<unsigned>(__popc(peers & ((1u << lane) - 1u)));
+  return slot;
+}
+
+// Exclusive block scan of t.count in place (block of whole warps; barriers inside).
+template <int C>
+__device__ __forceinline__ void scan_counts(GroupTable<C>& t, int tid, int nthreads) {
+  constexpr int n = GroupTable<C>::H;
+  const int per = (n + nthreads - 1) / nthreads;
+  const int lo = tid * per;
+  unsigned local = 0;
+  for (int q = 0; q < per; ++q)
+    if (lo + q < n) local += t.count[lo + q];
+  const int lane = tid & 31, warp = tid >> 5;
+  unsigned incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) t.warp_total[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = nthreads >> 5;
+    const unsigned v = lane < nw ? t.warp_total[lane] : 0;
+    unsigned vi = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const unsigned y = __shfl_up_sync(0xffffffffu, vi, o);
+      if (lane >= o) vi += y;
+    }
+    if (lane < nw) t.warp_total[lane] = vi - v;
+  }
+  __syncthreads();
+  unsigned run = t.warp_total[warp] + incl - local;
+  for (int q = 0; q < per; ++q) {
+    if (lo + q < n) {
+      const unsigned c = t.count[lo + q];
+      t.count[lo + q] = run;
+      run += c;
+    }
+  }
+  __syncthreads();
+}
+
+// One sub-warp's running sum over consecutive grouped pieces with one destination.
+// The sum starts at -0.0, the exact identity of IEEE addition (x + -0.0 == x for
+// every x, signed zeros included), so every piece is simply added.
+template <typename F, int V>
+struct Fold {
+  static constexpr int VE = V / sizeof(F);
+  using R = typename Raw<V>::T;
+  F acc[kScatterVecs][VE];
+  long long dflag = -1;
+
+  __device__ __forceinline__ void flush(unsigned char* out, int lig, int L, const ScatterShape& sh) {
+    if (dflag < 0) return;
+    const int len = static_cast<int>((dflag & 1) ? sh.last : sh.piece.vecs);
+    unsigned char* base = out + (dflag & ~1ll);
+#pragma unroll
+    for (int j = 0; j < kScatterVecs; ++j) {
+      const int v = lig + L * j;
+      if (v < len) red_add<F, V>(base + static_cast<long long>(v) * V, acc[j]);
+    }
+  }
+
+  // Adds one piece (its lane's vectors in x); a new destination first flushes.
+  __device__ __forceinline__ void take(unsigned char* out, int lig, int L, const ScatterShape& sh, long long edflag,
+                                       const R (&x)[kScatterVecs]) {
+    if (edflag != dflag) {
+      flush(out, lig, L, sh);
+      dflag = edflag;
+#pragma unroll
+      for (int j = 0; j < kScatterVecs; ++j)
+#pragma unroll
+        for (int q = 0; q < VE; ++q) acc[j][q] = F(-0.0);
+    }
+    const int len = static_cast<int>((edflag & 1) ? sh.last : sh.piece.vecs);
+#pragma unroll
+    for (int j = 0; j < kScatterVecs; ++j) {
+      if (lig + L * j < len) {
+        F y[VE];
+        raw_to_f<F, V>(x[j], y);
+#pragma unroll
+        for (int q = 0; q < VE; ++q) acc[j][q] += y[q];
+      }
+    }
+  }
+};
+
+// ---- one-kernel path ----------------------------------------------------------
+constexpr int kScatterChunk = 1024;  // pieces grouped per block and step
+
+struct ScatterSmem {
+  GroupTable<kScatterChunk> t;
+  long long src[kScatterChunk];          // updates byte offset, by position in the chunk
+  unsigned short slot[kScatterChunk];    // hash slot, by position
+  unsigned short rank[kScatterChunk];    // rank within the slot's pieces, by position
+  unsigned short order[kScatterChunk];   // positions in group order
+};
+
+// Groups the chunk of pieces [c0, c0 + n) into sm.order (barriers included).
+template <typename I, int V>
+__device__ __forceinline__ void group_chunk(const WindowPlan& p, const I* __restrict__ idx, long long c0, int n,
+                                            const ScatterShape& sh, ScatterSmem& sm, int tid, int nthreads) {
+  clear_table(sm.t, tid, nthreads);
+  __syncthreads();
+  // Every lane of a warp takes the same number of turns (insert_key is warp-wide).
+  for (int i0 = tid - (tid & 31); i0 < kScatterChunk; i0 += nthreads) {
+    const int i = i0 + (tid & 31);
+    long long dflag = 0, s = 0;
+    unsigned long long key = kEmptySlot;
+    if (i < n) {
+      piece_offsets<I, V>(p, idx, c0 + i, sh, &dflag, &s);
+      key = key_of(dflag, V);
+    }
+    unsigned rank;
+    const unsigned slot = insert_key(sm.t, key, &rank);
+    if (i < n) {
+      sm.slot[i] = static_cast<unsigned short>(slot);
+      sm.rank[i] = static_cast<unsigned short>(rank);
+      sm.src[i] = s;
+    }
+  }
+  __syncthreads();
+  scan_counts(sm.t, tid, nthreads);
+  for (int i = tid; i < n; i += nthreads) sm.order[sm.t.count[sm.slot[i]] + sm.rank[i]] = static_cast<unsigned short>(i);
+  __syncthreads();
+}
+
+// Folds the grouped chunk, warp w taking [beg, end), sub-warps consecutive pieces.
+template <typename F, int V>
+__device__ __forceinline__ void fold_chunk(const ScatterSmem& sm, unsigned char* __restrict__ out,
+                                           const unsigned char* __restrict__ upd, const ScatterShape& sh, int beg,
+                                           int end, int lane) {
+  using R = typename Raw<V>::T;
+  const int L = 1 << sh.lshift;
+  const int E = 32 >> sh.lshift;
+  const int sub = lane >> sh.lshift;
+  const int lig = lane & (L - 1);
+  Fold<F, V> f;
+  for (int e0 = beg; e0 < end; e0 += E) {
+    const int e = e0 + sub;
+    if (e < end) {
+      const int i = sm.order[e];
+      const long long dflag = dflag_of(sm.t.key[sm.slot[i]], V);
+      const long long src = sm.src[i];
+      const int len = static_cast<int>((dflag & 1) ? sh.last : sh.piece.vecs);
+      R x[kScatterVecs];
+#pragma unroll
+      for (int j = 0; j < kScatterVecs; ++j) {
+        const int v = lig + L * j;
+        if (v < len) x[j] = ld_stream<V>(upd + src + static_cast<long long>(v) * V);
+      }
+      f.take(out, lig, L, sh, dflag, x);
+    }
+  }
+  f.flush(out, lig, L, sh);
+}
+
+// One-kernel scatter of `units` update runs of `nvec` V-byte vectors (block of whole warps).
+template <typename F, typename I, int V>
 __device__ __forceinline__ void scatter_units(const WindowPlan& p, unsigned char* __restrict__ out,
                                               const unsigned char* __restrict__ upd, const I* __restrict__ idx,
                                               long long units, long long nvec, ScatterSmem& sm) {
-  using R = typename Raw<V>::T;
-  constexpr int VE = V / sizeof(F);
-  constexpr int D = JB >= 4 ? 2 : 4;  // pieces in flight per warp
-  const Pieces piece = make_pieces(nvec, 32ll * JB);
-  const long long total = units * piece.count;
+  const ScatterShape sh = scatter_shape(nvec);
+  const long long total = units * sh.piece.count;
   const int tid = threadIdx.x;
   const int nthreads = blockDim.x;
   const int lane = tid & 31;
+  const int warp = tid >> 5;
   const int nwarps = nthreads >> 5;
-  const int per_warp = (kScatterChunk + nwarps - 1) / nwarps;
-  const int beg = (tid >> 5) * per_warp;
-  const int end = beg + per_warp < kScatterChunk ? beg + per_warp : kScatterChunk;
   for (long long c0 = static_cast<long long>(blockIdx.x) * kScatterChunk; c0 < total;
        c0 += static_cast<long long>(gridDim.x) * kScatterChunk) {
-    for (int i = tid; i < kScatterChunk; i += nthreads) {
-      const long long w = c0 + i;
-      long long d = kScatterSentinel, s = 0, pc = 0;
-      if (w < total) {
-        long long u = w;
-        if (piece.count > 1) {
-          u = w / piece.count;
-          pc = w - u * piece.count;
-        }
-        long long oa, ob;
-        unit_offsets<I>(p, idx, u, &oa, &ob);
-        d = oa * p.esize + pc * piece.vecs * V;
-        s = ob * p.esize + pc * piece.vecs * V;
-      }
-      sm.dst[i] = d;
-      sm.src[i] = s;
-      sm.piece[i] = static_cast<int>(pc);
-    }
+    const int n = total - c0 < kScatterChunk ? static_cast<int>(total - c0) : kScatterChunk;
+    group_chunk<I, V>(p, idx, c0, n, sh, sm, tid, nthreads);
+    const int per_warp = (n + nwarps - 1) / nwarps;
+    const int beg = warp * per_warp < n ? warp * per_warp : n;
+    const int end = beg + per_warp < n ? beg + per_warp : n;
+    fold_chunk<F, V>(sm, out, upd, sh, beg, end, lane);
     __syncthreads();
-    sort_chunk(sm, kScatterChunk, tid, nthreads);
+  }
+}
 
-    F acc[JB][VE];
-    long long cur_d = -1, cur_p = -1, cur_len = 0;
-    for (int e0 = beg; e0 < end; e0 += D) {
-      R x[D][JB];
-      long long ed[D], ep[D], elen[D];
+// ---- two-kernel path ---------------------------------------------------------
+// A grouped piece in the workspace list.
+struct alignas(16) GroupedPiece {
+  long long dflag;  // destination byte offset | short-piece flag
+  long long src;    // updates byte offset
+};
+
+constexpr int kGroupChunk = 2048;  // pieces grouped per block and step of pass 1
+constexpr int kGroupThreads = 512;
+constexpr int kGroupPer = kGroupChunk / kGroupThreads;
+
+// Pass 1: the grouped list of every chunk, in chunk order (one entry per piece).
+// Each thread keeps its kGroupPer pieces in registers and writes them straight to
+// their grouped positions.  Block of kGroupThreads.
+template <typename I, int V>
+__device__ __forceinline__ void scatter_group_pass(const WindowPlan& p, const I* __restrict__ idx, long long units,
+                                                   long long nvec, GroupedPiece* __restrict__ list,
+                                                   GroupTable<kGroupChunk>& t) {
+  const ScatterShape sh = scatter_shape(nvec);
+  const long long total = units * sh.piece.count;
+  const int tid = threadIdx.x;
+  for (long long c0 = static_cast<long long>(blockIdx.x) * kGroupChunk; c0 < total;
+       c0 += static_cast<long long>(gridDim.x) * kGroupChunk) {
+    const int n = total - c0 < kGroupChunk ? static_cast<int>(total - c0) : kGroupChunk;
+    clear_table(t, tid, kGroupThreads);
+    __syncthreads();
+    long long dflag[kGroupPer], src[kGroupPer];
+    unsigned long long key[kGroupPer];
+    unsigned slot[kGroupPer], rank[kGroupPer];
+    // Phases across the thread's pieces, so their index loads and shared atomics
+    // overlap instead of forming one dependent chain per piece.
 #pragma unroll
-      for (int dd = 0; dd < D; ++dd) {
-        const int e = e0 + dd;
-        ed[dd] = kScatterSentinel;
-        if (e < end) ed[dd] = sm.dst[e];
-        if (ed[dd] != kScatterSentinel) {
-          const long long s = sm.src[e];
-          ep[dd] = sm.piece[e];
-          const long long left = nvec - ep[dd] * piece.vecs;
-          elen[dd] = left < piece.vecs ? left : piece.vecs;
-#pragma unroll
-          for (int j = 0; j < JB; ++j) {
-            const long long v = lane + 32 * j;
-            if (v < elen[dd]) x[dd][j] = ld_stream<V>(upd + s + v * V);
-          }
-        }
-      }
-#pragma unroll
-      for (int dd = 0; dd < D; ++dd) {
-        if (ed[dd] == kScatterSentinel) continue;
-        const bool same = ed[dd] == cur_d && ep[dd] == cur_p;
-        if (!same && cur_d >= 0) {
-#pragma unroll
-          for (int j = 0; j < JB; ++j) {
-            const long long v = lane + 32 * j;
-            if (v < cur_len) red_add<F, V>(out + cur_d + v * V, acc[j]);
-          }
-        }
-#pragma unroll
-        for (int j = 0; j < JB; ++j) {
-          const long long v = lane + 32 * j;
-          if (v < elen[dd]) {
-            F y[VE];
-            raw_to_f<F, V>(x[dd][j], y);
-#pragma unroll
-            for (int q = 0; q < VE; ++q) acc[j][q] = same ? acc[j][q] + y[q] : y[q];
-          }
-        }
-        cur_d = ed[dd];
-        cur_p = ep[dd];
-        cur_len = elen[dd];
-      }
+    for (int q = 0; q < kGroupPer; ++q) {
+      const int i = tid + q * kGroupThreads;
+      dflag[q] = -1;
+      src[q] = 0;
+      if (i < n) piece_offsets<I, V>(p, idx, c0 + i, sh, &dflag[q], &src[q]);
+      key[q] = dflag[q] >= 0 ? key_of(dflag[q], V) : kEmptySlot;
+      slot[q] = __umulhi(static_cast<unsigned>((key[q] * 0x9E3779B97F4A7C15ull) >> 32), GroupTable<kGroupChunk>::H);
     }
-    if (cur_d >= 0) {
+    unsigned long long prev[kGroupPer];
 #pragma unroll
-      for (int j = 0; j < JB; ++j) {
-        const long long v = lane + 32 * j;
-        if (v < cur_len) red_add<F, V>(out + cur_d + v * V, acc[j]);
+    for (int q = 0; q < kGroupPer; ++q)
+      prev[q] = key[q] != kEmptySlot ? atomicCAS(&t.key[slot[q]], kEmptySlot, key[q]) : kEmptySlot;
+#pragma unroll
+    for (int q = 0; q < kGroupPer; ++q)
+      if (prev[q] != kEmptySlot && prev[q] != key[q]) slot[q] = find_slot(t, key[q]);  // occupied by another key
+#pragma unroll
+    for (int q = 0; q < kGroupPer; ++q)
+      if (key[q] != kEmptySlot) rank[q] = atomicAdd(&t.count[slot[q]], 1u);
+    __syncthreads();
+    scan_counts(t, tid, kGroupThreads);
+#pragma unroll
+    for (int q = 0; q < kGroupPer; ++q) {
+      if (dflag[q] >= 0) {
+        GroupedPiece g;
+        g.dflag = dflag[q];
+        g.src = src[q];
+        list[c0 + t.count[slot[q]] + rank[q]] = g;
       }
     }
     __syncthreads();
   }
+}
+
+constexpr int kFoldSlots = 4;  // steps in flight per lane in the streaming fold
+
+__host__ __device__ __forceinline__ int fold_stage_bytes_per_warp(int vbytes) {
+  return kFoldSlots * kScatterVecs * 32 * vbytes;
+}
+
+template <int V>
+__device__ __forceinline__ void cp_async_v(void* smem, const void* gmem) {
+  const unsigned a = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+  if constexpr (V == 16) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(a), "l"(gmem) : "memory");
+  } else if constexpr (V == 8) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(a), "l"(gmem) : "memory");
+  } else {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(a), "l"(gmem) : "memory");
+  }
+}
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// The list pieces of one warp, read 32 at a time (one per lane, the next batch
+// prefetched) and handed to the sub-warps by shuffles.  `at` must be called with
+// non-decreasing batches, advancing at most one batch a call, by the whole warp.
+struct ListCursor {
+  const GroupedPiece* list;
+  long long beg, end;
+  long long batch;
+  longlong2 cur, next;
+
+  __device__ __forceinline__ longlong2 load(long long b, int lane) const {
+    const long long q = beg + (b << 5) + lane;
+    if (q < end) return __ldg(reinterpret_cast<const longlong2*>(list) + q);
+    return make_longlong2(-1, 0);
+  }
+
+  __device__ __forceinline__ void start(int lane) {
+    batch = 0;
+    cur = load(0, lane);
+    next = load(1, lane);
+  }
+
+  __device__ __forceinline__ void at(long long e, int lane, long long* dflag, long long* src) {
+    if ((e >> 5) != batch) {
+      ++batch;
+      cur = next;
+      next = load(batch + 1, lane);
+    }
+    const int from = static_cast<int>(e & 31);
+    *dflag = __shfl_sync(0xffffffffu, cur.x, from);
+    *src = __shfl_sync(0xffffffffu, cur.y, from);
+  }
+};
+
+// Pass 2: fold the grouped list.  Warp w of the grid takes a contiguous range of the
+// list; step t hands piece t*E + sub of the range to sub-warp sub.  Each lane keeps
+// kFoldSlots steps of its own vectors in flight (cp.async into its ring slots; it
+// reads back only what it copied, so no warp barrier is needed).  The loop is
+// unrolled by kFoldSlots so the ring slot and the remembered destinations are static.
+template <typename F, int V>
+__device__ __forceinline__ void scatter_fold_pass(const GroupedPiece* __restrict__ list, long long total,
+                                                  long long nvec, unsigned char* __restrict__ out,
+                                                  const unsigned char* __restrict__ upd, unsigned char* stage) {
+  using R = typename Raw<V>::T;
+  constexpr int S = kFoldSlots;
+  const ScatterShape sh = scatter_shape(nvec);
+  const int lane = threadIdx.x & 31;
+  const long long nw = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  const long long w = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const long long per = (total + nw - 1) / nw;
+  const long long beg = w * per < total ? w * per : total;
+  const long long end = beg + per < total ? beg + per : total;
+  const int L = 1 << sh.lshift;
+  const int E = 32 >> sh.lshift;
+  const int sub = lane >> sh.lshift;
+  const int lig = lane & (L - 1);
+  const long long steps = (end - beg + E - 1) / E;
+  unsigned char* ring = stage + (threadIdx.x >> 5) * fold_stage_bytes_per_warp(V);
+  ListCursor cur{list, beg, end, 0, {}, {}};
+  cur.start(lane);
+  long long pend[S];  // destination | flag of the step in each slot (-1: none)
+  auto issue = [&](long long t, int slot) {
+    long long dflag = -1, src = 0;
+    if (t < steps) {
+      cur.at(t * E + sub, lane, &dflag, &src);
+      if (dflag >= 0) {
+        const int len = static_cast<int>((dflag & 1) ? sh.last : sh.piece.vecs);
+#pragma unroll
+        for (int j = 0; j < kScatterVecs; ++j) {
+          const int v = lig + L * j;
+          if (v < len)
+            cp_async_v<V>(ring + ((slot * kScatterVecs + j) * 32 + lane) * V, upd + src + static_cast<long long>(v) * V);
+        }
+      }
+    }
+    cp_async_commit();
+    return dflag;
+  };
+  Fold<F, V> f;
+#pragma unroll
+  for (int k = 0; k < S - 1; ++k) pend[k] = issue(k, k);
+  for (long long t0 = 0; t0 < steps; t0 += S) {
+#pragma unroll
+    for (int k = 0; k < S; ++k) {
+      pend[(k + S - 1) % S] = issue(t0 + k + S - 1, (k + S - 1) % S);
+      cp_async_wait<S - 1>();
+      const long long dflag = pend[k];
+      if (dflag >= 0) {
+        const int len = static_cast<int>((dflag & 1) ? sh.last : sh.piece.vecs);
+        R x[kScatterVecs];
+#pragma unroll
+        for (int j = 0; j < kScatterVecs; ++j)
+          if (lig + L * j < len) x[j] = *reinterpret_cast<const R*>(ring + ((k * kScatterVecs + j) * 32 + lane) * V);
+        f.take(out, lig, L, sh, dflag, x);
+      }
+    }
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  f.flush(out, lig, L, sh);
+}
+
+// ---- TMA fold (16-byte vectors) ------------------------------------------------
+// The streaming fold for rows whose pieces are whole 16-byte vectors: lane 0 moves
+// every piece with one bulk copy (cp.async.bulk, completion on a per-slot mbarrier)
+// into a ring in shared memory, and adds every group to memory with one bulk
+// reduction (cp.reduce.async.bulk .add) from there: a group of one piece goes back
+// out untouched, a longer group is summed by the warp into its last piece's slot
+// first.  Per piece the warp executes a few dozen instructions, whatever its size.
+constexpr int kBulkRingBytes = 8192;  // per warp
+constexpr int kBulkMaxSlots = 16;
+constexpr unsigned kBulkWaitLimit = 1u << 20;  // try_wait rounds before giving up
+
+__host__ __device__ __forceinline__ int bulk_stage_bytes_per_warp() { return kBulkRingBytes + kBulkMaxSlots * 8; }
+
+__device__ __forceinline__ unsigned smem_addr(const void* p) {
+  return static_cast<unsigned>(__cvta_generic_to_shared(p));
+}
+
+// Bounded wait for phase `parity` of an mbarrier; false when the limit ran out.  Each
+// try may suspend the thread for up to kBulkSuspendNs while the phase is pending,
+// so a waiting warp does not spin on the issue slots.
+constexpr unsigned kBulkSuspendNs = 2000;
+__device__ __forceinline__ bool bar_wait(unsigned bar, unsigned parity) {
+  for (unsigned it = 0; it < kBulkWaitLimit; ++it) {
+    unsigned ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "n"(kBulkSuspendNs)
+        : "memory");
+    if (ok) return true;
+  }
+  return false;
+}
+
+template <typename F>
+__device__ __forceinline__ void bulk_reduce(unsigned char* gdst, unsigned ssrc, unsigned bytes) {
+  if constexpr (sizeof(F) == 8) {
+    asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f64 [%0], [%1], %2;" ::"l"(gdst), "r"(ssrc),
+                 "r"(bytes)
+                 : "memory");
+  } else {
+    asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f32 [%0], [%1], %2;" ::"l"(gdst), "r"(ssrc),
+                 "r"(bytes)
+                 : "memory");
+  }
+}
+
+// Consume-side view of the list: the piece at e and the destination of e + 1.
+__device__ __forceinline__ long long next_dflag(const ListCursor& c, long long e, long long n) {
+  if (e + 1 >= n) return -1;
+  const int q = static_cast<int>((e + 1) & 31);
+  const long long from_cur = __shfl_sync(0xffffffffu, c.cur.x, q);
+  const long long from_next = __shfl_sync(0xffffffffu, c.next.x, 0);
+  return q == 0 ? from_next : from_cur;
+}
+
+// `status` receives 1 when a wait ran out (the warp then stops).
+template <typename F>
+__device__ __forceinline__ void scatter_fold_bulk(const GroupedPiece* __restrict__ list, long long total,
+                                                  long long nvec, unsigned char* __restrict__ out,
+                                                  const unsigned char* __restrict__ upd, unsigned char* stage,
+                                                  int* status) {
+  constexpr int V = 16;
+  constexpr int VE = V / sizeof(F);
+  const ScatterShape sh = scatter_shape(nvec);
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const long long nw = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  const long long w = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + warp;
+  const long long per = (total + nw - 1) / nw;
+  const long long beg = w * per < total ? w * per : total;
+  const long long end = beg + per < total ? beg + per : total;
+  const long long n = end - beg;
+  const int full_bytes = static_cast<int>(sh.piece.vecs) * V;
+  int slots = kBulkRingBytes / full_bytes;
+  if (slots > kBulkMaxSlots) slots = kBulkMaxSlots;
+  unsigned char* ring = stage + warp * bulk_stage_bytes_per_warp();
+  const unsigned bars = smem_addr(ring + kBulkRingBytes);
+  if (lane == 0) {
+    for (int q = 0; q < slots; ++q) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bars + 8 * q) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncwarp();
+  ListCursor ic{list, beg, end, 0, {}, {}};
+  ListCursor fc{list, beg, end, 0, {}, {}};
+  ic.start(lane);
+  fc.start(lane);
+  const int ahead = slots - 2;  // loads in flight; two slots drain their reductions
+  unsigned pending = 0;          // bit q: a load into slot q is in flight
+  // Lane 0 loads piece k into slot `slot`; reuse waits for the slot's previous
+  // reduction to finish reading (one bulk group is committed per consumed piece).
+  auto issue = [&](long long k, int slot) {
+    long long dflag, src;
+    ic.at(k, lane, &dflag, &src);
+    if (lane == 0) {
+      const unsigned bytes = static_cast<unsigned>(((dflag & 1) ? sh.last : sh.piece.vecs) * V);
+      if (k >= slots) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bars + 8 * slot), "r"(bytes)
+                   : "memory");
+      asm volatile("cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                       smem_addr(ring + slot * full_bytes)),
+                   "l"(upd + src), "r"(bytes), "r"(bars + 8 * slot)
+                   : "memory");
+    }
+    pending |= 1u << slot;
+  };
+  int islot = 0;
+  for (long long k = 0; k < ahead && k < n; ++k) {
+    issue(k, islot);
+    islot = islot + 1 == slots ? 0 : islot + 1;
+  }
+  unsigned phases = 0;  // bit q: parity to wait for on slot q
+  long long prev = -1;
+  F acc[kScatterVecs][VE];
+  bool failed = false;
+  int slot = 0;
+  for (long long k = 0; k < n; ++k) {
+    if (k + ahead < n) {
+      issue(k + ahead, islot);
+      islot = islot + 1 == slots ? 0 : islot + 1;
+    }
+    // The warp stops together if any lane's wait ran out.
+    if (__any_sync(0xffffffffu, !bar_wait(bars + 8 * slot, (phases >> slot) & 1u))) {
+      failed = true;
+      break;
+    }
+    phases ^= 1u << slot;
+    pending &= ~(1u << slot);
+    long long dflag, src;
+    fc.at(k, lane, &dflag, &src);
+    const long long nd = next_dflag(fc, k, n);
+    const bool first = dflag != prev;
+    const bool last = dflag != nd;
+    prev = dflag;
+    const int len = static_cast<int>((dflag & 1) ? sh.last : sh.piece.vecs);
+    unsigned char* sp = ring + slot * full_bytes;
+    if (!(first && last)) {
+#pragma unroll
+      for (int j = 0; j < kScatterVecs; ++j) {
+        const int v = lane + 32 * j;
+        if (v < len) {
+          F y[VE];
+          raw_to_f<F, V>(*reinterpret_cast<const uint4*>(sp + v * V), y);
+#pragma unroll
+          for (int q = 0; q < VE; ++q) acc[j][q] = first ? y[q] : acc[j][q] + y[q];
+        }
+      }
+      if (last) {
+#pragma unroll
+        for (int j = 0; j < kScatterVecs; ++j) {
+          const int v = lane + 32 * j;
+          if (v < len) memcpy(sp + v * V, &acc[j][0], V);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      }
+    }
+    __syncwarp();
+    if (lane == 0) {
+      if (last) bulk_reduce<F>(out + (dflag & ~1ll), smem_addr(sp), static_cast<unsigned>(len * V));
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    }
+    slot = slot + 1 == slots ? 0 : slot + 1;
+  }
+  if (failed) {
+    if (lane == 0) atomicExch(status, 1);
+    // Drain the loads still in flight (each wait bounded) before the ring goes away.
+    for (int q = 0; q < slots; ++q)
+      if ((pending >> q) & 1u) bar_wait(bars + 8 * q, (phases >> q) & 1u);
+  }
+  if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+  __syncwarp();
 }
 
 // One element per thread (any geometry): atomics per component, as the reference.

@@ -4,6 +4,8 @@
 // and launch a kernel compiled for that width and index type.
 #include <cuda_runtime.h>
 
+#include <atomic>
+
 #include "gather_scatter_core.cuh"
 #include "plan_common.h"
 #include "runtime.h"
@@ -20,17 +22,55 @@ __global__ void __launch_bounds__(kGatherThreads) k_gather(WindowPlan p, void* o
                      static_cast<const I*>(indices), units, nvec, pc, lshift, slots);
 }
 
-template <typename F, typename I, int V, int JB>
-__global__ void __launch_bounds__(kScatterThreads) k_scatter(WindowPlan p, void* out, const void* indices,
-                                                             const void* updates, long long units, long long nvec) {
+// One-kernel scatter: each block groups a chunk in shared memory and folds it.
+template <typename F, typename I, int V>
+__global__ void __launch_bounds__(kScatterThreads, 2) k_scatter(WindowPlan p, void* out, const void* indices,
+                                                                const void* updates, long long units,
+                                                                long long nvec) {
   __shared__ ScatterSmem sm;
-  scatter_units<F, I, V, JB>(p, static_cast<unsigned char*>(out), static_cast<const unsigned char*>(updates),
-                             static_cast<const I*>(indices), units, nvec, sm);
+  scatter_units<F, I, V>(p, static_cast<unsigned char*>(out), static_cast<const unsigned char*>(updates),
+                         static_cast<const I*>(indices), units, nvec, sm);
+}
+
+// Two-kernel scatter, pass 1: grouped list of every chunk; clears the status word.
+template <typename I, int V>
+__global__ void __launch_bounds__(kGroupThreads, 2) k_scatter_group(WindowPlan p, const void* indices,
+                                                                    long long units, long long nvec,
+                                                                    GroupedPiece* list, int* status) {
+  __shared__ GroupTable<kGroupChunk> t;
+  if (blockIdx.x == 0 && threadIdx.x == 0) *status = 0;
+  scatter_group_pass<I, V>(p, static_cast<const I*>(indices), units, nvec, list, t);
+}
+
+constexpr int kFoldThreads = 256;
+constexpr size_t kScatterStatusBytes = 16;  // leading status word of the workspace
+constexpr int kFoldBlocksPerSm = 3;
+
+// Two-kernel scatter, pass 2 for 16-byte vectors: bulk copies in, bulk reductions out.
+template <typename F>
+__global__ void __launch_bounds__(kFoldThreads, kFoldBlocksPerSm) k_scatter_fold_bulk(const GroupedPiece* list,
+                                                                                     long long total, long long nvec,
+                                                                                     void* out, const void* updates,
+                                                                                     int* status) {
+  extern __shared__ __align__(16) unsigned char stage[];
+  scatter_fold_bulk<F>(list, total, nvec, static_cast<unsigned char*>(out), static_cast<const unsigned char*>(updates),
+                       stage, status);
+}
+
+// Two-kernel scatter, pass 2: streaming fold of the list (no block barrier).
+template <typename F, int V>
+__global__ void __launch_bounds__(kFoldThreads, kFoldBlocksPerSm) k_scatter_fold(const GroupedPiece* list,
+                                                                                long long total, long long nvec,
+                                                                                void* out, const void* updates) {
+  extern __shared__ __align__(16) unsigned char stage[];
+  scatter_fold_pass<F, V>(list, total, nvec, static_cast<unsigned char*>(out),
+                          static_cast<const unsigned char*>(updates), stage);
 }
 
 constexpr int kGatherVariant = 48;
 constexpr int kScatterVariant = 49;
 constexpr unsigned long long kResidentBlocks = 148ull * 8;  // grid cap: a few waves of resident blocks
+constexpr unsigned long long kScatterBlocksPerSm = 2;
 
 int index_size(int index_dtype) {
   switch (index_dtype) {
@@ -189,10 +229,10 @@ t4a_launch scatter_geometry(const WindowPlan& p) {
   using namespace plan;
   const long long units = p.batch.len * p.wrest.len;
   if (units <= 0 || p.run <= 0 || !scatter_windows_fit(p)) return empty_launch();
-  const Pieces pc = make_pieces(p.run, 32ll * 2);
-  const unsigned long long chunks = ceil_div(static_cast<unsigned long long>(units * pc.count), kScatterChunk);
+  const ScatterShape sh = scatter_shape(p.run);  // the narrowest vectors bound the piece count
+  const unsigned long long chunks = ceil_div(static_cast<unsigned long long>(units * sh.piece.count), kScatterChunk);
   unsigned long long grid = chunks;
-  if (grid > kResidentBlocks) grid = kResidentBlocks;  // blocks are grid-stride over chunks
+  if (grid > 148 * kScatterBlocksPerSm) grid = 148 * kScatterBlocksPerSm;  // blocks are grid-stride over chunks
   return make_launch(grid, kScatterThreads, 1, 0, kScatterVariant);
 }
 
@@ -216,44 +256,76 @@ int launch_gather_typed(const WindowPlan& p, dim3 grid, cudaStream_t s, void* ou
   return runtime::check_launch();
 }
 
+// Raises a kernel's dynamic shared memory limit once on each device.
+template <typename K>
+int allow_dynamic_smem(K kernel, unsigned bytes, std::atomic<unsigned long long>& raised) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return runtime::check_launch();
+  const unsigned long long bit = 1ull << (dev & 63);
+  if ((raised.load(std::memory_order_relaxed) & bit) == 0) {
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+      return runtime::check_launch();
+    raised.fetch_or(bit);
+  }
+  return T4A_OK;
+}
+
 template <typename F, typename I, int V>
 void launch_scatter_width(const WindowPlan& p, dim3 grid, cudaStream_t s, void* out, const void* indices,
-                          const void* updates, long long units, long long nvec) {
-  const dim3 block(kScatterThreads);
-  if (nvec <= 32) {
-    k_scatter<F, I, V, 1><<<grid, block, 0, s>>>(p, out, indices, updates, units, nvec);
-  } else if (nvec <= 64) {
-    k_scatter<F, I, V, 2><<<grid, block, 0, s>>>(p, out, indices, updates, units, nvec);
+                          const void* updates, long long units, long long nvec, void* workspace) {
+  if (workspace == nullptr) {
+    k_scatter<F, I, V><<<grid, dim3(kScatterThreads), 0, s>>>(p, out, indices, updates, units, nvec);
+    return;
+  }
+  const ScatterShape sh = scatter_shape(nvec);
+  const long long total = units * sh.piece.count;
+  // Workspace: the status word (16 bytes), then the grouped list.
+  int* status = static_cast<int*>(workspace);
+  auto* list = reinterpret_cast<GroupedPiece*>(static_cast<unsigned char*>(workspace) + kScatterStatusBytes);
+  unsigned long long gg = plan::ceil_div(static_cast<unsigned long long>(total), kGroupChunk);
+  if (gg > 148ull * 8) gg = 148ull * 8;
+  if (gg == 0) gg = 1;
+  k_scatter_group<I, V><<<dim3(static_cast<unsigned>(gg)), dim3(kGroupThreads), 0, s>>>(p, indices, units, nvec,
+                                                                                        list, status);
+  const dim3 fgrid(148 * kFoldBlocksPerSm);
+  if constexpr (V == 16) {
+    const unsigned smem = (kFoldThreads / 32) * bulk_stage_bytes_per_warp();
+    static std::atomic<unsigned long long> raised{0};
+    if (allow_dynamic_smem(k_scatter_fold_bulk<F>, smem, raised) != T4A_OK) return;
+    k_scatter_fold_bulk<F><<<fgrid, dim3(kFoldThreads), smem, s>>>(list, total, nvec, out, updates, status);
   } else {
-    k_scatter<F, I, V, 4><<<grid, block, 0, s>>>(p, out, indices, updates, units, nvec);
+    const unsigned smem = (kFoldThreads / 32) * fold_stage_bytes_per_warp(V);
+    static std::atomic<unsigned long long> raised{0};
+    if (allow_dynamic_smem(k_scatter_fold<F, V>, smem, raised) != T4A_OK) return;
+    k_scatter_fold<F, V><<<fgrid, dim3(kFoldThreads), smem, s>>>(list, total, nvec, out, updates);
   }
 }
 
 template <typename F, typename I>
 int launch_scatter_typed(const WindowPlan& p, dim3 grid, cudaStream_t s, void* out, const void* indices,
-                         const void* updates) {
+                         const void* updates, void* workspace) {
   const long long units = p.batch.len * p.wrest.len;
   const int v = window_vec_bytes(p, reinterpret_cast<unsigned long long>(out),
                                  reinterpret_cast<unsigned long long>(updates));
   const long long nvec = p.run * p.esize / v;
   if (v >= 16) {
-    launch_scatter_width<F, I, 16>(p, grid, s, out, indices, updates, units, nvec);
+    launch_scatter_width<F, I, 16>(p, grid, s, out, indices, updates, units, nvec, workspace);
   } else if (v == 8) {
-    launch_scatter_width<F, I, 8>(p, grid, s, out, indices, updates, units, nvec);
+    launch_scatter_width<F, I, 8>(p, grid, s, out, indices, updates, units, nvec, workspace);
   } else if constexpr (sizeof(F) == 4) {
-    launch_scatter_width<F, I, 4>(p, grid, s, out, indices, updates, units, nvec);
+    launch_scatter_width<F, I, 4>(p, grid, s, out, indices, updates, units, nvec, workspace);
   }
   return runtime::check_launch();
 }
 
 template <typename F>
 int launch_scatter_index(int index_dtype, const WindowPlan& p, dim3 grid, cudaStream_t s, void* out,
-                         const void* indices, const void* updates) {
+                         const void* indices, const void* updates, void* workspace) {
   switch (index_dtype) {
-    case T4A_CUDA_F32: return launch_scatter_typed<F, float>(p, grid, s, out, indices, updates);
-    case T4A_CUDA_F64: return launch_scatter_typed<F, double>(p, grid, s, out, indices, updates);
-    case T4A_CUDA_I32: return launch_scatter_typed<F, int>(p, grid, s, out, indices, updates);
-    case T4A_CUDA_I64: return launch_scatter_typed<F, long long>(p, grid, s, out, indices, updates);
+    case T4A_CUDA_F32: return launch_scatter_typed<F, float>(p, grid, s, out, indices, updates, workspace);
+    case T4A_CUDA_F64: return launch_scatter_typed<F, double>(p, grid, s, out, indices, updates, workspace);
+    case T4A_CUDA_I32: return launch_scatter_typed<F, int>(p, grid, s, out, indices, updates, workspace);
+    case T4A_CUDA_I64: return launch_scatter_typed<F, long long>(p, grid, s, out, indices, updates, workspace);
     default: return T4A_ERR_UNSUPPORTED_DTYPE;
   }
 }
@@ -325,10 +397,15 @@ int t4a_launch_gather(const t4a_launch* launch, void* stream, void* out, const v
   }
 }
 
-int t4a_launch_scatter_add(const t4a_launch* launch, void* stream, void* out, const void* indices,
-                           const void* updates, int dtype, int index_dtype, const t4a_cuda_layout* out_layout,
-                           const t4a_cuda_layout* indices_layout, const t4a_cuda_layout* updates_layout,
-                           const t4a_cuda_scatter_plan* plan, long long update_len) {
+}  // extern "C"
+
+namespace {
+
+// Launch of a planned scatter; the two-kernel path when `workspace` is given.
+int scatter_launch(const t4a_launch* launch, void* stream, void* out, const void* indices, const void* updates,
+                   int dtype, int index_dtype, const t4a_cuda_layout* out_layout,
+                   const t4a_cuda_layout* indices_layout, const t4a_cuda_layout* updates_layout,
+                   const t4a_cuda_scatter_plan* plan, long long update_len, void* workspace) {
   if (launch == nullptr || out_layout == nullptr || indices_layout == nullptr || updates_layout == nullptr ||
       plan == nullptr)
     return T4A_ERR_NULL_ARGUMENT;
@@ -341,11 +418,57 @@ int t4a_launch_scatter_add(const t4a_launch* launch, void* stream, void* out, co
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (dtype) {
     case T4A_CUDA_F32:
-    case T4A_CUDA_C32: return launch_scatter_index<float>(index_dtype, p, grid, s, out, indices, updates);
+    case T4A_CUDA_C32: return launch_scatter_index<float>(index_dtype, p, grid, s, out, indices, updates, workspace);
     case T4A_CUDA_F64:
-    case T4A_CUDA_C64: return launch_scatter_index<double>(index_dtype, p, grid, s, out, indices, updates);
+    case T4A_CUDA_C64:
+      return launch_scatter_index<double>(index_dtype, p, grid, s, out, indices, updates, workspace);
     default: return T4A_ERR_UNSUPPORTED_DTYPE;
   }
+}
+
+// Grouped-list entries the two-kernel path needs: one per piece, counted at the
+// narrowest vectors the dtype allows (the most pieces).
+int scatter_list_bytes(int dtype, const t4a_cuda_layout& out, const t4a_cuda_layout& indices,
+                       const t4a_cuda_layout& updates, const t4a_cuda_scatter_plan& plan, size_t* bytes) {
+  const int es = plan::dtype_size(dtype);
+  if (es == 0) return T4A_ERR_UNSUPPORTED_DTYPE;
+  if (!scatter_maps_ok(out, indices, updates, plan)) return T4A_ERR_INVALID_AXIS;
+  const WindowPlan p = make_scatter_plan(out, indices, updates, plan, es);
+  const long long units = p.batch.len * p.wrest.len;
+  if (p.run <= 0 || units <= 0) {
+    *bytes = kScatterStatusBytes;
+    return T4A_OK;
+  }
+  const ScatterShape sh = scatter_shape(p.run);  // vectors are at least one element wide
+  long long n = 0;
+  if (__builtin_mul_overflow(units, sh.piece.count, &n)) return T4A_ERR_OVERFLOW;
+  *bytes = kScatterStatusBytes + static_cast<size_t>(n) * sizeof(GroupedPiece);
+  return T4A_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int t4a_launch_scatter_add(const t4a_launch* launch, void* stream, void* out, const void* indices,
+                           const void* updates, int dtype, int index_dtype, const t4a_cuda_layout* out_layout,
+                           const t4a_cuda_layout* indices_layout, const t4a_cuda_layout* updates_layout,
+                           const t4a_cuda_scatter_plan* plan, long long update_len) {
+  return scatter_launch(launch, stream, out, indices, updates, dtype, index_dtype, out_layout, indices_layout,
+                        updates_layout, plan, update_len, nullptr);
+}
+
+int t4a_scatter_add_workspace_bytes(int dtype, int index_dtype, const t4a_cuda_layout* out_layout,
+                                    const t4a_cuda_layout* indices_layout, const t4a_cuda_layout* updates_layout,
+                                    const t4a_cuda_scatter_plan* plan, size_t* bytes) {
+  if (out_layout == nullptr || indices_layout == nullptr || updates_layout == nullptr || plan == nullptr ||
+      bytes == nullptr)
+    return T4A_ERR_NULL_ARGUMENT;
+  T4A_TRY(require_index_dtype(index_dtype));
+  T4A_TRY(check_layout(out_layout));
+  T4A_TRY(check_layout(indices_layout));
+  T4A_TRY(check_layout(updates_layout));
+  return scatter_list_bytes(dtype, *out_layout, *indices_layout, *updates_layout, *plan, bytes);
 }
 
 int t4a_gather(void* stream, int dtype, int index_dtype, void* out, const t4a_cuda_layout* out_layout,
@@ -363,14 +486,20 @@ int t4a_gather(void* stream, int dtype, int index_dtype, void* out, const t4a_cu
 int t4a_scatter_add(void* stream, int dtype, int index_dtype, void* out, const t4a_cuda_layout* out_layout,
                     long long out_len, const void* indices, const t4a_cuda_layout* indices_layout,
                     long long indices_len, const void* updates, const t4a_cuda_layout* updates_layout,
-                    long long updates_len, const t4a_cuda_scatter_plan* plan) {
+                    long long updates_len, const t4a_cuda_scatter_plan* plan, void* workspace,
+                    size_t workspace_bytes) {
   t4a_launch l;
   T4A_TRY(t4a_plan_scatter_add(dtype, index_dtype, out_layout, out_len, indices_layout, indices_len, updates_layout,
                                updates_len, plan, &l));
   long long update_count = 0;
   T4A_TRY(element_count(*updates_layout, &update_count));
-  return t4a_launch_scatter_add(&l, stream, out, indices, updates, dtype, index_dtype, out_layout, indices_layout,
-                                updates_layout, plan, update_count);
+  if (workspace != nullptr) {
+    size_t need = 0;
+    T4A_TRY(scatter_list_bytes(dtype, *out_layout, *indices_layout, *updates_layout, *plan, &need));
+    if (workspace_bytes < need) return T4A_ERR_WORKSPACE;
+  }
+  return scatter_launch(&l, stream, out, indices, updates, dtype, index_dtype, out_layout, indices_layout,
+                        updates_layout, plan, update_count, workspace);
 }
 
 }  // extern "C"

@@ -49,7 +49,6 @@ struct WindowPlan {
   long long comp_dim[T4A_CUDA_MAX_RANK];     // operand extent of the component's axis
   long long comp_window[T4A_CUDA_MAX_RANK];  // window extent on that axis
   long long comp_stride_a[T4A_CUDA_MAX_RANK];  // side-A stride of that axis
-  int comp_axis[T4A_CUDA_MAX_RANK];
   // Scatter only: per side-A axis, the window extent, for the fit check.
   int a_rank;
   long long a_ext[T4A_CUDA_MAX_RANK];
@@ -68,20 +67,6 @@ T4A_HD void idx_push(IdxGroup& g, long long e, long long a, long long b) {
   g.b[g.n] = b;
   ++g.n;
   g.len *= e;
-}
-
-T4A_HD void idx_offsets(const IdxGroup& g, long long f, long long* oa, long long* ob) {
-  long long sa = 0, sb = 0;
-  for (int i = 0; i < T4A_CUDA_MAX_RANK; ++i) {
-    if (i < g.n) {
-      const long long c = f % g.ext[i];
-      f /= g.ext[i];
-      sa += c * g.a[i];
-      sb += c * g.b[i];
-    }
-  }
-  *oa = sa;
-  *ob = sb;
 }
 
 // Window axes (extents w[], side-A strides sa[], side-B strides sb[]) -> run + rest.
@@ -171,7 +156,6 @@ T4A_HD WindowPlan make_gather_plan(const t4a_cuda_layout& out, const t4a_cuda_la
   p.ncomp = g.start_map_len;
   for (int c = 0; c < g.start_map_len; ++c) {
     const int ax = static_cast<int>(g.start_index_map[c]);
-    p.comp_axis[c] = ax;
     p.comp_dim[c] = operand.extents[ax];
     p.comp_window[c] = g.slice_sizes[ax];
     p.comp_stride_a[c] = operand.strides[ax];
@@ -221,7 +205,6 @@ T4A_HD WindowPlan make_scatter_plan(const t4a_cuda_layout& out, const t4a_cuda_l
   p.ncomp = g.scatter_map_len;
   for (int c = 0; c < g.scatter_map_len; ++c) {
     const int ax = static_cast<int>(g.scatter_dims[c]);
-    p.comp_axis[c] = ax;
     p.comp_dim[c] = out.extents[ax];
     p.comp_window[c] = p.a_window[ax];
     p.comp_stride_a[c] = out.strides[ax];
@@ -255,6 +238,14 @@ T4A_HD int window_vec_bytes(const WindowPlan& p, unsigned long long base_a, unsi
   int v = 16;
   while (v > 1 && (bits & static_cast<unsigned long long>(v - 1)) != 0) v >>= 1;
   return v;
+}
+
+// Largest element offset a layout reaches (negative strides contribute nothing).
+T4A_HD long long layout_max_offset(const t4a_cuda_layout& l) {
+  long long hi = l.offset;
+  for (int d = 0; d < T4A_CUDA_MAX_RANK; ++d)
+    if (d < l.rank && l.extents[d] > 0 && l.strides[d] > 0) hi += (l.extents[d] - 1) * l.strides[d];
+  return hi;
 }
 
 // Clamped start (reference clamp_window_start): start <= 0 (or NaN) -> 0, else the

@@ -105,7 +105,9 @@ def _declare(l):
         "t4a_launch_scatter_add": (I, [ctypes.POINTER(Launch), P, P, P, P, I, I, LP, LP, LP,
                                        ctypes.POINTER(abi.ScatterPlan), LL]),
         "t4a_gather": (I, [P, I, I, P, LP, LL, P, LP, LL, P, LP, LL, ctypes.POINTER(abi.GatherPlan)]),
-        "t4a_scatter_add": (I, [P, I, I, P, LP, LL, P, LP, LL, P, LP, LL, ctypes.POINTER(abi.ScatterPlan)]),
+        "t4a_scatter_add": (I, [P, I, I, P, LP, LL, P, LP, LL, P, LP, LL, ctypes.POINTER(abi.ScatterPlan), P, SZ]),
+        "t4a_scatter_add_workspace_bytes": (I, [I, I, LP, LP, LP, ctypes.POINTER(abi.ScatterPlan),
+                                                ctypes.POINTER(SZ)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(l, name, None)
@@ -304,11 +306,21 @@ def gather_raw(stream, dtype, index_dtype, out_ptr, out_layout, out_len, operand
                            indices_len, ctypes.byref(plan)), "gather")
 
 
+def scatter_add_workspace_bytes(dtype, index_dtype, out_layout, indices_layout, updates_layout, plan):
+    n = ctypes.c_size_t(0)
+    check(lib().t4a_scatter_add_workspace_bytes(dtype, index_dtype, ctypes.byref(out_layout),
+                                                ctypes.byref(indices_layout), ctypes.byref(updates_layout),
+                                                ctypes.byref(plan), ctypes.byref(n)), "scatter_add_workspace_bytes")
+    return n.value
+
+
 def scatter_add_raw(stream, dtype, index_dtype, out_ptr, out_layout, out_len, indices_ptr, indices_layout,
-                    indices_len, updates_ptr, updates_layout, updates_len, plan):
+                    indices_len, updates_ptr, updates_layout, updates_len, plan, workspace=None, workspace_bytes=0):
+    """t4a_scatter_add: the two-kernel path with a workspace pointer, else one kernel."""
     check(lib().t4a_scatter_add(stream, dtype, index_dtype, out_ptr, ctypes.byref(out_layout), out_len,
                                 indices_ptr, ctypes.byref(indices_layout), indices_len, updates_ptr,
-                                ctypes.byref(updates_layout), updates_len, ctypes.byref(plan)), "scatter_add")
+                                ctypes.byref(updates_layout), updates_len, ctypes.byref(plan), workspace,
+                                workspace_bytes), "scatter_add")
 
 
 def _ptr(t):
@@ -330,12 +342,24 @@ def gather_rows(table, indices, out=None, stream=None):
     return out
 
 
-def scatter_add_rows(dest, indices, updates, stream=None):
+def scatter_add_rows(dest, indices, updates, workspace=None, stream=None):
     """dest[clamp(indices[i]), :] += updates[i, :] in place, for a row-major CUDA
-    destination [rows, cols] (the XLA additive scatter of whole rows)."""
+    destination [rows, cols] (the XLA additive scatter of whole rows).  `workspace`: a
+    CUDA uint8 tensor of scatter_add_workspace_bytes for the two-kernel path, or None."""
     n, cols = updates.shape
     plan = abi.scatter_plan([0], [0], [1], 1, 2, 2)
+    ws, nbytes = (None, 0) if workspace is None else (_ptr(workspace), workspace.numel())
     scatter_add_raw(stream_handle(stream), torch_dtype_tag(dest), torch_dtype_tag(indices), _ptr(dest),
                     tensor_layout(dest), span(dest), _ptr(indices), abi.layout([n, 1]), n, _ptr(updates),
-                    tensor_layout(updates), span(updates), plan)
+                    tensor_layout(updates), span(updates), plan, ws, nbytes)
     return dest
+
+
+def scatter_rows_workspace(dest, indices, updates):
+    """A CUDA workspace for scatter_add_rows' two-kernel path."""
+    import torch
+    n, cols = updates.shape
+    plan = abi.scatter_plan([0], [0], [1], 1, 2, 2)
+    nbytes = scatter_add_workspace_bytes(torch_dtype_tag(dest), torch_dtype_tag(indices), tensor_layout(dest),
+                                         abi.layout([n, 1]), tensor_layout(updates), plan)
+    return torch.empty(max(nbytes, 16), dtype=torch.uint8, device=dest.device)

@@ -8,7 +8,8 @@ destinations with holes, bool data, scatter collisions, complex updates with ind
 vectors, windows that do not fit, zero updates), BASELINE config 4 at reduced size
 (row gather from an F32 table with I64 indices; F64 scatter with Zipf(1.1) indices),
 the reference bench's column-major table, and random plans over every data and index
-dtype.  Every case runs through this library's launchers, its exported module symbols
+dtype.  Every case runs through this library's launchers (scatter: the one-kernel path and the
+two-kernel path with a workspace), its exported module symbols
 (planner geometry and the reference's flat geometry, grid ceil(len/256) x 256) and the
 reference's own kernels rebuilt from source (oracle/_ref).
 
@@ -330,9 +331,16 @@ class Scatter:
         d_out[:self.dest.nbytes] = dev(self.dest.view(np.uint8))
         d_upd = dev(self.updates.view(np.uint8)) if upd_len else torch.zeros(16, dtype=torch.uint8, device="cuda")
         d_idx = dev(self.indices.view(np.uint8)) if idx_len else torch.zeros(16, dtype=torch.uint8, device="cuda")
-        if route == "launcher":
+        if route in ("launcher", "launcher-ws"):
+            ws, nbytes = None, 0
+            if route == "launcher-ws":
+                nbytes = t4.scatter_add_workspace_bytes(self.dtype, self.index_dtype, self.dest_l, self.indices_l,
+                                                        self.updates_l, self.plan)
+                d_ws = torch.zeros(max(nbytes, 16), dtype=torch.uint8, device="cuda")
+                ws = vptr(d_ws)
             t4.scatter_add_raw(t4.stream_handle(), self.dtype, self.index_dtype, vptr(d_out), self.dest_l, dest_len,
-                               vptr(d_idx), self.indices_l, idx_len, vptr(d_upd), self.updates_l, upd_len, self.plan)
+                               vptr(d_idx), self.indices_l, idx_len, vptr(d_upd), self.updates_l, upd_len, self.plan,
+                               ws, nbytes)
         else:
             launch = t4.plan_scatter_add(self.dtype, self.index_dtype, self.dest_l, dest_len, self.indices_l,
                                          idx_len, self.updates_l, upd_len, self.plan)
@@ -348,9 +356,11 @@ class Scatter:
                     vptr(d_out), vptr(d_idx), vptr(d_upd), ctypes.c_int(self.dtype), ctypes.c_int(self.index_dtype),
                     self.dest_l, self.indices_l, self.updates_l, self.plan, ctypes.c_longlong(count)])
         torch.cuda.synchronize()
+        if route == "launcher-ws":
+            assert int(d_ws[:4].view(torch.int32).item()) == 0, "a bulk copy wait ran out"
         return take(d_out, self.dest.nbytes).view(self.comp)
 
-    def check(self, routes=ROUTES):
+    def check(self, routes=ROUTES + ["launcher-ws"]):
         want = self._oracle(self.dest, self.updates)
         mag = self._oracle(np.abs(self.dest), np.abs(self.updates))
         tol, atol = TOL[self.dtype]
@@ -532,7 +542,7 @@ def test_config4_full_size_properties(cuda):
     sidx = torch.clamp(torch.searchsorted(cdf, torch.rand(n, dtype=torch.float64, device="cuda", generator=g),
                                           right=True), max=rows - 1)
     dest = torch.zeros((rows, cols), dtype=torch.float64, device="cuda")
-    t4.scatter_add_rows(dest, sidx, upd)
+    t4.scatter_add_rows(dest, sidx, upd, workspace=t4.scatter_rows_workspace(dest, sidx, upd))
     torch.cuda.synchronize()
     col_got = dest.sum(dim=0)
     col_want = upd.sum(dim=0)
