@@ -269,6 +269,76 @@ int t4a_scatter_add(void* stream, int dtype, int index_dtype, void* out, const t
                     long long updates_len, const t4a_cuda_scatter_plan* plan, void* workspace,
                     size_t workspace_bytes);
 
+
+/* ------------------------------------------------------------------------- */
+/* RRQR primitives (reference src/lib.rs:2460-2774, rrqr.cu:513-705).          */
+/* Plane entries run one task (a reference 32-lane block) per warp, with the   */
+/* reference's lane order, so F32/F64 results are bit-identical.               */
+/* ------------------------------------------------------------------------- */
+
+/* plan_initialize_permutation (src/lib.rs:2512): permutation[pos] = pos % n. */
+int t4a_plan_initialize_permutation(long long n, long long len, t4a_launch* launch);
+/* plan_column_norms (src/lib.rs:2521): columns step..n measured over rows step..m. */
+int t4a_plan_column_norms(int dtype, const t4a_cuda_layout* work, long long work_len, const t4a_cuda_layout* norms,
+                          long long norms_len, long long step, t4a_launch* launch);
+/* plan_select_pivot (src/lib.rs:2561). */
+int t4a_plan_select_pivot(int dtype, const t4a_cuda_layout* norms, long long norms_len,
+                          const t4a_cuda_layout* permutation, long long permutation_len, long long pivots_len,
+                          long long status_len, long long step, t4a_launch* launch);
+/* plan_swap_columns (src/lib.rs:2598). */
+int t4a_plan_swap_columns(int dtype, const t4a_cuda_layout* work, long long work_len,
+                          const t4a_cuda_layout* permutation, long long permutation_len, long long pivots_len,
+                          long long step, t4a_launch* launch);
+/* plan_reflector (src/lib.rs:2635). */
+int t4a_plan_reflector(int dtype, const t4a_cuda_layout* work, long long work_len, const t4a_cuda_layout* coeff,
+                       long long coeff_len, long long step, t4a_launch* launch);
+/* plan_apply_reflector (src/lib.rs:2664): columns first_column..first_column+column_count. */
+int t4a_plan_apply_reflector(int dtype, const t4a_cuda_layout* packed, long long packed_len,
+                             const t4a_cuda_layout* target, long long target_len, const t4a_cuda_layout* coeff,
+                             long long coeff_len, long long step, long long first_column, long long column_count,
+                             t4a_launch* launch);
+/* plan_extract_r (src/lib.rs:2719), plan_prefix_rank (src/lib.rs:2748). */
+int t4a_plan_extract_r(int dtype, const t4a_cuda_layout* work, long long work_len, const t4a_cuda_layout* r,
+                       long long r_len, t4a_launch* launch);
+int t4a_plan_prefix_rank(int dtype, const t4a_cuda_layout* r, long long r_len, long long rank_len,
+                         long long status_len, double rtol, double atol, t4a_launch* launch);
+
+/* Launchers with the argument lists of rrqr.cu:513, :524, :546, :567, :576, :620, :678, :684. */
+int t4a_launch_initialize_permutation(const t4a_launch* launch, void* stream, void* permutation, long long n,
+                                      long long len);
+int t4a_launch_column_norms(const t4a_launch* launch, void* stream, const void* work, void* norms, int dtype,
+                            t4a_cuda_layout work_layout, t4a_cuda_layout norms_layout, long long step);
+int t4a_launch_select_pivot(const t4a_launch* launch, void* stream, const void* norms, const void* permutation,
+                            void* pivots, void* status, int dtype, t4a_cuda_layout norms_layout,
+                            t4a_cuda_layout permutation_layout, long long step);
+int t4a_launch_swap_columns(const t4a_launch* launch, void* stream, void* work, void* permutation,
+                            const void* pivots, int dtype, t4a_cuda_layout work_layout,
+                            t4a_cuda_layout permutation_layout, long long step);
+int t4a_launch_reflector(const t4a_launch* launch, void* stream, void* work, void* coeff, int dtype,
+                         t4a_cuda_layout work_layout, t4a_cuda_layout coeff_layout, long long step);
+int t4a_launch_apply_reflector(const t4a_launch* launch, void* stream, const void* packed, void* target,
+                               const void* coeff, int dtype, t4a_cuda_layout packed_layout,
+                               t4a_cuda_layout target_layout, t4a_cuda_layout coeff_layout, long long step,
+                               long long first_column, long long column_count);
+int t4a_launch_extract_r(const t4a_launch* launch, void* stream, const void* work, void* r, int dtype,
+                         t4a_cuda_layout work_layout, t4a_cuda_layout r_layout);
+int t4a_launch_prefix_rank(const t4a_launch* launch, void* stream, const void* r, void* rank, void* status, int dtype,
+                           t4a_cuda_layout r_layout, double rtol, double atol);
+
+
+/* No single counterpart in the reference (its loop lives with the caller, bench
+ * examples/bench_kernels.rs:2390-2623): `steps` steps of column_norms, select_pivot,
+ * swap_columns, reflector and apply_reflector over the trailing columns, for one
+ * column-major F32/F64 matrix (row stride 1), with results bit-identical to that loop
+ * of primitives.  permutation: n int64 (initialized here); coeff: `steps` entries;
+ * pivots: the pivot of each step (`steps` int64); status: one sticky int64 (set to 1
+ * when a column norm is non-finite; the caller zeroes it).  The workspace holds the
+ * norms and per-step scalars (t4a_rrqr_workspace_bytes). */
+int t4a_rrqr_workspace_bytes(int dtype, const t4a_cuda_layout* work, size_t* bytes);
+int t4a_rrqr(void* stream, int dtype, void* work, const t4a_cuda_layout* work_layout, long long work_len,
+             long long steps, void* permutation, void* coeff, void* pivots, void* status, void* workspace,
+             size_t workspace_bytes);
+
 #ifdef __cplusplus
 }
 #endif

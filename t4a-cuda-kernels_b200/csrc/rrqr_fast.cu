@@ -1,0 +1,633 @@
+// RRQR planning (reference src/lib.rs:2460-2774) and the host launchers of the RRQR
+// primitives.  Plane entries run one task per warp, kTaskWarps tasks per block;
+// flat entries are grid-stride walks.
+#include <cuda_runtime.h>
+
+#include "plan_common.h"
+#include "rrqr_core.cuh"
+#include "rrqr_step.cuh"
+#include "runtime.h"
+
+namespace t4a {
+namespace {
+
+using namespace rrqr;
+
+constexpr int kTaskWarps = 8;
+constexpr int kTaskThreads = kTaskWarps * 32;
+constexpr int kFlatThreads = 256;
+constexpr int kRrqrVariant = 64;  // t4a_launch.variant of the RRQR entries
+
+// ---- kernels (this library's geometry) -----------------------------------------
+__global__ void __launch_bounds__(kFlatThreads) k_init_perm(long long* perm, long long n, long long len) {
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long p = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; p < len; p += stride)
+    perm[p] = p % n;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kTaskThreads) k_column_norms(const T* w, typename RealOf<T>::F* norms,
+                                                               t4a_cuda_layout wl, t4a_cuda_layout nl, long long step,
+                                                               long long tasks) {
+  const long long task = warp_task();
+  if (task < tasks) column_norms_task<T>(w, norms, wl, nl, step, task);
+}
+
+template <typename F>
+__global__ void __launch_bounds__(kTaskThreads) k_select_pivot(const F* norms, const long long* perm,
+                                                               long long* pivots, long long* status,
+                                                               t4a_cuda_layout nl, t4a_cuda_layout pl,
+                                                               long long step, long long tasks) {
+  const long long batch = warp_task();
+  if (batch < tasks) select_pivot_task<F>(norms, perm, pivots, status, nl, pl, step, batch);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kFlatThreads) k_swap(T* w, long long* perm, const long long* pivots,
+                                                       t4a_cuda_layout wl, t4a_cuda_layout pl, long long step,
+                                                       long long len) {
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long p = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; p < len; p += stride)
+    swap_columns_elem<T>(w, perm, pivots, wl, pl, step, p);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kTaskThreads) k_reflector(T* w, T* coeff, t4a_cuda_layout wl, t4a_cuda_layout cl,
+                                                            long long step, long long tasks) {
+  const long long batch = warp_task();
+  if (batch >= tasks) return;
+  const long long base = wl.offset + step * wl.strides[1] + batch_offset(batch, wl, 2);
+  const long long ci = cl.offset + step * cl.strides[0] + batch_offset(batch, cl, 1);
+  reflector_task<T>(w, coeff, base, wl.strides[0], ci, step, wl.extents[0]);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kTaskThreads) k_apply(const T* packed, T* target, const T* coeff,
+                                                        t4a_cuda_layout pl, t4a_cuda_layout tl, t4a_cuda_layout cl,
+                                                        long long step, long long first_column,
+                                                        long long column_count, long long tasks) {
+  const long long task = warp_task();
+  if (task >= tasks) return;
+  const long long batch = task / column_count;
+  const long long column = first_column + task % column_count;
+  const long long pb = pl.offset + step * pl.strides[1] + batch_offset(batch, pl, 2);
+  const long long tb = tl.offset + column * tl.strides[1] + batch_offset(batch, tl, 2);
+  const long long ci = cl.offset + step * cl.strides[0] + batch_offset(batch, cl, 1);
+  apply_task<T>(packed, target, coeff, pb, tb, ci, step, pl.extents[0], pl.strides[0], tl.strides[0]);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kFlatThreads) k_extract_r(const T* w, T* r, t4a_cuda_layout wl, t4a_cuda_layout rl,
+                                                            long long len) {
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long f = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; f < len; f += stride)
+    extract_r_elem<T>(w, r, wl, rl, f);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kTaskThreads) k_prefix_rank(const T* r, long long* rank, long long* status,
+                                                              t4a_cuda_layout rl, double rtol, double atol,
+                                                              long long tasks) {
+  using F = typename RealOf<T>::F;
+  const long long batch = warp_task();
+  if (batch < tasks) prefix_rank_task<T>(r, rank, status, rl, static_cast<F>(rtol), static_cast<F>(atol), batch);
+}
+
+// ---- fused step driver kernels ---------------------------------------------------
+template <typename F>
+__global__ void __launch_bounds__(32) k_fused_norms(FusedArgs<F> a, long long step, int walk_max) {
+  fused_norms<F>(a, step, walk_max != 0);
+}
+template <typename F>
+__global__ void __launch_bounds__(32) k_fused_pivot(FusedArgs<F> a, long long step) {
+  fused_pivot<F>(a, step);
+}
+template <typename F>
+__global__ void __launch_bounds__(kFlatThreads) k_fused_swap(FusedArgs<F> a, long long step) {
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long row = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; row < a.m; row += stride)
+    fused_swap<F>(a, step, row);
+}
+template <typename F>
+__global__ void __launch_bounds__(32) k_fused_dot(FusedArgs<F> a, long long step) {
+  fused_dot<F>(a, step);
+}
+template <typename F>
+__global__ void __launch_bounds__(kUpdateThreads) k_fused_update(FusedArgs<F> a, long long step) {
+  fused_update<F>(a, step, step + 1 + blockIdx.y, blockIdx.x);
+}
+
+struct FusedLayout {
+  size_t norms, dots, colmax, colbad, rec, total;
+};
+
+FusedLayout fused_layout(long long n, int fsize) {
+  auto up = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
+  FusedLayout l;
+  l.norms = 0;
+  l.dots = up(l.norms + n * fsize);
+  l.colmax = up(l.dots + n * fsize);
+  l.colbad = up(l.colmax + n * 8);
+  l.rec = up(l.colbad + n * 4);
+  l.total = up(l.rec + 64);
+  return l;
+}
+
+template <typename F>
+int run_fused(cudaStream_t s, F* w, long long m, long long n, long long ld, long long steps, long long* perm, F* coeff,
+              long long* pivots, long long* status, unsigned char* ws) {
+  const FusedLayout L = fused_layout(n, sizeof(F));
+  FusedArgs<F> a;
+  a.w = w;
+  a.m = m;
+  a.n = n;
+  a.ld = ld;
+  a.perm = perm;
+  a.coeff = coeff;
+  a.pivots = pivots;
+  a.status = status;
+  a.norms = reinterpret_cast<F*>(ws + L.norms);
+  a.dots = reinterpret_cast<F*>(ws + L.dots);
+  a.colmax = reinterpret_cast<unsigned long long*>(ws + L.colmax);
+  a.colbad = reinterpret_cast<int*>(ws + L.colbad);
+  a.rec = reinterpret_cast<StepRecord<F>*>(ws + L.rec);
+  k_init_perm<<<dim3(static_cast<unsigned>((n + kFlatThreads - 1) / kFlatThreads)), dim3(kFlatThreads), 0, s>>>(
+      perm, n, n);
+  const unsigned swap_grid = static_cast<unsigned>(m < 148ll * 8 * kFlatThreads ? (m + kFlatThreads - 1) / kFlatThreads
+                                                                                : 148 * 8);
+  for (long long step = 0; step < steps; ++step) {
+    k_fused_norms<F><<<dim3(static_cast<unsigned>(n - step)), dim3(32), 0, s>>>(a, step, step == 0 ? 1 : 0);
+    k_fused_pivot<F><<<dim3(1), dim3(32), 0, s>>>(a, step);
+    k_fused_swap<F><<<dim3(swap_grid), dim3(kFlatThreads), 0, s>>>(a, step);
+    const long long trailing = n - step - 1;
+    if (trailing > 0) {
+      k_fused_dot<F><<<dim3(static_cast<unsigned>(trailing)), dim3(32), 0, s>>>(a, step);
+      const dim3 ug(static_cast<unsigned>((m - step + kUpdateRows - 1) / kUpdateRows),
+                    static_cast<unsigned>(trailing));
+      k_fused_update<F><<<ug, dim3(kUpdateThreads), 0, s>>>(a, step);
+    }
+  }
+  return runtime::check_launch();
+}
+
+// ---- planning helpers (src/lib.rs:2460-2774) -------------------------------------
+int check_algebra(int dtype) {
+  return dtype == T4A_CUDA_F32 || dtype == T4A_CUDA_F64 || dtype == T4A_CUDA_C32 || dtype == T4A_CUDA_C64
+             ? T4A_OK
+             : T4A_ERR_UNSUPPORTED_DTYPE;
+}
+
+int check_numeric(int dtype) {
+  return check_algebra(dtype) == T4A_OK || dtype == T4A_CUDA_I32 || dtype == T4A_CUDA_I64 ? T4A_OK
+                                                                                          : T4A_ERR_UNSUPPORTED_DTYPE;
+}
+
+int component_size(int dtype) {
+  switch (dtype) {
+    case T4A_CUDA_C32: return 4;
+    case T4A_CUDA_C64: return 8;
+    default: return plan::dtype_size(dtype);
+  }
+}
+
+int batches_of(const t4a_cuda_layout& l, int first, long long* out) {
+  return plan::extent_product(l.extents + first, l.rank > first ? l.rank - first : 0, out);
+}
+
+// require_shorter (src/lib.rs:2493).
+int require_shorter(const t4a_cuda_layout& shorter, const t4a_cuda_layout& matrix) {
+  T4A_TRY(plan::require_matrix(matrix));
+  if (shorter.rank + 1 != matrix.rank) return T4A_ERR_SHAPE_MISMATCH;
+  for (int ax = 1; ax < shorter.rank; ++ax)
+    if (shorter.extents[ax] != matrix.extents[ax + 1]) return T4A_ERR_SHAPE_MISMATCH;
+  return T4A_OK;
+}
+
+bool same_batch(const t4a_cuda_layout& a, const t4a_cuda_layout& b) {
+  if (a.rank != b.rank) return false;
+  for (int ax = 2; ax < a.rank; ++ax)
+    if (a.extents[ax] != b.extents[ax]) return false;
+  return true;
+}
+
+// plane_launch (src/lib.rs:2472): one task per warp here.
+int plane_geometry(long long tasks, t4a_launch* launch) {
+  using namespace plan;
+  if (tasks < 0) return T4A_ERR_NEGATIVE_COUNT;
+  if (tasks == 0) {
+    *launch = empty_launch();
+    return T4A_OK;
+  }
+  unsigned long long grid = 0;
+  T4A_TRY(grid_of(static_cast<unsigned long long>(tasks), kTaskWarps, &grid));
+  *launch = make_launch(grid, kTaskThreads, 1, 0, kRrqrVariant);
+  return T4A_OK;
+}
+
+// flat_launch (src/lib.rs:1465), grid capped: the walks are grid-stride.
+int flat_geometry(long long len, t4a_launch* launch) {
+  using namespace plan;
+  if (len < 0) return T4A_ERR_NEGATIVE_COUNT;
+  if (len == 0) {
+    *launch = empty_launch();
+    return T4A_OK;
+  }
+  unsigned long long grid = ceil_div(static_cast<unsigned long long>(len), kFlatThreads);
+  if (grid > 148ull * 64) grid = 148ull * 64;
+  *launch = make_launch(grid, kFlatThreads, 1, 0, kRrqrVariant + 1);
+  return T4A_OK;
+}
+
+dim3 grid_of_launch(const t4a_launch* l) { return dim3(l->grid[0], l->grid[1] ? l->grid[1] : 1, l->grid[2] ? l->grid[2] : 1); }
+dim3 block_of_launch(const t4a_launch* l) { return dim3(l->block[0], l->block[1] ? l->block[1] : 1, l->block[2] ? l->block[2] : 1); }
+bool launch_empty(const t4a_launch* l) { return l->grid[0] == 0 || l->block[0] == 0; }
+
+}  // namespace
+}  // namespace t4a
+
+using namespace t4a;
+using namespace t4a::plan;
+using namespace t4a::rrqr;
+
+extern "C" {
+
+int t4a_plan_initialize_permutation(long long n, long long len, t4a_launch* launch) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  if (n <= 0) return T4A_ERR_NEGATIVE_COUNT;
+  return flat_geometry(len, launch);
+}
+
+int t4a_plan_column_norms(int dtype, const t4a_cuda_layout* work, long long work_len, const t4a_cuda_layout* norms,
+                          long long norms_len, long long step, t4a_launch* launch) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  T4A_TRY(check_layout(work));
+  T4A_TRY(check_layout(norms));
+  T4A_TRY(check_algebra(dtype));
+  T4A_TRY(require_shorter(*norms, *work));
+  const long long rows = work->extents[0], cols = work->extents[1];
+  if (norms->extents[0] != cols) return T4A_ERR_SHAPE_MISMATCH;
+  if (step < 0 || step > cols) return T4A_ERR_SHAPE_MISMATCH;
+  if (step < cols && step >= rows) return T4A_ERR_SHAPE_MISMATCH;
+  T4A_TRY(require_destination(*norms));
+  T4A_TRY(check_span(*work, work_len, dtype_size(dtype)));
+  T4A_TRY(check_span(*norms, norms_len, component_size(dtype)));
+  long long batches = 0, tasks = 0;
+  T4A_TRY(batches_of(*work, 2, &batches));
+  if (mul_overflows(batches, cols - step, &tasks)) return T4A_ERR_OVERFLOW;
+  return plane_geometry(tasks, launch);
+}
+
+int t4a_plan_select_pivot(int dtype, const t4a_cuda_layout* norms, long long norms_len,
+                          const t4a_cuda_layout* permutation, long long permutation_len, long long pivots_len,
+                          long long status_len, long long step, t4a_launch* launch) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  T4A_TRY(check_layout(norms));
+  T4A_TRY(check_layout(permutation));
+  if (dtype != T4A_CUDA_F32 && dtype != T4A_CUDA_F64) return T4A_ERR_UNSUPPORTED_DTYPE;
+  if (norms->rank == 0 || permutation->rank != norms->rank) return T4A_ERR_SHAPE_MISMATCH;
+  for (int ax = 0; ax < norms->rank; ++ax)
+    if (permutation->extents[ax] != norms->extents[ax]) return T4A_ERR_SHAPE_MISMATCH;
+  const long long cols = norms->extents[0];
+  if (step < 0 || step > cols) return T4A_ERR_SHAPE_MISMATCH;
+  long long batches = 0;
+  T4A_TRY(batches_of(*norms, 1, &batches));
+  if (pivots_len < batches || status_len < batches) return T4A_ERR_SHAPE_MISMATCH;
+  T4A_TRY(check_span(*norms, norms_len, dtype_size(dtype)));
+  T4A_TRY(check_span(*permutation, permutation_len, 8));
+  return plane_geometry(batches, launch);
+}
+
+int t4a_plan_swap_columns(int dtype, const t4a_cuda_layout* work, long long work_len,
+                          const t4a_cuda_layout* permutation, long long permutation_len, long long pivots_len,
+                          long long step, t4a_launch* launch) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  T4A_TRY(check_layout(work));
+  T4A_TRY(check_layout(permutation));
+  T4A_TRY(check_numeric(dtype));
+  T4A_TRY(require_shorter(*permutation, *work));
+  const long long cols = work->extents[1];
+  if (permutation->extents[0] != cols) return T4A_ERR_SHAPE_MISMATCH;
+  if (step < 0 || step >= cols) return T4A_ERR_SHAPE_MISMATCH;
+  T4A_TRY(require_destination(*work));
+  T4A_TRY(require_destination(*permutation));
+  T4A_TRY(check_span(*work, work_len, dtype_size(dtype)));
+  T4A_TRY(check_span(*permutation, permutation_len, 8));
+  long long batches = 0, len = 0;
+  T4A_TRY(batches_of(*work, 2, &batches));
+  if (pivots_len < batches) return T4A_ERR_SHAPE_MISMATCH;
+  if (mul_overflows(work->extents[0], batches, &len)) return T4A_ERR_OVERFLOW;
+  return flat_geometry(len, launch);
+}
+
+int t4a_plan_reflector(int dtype, const t4a_cuda_layout* work, long long work_len, const t4a_cuda_layout* coeff,
+                       long long coeff_len, long long step, t4a_launch* launch) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  T4A_TRY(check_layout(work));
+  T4A_TRY(check_layout(coeff));
+  T4A_TRY(check_algebra(dtype));
+  T4A_TRY(require_shorter(*coeff, *work));
+  long long limit = work->extents[0] < work->extents[1] ? work->extents[0] : work->extents[1];
+  if (coeff->extents[0] < limit) limit = coeff->extents[0];
+  if (step < 0 || step >= limit) return T4A_ERR_SHAPE_MISMATCH;
+  T4A_TRY(require_destination(*work));
+  T4A_TRY(require_destination(*coeff));
+  T4A_TRY(check_span(*work, work_len, dtype_size(dtype)));
+  T4A_TRY(check_span(*coeff, coeff_len, dtype_size(dtype)));
+  long long batches = 0;
+  T4A_TRY(batches_of(*work, 2, &batches));
+  return plane_geometry(batches, launch);
+}
+
+int t4a_plan_apply_reflector(int dtype, const t4a_cuda_layout* packed, long long packed_len,
+                             const t4a_cuda_layout* target, long long target_len, const t4a_cuda_layout* coeff,
+                             long long coeff_len, long long step, long long first_column, long long column_count,
+                             t4a_launch* launch) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  T4A_TRY(check_layout(packed));
+  T4A_TRY(check_layout(target));
+  T4A_TRY(check_layout(coeff));
+  T4A_TRY(check_algebra(dtype));
+  T4A_TRY(require_destination(*target));
+  T4A_TRY(require_matrix(*packed));
+  if (packed->rank != target->rank || packed->extents[0] != target->extents[0] || !same_batch(*packed, *target))
+    return T4A_ERR_SHAPE_MISMATCH;
+  T4A_TRY(require_shorter(*coeff, *packed));
+  if (coeff->extents[0] <= step) return T4A_ERR_SHAPE_MISMATCH;
+  if (step < 0 || step >= packed->extents[0] || step >= packed->extents[1]) return T4A_ERR_SHAPE_MISMATCH;
+  if (first_column < 0 || column_count < 0) return T4A_ERR_NEGATIVE_COUNT;
+  long long last = 0;
+  if (add_overflows(first_column, column_count, &last)) return T4A_ERR_OVERFLOW;
+  if (last > target->extents[1]) return T4A_ERR_SHAPE_MISMATCH;
+  T4A_TRY(check_span(*packed, packed_len, dtype_size(dtype)));
+  T4A_TRY(check_span(*target, target_len, dtype_size(dtype)));
+  T4A_TRY(check_span(*coeff, coeff_len, dtype_size(dtype)));
+  long long batches = 0, tasks = 0;
+  T4A_TRY(batches_of(*packed, 2, &batches));
+  if (mul_overflows(batches, column_count, &tasks)) return T4A_ERR_OVERFLOW;
+  return plane_geometry(tasks, launch);
+}
+
+int t4a_plan_extract_r(int dtype, const t4a_cuda_layout* work, long long work_len, const t4a_cuda_layout* r,
+                       long long r_len, t4a_launch* launch) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  T4A_TRY(check_layout(work));
+  T4A_TRY(check_layout(r));
+  T4A_TRY(check_algebra(dtype));
+  T4A_TRY(require_destination(*r));
+  T4A_TRY(require_matrix(*work));
+  T4A_TRY(require_matrix(*r));
+  if (r->rank != work->rank || r->extents[1] != work->extents[1] || !same_batch(*r, *work))
+    return T4A_ERR_SHAPE_MISMATCH;
+  if (r->extents[0] > work->extents[0]) return T4A_ERR_SHAPE_MISMATCH;
+  long long len = 0;
+  T4A_TRY(element_count(*r, &len));
+  T4A_TRY(check_span(*r, r_len, dtype_size(dtype)));
+  T4A_TRY(check_span(*work, work_len, dtype_size(dtype)));
+  return flat_geometry(len, launch);
+}
+
+int t4a_plan_prefix_rank(int dtype, const t4a_cuda_layout* r, long long r_len, long long rank_len,
+                         long long status_len, double rtol, double atol, t4a_launch* launch) {
+  (void)rtol;
+  (void)atol;
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  T4A_TRY(check_layout(r));
+  T4A_TRY(check_algebra(dtype));
+  T4A_TRY(require_matrix(*r));
+  const long long rows = r->extents[0], cols = r->extents[1];
+  if (rows < 1 || cols < 1 || rows > cols) return T4A_ERR_SHAPE_MISMATCH;
+  long long batches = 0;
+  T4A_TRY(batches_of(*r, 2, &batches));
+  if (rank_len < batches || status_len < batches) return T4A_ERR_SHAPE_MISMATCH;
+  T4A_TRY(check_span(*r, r_len, dtype_size(dtype)));
+  return plane_geometry(batches, launch);
+}
+
+// ---- launchers (argument lists of rrqr.cu:513-705) ---------------------------------
+
+int t4a_launch_initialize_permutation(const t4a_launch* launch, void* stream, void* permutation, long long n,
+                                      long long len) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  if (launch_empty(launch) || len <= 0 || n <= 0) return T4A_OK;
+  k_init_perm<<<grid_of_launch(launch), block_of_launch(launch), 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<long long*>(permutation), n, len);
+  return runtime::check_launch();
+}
+
+int t4a_launch_column_norms(const t4a_launch* launch, void* stream, const void* work, void* norms, int dtype,
+                            t4a_cuda_layout work_layout, t4a_cuda_layout norms_layout, long long step) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  if (launch_empty(launch)) return T4A_OK;
+  long long batches = 1;
+  for (int ax = 2; ax < work_layout.rank; ++ax) batches *= work_layout.extents[ax];
+  const long long tasks = batches * (work_layout.extents[1] - step);
+  const dim3 g = grid_of_launch(launch), b = block_of_launch(launch);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case T4A_CUDA_F32:
+      k_column_norms<float><<<g, b, 0, s>>>(static_cast<const float*>(work), static_cast<float*>(norms), work_layout,
+                                            norms_layout, step, tasks);
+      break;
+    case T4A_CUDA_F64:
+      k_column_norms<double><<<g, b, 0, s>>>(static_cast<const double*>(work), static_cast<double*>(norms),
+                                             work_layout, norms_layout, step, tasks);
+      break;
+    case T4A_CUDA_C32:
+      k_column_norms<c32><<<g, b, 0, s>>>(static_cast<const c32*>(work), static_cast<float*>(norms), work_layout,
+                                          norms_layout, step, tasks);
+      break;
+    case T4A_CUDA_C64:
+      k_column_norms<c64><<<g, b, 0, s>>>(static_cast<const c64*>(work), static_cast<double*>(norms), work_layout,
+                                          norms_layout, step, tasks);
+      break;
+    default: return T4A_ERR_UNSUPPORTED_DTYPE;
+  }
+  return runtime::check_launch();
+}
+
+int t4a_launch_select_pivot(const t4a_launch* launch, void* stream, const void* norms, const void* permutation,
+                            void* pivots, void* status, int dtype, t4a_cuda_layout norms_layout,
+                            t4a_cuda_layout permutation_layout, long long step) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  if (launch_empty(launch)) return T4A_OK;
+  long long batches = 1;
+  for (int ax = 1; ax < norms_layout.rank; ++ax) batches *= norms_layout.extents[ax];
+  const dim3 g = grid_of_launch(launch), b = block_of_launch(launch);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto* piv = static_cast<long long*>(pivots);
+  auto* st = static_cast<long long*>(status);
+  const auto* perm = static_cast<const long long*>(permutation);
+  switch (dtype) {
+    case T4A_CUDA_F32:
+      k_select_pivot<float><<<g, b, 0, s>>>(static_cast<const float*>(norms), perm, piv, st, norms_layout,
+                                            permutation_layout, step, batches);
+      break;
+    case T4A_CUDA_F64:
+      k_select_pivot<double><<<g, b, 0, s>>>(static_cast<const double*>(norms), perm, piv, st, norms_layout,
+                                             permutation_layout, step, batches);
+      break;
+    default: return T4A_ERR_UNSUPPORTED_DTYPE;
+  }
+  return runtime::check_launch();
+}
+
+int t4a_launch_swap_columns(const t4a_launch* launch, void* stream, void* work, void* permutation,
+                            const void* pivots, int dtype, t4a_cuda_layout work_layout,
+                            t4a_cuda_layout permutation_layout, long long step) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  if (launch_empty(launch)) return T4A_OK;
+  long long batches = 1;
+  for (int ax = 2; ax < work_layout.rank; ++ax) batches *= work_layout.extents[ax];
+  const long long len = work_layout.extents[0] * batches;
+  const dim3 g = grid_of_launch(launch), b = block_of_launch(launch);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto* perm = static_cast<long long*>(permutation);
+  const auto* piv = static_cast<const long long*>(pivots);
+#define T4A_SWAP(T) \
+  k_swap<T><<<g, b, 0, s>>>(static_cast<T*>(work), perm, piv, work_layout, permutation_layout, step, len)
+  switch (dtype) {
+    case T4A_CUDA_F32: T4A_SWAP(float); break;
+    case T4A_CUDA_F64: T4A_SWAP(double); break;
+    case T4A_CUDA_I32: T4A_SWAP(int); break;
+    case T4A_CUDA_I64: T4A_SWAP(long long); break;
+    case T4A_CUDA_C32: T4A_SWAP(c32); break;
+    case T4A_CUDA_C64: T4A_SWAP(c64); break;
+    default: return T4A_ERR_UNSUPPORTED_DTYPE;
+  }
+#undef T4A_SWAP
+  return runtime::check_launch();
+}
+
+int t4a_launch_reflector(const t4a_launch* launch, void* stream, void* work, void* coeff, int dtype,
+                         t4a_cuda_layout work_layout, t4a_cuda_layout coeff_layout, long long step) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  if (launch_empty(launch)) return T4A_OK;
+  long long batches = 1;
+  for (int ax = 2; ax < work_layout.rank; ++ax) batches *= work_layout.extents[ax];
+  const dim3 g = grid_of_launch(launch), b = block_of_launch(launch);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+#define T4A_REFL(T) \
+  k_reflector<T><<<g, b, 0, s>>>(static_cast<T*>(work), static_cast<T*>(coeff), work_layout, coeff_layout, step, batches)
+  switch (dtype) {
+    case T4A_CUDA_F32: T4A_REFL(float); break;
+    case T4A_CUDA_F64: T4A_REFL(double); break;
+    case T4A_CUDA_C32: T4A_REFL(c32); break;
+    case T4A_CUDA_C64: T4A_REFL(c64); break;
+    default: return T4A_ERR_UNSUPPORTED_DTYPE;
+  }
+#undef T4A_REFL
+  return runtime::check_launch();
+}
+
+int t4a_launch_apply_reflector(const t4a_launch* launch, void* stream, const void* packed, void* target,
+                               const void* coeff, int dtype, t4a_cuda_layout packed_layout,
+                               t4a_cuda_layout target_layout, t4a_cuda_layout coeff_layout, long long step,
+                               long long first_column, long long column_count) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  if (launch_empty(launch) || column_count <= 0) return T4A_OK;
+  long long batches = 1;
+  for (int ax = 2; ax < packed_layout.rank; ++ax) batches *= packed_layout.extents[ax];
+  const long long tasks = batches * column_count;
+  const dim3 g = grid_of_launch(launch), b = block_of_launch(launch);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+#define T4A_APPLY(T)                                                                                               \
+  k_apply<T><<<g, b, 0, s>>>(static_cast<const T*>(packed), static_cast<T*>(target), static_cast<const T*>(coeff), \
+                             packed_layout, target_layout, coeff_layout, step, first_column, column_count, tasks)
+  switch (dtype) {
+    case T4A_CUDA_F32: T4A_APPLY(float); break;
+    case T4A_CUDA_F64: T4A_APPLY(double); break;
+    case T4A_CUDA_C32: T4A_APPLY(c32); break;
+    case T4A_CUDA_C64: T4A_APPLY(c64); break;
+    default: return T4A_ERR_UNSUPPORTED_DTYPE;
+  }
+#undef T4A_APPLY
+  return runtime::check_launch();
+}
+
+int t4a_launch_extract_r(const t4a_launch* launch, void* stream, const void* work, void* r, int dtype,
+                         t4a_cuda_layout work_layout, t4a_cuda_layout r_layout) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  if (launch_empty(launch)) return T4A_OK;
+  long long len = 1;
+  for (int ax = 0; ax < r_layout.rank; ++ax) len *= r_layout.extents[ax];
+  const dim3 g = grid_of_launch(launch), b = block_of_launch(launch);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+#define T4A_EXTRACT(T) \
+  k_extract_r<T><<<g, b, 0, s>>>(static_cast<const T*>(work), static_cast<T*>(r), work_layout, r_layout, len)
+  switch (dtype) {
+    case T4A_CUDA_F32: T4A_EXTRACT(float); break;
+    case T4A_CUDA_F64: T4A_EXTRACT(double); break;
+    case T4A_CUDA_C32: T4A_EXTRACT(c32); break;
+    case T4A_CUDA_C64: T4A_EXTRACT(c64); break;
+    default: return T4A_ERR_UNSUPPORTED_DTYPE;
+  }
+#undef T4A_EXTRACT
+  return runtime::check_launch();
+}
+
+int t4a_launch_prefix_rank(const t4a_launch* launch, void* stream, const void* r, void* rank, void* status, int dtype,
+                           t4a_cuda_layout r_layout, double rtol, double atol) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  if (launch_empty(launch)) return T4A_OK;
+  long long batches = 1;
+  for (int ax = 2; ax < r_layout.rank; ++ax) batches *= r_layout.extents[ax];
+  const dim3 g = grid_of_launch(launch), b = block_of_launch(launch);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto* rk = static_cast<long long*>(rank);
+  auto* st = static_cast<long long*>(status);
+#define T4A_RANK(T) \
+  k_prefix_rank<T><<<g, b, 0, s>>>(static_cast<const T*>(r), rk, st, r_layout, rtol, atol, batches)
+  switch (dtype) {
+    case T4A_CUDA_F32: T4A_RANK(float); break;
+    case T4A_CUDA_F64: T4A_RANK(double); break;
+    case T4A_CUDA_C32: T4A_RANK(c32); break;
+    case T4A_CUDA_C64: T4A_RANK(c64); break;
+    default: return T4A_ERR_UNSUPPORTED_DTYPE;
+  }
+#undef T4A_RANK
+  return runtime::check_launch();
+}
+
+// ---- whole factorization (fused steps) ----------------------------------------------
+
+int t4a_rrqr_workspace_bytes(int dtype, const t4a_cuda_layout* work, size_t* bytes) {
+  if (work == nullptr || bytes == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  T4A_TRY(check_layout(work));
+  if (dtype != T4A_CUDA_F32 && dtype != T4A_CUDA_F64) return T4A_ERR_UNSUPPORTED_DTYPE;
+  T4A_TRY(require_matrix(*work));
+  *bytes = fused_layout(work->extents[1], dtype_size(dtype)).total;
+  return T4A_OK;
+}
+
+int t4a_rrqr(void* stream, int dtype, void* work, const t4a_cuda_layout* work_layout, long long work_len,
+             long long steps, void* permutation, void* coeff, void* pivots, void* status, void* workspace,
+             size_t workspace_bytes) {
+  if (work_layout == nullptr || work == nullptr || permutation == nullptr || coeff == nullptr || pivots == nullptr ||
+      status == nullptr)
+    return T4A_ERR_NULL_ARGUMENT;
+  T4A_TRY(check_layout(work_layout));
+  if (dtype != T4A_CUDA_F32 && dtype != T4A_CUDA_F64) return T4A_ERR_UNSUPPORTED_DTYPE;
+  if (work_layout->rank != 2) return T4A_ERR_RANK_OUT_OF_RANGE;
+  const long long m = work_layout->extents[0], n = work_layout->extents[1];
+  // One column-major matrix: unit row stride, columns apart by at least a column.
+  if (work_layout->strides[0] != 1 || work_layout->strides[1] < m) return T4A_ERR_INVALID_STRIDE;
+  if (steps < 0 || steps > (m < n ? m : n)) return T4A_ERR_SHAPE_MISMATCH;
+  T4A_TRY(check_span(*work_layout, work_len, dtype_size(dtype)));
+  size_t need = 0;
+  T4A_TRY(t4a_rrqr_workspace_bytes(dtype, work_layout, &need));
+  if (workspace == nullptr || workspace_bytes < need) return T4A_ERR_WORKSPACE;
+  if (m == 0 || n == 0) return T4A_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto* ws = static_cast<unsigned char*>(workspace);
+  auto* perm = static_cast<long long*>(permutation);
+  auto* piv = static_cast<long long*>(pivots);
+  auto* st = static_cast<long long*>(status);
+  const long long ld = work_layout->strides[1];
+  if (dtype == T4A_CUDA_F64)
+    return run_fused<double>(s, static_cast<double*>(work) + work_layout->offset, m, n, ld, steps, perm,
+                             static_cast<double*>(coeff), piv, st, ws);
+  return run_fused<float>(s, static_cast<float*>(work) + work_layout->offset, m, n, ld, steps, perm,
+                          static_cast<float*>(coeff), piv, st, ws);
+}
+
+}  // extern "C"

@@ -105,6 +105,24 @@ def _declare(l):
         "t4a_launch_scatter_add": (I, [ctypes.POINTER(Launch), P, P, P, P, I, I, LP, LP, LP,
                                        ctypes.POINTER(abi.ScatterPlan), LL]),
         "t4a_gather": (I, [P, I, I, P, LP, LL, P, LP, LL, P, LP, LL, ctypes.POINTER(abi.GatherPlan)]),
+        "t4a_plan_initialize_permutation": (I, [LL, LL, ctypes.POINTER(Launch)]),
+        "t4a_plan_column_norms": (I, [I, LP, LL, LP, LL, LL, ctypes.POINTER(Launch)]),
+        "t4a_plan_select_pivot": (I, [I, LP, LL, LP, LL, LL, LL, LL, ctypes.POINTER(Launch)]),
+        "t4a_plan_swap_columns": (I, [I, LP, LL, LP, LL, LL, LL, ctypes.POINTER(Launch)]),
+        "t4a_plan_reflector": (I, [I, LP, LL, LP, LL, LL, ctypes.POINTER(Launch)]),
+        "t4a_plan_apply_reflector": (I, [I, LP, LL, LP, LL, LP, LL, LL, LL, LL, ctypes.POINTER(Launch)]),
+        "t4a_plan_extract_r": (I, [I, LP, LL, LP, LL, ctypes.POINTER(Launch)]),
+        "t4a_plan_prefix_rank": (I, [I, LP, LL, LL, LL, ctypes.c_double, ctypes.c_double, ctypes.POINTER(Launch)]),
+        "t4a_launch_initialize_permutation": (I, [ctypes.POINTER(Launch), P, P, LL, LL]),
+        "t4a_launch_column_norms": (I, [ctypes.POINTER(Launch), P, P, P, I, LB, LB, LL]),
+        "t4a_launch_select_pivot": (I, [ctypes.POINTER(Launch), P, P, P, P, P, I, LB, LB, LL]),
+        "t4a_launch_swap_columns": (I, [ctypes.POINTER(Launch), P, P, P, P, I, LB, LB, LL]),
+        "t4a_launch_reflector": (I, [ctypes.POINTER(Launch), P, P, P, I, LB, LB, LL]),
+        "t4a_launch_apply_reflector": (I, [ctypes.POINTER(Launch), P, P, P, P, I, LB, LB, LB, LL, LL, LL]),
+        "t4a_launch_extract_r": (I, [ctypes.POINTER(Launch), P, P, P, I, LB, LB]),
+        "t4a_launch_prefix_rank": (I, [ctypes.POINTER(Launch), P, P, P, P, I, LB, ctypes.c_double, ctypes.c_double]),
+        "t4a_rrqr_workspace_bytes": (I, [I, LP, ctypes.POINTER(SZ)]),
+        "t4a_rrqr": (I, [P, I, P, LP, LL, LL, P, P, P, P, P, SZ]),
         "t4a_scatter_add": (I, [P, I, I, P, LP, LL, P, LP, LL, P, LP, LL, ctypes.POINTER(abi.ScatterPlan), P, SZ]),
         "t4a_scatter_add_workspace_bytes": (I, [I, I, LP, LP, LP, ctypes.POINTER(abi.ScatterPlan),
                                                 ctypes.POINTER(SZ)]),
@@ -363,3 +381,44 @@ def scatter_rows_workspace(dest, indices, updates):
     nbytes = scatter_add_workspace_bytes(torch_dtype_tag(dest), torch_dtype_tag(indices), tensor_layout(dest),
                                          abi.layout([n, 1]), tensor_layout(updates), plan)
     return torch.empty(max(nbytes, 16), dtype=torch.uint8, device=dest.device)
+
+
+# ---- RRQR primitives (reference src/lib.rs:2460-2774) -----------------------------
+
+def plan_rrqr(name, *args):
+    """t4a_plan_<name>(*args, &launch) for the RRQR planners; layouts by reference."""
+    conv = [ctypes.byref(a) if isinstance(a, abi.Layout) else a for a in args]
+    return _plan("t4a_plan_" + name, *conv)
+
+
+def launch_rrqr(name, launch, stream, *args):
+    """t4a_launch_<name>(&launch, stream, *args): the kernel's own argument list."""
+    check(getattr(lib(), "t4a_launch_" + name)(ctypes.byref(launch), stream, *args), "launch_" + name)
+
+
+def rrqr_workspace_bytes(dtype, work_layout):
+    n = ctypes.c_size_t(0)
+    check(lib().t4a_rrqr_workspace_bytes(dtype, ctypes.byref(work_layout), ctypes.byref(n)), "rrqr_workspace_bytes")
+    return n.value
+
+
+def rrqr(work, steps=None, stream=None, workspace=None):
+    """Tall-skinny RRQR of a CUDA F32/F64 matrix in place: `work` is a torch tensor
+    whose transpose is contiguous (column-major [m, n]).  Runs `steps` (default
+    min(m, n)) steps of the reference loop; returns (perm, coeff, pivots, status)."""
+    import torch
+    m, n = work.shape
+    steps = min(m, n) if steps is None else steps
+    layout = abi.layout([m, n], [work.stride(0), work.stride(1)])
+    dev = work.device
+    perm = torch.empty(n, dtype=torch.int64, device=dev)
+    coeff = torch.zeros(max(steps, 1), dtype=work.dtype, device=dev)
+    pivots = torch.zeros(max(steps, 1), dtype=torch.int64, device=dev)
+    status = torch.zeros(1, dtype=torch.int64, device=dev)
+    nbytes = rrqr_workspace_bytes(torch_dtype_tag(work), layout)
+    if workspace is None:
+        workspace = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    check(lib().t4a_rrqr(stream_handle(stream), torch_dtype_tag(work), _ptr(work), ctypes.byref(layout),
+                         span(work), steps, _ptr(perm), _ptr(coeff), _ptr(pivots), _ptr(status), _ptr(workspace),
+                         workspace.numel()), "rrqr")
+    return perm, coeff, pivots, status

@@ -1,0 +1,405 @@
+"""GPU parity of the RRQR primitives and of the fused factorization (t4a_rrqr).
+
+Each entry runs through this library's launcher, its exported module symbol (the
+planner's geometry and the reference's: one 32-lane block per task, flat entries
+ceil(len/256) x 256) and the reference's own kernel rebuilt from source (oracle/_ref),
+and is compared with the CPU oracle: bit for bit for F32/F64 (norms, pivots, status,
+reflectors, updates), and for C32/C64 within 1e-5 / 1e-12 relative to the column
+scale (the oracle's complex sums are not contracted like the device's; against the
+reference's own kernels complex results are bit-identical).  Destinations carry
+sentinel bytes and guard bytes, as in the reference tests (tests/gpu_rrqr.rs:193-360).
+Cases follow tests/gpu_rrqr.rs: norms with the -1 sentinel, pivot tie breaks, swap,
+reflector, apply, extract_r, prefix_rank, initialize_permutation; and the whole loop
+of BASELINE config 5 (A = U V^T + 1e-10 N) at reduced and full size.
+"""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+import t4a_b200 as t4
+from cuda_module import Module
+from t4a_b200 import abi
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+OUR_CUBIN = os.path.join(ROOT, "t4a-cuda-kernels_b200", "t4a_b200", "lib", "rrqr.cubin")
+REF_CUBIN = os.path.join(ROOT, "oracle", "_ref", "rrqr.cubin")
+SENTINEL, GUARD = 0xCD, 256
+THREADS = os.cpu_count() or 4
+NP = {abi.F32: np.float32, abi.F64: np.float64, abi.C32: np.complex64, abi.C64: np.complex128,
+      abi.I32: np.int32, abi.I64: np.int64}
+REAL = {abi.F32: abi.F32, abi.F64: abi.F64, abi.C32: abi.F32, abi.C64: abi.F64}
+ROUTES = ["launcher", "module", "module-refgeom", "reference"]
+_MODULES = {}
+
+
+def module(path):
+    if path not in _MODULES:
+        if not os.path.exists(path):
+            pytest.skip(f"{os.path.basename(path)} not built")
+        _MODULES[path] = Module(path)
+    return _MODULES[path]
+
+
+def dev(arr):
+    import torch
+    b = np.ascontiguousarray(arr).view(np.uint8).ravel()
+    return torch.from_numpy(np.concatenate([b, np.full(GUARD, SENTINEL, np.uint8)])).cuda()
+
+
+def sentinel_dev(nbytes):
+    import torch
+    return torch.full((nbytes + GUARD,), SENTINEL, dtype=torch.uint8, device="cuda")
+
+
+def host(t, nbytes, dtype):
+    h = t.cpu().numpy()
+    assert (h[nbytes:] == SENTINEL).all(), "a store landed past the buffer"
+    return h[:nbytes].view(dtype).copy()
+
+
+def vp(t):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def launch(route, name, plan_launch, ref_geom, args):
+    """Run entry `name` by `route`; args: ctypes objects in kernel order."""
+    import torch
+    if route == "launcher":
+        t4.launch_rrqr(name, plan_launch, t4.stream_handle(), *args)
+    else:
+        if route == "module":
+            mod = module(OUR_CUBIN)
+            geom = (tuple(plan_launch.grid), tuple(plan_launch.block), plan_launch.shared_bytes)
+        else:
+            mod = module(OUR_CUBIN if route == "module-refgeom" else REF_CUBIN)
+            geom = ref_geom
+        if plan_launch.grid[0] > 0:
+            mod.launch("t4a_cuda_" + name, *geom, list(args))
+    torch.cuda.synchronize()
+
+
+def plane(tasks):
+    return ((max(1, tasks),), (32,), 0)
+
+
+def flat(n):
+    return ((max(1, (n + 255) // 256),), (256,), 0)
+
+
+def rand_matrix(rng, dtype, m, n, shift=0.0):
+    if dtype in (abi.C32, abi.C64):
+        a = rng.standard_normal((n, m)) + 1j * rng.standard_normal((n, m)) + shift
+    else:
+        a = rng.standard_normal((n, m)) + shift
+    return a.astype(NP[dtype])  # row j = column j (column-major [m, n])
+
+
+def same(dtype, got, want, scale=None):
+    if dtype in (abi.F32, abi.F64, abi.I32, abi.I64):
+        return np.array_equal(np.asarray(got).view(np.uint8), np.asarray(want).view(np.uint8))
+    tol = 1e-5 if dtype == abi.C32 else 1e-12
+    s = np.abs(want).max() if scale is None else scale
+    return np.allclose(got, want, rtol=0, atol=tol * max(s, 1e-30))
+
+
+# ---- column_norms ---------------------------------------------------------------
+
+@pytest.mark.parametrize("dtype", [abi.F32, abi.F64, abi.C32, abi.C64])
+@pytest.mark.parametrize("m,n,step", [(1000, 12, 0), (4099, 40, 7), (64, 70, 63), (33, 5, 32)])
+def test_column_norms(cuda, dtype, m, n, step):
+    rng = np.random.default_rng(m + n + step + dtype)
+    a = rand_matrix(rng, dtype, m, n)
+    a[1, 3 % m] = np.nan            # column 1: non-finite -> -1
+    if n > 2:
+        a[2, m - 1] = np.inf         # column 2: non-finite -> -1
+    a[n - 1] *= 1e30 if dtype in (abi.F64, abi.C64) else 1e18  # a large column (scaling)
+    wl, nl = abi.layout([m, n]), abi.layout([n])
+    rd = REAL[dtype]
+    want = np.full(n, -7.0, dtype=NP[rd])
+    assert oracle.lib().t4a_oracle_column_norms(dtype, oracle.ptr(a), oracle.ptr(want), ctypes.byref(wl),
+                                                ctypes.byref(nl), step, THREADS) == 0
+    pl = t4.plan_rrqr("column_norms", dtype, wl, m * n, nl, n, step)
+    got = {}
+    for route in ROUTES:
+        d_a = dev(a)
+        d_n = dev(np.full(n, -7.0, dtype=NP[rd]))
+        launch(route, "column_norms", pl, plane(n - step),
+               [vp(d_a), vp(d_n), ctypes.c_int(dtype), wl, nl, ctypes.c_longlong(step)])
+        got[route] = host(d_n, n * np.dtype(NP[rd]).itemsize, NP[rd])
+        assert np.array_equal(got[route][:step], want[:step]), route  # untouched
+        if dtype in (abi.F32, abi.F64):
+            assert same(rd, got[route], want), (route, got[route][:6], want[:6])
+        else:
+            assert np.allclose(got[route], want, rtol=1e-5 if dtype == abi.C32 else 1e-12), route
+    # The reference's own kernel and this library's agree bit for bit (complex too).
+    assert np.array_equal(got["launcher"].view(np.uint8), got["reference"].view(np.uint8))
+
+
+# ---- select_pivot -----------------------------------------------------------------
+
+def pivot_case(route, dtype, norms, perm, step, tasks_layout=None):
+    norms = np.asarray(norms, dtype=NP[dtype])
+    perm = np.asarray(perm, dtype=np.int64)
+    n = norms.size
+    nl = abi.layout([n])
+    pl = t4.plan_rrqr("select_pivot", dtype, nl, n, nl, n, 1, 1, step)
+    d_norms, d_perm = dev(norms), dev(perm)
+    d_piv, d_st = dev(np.zeros(1, np.int64)), dev(np.zeros(1, np.int64))
+    launch(route, "select_pivot", pl, plane(1),
+           [vp(d_norms), vp(d_perm), vp(d_piv), vp(d_st), ctypes.c_int(dtype), nl, nl, ctypes.c_longlong(step)])
+    return int(host(d_piv, 8, np.int64)[0]), int(host(d_st, 8, np.int64)[0])
+
+
+@pytest.mark.parametrize("route", ROUTES)
+def test_select_pivot_tie_breaks(cuda, route):
+    f = abi.F32
+    assert pivot_case(route, f, [1, 5, 3, 2, 4, 0], range(6), 0) == (1, 0)     # clear maximum
+    assert pivot_case(route, f, [1, 5, 5, 2], [0, 3, 1, 2], 0) == (2, 0)       # smaller original wins
+    assert pivot_case(route, f, [5, 5], [7, 7], 0) == (0, 0)                   # then the smaller column
+    assert pivot_case(route, f, [9, 1, 4, 5], range(4), 2) == (3, 0)           # step skips leading columns
+    assert pivot_case(route, f, [1, -1, 3], range(3), 0) == (2, 1)             # negative norm -> status
+    assert pivot_case(route, f, [-1, -1], range(2), 0) == (0, 1)               # nothing valid -> step
+
+
+@pytest.mark.parametrize("dtype", [abi.F32, abi.F64])
+def test_select_pivot_random(cuda, dtype):
+    rng = np.random.default_rng(11 + dtype)
+    for _ in range(20):
+        n = int(rng.integers(1, 300))
+        step = int(rng.integers(0, n + 1))
+        norms = rng.integers(0, 6, n).astype(NP[dtype])   # many ties
+        perm = rng.permutation(n).astype(np.int64)
+        want_p = np.zeros(1, np.int64)
+        want_s = np.zeros(1, np.int64)
+        nl = abi.layout([n])
+        assert oracle.lib().t4a_oracle_select_pivot(dtype, oracle.ptr(norms), oracle.ptr(perm), oracle.ptr(want_p),
+                                                    oracle.ptr(want_s), ctypes.byref(nl), ctypes.byref(nl),
+                                                    step) == 0
+        for route in ROUTES:
+            assert pivot_case(route, dtype, norms, perm, step) == (int(want_p[0]), int(want_s[0])), route
+
+
+# ---- swap_columns -------------------------------------------------------------------
+
+@pytest.mark.parametrize("dtype", [abi.F32, abi.F64, abi.I32, abi.I64, abi.C32, abi.C64])
+def test_swap_columns(cuda, dtype):
+    rng = np.random.default_rng(20 + dtype)
+    m, n = 3001, 9
+    a = (rng.integers(-1000, 1000, (n, m)) if dtype in (abi.I32, abi.I64) else rand_matrix(rng, dtype, m, n))
+    a = a.astype(NP[dtype])
+    wl, pl_ = abi.layout([m, n]), abi.layout([n])
+    for step, pivot in [(2, 7), (4, 4), (0, 8)]:
+        perm = rng.permutation(n).astype(np.int64)
+        want_a, want_p = a.copy(), perm.copy()
+        piv = np.array([pivot], np.int64)
+        assert oracle.lib().t4a_oracle_swap_columns(dtype, oracle.ptr(want_a), oracle.ptr(want_p), oracle.ptr(piv),
+                                                    ctypes.byref(wl), ctypes.byref(pl_), step) == 0
+        plan = t4.plan_rrqr("swap_columns", dtype, wl, m * n, pl_, n, 1, step)
+        for route in ROUTES:
+            d_a, d_p, d_piv = dev(a), dev(perm), dev(piv)
+            launch(route, "swap_columns", plan, flat(m),
+                   [vp(d_a), vp(d_p), vp(d_piv), ctypes.c_int(dtype), wl, pl_, ctypes.c_longlong(step)])
+            assert same(abi.I64, host(d_a, a.nbytes, NP[dtype]).view(np.uint8), want_a.view(np.uint8)), route
+            assert np.array_equal(host(d_p, perm.nbytes, np.int64), want_p), route
+
+
+# ---- reflector and apply_reflector -----------------------------------------------------
+
+@pytest.mark.parametrize("dtype", [abi.F32, abi.F64, abi.C32, abi.C64])
+@pytest.mark.parametrize("m,n,step", [(2000, 8, 0), (4097, 20, 5), (40, 40, 39)])
+def test_reflector_and_apply(cuda, dtype, m, n, step):
+    rng = np.random.default_rng(m * 3 + n + step + dtype)
+    a = rand_matrix(rng, dtype, m, n, shift=0.5)
+    wl, cl = abi.layout([m, n]), abi.layout([n])
+    coeff0 = np.zeros(n, NP[dtype])
+    want_a, want_c = a.copy(), coeff0.copy()
+    assert oracle.lib().t4a_oracle_reflector(dtype, oracle.ptr(want_a), oracle.ptr(want_c), ctypes.byref(wl),
+                                             ctypes.byref(cl), step) == 0
+    plan = t4.plan_rrqr("reflector", dtype, wl, m * n, cl, n, step)
+    results = {}
+    for route in ROUTES:
+        d_a, d_c = dev(a), dev(coeff0)
+        launch(route, "reflector", plan, plane(1),
+               [vp(d_a), vp(d_c), ctypes.c_int(dtype), wl, cl, ctypes.c_longlong(step)])
+        got_a, got_c = host(d_a, a.nbytes, NP[dtype]), host(d_c, coeff0.nbytes, NP[dtype])
+        results[route] = (got_a, got_c)
+        assert same(dtype, got_a, want_a), route
+        assert same(dtype, got_c, want_c), route
+    if dtype in (abi.C32, abi.C64):
+        assert np.array_equal(results["launcher"][0].view(np.uint8), results["reference"][0].view(np.uint8))
+    # apply_reflector: the reflector of `step` (packed = a copy of the reflected matrix)
+    # onto the trailing columns step+1..n of the reflected matrix.
+    packed = want_a.copy()
+    first, count = step + 1, n - step - 1
+    if count == 0:
+        return
+    want_t = want_a.copy()
+    assert oracle.lib().t4a_oracle_apply_reflector(dtype, oracle.ptr(packed), oracle.ptr(want_t), oracle.ptr(want_c),
+                                                   ctypes.byref(wl), ctypes.byref(wl), ctypes.byref(cl), step, first,
+                                                   count, THREADS) == 0
+    plan = t4.plan_rrqr("apply_reflector", dtype, wl, m * n, wl, m * n, cl, n, step, first, count)
+    got = {}
+    for route in ROUTES:
+        d_p, d_t, d_c = dev(packed), dev(want_a), dev(want_c)
+        launch(route, "apply_reflector", plan, plane(count),
+               [vp(d_p), vp(d_t), vp(d_c), ctypes.c_int(dtype), wl, wl, cl, ctypes.c_longlong(step),
+                ctypes.c_longlong(first), ctypes.c_longlong(count)])
+        got[route] = host(d_t, a.nbytes, NP[dtype])
+        assert same(dtype, got[route], want_t, scale=np.abs(want_a).max() * 4), route
+    if dtype in (abi.C32, abi.C64):
+        assert np.array_equal(got["launcher"].view(np.uint8), got["reference"].view(np.uint8))
+
+
+# ---- extract_r, prefix_rank, initialize_permutation ------------------------------------
+
+@pytest.mark.parametrize("dtype", [abi.F32, abi.F64, abi.C32, abi.C64])
+def test_extract_r_and_prefix_rank(cuda, dtype):
+    rng = np.random.default_rng(30 + dtype)
+    m, n, k = 50, 12, 12
+    a = rand_matrix(rng, dtype, m, n)
+    wl, rl = abi.layout([m, n]), abi.layout([k, n])
+    want_r = np.zeros(k * n, NP[dtype])
+    assert oracle.lib().t4a_oracle_extract_r(dtype, oracle.ptr(a), oracle.ptr(want_r), ctypes.byref(wl),
+                                             ctypes.byref(rl)) == 0
+    plan = t4.plan_rrqr("extract_r", dtype, wl, m * n, rl, k * n)
+    for route in ROUTES:
+        d_a, d_r = dev(a), sentinel_dev(want_r.nbytes)
+        launch(route, "extract_r", plan, flat(k * n), [vp(d_a), vp(d_r), ctypes.c_int(dtype), wl, rl])
+        assert np.array_equal(host(d_r, want_r.nbytes, NP[dtype]).view(np.uint8), want_r.view(np.uint8)), route
+    # prefix_rank: a diagonal that decays, one non-finite entry variant.
+    diag = np.geomspace(1.0, 1e-14, k)
+    for bad in (False, True):
+        r = np.zeros((n, k), NP[dtype])  # column-major [k, n]
+        for d in range(k):
+            r[d, d] = diag[d]
+        if bad:
+            r[5, 5] = np.nan
+        rl2 = abi.layout([k, n])
+        for rtol, atol in [(1e-8, 0.0), (0.0, 1e-3), (1e-16, 1e-20)]:
+            want_rank, want_st = np.zeros(1, np.int64), np.zeros(1, np.int64)
+            assert oracle.lib().t4a_oracle_prefix_rank(dtype, oracle.ptr(r), oracle.ptr(want_rank),
+                                                       oracle.ptr(want_st), ctypes.byref(rl2), rtol, atol) == 0
+            plan = t4.plan_rrqr("prefix_rank", dtype, rl2, k * n, 1, 1, rtol, atol)
+            for route in ROUTES:
+                d_r, d_rank, d_st = dev(r), dev(np.zeros(1, np.int64)), dev(np.zeros(1, np.int64))
+                launch(route, "prefix_rank", plan, plane(1),
+                       [vp(d_r), vp(d_rank), vp(d_st), ctypes.c_int(dtype), rl2, ctypes.c_double(rtol),
+                        ctypes.c_double(atol)])
+                assert int(host(d_rank, 8, np.int64)[0]) == int(want_rank[0]), (route, rtol, atol, bad)
+                assert int(host(d_st, 8, np.int64)[0]) == int(want_st[0]), (route, bad)
+
+
+@pytest.mark.parametrize("route", ROUTES)
+def test_initialize_permutation(cuda, route):
+    n, length = 37, 37 * 5
+    plan = t4.plan_rrqr("initialize_permutation", n, length)
+    d = sentinel_dev(length * 8)
+    launch(route, "initialize_permutation", plan, flat(length),
+           [vp(d), ctypes.c_longlong(n), ctypes.c_longlong(length)])
+    assert np.array_equal(host(d, length * 8, np.int64), np.arange(length) % n)
+
+
+# ---- the whole loop ---------------------------------------------------------------------
+
+def config5_matrix(m, n, rank, seed=10):
+    rng = np.random.default_rng(seed)
+    u = rng.standard_normal((m, rank))
+    v = rng.standard_normal((n, rank))
+    noise = rng.standard_normal((m, n))
+    a = u @ v.T + 1e-10 * noise
+    return np.asfortranarray(a)  # column-major [m, n]
+
+
+def oracle_rrqr(a, steps):
+    m, n = a.shape
+    work = np.asfortranarray(a).copy(order="F")
+    perm = np.zeros(n, np.int64)
+    coeff = np.zeros(max(steps, 1))
+    rank = oracle.lib().t4a_oracle_rrqr_f64(oracle.ptr(work.ravel(order="K")), m, n, steps, oracle.ptr(perm),
+                                            oracle.ptr(coeff), 1e-8, 0.0, THREADS)
+    return work, perm, coeff, rank
+
+
+def primitives_rrqr(a, steps):
+    """The reference bench's loop through this library's launchers."""
+    import torch
+    m, n = a.shape
+    dtype = abi.F64
+    wl, vl, cl = abi.layout([m, n]), abi.layout([n]), abi.layout([steps])
+    packed_l = abi.layout([m, n], [1, 0])
+    d_w = torch.from_numpy(np.asfortranarray(a).ravel(order="K").copy()).cuda()
+    d_perm = torch.zeros(n, dtype=torch.int64, device="cuda")
+    d_norms = torch.zeros(n, dtype=torch.float64, device="cuda")
+    d_piv = torch.zeros(1, dtype=torch.int64, device="cuda")
+    d_st = torch.zeros(1, dtype=torch.int64, device="cuda")
+    d_coeff = torch.zeros(steps, dtype=torch.float64, device="cuda")
+    d_packed = torch.zeros(m, dtype=torch.float64, device="cuda")
+    s = t4.stream_handle()
+    pivots = []
+    t4.launch_rrqr("initialize_permutation", t4.plan_rrqr("initialize_permutation", n, n), s, vp(d_perm),
+                   ctypes.c_longlong(n), ctypes.c_longlong(n))
+    for step in range(steps):
+        st = ctypes.c_longlong(step)
+        t4.launch_rrqr("column_norms", t4.plan_rrqr("column_norms", dtype, wl, m * n, vl, n, step), s, vp(d_w),
+                       vp(d_norms), ctypes.c_int(dtype), wl, vl, st)
+        t4.launch_rrqr("select_pivot", t4.plan_rrqr("select_pivot", dtype, vl, n, vl, n, 1, 1, step), s,
+                       vp(d_norms), vp(d_perm), vp(d_piv), vp(d_st), ctypes.c_int(dtype), vl, vl, st)
+        pivots.append(d_piv.clone())
+        t4.launch_rrqr("swap_columns", t4.plan_rrqr("swap_columns", dtype, wl, m * n, vl, n, 1, step), s, vp(d_w),
+                       vp(d_perm), vp(d_piv), ctypes.c_int(dtype), wl, vl, st)
+        t4.launch_rrqr("reflector", t4.plan_rrqr("reflector", dtype, wl, m * n, cl, steps, step), s, vp(d_w),
+                       vp(d_coeff), ctypes.c_int(dtype), wl, cl, st)
+        if n - step - 1 > 0:
+            d_packed.copy_(d_w[step * m:(step + 1) * m])
+            t4.launch_rrqr("apply_reflector",
+                           t4.plan_rrqr("apply_reflector", dtype, packed_l, m, wl, m * n, cl, steps, step, step + 1,
+                                        n - step - 1), s,
+                           vp(d_packed), vp(d_w), vp(d_coeff), ctypes.c_int(dtype), packed_l, wl, cl, st,
+                           ctypes.c_longlong(step + 1), ctypes.c_longlong(n - step - 1))
+    torch.cuda.synchronize()
+    return (d_w.cpu().numpy().reshape(n, m).T, d_perm.cpu().numpy(), d_coeff.cpu().numpy(),
+            np.array([int(p.item()) for p in pivots]))
+
+
+def fused_rrqr(a, steps):
+    import torch
+    m, n = a.shape
+    t = torch.from_numpy(np.asfortranarray(a).ravel(order="K").copy()).cuda().view(n, m).t()
+    perm, coeff, pivots, status = t4.rrqr(t, steps)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    return t.cpu().numpy(), perm.cpu().numpy(), coeff.cpu().numpy()[:steps], pivots.cpu().numpy()[:steps]
+
+
+@pytest.mark.parametrize("m,n,rank", [(600, 40, 10), (4096, 96, 24)])
+def test_rrqr_loop_matches_oracle_bit_for_bit(cuda, m, n, rank):
+    a = config5_matrix(m, n, rank, seed=m + n)
+    steps = min(m, n)
+    w_o, perm_o, coeff_o, _ = oracle_rrqr(a, steps)
+    w_p, perm_p, coeff_p, piv_p = primitives_rrqr(a, steps)
+    w_f, perm_f, coeff_f, piv_f = fused_rrqr(a, steps)
+    assert np.array_equal(perm_p, perm_o) and np.array_equal(perm_f, perm_o)
+    assert np.array_equal(piv_f, piv_p)
+    assert np.array_equal(coeff_p.view(np.uint64), coeff_o.view(np.uint64))
+    assert np.array_equal(coeff_f.view(np.uint64), coeff_o.view(np.uint64))
+    assert np.array_equal(np.asarray(w_p, order="F").view(np.uint64), np.asarray(w_o, order="F").view(np.uint64))
+    assert np.array_equal(np.asarray(w_f, order="F").view(np.uint64), np.asarray(w_o, order="F").view(np.uint64))
+
+
+def test_rrqr_config5_full_size(cuda):
+    """BASELINE config 5 at full size: A = U V^T + 1e-10 N, U [65536,64], V [256,64],
+    256 steps.  The fused loop's pivots, permutation, coefficients and matrix equal the
+    oracle's bit for bit, and the prefix rank at rtol 1e-8 is 64."""
+    m, n, rank = 65536, 256, 64
+    a = config5_matrix(m, n, rank, seed=10)
+    w_o, perm_o, coeff_o, rank_o = oracle_rrqr(a, n)
+    w_f, perm_f, coeff_f, piv_f = fused_rrqr(a, n)
+    assert rank_o == 64
+    assert np.array_equal(perm_f, perm_o)
+    assert np.array_equal(coeff_f.view(np.uint64), coeff_o.view(np.uint64))
+    assert np.array_equal(np.asarray(w_f, order="F").view(np.uint64), np.asarray(w_o, order="F").view(np.uint64))
