@@ -14,8 +14,8 @@ workload (weak scaling, no collective: the movement ops shard by independent
 tensors).  L2 is flushed before every op (a 256 MiB read, outside the timed events),
 so every kernel streams from HBM and starts without another kernel's dirty lines.
 
-`--op` selects another BASELINE config as the workload (reduce, gather, scatter,
-rrqr) for the secondary lines; the driver's runs use the default.
+`--op` selects another BASELINE config as the workload (reduce; gather = gather and
+scatter_add; rrqr) for the secondary lines; the driver's runs use the default.
 
 `--impl reference` times the reference path's CPU implementation on this box's host
 cores: the reference library has no CPU path of its own (its Rust crate only plans),
@@ -499,7 +499,87 @@ class GatherScatterWorkload(Workload):
         assert rc == 0
 
 
-WORKLOADS = {"movement": MovementWorkload, "reduce": ReduceWorkload, "gather": GatherScatterWorkload}
+
+class RrqrWorkload(Workload):
+    """tall-skinny F64 RRQR of A = U V^T + 1e-10 N, U [65536,64],
+    V [256,64], N [65536,256] normal(0,1) (NumPy generators seeded 10, 11, 12): 256
+    steps of column_norms -> select_pivot -> swap_columns -> reflector ->
+    apply_reflector (t4a_rrqr, bit-identical to that loop of primitives).  Algorithmic
+    bytes per factorization: sum over steps s of norms 8(m-s)(n-s) + apply
+    16(m-s)(n-s-1) + swap 32m + reflector 16(m-s).  Each step restores A from a
+    pristine device copy outside the timed events; in the end-to-end leg the timed
+    host-to-device copy of A is the restore."""
+
+    name = "config5-rrqr-65536x256-f64"
+    dtype = "f64"
+    e2e_restores = True
+    M, N, RANK = 65536, 256, 64
+
+    def __init__(self, device=None):
+        import numpy as np
+        import torch
+        import t4a_b200 as t4
+        from t4a_b200 import abi
+        self.t4, self.abi = t4, abi
+        self.device = device
+        m, n, k = self.M, self.N, self.RANK
+        u = np.random.default_rng(10).standard_normal((m, k))
+        v = np.random.default_rng(11).standard_normal((n, k))
+        noise = np.random.default_rng(12).standard_normal((m, n))
+        a = np.asfortranarray(u @ v.T + 1e-10 * noise)
+        self.a_host = torch.from_numpy(a.ravel(order="K").copy())  # column-major buffer
+        self.steps = n
+        self.ops = [dict(tag="rrqr-f64-65536x256-256steps", i=0, launches=1 + 5 * n, bytes=self.algorithmic_bytes())]
+        if device is not None:
+            self.host_in = [self.a_host.pin_memory()]
+            self.pristine = self.a_host.to(device)
+            self.work = torch.empty_like(self.pristine)
+            self.dev_in = [self.work]
+            self.perm = torch.empty(n, dtype=torch.int64, device=device)
+            self.coeff = torch.empty(n, dtype=torch.float64, device=device)
+            self.pivots = torch.empty(n, dtype=torch.int64, device=device)
+            self.status = torch.zeros(1, dtype=torch.int64, device=device)
+            self.layout = abi.layout([m, n])
+            self.ws = torch.empty(t4.rrqr_workspace_bytes(abi.F64, self.layout), dtype=torch.uint8, device=device)
+            self.dev_out = [self.pivots]
+            self.host_out = [torch.empty(n, dtype=torch.int64).pin_memory()]
+
+    def algorithmic_bytes(self):
+        m, n = self.M, self.N
+        return sum(8 * (m - s) * (n - s) + 16 * (m - s) * (n - s - 1) + 32 * m + 16 * (m - s) for s in range(n))
+
+    def units(self):
+        return sum(op["bytes"] for op in self.ops)
+
+    def prepare(self, op):
+        """Untimed: restore A before a factorization."""
+        self.work.copy_(self.pristine)
+
+    def run_op(self, op, stream_handle, dev_in=None, dev_out=None):
+        t4, abi = self.t4, self.abi
+        vp = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+        t4.check(t4.lib().t4a_rrqr(stream_handle, abi.F64, vp(self.work), ctypes.byref(self.layout),
+                                   self.M * self.N, self.steps, vp(self.perm), vp(self.coeff), vp(self.pivots),
+                                   vp(self.status), vp(self.ws), self.ws.numel()), "rrqr")
+
+    def host_arrays(self):
+        return [self.a_host.numpy()], [None]
+
+    def cpu_sample(self):
+        return f"one full {self.name} factorization"
+
+    def cpu_op(self, op, threads, srcs, dsts):
+        import numpy as np
+        oracle = _oracle()
+        work = srcs[0].copy()
+        perm = np.zeros(self.N, np.int64)
+        coeff = np.zeros(self.N)
+        oracle.lib().t4a_oracle_rrqr_f64(oracle.ptr(work), self.M, self.N, self.steps, oracle.lptr(perm),
+                                         oracle.ptr(coeff), 1e-8, 0.0, threads)
+
+
+WORKLOADS = {"movement": MovementWorkload, "reduce": ReduceWorkload, "gather": GatherScatterWorkload,
+             "rrqr": RrqrWorkload}
 
 
 def torch_int64():
@@ -531,8 +611,11 @@ def run_ours(args, rank, world, local_rank):
         if dist:
             torch.distributed.barrier()
 
+    prepare = getattr(wl, "prepare", None)
     for _ in range(args.warmup):
         for op in wl.ops:
+            if prepare:
+                prepare(op)
             wl.run_op(op, sh)
         flush_l2(flush)
     torch.cuda.synchronize()
@@ -550,6 +633,8 @@ def run_ours(args, rank, world, local_rank):
         torch.cuda._sleep(int(2e8))
         for k in range(args.steps):
             for j, op in enumerate(wl.ops):
+                if prepare:
+                    prepare(op)
                 flush_l2(flush)
                 events[k][j][0].record(stream)
                 wl.run_op(op, sh)
@@ -579,6 +664,8 @@ def run_ours(args, rank, world, local_rank):
         for op in wl.ops:
             for h, d in wl.e2e_inputs(op):
                 d.copy_(h, non_blocking=True)
+            if prepare and not getattr(wl, "e2e_restores", False):
+                prepare(op)
             wl.run_op(op, sh)
             for d, h in wl.e2e_outputs(op):
                 h.copy_(d, non_blocking=True)
