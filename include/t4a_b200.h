@@ -331,9 +331,12 @@ int t4a_launch_prefix_rank(const t4a_launch* launch, void* stream, const void* r
  * swap_columns, reflector and apply_reflector over the trailing columns, for one
  * column-major F32/F64 matrix (row stride 1), with results bit-identical to that loop
  * of primitives.  permutation: n int64 (initialized here); coeff: `steps` entries;
- * pivots: the pivot of each step (`steps` int64); status: one sticky int64 (set to 1
- * when a column norm is non-finite; the caller zeroes it).  The workspace holds the
- * norms and per-step scalars (t4a_rrqr_workspace_bytes). */
+ * pivots: the pivot of each step (`steps` int64); status: one sticky int64 (bit 0 set
+ * when a column norm is non-finite, as the reference's select_pivot does; bit 1 set
+ * when a bounded wait for a bulk copy ran out, the results are then invalid; the
+ * caller zeroes it).  work and status must be naturally aligned
+ * (T4A_ERR_INVALID_STRIDE otherwise).  The workspace holds the norms and per-step
+ * scalars (t4a_rrqr_workspace_bytes). */
 int t4a_rrqr_workspace_bytes(int dtype, const t4a_cuda_layout* work, size_t* bytes);
 int t4a_rrqr(void* stream, int dtype, void* work, const t4a_cuda_layout* work_layout, long long work_len,
              long long steps, void* permutation, void* coeff, void* pivots, void* status, void* workspace,

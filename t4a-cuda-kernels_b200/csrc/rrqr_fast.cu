@@ -3,6 +3,8 @@
 // flat entries are grid-stride walks.
 #include <cuda_runtime.h>
 
+#include <atomic>
+
 #include "plan_common.h"
 #include "rrqr_core.cuh"
 #include "rrqr_step.cuh"
@@ -95,8 +97,9 @@ __global__ void __launch_bounds__(kTaskThreads) k_prefix_rank(const T* r, long l
 
 // ---- fused step driver kernels ---------------------------------------------------
 template <typename F>
-__global__ void __launch_bounds__(32) k_fused_norms(FusedArgs<F> a, long long step, int walk_max) {
-  fused_norms<F>(a, step, walk_max != 0);
+__global__ void __launch_bounds__(kColThreads, 2) k_col_first(FusedArgs<F> a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  column_first<F>(a, *reinterpret_cast<ColSmem<F>*>(smem));
 }
 template <typename F>
 __global__ void __launch_bounds__(32) k_fused_pivot(FusedArgs<F> a, long long step) {
@@ -109,26 +112,34 @@ __global__ void __launch_bounds__(kFlatThreads) k_fused_swap(FusedArgs<F> a, lon
     fused_swap<F>(a, step, row);
 }
 template <typename F>
-__global__ void __launch_bounds__(32) k_fused_dot(FusedArgs<F> a, long long step) {
-  fused_dot<F>(a, step);
+__global__ void __launch_bounds__(kColThreads, 2) k_col_step(FusedArgs<F> a, long long step, int next_norm) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  column_step<F>(a, step, next_norm != 0, *reinterpret_cast<ColSmem<F>*>(smem));
 }
-template <typename F>
-__global__ void __launch_bounds__(kUpdateThreads) k_fused_update(FusedArgs<F> a, long long step) {
-  fused_update<F>(a, step, step + 1 + blockIdx.y, blockIdx.x);
+
+// Raises a kernel's dynamic shared memory limit once on each device.
+template <typename K>
+int allow_smem(K kernel, unsigned bytes, std::atomic<unsigned long long>& raised) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return runtime::check_launch();
+  const unsigned long long bit = 1ull << (dev & 63);
+  if ((raised.load(std::memory_order_relaxed) & bit) == 0) {
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+      return runtime::check_launch();
+    raised.fetch_or(bit);
+  }
+  return T4A_OK;
 }
 
 struct FusedLayout {
-  size_t norms, dots, colmax, colbad, rec, total;
+  size_t norms, rec, total;
 };
 
 FusedLayout fused_layout(long long n, int fsize) {
   auto up = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
   FusedLayout l;
   l.norms = 0;
-  l.dots = up(l.norms + n * fsize);
-  l.colmax = up(l.dots + n * fsize);
-  l.colbad = up(l.colmax + n * 8);
-  l.rec = up(l.colbad + n * 4);
+  l.rec = up(l.norms + n * fsize);
   l.total = up(l.rec + 64);
   return l;
 }
@@ -147,25 +158,25 @@ int run_fused(cudaStream_t s, F* w, long long m, long long n, long long ld, long
   a.pivots = pivots;
   a.status = status;
   a.norms = reinterpret_cast<F*>(ws + L.norms);
-  a.dots = reinterpret_cast<F*>(ws + L.dots);
-  a.colmax = reinterpret_cast<unsigned long long*>(ws + L.colmax);
-  a.colbad = reinterpret_cast<int*>(ws + L.colbad);
+  a.span = ld * (n - 1) + m;
   a.rec = reinterpret_cast<StepRecord<F>*>(ws + L.rec);
+  static std::atomic<unsigned long long> raised_first{0}, raised_step{0};
+  const unsigned smem = sizeof(ColSmem<F>);
+  T4A_TRY(allow_smem(k_col_first<F>, smem, raised_first));
+  T4A_TRY(allow_smem(k_col_step<F>, smem, raised_step));
   k_init_perm<<<dim3(static_cast<unsigned>((n + kFlatThreads - 1) / kFlatThreads)), dim3(kFlatThreads), 0, s>>>(
       perm, n, n);
+  if (steps == 0) return runtime::check_launch();
   const unsigned swap_grid = static_cast<unsigned>(m < 148ll * 8 * kFlatThreads ? (m + kFlatThreads - 1) / kFlatThreads
                                                                                 : 148 * 8);
+  k_col_first<F><<<dim3(static_cast<unsigned>(n)), dim3(kColThreads), smem, s>>>(a);
   for (long long step = 0; step < steps; ++step) {
-    k_fused_norms<F><<<dim3(static_cast<unsigned>(n - step)), dim3(32), 0, s>>>(a, step, step == 0 ? 1 : 0);
     k_fused_pivot<F><<<dim3(1), dim3(32), 0, s>>>(a, step);
     k_fused_swap<F><<<dim3(swap_grid), dim3(kFlatThreads), 0, s>>>(a, step);
     const long long trailing = n - step - 1;
-    if (trailing > 0) {
-      k_fused_dot<F><<<dim3(static_cast<unsigned>(trailing)), dim3(32), 0, s>>>(a, step);
-      const dim3 ug(static_cast<unsigned>((m - step + kUpdateRows - 1) / kUpdateRows),
-                    static_cast<unsigned>(trailing));
-      k_fused_update<F><<<ug, dim3(kUpdateThreads), 0, s>>>(a, step);
-    }
+    if (trailing > 0)
+      k_col_step<F><<<dim3(static_cast<unsigned>(trailing)), dim3(kColThreads), smem, s>>>(a, step,
+                                                                                        step + 1 < steps ? 1 : 0);
   }
   return runtime::check_launch();
 }
@@ -616,6 +627,11 @@ int t4a_rrqr(void* stream, int dtype, void* work, const t4a_cuda_layout* work_la
   size_t need = 0;
   T4A_TRY(t4a_rrqr_workspace_bytes(dtype, work_layout, &need));
   if (workspace == nullptr || workspace_bytes < need) return T4A_ERR_WORKSPACE;
+  // The chain passes read columns with bulk copies placed by address modulo 16, so the
+  // matrix (and the int64 status word) must be naturally aligned.
+  if (reinterpret_cast<unsigned long long>(work) % dtype_size(dtype) != 0 ||
+      reinterpret_cast<unsigned long long>(status) % 8 != 0)
+    return T4A_ERR_INVALID_STRIDE;
   if (m == 0 || n == 0) return T4A_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   auto* ws = static_cast<unsigned char*>(workspace);

@@ -2,7 +2,7 @@
 //
 // One step of the reference loop -- column_norms, select_pivot, swap_columns,
 // reflector, apply_reflector over the trailing columns (reference bench
-// examples/bench_kernels.rs:2390-2623) -- in four passes with the same arithmetic:
+// examples/bench_kernels.rs:2390-2623) -- in three passes with the same arithmetic:
 //
 //  pivot   one warp: the reference's pivot choice from the norms; the reflector's
 //          scalars (x0, alpha, denominator, coefficient) from the pivot column's norm,
@@ -10,13 +10,11 @@
 //          same walk and the same operations); otherwise the norm is walked again.
 //  swap    flat over rows: column swap, permutation swap, the reflector's scaling of
 //          the new column `step` and its alpha, in one pass.
-//  dot     one warp per trailing column: the reference's 32-lane dot chain times the
-//          coefficient, into `dots`.
-//  update  flat over trailing elements: t -= v * dot (the reference's fma), and for
-//          rows > step the next step's column maximum and non-finite flag (a maximum
-//          is exact in any order), so the next step's norms need one walk only.
-//  norms   one warp per column: the reference's scaled sum-of-squares chain with the
-//          maximum from `update` (step 0 walks for the maximum as well).
+//  column  one block per trailing column: the reference's 32-lane dot chain times the
+//          coefficient, the update t -= v * dot (the reference's fma), and the next
+//          step's scaled sum-of-squares norm chain of the updated column, whose
+//          maximum the update found (a maximum is exact in any order).
+// Step 0's norms run the column pass's norm chain after a walk for the maximum.
 #pragma once
 
 #include "rrqr_core.cuh"
@@ -43,63 +41,9 @@ struct FusedArgs {
   long long* pivots;  // pivot of each step
   long long* status;  // sticky non-finite flag
   F* norms;           // n
-  F* dots;            // n
-  unsigned long long* colmax;  // n: bits of the next step's column maximum
-  int* colbad;                 // n: next step's non-finite flag
+  long long span;     // elements from w to the end of the matrix
   StepRecord<F>* rec;
 };
-
-// Maximum as ordered bits: positive finite doubles/floats order like their bits.
-__device__ __forceinline__ unsigned long long max_bits(double v) { return __double_as_longlong(v); }
-__device__ __forceinline__ unsigned long long max_bits(float v) { return __float_as_uint(v); }
-template <typename F>
-__device__ __forceinline__ F from_bits(unsigned long long b) {
-  if constexpr (sizeof(F) == 8) {
-    return __longlong_as_double(static_cast<long long>(b));
-  } else {
-    return __uint_as_float(static_cast<unsigned>(b));
-  }
-}
-
-// norms pass: columns [step, n), one warp each.  `walk_max`: step 0 (no update pass
-// has produced the maximum yet).
-template <typename F>
-__device__ __forceinline__ void fused_norms(const FusedArgs<F>& a, long long step, bool walk_max) {
-  const long long j = step + warp_task();
-  if (j >= a.n) return;
-  const int lane = threadIdx.x & 31;
-  const F* col = a.w + j * a.ld;
-  F scale;
-  bool bad;
-  if (walk_max) {
-    F local_max = F(0);
-    bool invalid = false;
-#pragma unroll 8
-    for (long long row = step + lane; row < a.m; row += kPlane) {
-      const F value = mag(col[row]);
-      if (not_finite(value)) {
-        invalid = true;
-      } else if (value > local_max) {
-        local_max = value;
-      }
-    }
-    scale = plane_max(local_max);
-    bad = __any_sync(kFull, invalid);
-  } else {
-    scale = from_bits<F>(a.colmax[j]);
-    bad = a.colbad[j] != 0;
-  }
-  F local_sum = F(0);
-  if (!bad && scale > F(0)) {
-#pragma unroll 8
-    for (long long row = step + lane; row < a.m; row += kPlane) {
-      const F scaled = mag(col[row]) / scale;
-      local_sum = fused(scaled, scaled, local_sum);
-    }
-  }
-  const F norm = scale * sqrt(plane_sum(local_sum));
-  if (lane == 0) a.norms[j] = (bad || not_finite(norm)) ? F(-1) : norm;
-}
 
 // pivot pass: one warp.
 template <typename F>
@@ -179,78 +123,503 @@ __device__ __forceinline__ void fused_swap(const FusedArgs<F>& a, long long step
   }
 }
 
-// dot pass: trailing columns (step, n), one warp each.
+// a / b for 0 <= a <= b, b > 0 fixed per column, equal to the IEEE quotient, without a
+// division per element.  With r = RN(1/b) (within half an ulp of 1/b):
+//   q0 = RN(a r);  q1 = RN(q0 + (a - b q0) r);  q2 = RN(q1 + (a - b q1) r).
+// The remainders are exact (one fma each).  q0 is within 1.5 ulp of a/b, so
+// q0 + (a - b q0) r = a/b + (a/b - q0)(b r - 1) is within 2^-51 ulp of a/b, and q1, its
+// nearest double, is within one ulp of a/b.  Markstein's theorem (y within half an
+// ulp of 1/b, q within one ulp of a/b, remainder exact => RN(q + (a - b q) y) =
+// RN(a/b)) then makes q2 the IEEE quotient.  The theorem needs every quantity normal
+// and exact: b in [2^-900, 2^900] (checked once per column; otherwise every element
+// divides) and a = 0 or a >= max(b 2^-900, 2^-960) (q >= 2^-900, remainders above
+// 2^-1012); smaller a divide.  F32: the same with 2^-60, 2^60, b 2^-60 and 2^-90.
 template <typename F>
-__device__ __forceinline__ void fused_dot(const FusedArgs<F>& a, long long step) {
-  const long long j = step + 1 + warp_task();
-  if (j >= a.n) return;
-  const int lane = threadIdx.x & 31;
-  const F* v = a.w + step * a.ld;
-  const F* t = a.w + j * a.ld;
-  F dot = F(0);
-#pragma unroll 8
-  for (long long row = step + lane; row < a.m; row += kPlane) {
-    const F vv = row == step ? F(1) : v[row];
-    dot = fused(vv, t[row], dot);
+struct ScaledQuotient {
+  F b, r, threshold;
+  bool fast;
+};
+
+__device__ __noinline__ double ieee_quotient(double a, double b) { return a / b; }
+__device__ __noinline__ float ieee_quotient(float a, float b) { return a / b; }
+
+__device__ __forceinline__ ScaledQuotient<double> make_quotient(double b) {
+  ScaledQuotient<double> q;
+  q.b = b;
+  q.r = 1.0 / b;
+  q.fast = b >= 0x1p-900 && b <= 0x1p900;
+  q.threshold = fmax(b * 0x1p-900, 0x1p-960);
+  return q;
+}
+__device__ __forceinline__ ScaledQuotient<float> make_quotient(float b) {
+  ScaledQuotient<float> q;
+  q.b = b;
+  q.r = 1.0f / b;
+  q.fast = b >= 0x1p-60f && b <= 0x1p60f;
+  q.threshold = fmaxf(b * 0x1p-60f, 0x1p-90f);
+  return q;
+}
+
+__device__ __forceinline__ double quotient(const ScaledQuotient<double>& s, double a) {
+  if (s.fast && (a == 0.0 || a >= s.threshold)) {
+    const double q0 = __dmul_rn(a, s.r);
+    const double q1 = __fma_rn(__fma_rn(-s.b, q0, a), s.r, q0);
+    return __fma_rn(__fma_rn(-s.b, q1, a), s.r, q1);
   }
-  dot = plane_sum(dot) * a.coeff[step];
-  if (lane == 0) {
-    a.dots[j] = dot;
-    a.colmax[j] = 0;
-    a.colbad[j] = 0;
+  return ieee_quotient(a, s.b);
+}
+__device__ __forceinline__ float quotient(const ScaledQuotient<float>& s, float a) {
+  if (s.fast && (a == 0.0f || a >= s.threshold)) {
+    const float q0 = __fmul_rn(a, s.r);
+    const float q1 = __fmaf_rn(__fmaf_rn(-s.b, q0, a), s.r, q0);
+    return __fmaf_rn(__fmaf_rn(-s.b, q1, a), s.r, q1);
+  }
+  return ieee_quotient(a, s.b);
+}
+
+// ---- column pass: one block per column ----------------------------------------------
+// For trailing column j of step s the block runs, in order:
+//   dot     the reference's 32-lane chain (lane l folds rows s + l, s + l + 32, ...)
+//           of v_i t_ij over rows [s, m), v_s = 1, plane-summed, times coeff[s];
+//   update  t_ij = fma(-v_i, dot, t_ij) over rows [s, m), last rows first, with the
+//           maximum magnitude and the non-finite flag of rows (s, m);
+//   norm    (when step s + 1 runs) the reference's scaled sum-of-squares chain of the
+//           updated rows [s + 1, m) with that maximum, into norms[j].
+// The update re-reads what the dot just streamed and the norm re-reads what the update
+// just wrote (last written first), so both mostly hit L2.  Step 0's norms run the norm
+// chain after a walk for the maximum (the "first" pass, one block per column).
+//
+// Roles: warp 0 runs the chains; thread 32 (warp 1) streams segments into a ring of
+// kColStages shared-memory stages with bulk copies (cp.async.bulk), completing on the
+// stage's `full` mbarrier, and reuses a stage once warp 0 has released it on its
+// `empty` mbarrier; for the norm, warps 2-9 turn each landed segment into scaled
+// magnitudes in place and signal the stage's `ready` mbarrier.  The update uses every
+// thread.  Every wait is bounded: one that runs out stops the block and sets bit 1 of
+// the status word.
+//
+// Stage placement: element e of a segment sits at slot sh + e, where sh * sizeof(F)
+// is the operand's address modulo 16 at its first row (segments are multiples of 16
+// bytes), so the 16-byte-aligned bytes covering a segment copy to slot 0.  Those
+// bytes may include neighbouring rows or columns of the matrix; only where they would
+// leave the matrix's span are edge elements loaded one by one instead.
+constexpr int kColHelpers = 256;
+constexpr int kColThreads = 64 + kColHelpers;
+constexpr int kColWarps = kColThreads / 32;
+constexpr int kColStages = 6;
+constexpr int kColStageBytes = 16384;
+constexpr unsigned kColWaitLimit = 1u << 20;  // try_wait rounds before giving up
+constexpr unsigned kColSuspendNs = 1000;
+constexpr int kUpdateUnroll = 4;
+
+template <typename F>
+struct ColSmem {
+  static constexpr int kPad = 16 / static_cast<int>(sizeof(F));
+  static constexpr int kSeg1 = kColStageBytes / static_cast<int>(sizeof(F));  // norm: elements per segment
+  static constexpr int kSeg2 = kSeg1 / 2;                                      // dot: per operand and segment
+  static constexpr int kRegion2 = kSeg2 + kPad;                                // dot: slots of one operand
+  static constexpr int kStage = kSeg1 + 2 * kPad;
+  F raw[kColStages][kStage];
+  unsigned long long full[kColStages];
+  unsigned long long empty[kColStages];
+  unsigned long long ready[kColStages];
+  F red[kColWarps];
+  int bad[kColWarps];
+  F dot;
+  int abort;
+};
+
+__device__ __forceinline__ unsigned col_smem(const void* p) {
+  return static_cast<unsigned>(__cvta_generic_to_shared(p));
+}
+
+// Bounded wait for phase `parity` of an mbarrier; false when the limit ran out.
+__device__ __forceinline__ bool col_wait(const unsigned long long* bar, unsigned parity) {
+  const unsigned addr = col_smem(bar);
+  for (unsigned it = 0; it < kColWaitLimit; ++it) {
+    unsigned ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(addr), "r"(parity), "n"(kColSuspendNs)
+        : "memory");
+    if (ok) return true;
+  }
+  return false;
+}
+
+__device__ __forceinline__ void col_arrive(unsigned long long* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(col_smem(bar)) : "memory");
+}
+
+// Orders this thread's generic-proxy writes before later bulk copies (async proxy).
+__device__ __forceinline__ void col_fence_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void col_fence_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
+__device__ __forceinline__ int ring_stage(long long p) { return static_cast<int>(p % kColStages); }
+__device__ __forceinline__ unsigned ring_parity(long long p) { return static_cast<unsigned>((p / kColStages) & 1); }
+
+template <typename F>
+__device__ __forceinline__ int slot_shift(const F* p) {
+  return static_cast<int>((reinterpret_cast<unsigned long long>(p) & 15) / sizeof(F));
+}
+
+// One operand streamed by segments: rows [0, rows) from `base`.
+template <typename F>
+struct ColStream {
+  const F* base;
+  long long rows;
+  int seg;     // elements per segment
+  int sh;      // slot of element 0 (address of base modulo 16, in elements)
+  int region;  // first slot of this operand within a stage
+};
+
+template <typename F>
+__device__ __forceinline__ void col_fail(ColSmem<F>& sm, long long* status) {
+  *reinterpret_cast<volatile int*>(&sm.abort) = 1;
+  atomicOr(reinterpret_cast<unsigned long long*>(status), 2ull);
+}
+template <typename F>
+__device__ __forceinline__ bool col_aborted(ColSmem<F>& sm) {
+  return *reinterpret_cast<volatile int*>(&sm.abort) != 0;
+}
+
+// Producer: ring position p holds segment g of every operand.  Waits (bounded) until
+// warp 0 has released the stage's previous use, then issues the bulk copies.
+template <typename F, int Ops>
+__device__ __forceinline__ bool col_issue(ColSmem<F>& sm, const ColStream<F>* ops, long long p, long long g,
+                                          const F* span_lo, const F* span_hi) {
+  constexpr unsigned long long es = sizeof(F);
+  const int st = ring_stage(p);
+  if (p >= kColStages && !col_wait(&sm.empty[st], ring_parity(p - kColStages))) return false;
+  const unsigned long long w0 = (reinterpret_cast<unsigned long long>(span_lo) + 15) & ~15ull;
+  const unsigned long long w1 = reinterpret_cast<unsigned long long>(span_hi) & ~15ull;
+  unsigned long long c0[Ops], c1[Ops], g0[Ops];
+  unsigned tx = 0;
+  bool edges = false;
+#pragma unroll
+  for (int o = 0; o < Ops; ++o) {
+    const long long e0 = g * ops[o].seg;
+    const long long e1 = ops[o].rows < e0 + ops[o].seg ? ops[o].rows : e0 + ops[o].seg;
+    g0[o] = reinterpret_cast<unsigned long long>(ops[o].base + e0);
+    const unsigned long long g1 = reinterpret_cast<unsigned long long>(ops[o].base + e1);
+    c0[o] = (g0[o] & ~15ull) > w0 ? (g0[o] & ~15ull) : w0;
+    c1[o] = ((g1 + 15) & ~15ull) < w1 ? ((g1 + 15) & ~15ull) : w1;
+    if (c1[o] < c0[o]) c1[o] = c0[o];
+    // Elements outside [c0, c1): only where the aligned bytes would leave the span.
+    F* slots = sm.raw[st] + ops[o].region + ops[o].sh;
+    for (unsigned long long x = g0[o]; x < g1 && x < c0[o]; x += es) {
+      slots[(x - g0[o]) / es] = *reinterpret_cast<const F*>(x);
+      edges = true;
+    }
+    for (unsigned long long x = c1[o] > g0[o] ? c1[o] : g0[o]; x < g1; x += es) {
+      slots[(x - g0[o]) / es] = *reinterpret_cast<const F*>(x);
+      edges = true;
+    }
+    tx += static_cast<unsigned>(c1[o] - c0[o]);
+  }
+  if (edges) col_fence_shared();
+  const unsigned bar = col_smem(&sm.full[st]);
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(tx) : "memory");
+#pragma unroll
+  for (int o = 0; o < Ops; ++o) {
+    if (c1[o] > c0[o]) {
+      const unsigned dst = col_smem(sm.raw[st] + ops[o].region + ops[o].sh) +
+                           static_cast<unsigned>(static_cast<long long>(c0[o]) - static_cast<long long>(g0[o]));
+      asm volatile("cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                   "l"(c0[o]), "r"(static_cast<unsigned>(c1[o] - c0[o])), "r"(bar)
+                   : "memory");
+    }
+  }
+  return true;
+}
+
+// Chain folds over one full segment (N elements per lane), loads grouped so that
+// they run ahead of the dependent fma chain.
+template <typename F, int N>
+__device__ __forceinline__ F fold_dot(const F* bv, const F* bt, int lane, F acc) {
+#pragma unroll 1
+  for (int k0 = 0; k0 < N; k0 += 32) {
+#pragma unroll
+    for (int k = 0; k < 32; ++k) acc = fused(bv[lane + 32 * (k0 + k)], bt[lane + 32 * (k0 + k)], acc);
+  }
+  return acc;
+}
+template <typename F, int N>
+__device__ __forceinline__ F fold_squares(const F* b, int lane, F acc) {
+#pragma unroll 1
+  for (int k0 = 0; k0 < N; k0 += 32) {
+#pragma unroll
+    for (int k = 0; k < 32; ++k) {
+      const F x = b[lane + 32 * (k0 + k)];
+      acc = fused(x, x, acc);
+    }
+  }
+  return acc;
+}
+
+// Block-wide maximum and any-flag, broadcast to every thread.
+template <typename F>
+__device__ __forceinline__ void col_block_max(ColSmem<F>& sm, F local_max, bool invalid, F* scale, bool* bad) {
+  const F wm = plane_max(local_max);
+  const bool wb = __any_sync(kFull, invalid);
+  const int warp = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) {
+    sm.red[warp] = wm;
+    sm.bad[warp] = wb ? 1 : 0;
+  }
+  __syncthreads();
+  F mx = F(0);
+  int bb = 0;
+#pragma unroll
+  for (int q = 0; q < kColWarps; ++q) {
+    mx = sm.red[q] > mx ? sm.red[q] : mx;
+    bb |= sm.bad[q];
+  }
+  __syncthreads();
+  *scale = mx;
+  *bad = bb != 0;
+}
+
+template <typename F>
+__device__ __forceinline__ void track_max(F value, F* local_max, bool* invalid) {
+  const F m = mag(value);
+  if (not_finite(m)) {
+    *invalid = true;
+  } else if (m > *local_max) {
+    *local_max = m;
   }
 }
 
-// update pass: block (row tile, column j), kUpdateRows rows of column j per block.
-constexpr int kUpdateThreads = 256;
-constexpr int kUpdatePerThread = 8;
-constexpr int kUpdateRows = kUpdateThreads * kUpdatePerThread;
+// The norm chain over rows [0, rows) of `base` (ring positions from p0); returns the
+// chain warp's lane sums (zero elsewhere).  `issued` counts the producer's positions.
+template <typename F>
+__device__ __forceinline__ F col_norm_chain(ColSmem<F>& sm, const FusedArgs<F>& a, const F* base, long long rows,
+                                            F scale, long long p0, long long* issued) {
+  using S = ColSmem<F>;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const long long nseg = (rows + S::kSeg1 - 1) / S::kSeg1;
+  ColStream<F> op;
+  op.base = base;
+  op.rows = rows;
+  op.seg = S::kSeg1;
+  op.sh = slot_shift(base);
+  op.region = 0;
+  F acc = F(0);
+  if (tid == 32) {
+    for (long long g = 0; g < nseg && !col_aborted(sm); ++g) {
+      if (!col_issue<F, 1>(sm, &op, p0 + g, g, a.w, a.w + a.span)) {
+        col_fail(sm, a.status);
+        break;
+      }
+      *issued = p0 + g + 1;
+    }
+  } else if (warp >= 2) {
+    // Helpers: scaled magnitudes in place, then the stage's `ready` arrival.  `ready`
+    // is used by the norm chain only: its phase for position p counts the earlier
+    // norm positions on the same stage.
+    const ScaledQuotient<F> quo = make_quotient(scale);
+    const int h = tid - 64;
+    for (long long g = 0; g < nseg; ++g) {
+      if (__any_sync(kFull, col_aborted(sm))) break;
+      const long long p = p0 + g;
+      const int st = ring_stage(p);
+      if (!__all_sync(kFull, col_wait(&sm.full[st], ring_parity(p)))) {
+        if (lane == 0) col_fail(sm, a.status);
+        break;
+      }
+      const long long e0 = g * S::kSeg1;
+      const int len = static_cast<int>(rows - e0 < S::kSeg1 ? rows - e0 : S::kSeg1);
+      F* b = sm.raw[st] + op.sh;
+#pragma unroll
+      for (int q = 0; q < S::kSeg1 / kColHelpers; ++q) {
+        const int i = h + kColHelpers * q;
+        if (i < len) b[i] = quotient(quo, mag(b[i]));
+      }
+      col_fence_shared();
+      __syncwarp();
+      if (lane == 0) col_arrive(&sm.ready[st]);
+    }
+  } else if (warp == 0) {
+    for (long long g = 0; g < nseg; ++g) {
+      if (__any_sync(kFull, col_aborted(sm))) break;
+      const long long p = p0 + g;
+      const int st = ring_stage(p);
+      const long long before = p0 > st ? (p0 - st + kColStages - 1) / kColStages : 0;  // earlier uses, not norm
+      const unsigned parity = static_cast<unsigned>((p / kColStages - before) & 1);
+      if (!__all_sync(kFull, col_wait(&sm.ready[st], parity))) {
+        if (lane == 0) col_fail(sm, a.status);
+        break;
+      }
+      const F* b = sm.raw[st] + op.sh;
+      const long long e0 = g * S::kSeg1;
+      if (e0 + S::kSeg1 <= rows) {
+        acc = fold_squares<F, S::kSeg1 / 32>(b, lane, acc);
+      } else {
+        const int len = static_cast<int>(rows - e0);
+        for (int i = lane; i < len; i += 32) acc = fused(b[i], b[i], acc);
+      }
+      __syncwarp();
+      if (lane == 0) col_arrive(&sm.empty[st]);
+    }
+  }
+  return acc;
+}
 
 template <typename F>
-__device__ __forceinline__ void fused_update(const FusedArgs<F>& a, long long step, long long j, long long tile) {
-  __shared__ unsigned long long wmax[kUpdateThreads / 32];
-  __shared__ int wbad[kUpdateThreads / 32];
-  const F* v = a.w + step * a.ld;
-  F* t = a.w + j * a.ld;
-  const F d = a.dots[j];
-  const long long r0 = step + tile * kUpdateRows + threadIdx.x;
+__device__ __forceinline__ void col_init(ColSmem<F>& sm) {
+  if (threadIdx.x == 0) {
+    for (int q = 0; q < kColStages; ++q) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(col_smem(&sm.full[q])) : "memory");
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(col_smem(&sm.empty[q])) : "memory");
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(col_smem(&sm.ready[q])), "n"(kColHelpers / 32)
+                   : "memory");
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    sm.abort = 0;
+  }
+  __syncthreads();
+}
+
+// Waits (bounded) for the last position issued on every stage, so that no bulk copy
+// is in flight when the block exits.
+template <typename F>
+__device__ __forceinline__ void col_drain(ColSmem<F>& sm, long long issued, long long* status) {
+  const long long first = issued > kColStages ? issued - kColStages : 0;
+  for (long long p = first; p < issued; ++p)
+    if (!col_wait(&sm.full[ring_stage(p)], ring_parity(p)))
+      atomicOr(reinterpret_cast<unsigned long long*>(status), 2ull);
+}
+
+template <typename F>
+__device__ __forceinline__ void col_write_norm(ColSmem<F>& sm, const FusedArgs<F>& a, long long j, F acc, F scale,
+                                               bool bad) {
+  if ((threadIdx.x >> 5) == 0) {
+    const F norm = scale * sqrt(plane_sum(acc));
+    if ((threadIdx.x & 31) == 0) a.norms[j] = (bad || not_finite(norm) || col_aborted(sm)) ? F(-1) : norm;
+  }
+}
+
+// First pass: column j = blockIdx.x, its maximum by a walk, then its norm (step 0).
+template <typename F>
+__device__ __forceinline__ void column_first(const FusedArgs<F>& a, ColSmem<F>& sm) {
+  const long long j = blockIdx.x;
+  if (j >= a.n) return;
+  const F* col = a.w + j * a.ld;
+  col_init(sm);
   F local_max = F(0);
   bool invalid = false;
+  for (long long row = threadIdx.x; row < a.m; row += kColThreads) track_max(col[row], &local_max, &invalid);
+  F scale;
+  bool bad;
+  col_block_max(sm, local_max, invalid, &scale, &bad);
+  long long issued = 0;
+  F acc = F(0);
+  if (!bad && scale > F(0)) acc = col_norm_chain(sm, a, col, a.m, scale, 0, &issued);
+  __syncthreads();
+  if (threadIdx.x == 32) col_drain(sm, issued, a.status);
+  col_write_norm(sm, a, j, acc, scale, bad);
+}
+
+// Step pass: trailing column j = step + 1 + blockIdx.x.
+template <typename F>
+__device__ __forceinline__ void column_step(const FusedArgs<F>& a, long long step, bool next_norm, ColSmem<F>& sm) {
+  using S = ColSmem<F>;
+  const long long j = step + 1 + blockIdx.x;
+  if (j >= a.n) return;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const F* vcol = a.w + step * a.ld;
+  F* tcol = a.w + j * a.ld;
+  const long long rows = a.m - step;
+  col_init(sm);
+  long long issued = 0;
+  // dot
+  const long long nseg = (rows + S::kSeg2 - 1) / S::kSeg2;
+  ColStream<F> ops[2];
+  ops[0].base = vcol + step;
+  ops[1].base = tcol + step;
 #pragma unroll
-  for (int q = 0; q < kUpdatePerThread; ++q) {
-    const long long row = r0 + static_cast<long long>(q) * kUpdateThreads;
-    if (row < a.m) {
-      const F vv = row == step ? F(1) : v[row];
-      const F nt = fused(-vv, d, t[row]);
-      t[row] = nt;
-      if (row > step) {
-        const F value = mag(nt);
-        if (not_finite(value)) {
-          invalid = true;
-        } else if (value > local_max) {
-          local_max = value;
+  for (int o = 0; o < 2; ++o) {
+    ops[o].rows = rows;
+    ops[o].seg = S::kSeg2;
+    ops[o].sh = slot_shift(ops[o].base);
+    ops[o].region = o * S::kRegion2;
+  }
+  if (tid == 32) {
+    for (long long g = 0; g < nseg && !col_aborted(sm); ++g) {
+      if (!col_issue<F, 2>(sm, ops, g, g, a.w, a.w + a.span)) {
+        col_fail(sm, a.status);
+        break;
+      }
+      issued = g + 1;
+    }
+  } else if (warp == 0) {
+    F acc = F(0);
+    for (long long g = 0; g < nseg; ++g) {
+      if (__any_sync(kFull, col_aborted(sm))) break;
+      const int st = ring_stage(g);
+      if (!__all_sync(kFull, col_wait(&sm.full[st], ring_parity(g)))) {
+        if (lane == 0) col_fail(sm, a.status);
+        break;
+      }
+      const F* bv = sm.raw[st] + ops[0].sh;
+      const F* bt = sm.raw[st] + S::kRegion2 + ops[1].sh;
+      const long long e0 = g * S::kSeg2;
+      if (g == 0) {
+        // Row `step` of the reflector is an implicit 1.
+        const int len = static_cast<int>(rows < S::kSeg2 ? rows : S::kSeg2);
+        for (int i = lane; i < len; i += 32) acc = fused(i == 0 ? F(1) : bv[i], bt[i], acc);
+      } else if (e0 + S::kSeg2 <= rows) {
+        acc = fold_dot<F, S::kSeg2 / 32>(bv, bt, lane, acc);
+      } else {
+        const int len = static_cast<int>(rows - e0);
+        for (int i = lane; i < len; i += 32) acc = fused(bv[i], bt[i], acc);
+      }
+      __syncwarp();
+      if (lane == 0) col_arrive(&sm.empty[st]);
+    }
+    const F d = plane_sum(acc) * a.coeff[step];
+    if (lane == 0) sm.dot = d;
+  }
+  __syncthreads();
+  const F d = sm.dot;
+  // update, last rows first
+  F local_max = F(0);
+  bool invalid = false;
+  if (!col_aborted(sm)) {
+    constexpr long long chunk = static_cast<long long>(kColThreads) * kUpdateUnroll;
+    for (long long hi = rows; hi > 0; hi -= chunk) {
+      const long long lo = hi - chunk;
+      F tv[kUpdateUnroll], vv[kUpdateUnroll];
+#pragma unroll
+      for (int u = 0; u < kUpdateUnroll; ++u) {
+        const long long i = lo + u * kColThreads + tid;
+        if (i >= 0) {
+          tv[u] = tcol[step + i];
+          vv[u] = i == 0 ? F(1) : __ldg(vcol + step + i);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kUpdateUnroll; ++u) {
+        const long long i = lo + u * kColThreads + tid;
+        if (i >= 0) {
+          const F nt = fused(-vv[u], d, tv[u]);
+          tcol[step + i] = nt;
+          if (i > 0) track_max(nt, &local_max, &invalid);
         }
       }
     }
+    col_fence_global();
   }
-  const F m = plane_max(local_max);
-  const bool bad = __any_sync(kFull, invalid);
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (lane == 0) {
-    wmax[warp] = m > F(0) ? max_bits(m) : 0ull;
-    wbad[warp] = bad ? 1 : 0;
-  }
+  F scale;
+  bool bad;
+  col_block_max(sm, local_max, invalid, &scale, &bad);
+  // the next step's norm of rows [step + 1, m)
+  F acc = F(0);
+  if (next_norm && !col_aborted(sm) && !bad && scale > F(0))
+    acc = col_norm_chain(sm, a, tcol + step + 1, rows - 1, scale, nseg, &issued);
   __syncthreads();
-  if (threadIdx.x == 0) {
-    unsigned long long bm = 0;
-    int bb = 0;
-    for (int q = 0; q < kUpdateThreads / 32; ++q) {
-      bm = wmax[q] > bm ? wmax[q] : bm;
-      bb |= wbad[q];
-    }
-    if (bm != 0) atomicMax(&a.colmax[j], bm);
-    if (bb) atomicOr(&a.colbad[j], 1);
-  }
+  if (tid == 32) col_drain(sm, issued, a.status);
+  if (next_norm) col_write_norm(sm, a, j, acc, scale, bad);
 }
 
 }  // namespace rrqr

@@ -329,55 +329,75 @@ def oracle_rrqr(a, steps):
     return work, perm, coeff, rank
 
 
-def primitives_rrqr(a, steps):
-    """The reference bench's loop through this library's launchers."""
+def primitives_rrqr(a, steps, dtype=abi.F64, ld=None):
+    """The reference bench's loop through this library's launchers (column stride
+    `ld`, default m)."""
     import torch
     m, n = a.shape
-    dtype = abi.F64
-    wl, vl, cl = abi.layout([m, n]), abi.layout([n]), abi.layout([steps])
+    ld = m if ld is None else ld
+    tdt = torch.float64 if dtype == abi.F64 else torch.float32
+    span = ld * (n - 1) + m
+    wl, vl, cl = abi.layout([m, n], [1, ld]), abi.layout([n]), abi.layout([steps])
     packed_l = abi.layout([m, n], [1, 0])
-    d_w = torch.from_numpy(np.asfortranarray(a).ravel(order="K").copy()).cuda()
+    d_w = to_strided(a, ld, tdt)
     d_perm = torch.zeros(n, dtype=torch.int64, device="cuda")
-    d_norms = torch.zeros(n, dtype=torch.float64, device="cuda")
+    d_norms = torch.zeros(n, dtype=tdt, device="cuda")
     d_piv = torch.zeros(1, dtype=torch.int64, device="cuda")
     d_st = torch.zeros(1, dtype=torch.int64, device="cuda")
-    d_coeff = torch.zeros(steps, dtype=torch.float64, device="cuda")
-    d_packed = torch.zeros(m, dtype=torch.float64, device="cuda")
+    d_coeff = torch.zeros(steps, dtype=tdt, device="cuda")
+    d_packed = torch.zeros(m, dtype=tdt, device="cuda")
     s = t4.stream_handle()
     pivots = []
     t4.launch_rrqr("initialize_permutation", t4.plan_rrqr("initialize_permutation", n, n), s, vp(d_perm),
                    ctypes.c_longlong(n), ctypes.c_longlong(n))
     for step in range(steps):
         st = ctypes.c_longlong(step)
-        t4.launch_rrqr("column_norms", t4.plan_rrqr("column_norms", dtype, wl, m * n, vl, n, step), s, vp(d_w),
+        t4.launch_rrqr("column_norms", t4.plan_rrqr("column_norms", dtype, wl, span, vl, n, step), s, vp(d_w),
                        vp(d_norms), ctypes.c_int(dtype), wl, vl, st)
         t4.launch_rrqr("select_pivot", t4.plan_rrqr("select_pivot", dtype, vl, n, vl, n, 1, 1, step), s,
                        vp(d_norms), vp(d_perm), vp(d_piv), vp(d_st), ctypes.c_int(dtype), vl, vl, st)
         pivots.append(d_piv.clone())
-        t4.launch_rrqr("swap_columns", t4.plan_rrqr("swap_columns", dtype, wl, m * n, vl, n, 1, step), s, vp(d_w),
+        t4.launch_rrqr("swap_columns", t4.plan_rrqr("swap_columns", dtype, wl, span, vl, n, 1, step), s, vp(d_w),
                        vp(d_perm), vp(d_piv), ctypes.c_int(dtype), wl, vl, st)
-        t4.launch_rrqr("reflector", t4.plan_rrqr("reflector", dtype, wl, m * n, cl, steps, step), s, vp(d_w),
+        t4.launch_rrqr("reflector", t4.plan_rrqr("reflector", dtype, wl, span, cl, steps, step), s, vp(d_w),
                        vp(d_coeff), ctypes.c_int(dtype), wl, cl, st)
         if n - step - 1 > 0:
-            d_packed.copy_(d_w[step * m:(step + 1) * m])
+            d_packed.copy_(d_w[step * ld:step * ld + m])
             t4.launch_rrqr("apply_reflector",
-                           t4.plan_rrqr("apply_reflector", dtype, packed_l, m, wl, m * n, cl, steps, step, step + 1,
+                           t4.plan_rrqr("apply_reflector", dtype, packed_l, m, wl, span, cl, steps, step, step + 1,
                                         n - step - 1), s,
                            vp(d_packed), vp(d_w), vp(d_coeff), ctypes.c_int(dtype), packed_l, wl, cl, st,
                            ctypes.c_longlong(step + 1), ctypes.c_longlong(n - step - 1))
     torch.cuda.synchronize()
-    return (d_w.cpu().numpy().reshape(n, m).T, d_perm.cpu().numpy(), d_coeff.cpu().numpy(),
+    return (from_strided(d_w, m, n, ld), d_perm.cpu().numpy(), d_coeff.cpu().numpy(),
             np.array([int(p.item()) for p in pivots]))
 
 
-def fused_rrqr(a, steps):
+def to_strided(a, ld, tdt):
+    """Column-major device copy of `a` with column stride `ld` (padding rows NaN)."""
     import torch
     m, n = a.shape
-    t = torch.from_numpy(np.asfortranarray(a).ravel(order="K").copy()).cuda().view(n, m).t()
+    buf = np.full((n, ld), np.nan, dtype=a.dtype)
+    buf[:, :m] = a.T
+    return torch.from_numpy(buf.ravel()[:ld * (n - 1) + m].copy()).to(tdt).cuda()
+
+
+def from_strided(d_w, m, n, ld):
+    flat = d_w.cpu().numpy()
+    return np.stack([flat[c * ld:c * ld + m] for c in range(n)], axis=1)
+
+
+def fused_rrqr(a, steps, dtype=abi.F64, ld=None):
+    import torch
+    m, n = a.shape
+    ld = m if ld is None else ld
+    tdt = torch.float64 if dtype == abi.F64 else torch.float32
+    d_w = to_strided(a, ld, tdt)
+    t = torch.as_strided(d_w, (m, n), (1, ld))
     perm, coeff, pivots, status = t4.rrqr(t, steps)
     torch.cuda.synchronize()
     assert int(status.item()) == 0
-    return t.cpu().numpy(), perm.cpu().numpy(), coeff.cpu().numpy()[:steps], pivots.cpu().numpy()[:steps]
+    return from_strided(d_w, m, n, ld), perm.cpu().numpy(), coeff.cpu().numpy()[:steps], pivots.cpu().numpy()[:steps]
 
 
 @pytest.mark.parametrize("m,n,rank", [(600, 40, 10), (4096, 96, 24)])
@@ -406,4 +426,75 @@ def test_rrqr_config5_full_size(cuda):
     assert rank_o == 64
     assert np.array_equal(perm_f, perm_o)
     assert np.array_equal(coeff_f.view(np.uint64), coeff_o.view(np.uint64))
+    assert np.array_equal(np.asarray(w_f, order="F").view(np.uint64), np.asarray(w_o, order="F").view(np.uint64))
+
+
+@pytest.mark.parametrize("m,n,dtype,ld", [(1001, 40, abi.F64, 1001), (1001, 40, abi.F64, 1003),
+                                          (777, 33, abi.F32, 777), (9001, 24, abi.F32, 9003),
+                                          (20001, 12, abi.F64, 20001)])
+def test_rrqr_loop_odd_rows_and_strides(cuda, m, n, dtype, ld):
+    """Odd row counts and padded column strides put the pivot column and the trailing
+    columns at different addresses modulo 16, so the chain passes' aligned bulk spans
+    and their plain-load edges differ per operand: the fused loop still equals the
+    loop of primitives bit for bit (and the oracle, for F64)."""
+    a = config5_matrix(m, n, 8, seed=m + ld)
+    if dtype == abi.F32:
+        a = a.astype(np.float32)
+    steps = min(m, n)
+    w_p, perm_p, coeff_p, piv_p = primitives_rrqr(a, steps, dtype, ld)
+    w_f, perm_f, coeff_f, piv_f = fused_rrqr(a, steps, dtype, ld)
+    assert np.array_equal(perm_f, perm_p) and np.array_equal(piv_f, piv_p)
+    assert np.array_equal(coeff_f, coeff_p) and np.array_equal(coeff_f.view(np.uint8), coeff_p.view(np.uint8))
+    assert np.array_equal(w_f.view(np.uint8), w_p.view(np.uint8))
+    if dtype == abi.F64:
+        w_o, perm_o, coeff_o, _ = oracle_rrqr(a, steps)
+        assert np.array_equal(perm_f, perm_o)
+        assert np.array_equal(coeff_f.view(np.uint64), coeff_o.view(np.uint64))
+        assert np.array_equal(np.ascontiguousarray(w_f).view(np.uint64), np.ascontiguousarray(w_o).view(np.uint64))
+
+
+@pytest.mark.parametrize("dtype,offset", [(abi.F64, 1), (abi.F32, 1), (abi.F32, 3)])
+def test_rrqr_loop_unaligned_base(cuda, dtype, offset):
+    """A matrix that starts `offset` elements past a 16-byte boundary: the chain
+    passes' aligned copies must not reach before the matrix, so the first column's
+    leading elements are loaded one by one; the results still equal the loop of
+    primitives (on an aligned copy) bit for bit."""
+    import torch
+    m, n = 1003, 24
+    a = config5_matrix(m, n, 6, seed=5 + offset)
+    if dtype == abi.F32:
+        a = a.astype(np.float32)
+    tdt = torch.float64 if dtype == abi.F64 else torch.float32
+    w_p, perm_p, coeff_p, piv_p = primitives_rrqr(a, n, dtype)
+    flat = torch.from_numpy(np.asfortranarray(a).ravel(order="K").copy()).to(tdt)
+    buf = torch.cat([torch.full((offset,), float("nan"), dtype=tdt), flat]).cuda()
+    t = torch.as_strided(buf, (m, n), (1, m), storage_offset=offset)
+    assert t.data_ptr() % 16 != 0
+    perm, coeff, pivots, status = t4.rrqr(t, n)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    w_f = from_strided(buf[offset:], m, n, m)
+    assert np.array_equal(perm.cpu().numpy(), perm_p) and np.array_equal(pivots.cpu().numpy()[:n], piv_p)
+    assert np.array_equal(coeff.cpu().numpy()[:n].view(np.uint8), coeff_p.view(np.uint8))
+    assert np.array_equal(w_f.view(np.uint8), w_p.view(np.uint8))
+    assert torch.isnan(buf[:offset]).all()
+
+
+def test_rrqr_loop_special_values(cuda):
+    """Integer entries (exact quotients, powers of two, ties in the pivot norms) and a
+    tiny and a huge column (operands outside the fast quotient's range): the fused loop
+    still equals the oracle and the loop of primitives bit for bit."""
+    rng = np.random.default_rng(77)
+    m, n = 2048, 48
+    a = np.asfortranarray(rng.integers(-3, 4, (m, n)).astype(np.float64))
+    a[:, 5] *= 1e-290
+    a[:, 7] *= 1e280
+    steps = n
+    w_o, perm_o, coeff_o, _ = oracle_rrqr(a, steps)
+    w_p, perm_p, coeff_p, piv_p = primitives_rrqr(a, steps)
+    w_f, perm_f, coeff_f, piv_f = fused_rrqr(a, steps)
+    assert np.array_equal(perm_p, perm_o) and np.array_equal(perm_f, perm_o)
+    assert np.array_equal(piv_f, piv_p)
+    assert np.array_equal(coeff_f.view(np.uint64), coeff_o.view(np.uint64))
+    assert np.array_equal(np.asarray(w_p, order="F").view(np.uint64), np.asarray(w_o, order="F").view(np.uint64))
     assert np.array_equal(np.asarray(w_f, order="F").view(np.uint64), np.asarray(w_o, order="F").view(np.uint64))
