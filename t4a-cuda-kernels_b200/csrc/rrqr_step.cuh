@@ -160,21 +160,21 @@ __device__ __forceinline__ ScaledQuotient<float> make_quotient(float b) {
   return q;
 }
 
-__device__ __forceinline__ double quotient(const ScaledQuotient<double>& s, double a) {
-  if (s.fast && (a == 0.0 || a >= s.threshold)) {
-    const double q0 = __dmul_rn(a, s.r);
-    const double q1 = __fma_rn(__fma_rn(-s.b, q0, a), s.r, q0);
-    return __fma_rn(__fma_rn(-s.b, q1, a), s.r, q1);
-  }
-  return ieee_quotient(a, s.b);
+// The fast quotient (exact when quotient_safe holds) and its precondition, kept apart
+// so that a thread's quotients interleave without a call between them.
+__device__ __forceinline__ double quotient_fast(const ScaledQuotient<double>& s, double a) {
+  const double q0 = __dmul_rn(a, s.r);
+  const double q1 = __fma_rn(__fma_rn(-s.b, q0, a), s.r, q0);
+  return __fma_rn(__fma_rn(-s.b, q1, a), s.r, q1);
 }
-__device__ __forceinline__ float quotient(const ScaledQuotient<float>& s, float a) {
-  if (s.fast && (a == 0.0f || a >= s.threshold)) {
-    const float q0 = __fmul_rn(a, s.r);
-    const float q1 = __fmaf_rn(__fmaf_rn(-s.b, q0, a), s.r, q0);
-    return __fmaf_rn(__fmaf_rn(-s.b, q1, a), s.r, q1);
-  }
-  return ieee_quotient(a, s.b);
+__device__ __forceinline__ float quotient_fast(const ScaledQuotient<float>& s, float a) {
+  const float q0 = __fmul_rn(a, s.r);
+  const float q1 = __fmaf_rn(__fmaf_rn(-s.b, q0, a), s.r, q0);
+  return __fmaf_rn(__fmaf_rn(-s.b, q1, a), s.r, q1);
+}
+template <typename F>
+__device__ __forceinline__ bool quotient_safe(const ScaledQuotient<F>& s, F a) {
+  return s.fast && (a == F(0) || a >= s.threshold);
 }
 
 // ---- column pass: one block per column ----------------------------------------------
@@ -189,13 +189,18 @@ __device__ __forceinline__ float quotient(const ScaledQuotient<float>& s, float 
 // just wrote (last written first), so both mostly hit L2.  Step 0's norms run the norm
 // chain after a walk for the maximum (the "first" pass, one block per column).
 //
-// Roles: warp 0 runs the chains; thread 32 (warp 1) streams segments into a ring of
-// kColStages shared-memory stages with bulk copies (cp.async.bulk), completing on the
-// stage's `full` mbarrier, and reuses a stage once warp 0 has released it on its
-// `empty` mbarrier; for the norm, warps 2-9 turn each landed segment into scaled
-// magnitudes in place and signal the stage's `ready` mbarrier.  The update uses every
-// thread.  Every wait is bounded: one that runs out stops the block and sets bit 1 of
-// the status word.
+// Roles: warp 0 runs the chains.  Lane 0 of warps 1-3 (the producers) stream segments
+// into a ring of kColStages shared-memory stages with bulk copies (cp.async.bulk),
+// completing on the stage's `full` mbarrier; ring position p belongs to producer
+// p mod 3, which reuses a stage once its consumer has released it on the stage's
+// `empty` mbarrier (warp 0 for chain segments, the helper warps 4-11 for update
+// segments).  One warp's bulk copies are served one after another (about 55 GB/s of
+// 16 KB copies from L2), so three producers keep three streams going per block.  The
+// update's segments (v and t, last first) follow the dot's in the same ring, so their
+// copies start while the dot chain finishes; the helpers compute and store them.  For
+// the norm, the helpers turn each landed segment into scaled magnitudes in place and
+// signal the stage's `ready` mbarrier.  Every wait is bounded: one that runs out stops
+// the block and sets bit 1 of the status word.
 //
 // Stage placement: element e of a segment sits at slot sh + e, where sh * sizeof(F)
 // is the operand's address modulo 16 at its first row (segments are multiples of 16
@@ -203,13 +208,14 @@ __device__ __forceinline__ float quotient(const ScaledQuotient<float>& s, float 
 // bytes may include neighbouring rows or columns of the matrix; only where they would
 // leave the matrix's span are edge elements loaded one by one instead.
 constexpr int kColHelpers = 256;
-constexpr int kColThreads = 64 + kColHelpers;
+constexpr int kColProducers = 3;                     // divides kColStages
+constexpr int kColHelperWarp0 = 1 + kColProducers;  // first helper warp
+constexpr int kColThreads = 32 * kColHelperWarp0 + kColHelpers;
 constexpr int kColWarps = kColThreads / 32;
 constexpr int kColStages = 6;
 constexpr int kColStageBytes = 16384;
 constexpr unsigned kColWaitLimit = 1u << 20;  // try_wait rounds before giving up
 constexpr unsigned kColSuspendNs = 1000;
-constexpr int kUpdateUnroll = 4;
 
 template <typename F>
 struct ColSmem {
@@ -222,6 +228,7 @@ struct ColSmem {
   unsigned long long full[kColStages];
   unsigned long long empty[kColStages];
   unsigned long long ready[kColStages];
+  unsigned long long dot_ready;
   F red[kColWarps];
   int bad[kColWarps];
   F dot;
@@ -250,6 +257,10 @@ __device__ __forceinline__ bool col_wait(const unsigned long long* bar, unsigned
 __device__ __forceinline__ void col_arrive(unsigned long long* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(col_smem(bar)) : "memory");
 }
+// `empty` expects one arrival per helper warp: the chain warp arrives for all of them.
+__device__ __forceinline__ void col_release_all(unsigned long long* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(col_smem(bar)), "n"(kColHelpers / 32) : "memory");
+}
 
 // Orders this thread's generic-proxy writes before later bulk copies (async proxy).
 __device__ __forceinline__ void col_fence_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
@@ -272,6 +283,16 @@ struct ColStream {
   int sh;      // slot of element 0 (address of base modulo 16, in elements)
   int region;  // first slot of this operand within a stage
 };
+
+// Producer index of this thread (lane 0 of warps 1 .. kColProducers), or -1.
+__device__ __forceinline__ int col_producer() {
+  const int warp = threadIdx.x >> 5;
+  return (threadIdx.x & 31) == 0 && warp >= 1 && warp <= kColProducers ? warp - 1 : -1;
+}
+// First ring position >= p0 that producer k owns.
+__device__ __forceinline__ long long col_first_position(long long p0, int k) {
+  return p0 + ((k - p0 % kColProducers) % kColProducers + kColProducers) % kColProducers;
+}
 
 template <typename F>
 __device__ __forceinline__ void col_fail(ColSmem<F>& sm, long long* status) {
@@ -333,26 +354,39 @@ __device__ __forceinline__ bool col_issue(ColSmem<F>& sm, const ColStream<F>* op
   return true;
 }
 
-// Chain folds over one full segment (N elements per lane), loads grouped so that
-// they run ahead of the dependent fma chain.
+// Chain folds over one full segment (N elements per lane).  Each load is issued
+// kFoldAhead elements before its fma, which covers the shared-memory latency with the
+// dependent fma chain (8 cycles per FP64 fma) in a few registers.
+constexpr int kFoldAhead = 6;
 template <typename F, int N>
 __device__ __forceinline__ F fold_dot(const F* bv, const F* bt, int lane, F acc) {
-#pragma unroll 1
-  for (int k0 = 0; k0 < N; k0 += 32) {
+  F xv[kFoldAhead], xt[kFoldAhead];
 #pragma unroll
-    for (int k = 0; k < 32; ++k) acc = fused(bv[lane + 32 * (k0 + k)], bt[lane + 32 * (k0 + k)], acc);
+  for (int k = 0; k < kFoldAhead; ++k) {
+    xv[k] = bv[lane + 32 * k];
+    xt[k] = bt[lane + 32 * k];
+  }
+#pragma unroll
+  for (int k = 0; k < N; ++k) {
+    const F v = xv[k % kFoldAhead], t = xt[k % kFoldAhead];
+    if (k + kFoldAhead < N) {
+      xv[k % kFoldAhead] = bv[lane + 32 * (k + kFoldAhead)];
+      xt[k % kFoldAhead] = bt[lane + 32 * (k + kFoldAhead)];
+    }
+    acc = fused(v, t, acc);
   }
   return acc;
 }
 template <typename F, int N>
 __device__ __forceinline__ F fold_squares(const F* b, int lane, F acc) {
-#pragma unroll 1
-  for (int k0 = 0; k0 < N; k0 += 32) {
+  F x[kFoldAhead];
 #pragma unroll
-    for (int k = 0; k < 32; ++k) {
-      const F x = b[lane + 32 * (k0 + k)];
-      acc = fused(x, x, acc);
-    }
+  for (int k = 0; k < kFoldAhead; ++k) x[k] = b[lane + 32 * k];
+#pragma unroll
+  for (int k = 0; k < N; ++k) {
+    const F v = x[k % kFoldAhead];
+    if (k + kFoldAhead < N) x[k % kFoldAhead] = b[lane + 32 * (k + kFoldAhead)];
+    acc = fused(v, v, acc);
   }
   return acc;
 }
@@ -383,11 +417,9 @@ __device__ __forceinline__ void col_block_max(ColSmem<F>& sm, F local_max, bool 
 template <typename F>
 __device__ __forceinline__ void track_max(F value, F* local_max, bool* invalid) {
   const F m = mag(value);
-  if (not_finite(m)) {
-    *invalid = true;
-  } else if (m > *local_max) {
-    *local_max = m;
-  }
+  const bool nf = not_finite(m);
+  *invalid = *invalid || nf;
+  *local_max = (!nf && m > *local_max) ? m : *local_max;
 }
 
 // The norm chain over rows [0, rows) of `base` (ring positions from p0); returns the
@@ -405,20 +437,21 @@ __device__ __forceinline__ F col_norm_chain(ColSmem<F>& sm, const FusedArgs<F>& 
   op.sh = slot_shift(base);
   op.region = 0;
   F acc = F(0);
-  if (tid == 32) {
-    for (long long g = 0; g < nseg && !col_aborted(sm); ++g) {
-      if (!col_issue<F, 1>(sm, &op, p0 + g, g, a.w, a.w + a.span)) {
+  const int k = col_producer();
+  if (k >= 0) {
+    for (long long p = col_first_position(p0, k); p < p0 + nseg && !col_aborted(sm); p += kColProducers) {
+      if (!col_issue<F, 1>(sm, &op, p, p - p0, a.w, a.w + a.span)) {
         col_fail(sm, a.status);
         break;
       }
-      *issued = p0 + g + 1;
+      *issued = p + 1;
     }
-  } else if (warp >= 2) {
+  } else if (warp >= kColHelperWarp0) {
     // Helpers: scaled magnitudes in place, then the stage's `ready` arrival.  `ready`
     // is used by the norm chain only: its phase for position p counts the earlier
     // norm positions on the same stage.
     const ScaledQuotient<F> quo = make_quotient(scale);
-    const int h = tid - 64;
+    const int h = tid - 32 * kColHelperWarp0;
     for (long long g = 0; g < nseg; ++g) {
       if (__any_sync(kFull, col_aborted(sm))) break;
       const long long p = p0 + g;
@@ -430,10 +463,29 @@ __device__ __forceinline__ F col_norm_chain(ColSmem<F>& sm, const FusedArgs<F>& 
       const long long e0 = g * S::kSeg1;
       const int len = static_cast<int>(rows - e0 < S::kSeg1 ? rows - e0 : S::kSeg1);
       F* b = sm.raw[st] + op.sh;
+      constexpr int kPer = S::kSeg1 / kColHelpers;
+      F qv[kPer];
+      bool unsafe = false;
 #pragma unroll
-      for (int q = 0; q < S::kSeg1 / kColHelpers; ++q) {
+      for (int q = 0; q < kPer; ++q) {
         const int i = h + kColHelpers * q;
-        if (i < len) b[i] = quotient(quo, mag(b[i]));
+        const F x = i < len ? mag(b[i]) : F(0);
+        qv[q] = quotient_fast(quo, x);
+        unsafe |= !quotient_safe(quo, x);
+      }
+      if (unsafe) {
+        // Operands outside the fast quotient's range: IEEE division for those.
+#pragma unroll
+        for (int q = 0; q < kPer; ++q) {
+          const int i = h + kColHelpers * q;
+          const F x = i < len ? mag(b[i]) : F(0);
+          if (!quotient_safe(quo, x)) qv[q] = ieee_quotient(x, quo.b);
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < kPer; ++q) {
+        const int i = h + kColHelpers * q;
+        if (i < len) b[i] = qv[q];
       }
       col_fence_shared();
       __syncwarp();
@@ -459,7 +511,7 @@ __device__ __forceinline__ F col_norm_chain(ColSmem<F>& sm, const FusedArgs<F>& 
         for (int i = lane; i < len; i += 32) acc = fused(b[i], b[i], acc);
       }
       __syncwarp();
-      if (lane == 0) col_arrive(&sm.empty[st]);
+      if (lane == 0) col_release_all(&sm.empty[st]);
     }
   }
   return acc;
@@ -470,22 +522,24 @@ __device__ __forceinline__ void col_init(ColSmem<F>& sm) {
   if (threadIdx.x == 0) {
     for (int q = 0; q < kColStages; ++q) {
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(col_smem(&sm.full[q])) : "memory");
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(col_smem(&sm.empty[q])) : "memory");
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(col_smem(&sm.empty[q])), "n"(kColHelpers / 32)
+                   : "memory");
       asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(col_smem(&sm.ready[q])), "n"(kColHelpers / 32)
                    : "memory");
     }
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(col_smem(&sm.dot_ready)) : "memory");
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     sm.abort = 0;
   }
   __syncthreads();
 }
 
-// Waits (bounded) for the last position issued on every stage, so that no bulk copy
-// is in flight when the block exits.
+// Producer k waits (bounded) for the last position it issued on each of its stages, so
+// that no bulk copy is in flight when the block exits.
 template <typename F>
-__device__ __forceinline__ void col_drain(ColSmem<F>& sm, long long issued, long long* status) {
+__device__ __forceinline__ void col_drain(ColSmem<F>& sm, long long issued, int k, long long* status) {
   const long long first = issued > kColStages ? issued - kColStages : 0;
-  for (long long p = first; p < issued; ++p)
+  for (long long p = col_first_position(first, k); p < issued; p += kColProducers)
     if (!col_wait(&sm.full[ring_stage(p)], ring_parity(p)))
       atomicOr(reinterpret_cast<unsigned long long*>(status), 2ull);
 }
@@ -516,7 +570,7 @@ __device__ __forceinline__ void column_first(const FusedArgs<F>& a, ColSmem<F>& 
   F acc = F(0);
   if (!bad && scale > F(0)) acc = col_norm_chain(sm, a, col, a.m, scale, 0, &issued);
   __syncthreads();
-  if (threadIdx.x == 32) col_drain(sm, issued, a.status);
+  if (col_producer() >= 0) col_drain(sm, issued, col_producer(), a.status);
   col_write_norm(sm, a, j, acc, scale, bad);
 }
 
@@ -532,7 +586,8 @@ __device__ __forceinline__ void column_step(const FusedArgs<F>& a, long long ste
   const long long rows = a.m - step;
   col_init(sm);
   long long issued = 0;
-  // dot
+  // Ring positions [0, nseg): the dot's segments; [nseg, 2 nseg): the update's, last
+  // segment first; then the norm's.
   const long long nseg = (rows + S::kSeg2 - 1) / S::kSeg2;
   ColStream<F> ops[2];
   ops[0].base = vcol + step;
@@ -544,13 +599,17 @@ __device__ __forceinline__ void column_step(const FusedArgs<F>& a, long long ste
     ops[o].sh = slot_shift(ops[o].base);
     ops[o].region = o * S::kRegion2;
   }
-  if (tid == 32) {
-    for (long long g = 0; g < nseg && !col_aborted(sm); ++g) {
-      if (!col_issue<F, 2>(sm, ops, g, g, a.w, a.w + a.span)) {
+  F local_max = F(0);
+  bool invalid = false;
+  const int k = col_producer();
+  if (k >= 0) {
+    for (long long p = k; p < 2 * nseg && !col_aborted(sm); p += kColProducers) {
+      const long long g = p < nseg ? p : 2 * nseg - 1 - p;
+      if (!col_issue<F, 2>(sm, ops, p, g, a.w, a.w + a.span)) {
         col_fail(sm, a.status);
         break;
       }
-      issued = g + 1;
+      issued = p + 1;
     }
   } else if (warp == 0) {
     F acc = F(0);
@@ -575,38 +634,44 @@ __device__ __forceinline__ void column_step(const FusedArgs<F>& a, long long ste
         for (int i = lane; i < len; i += 32) acc = fused(bv[i], bt[i], acc);
       }
       __syncwarp();
-      if (lane == 0) col_arrive(&sm.empty[st]);
+      if (lane == 0) col_release_all(&sm.empty[st]);
     }
     const F d = plane_sum(acc) * a.coeff[step];
-    if (lane == 0) sm.dot = d;
-  }
-  __syncthreads();
-  const F d = sm.dot;
-  // update, last rows first
-  F local_max = F(0);
-  bool invalid = false;
-  if (!col_aborted(sm)) {
-    constexpr long long chunk = static_cast<long long>(kColThreads) * kUpdateUnroll;
-    for (long long hi = rows; hi > 0; hi -= chunk) {
-      const long long lo = hi - chunk;
-      F tv[kUpdateUnroll], vv[kUpdateUnroll];
+    if (lane == 0) {
+      sm.dot = d;
+      col_arrive(&sm.dot_ready);
+    }
+  } else if (warp >= kColHelperWarp0) {
+    // update: t = fma(-v, dot, t) from the staged segments, stored straight to memory
+    const int h = tid - 32 * kColHelperWarp0;
+    const bool ok = __all_sync(kFull, col_wait(&sm.dot_ready, 0));
+    if (!ok && lane == 0) col_fail(sm, a.status);
+    const F d = sm.dot;
+    for (long long k = 0; ok && k < nseg; ++k) {
+      if (__any_sync(kFull, col_aborted(sm))) break;
+      const long long p = nseg + k, g = nseg - 1 - k;
+      const int st = ring_stage(p);
+      if (!__all_sync(kFull, col_wait(&sm.full[st], ring_parity(p)))) {
+        if (lane == 0) col_fail(sm, a.status);
+        break;
+      }
+      const F* bv = sm.raw[st] + ops[0].sh;
+      const F* bt = sm.raw[st] + S::kRegion2 + ops[1].sh;
+      const long long e0 = g * S::kSeg2;
+      const int len = static_cast<int>(rows - e0 < S::kSeg2 ? rows - e0 : S::kSeg2);
+      F* out = tcol + step + e0;
 #pragma unroll
-      for (int u = 0; u < kUpdateUnroll; ++u) {
-        const long long i = lo + u * kColThreads + tid;
-        if (i >= 0) {
-          tv[u] = tcol[step + i];
-          vv[u] = i == 0 ? F(1) : __ldg(vcol + step + i);
+      for (int q = 0; q < S::kSeg2 / kColHelpers; ++q) {
+        const int i = h + kColHelpers * q;
+        if (i < len) {
+          const bool lead = e0 + i == 0;
+          const F nt = fused(-(lead ? F(1) : bv[i]), d, bt[i]);
+          out[i] = nt;
+          if (!lead) track_max(nt, &local_max, &invalid);
         }
       }
-#pragma unroll
-      for (int u = 0; u < kUpdateUnroll; ++u) {
-        const long long i = lo + u * kColThreads + tid;
-        if (i >= 0) {
-          const F nt = fused(-vv[u], d, tv[u]);
-          tcol[step + i] = nt;
-          if (i > 0) track_max(nt, &local_max, &invalid);
-        }
-      }
+      __syncwarp();
+      if (lane == 0) col_arrive(&sm.empty[st]);
     }
     col_fence_global();
   }
@@ -616,9 +681,9 @@ __device__ __forceinline__ void column_step(const FusedArgs<F>& a, long long ste
   // the next step's norm of rows [step + 1, m)
   F acc = F(0);
   if (next_norm && !col_aborted(sm) && !bad && scale > F(0))
-    acc = col_norm_chain(sm, a, tcol + step + 1, rows - 1, scale, nseg, &issued);
+    acc = col_norm_chain(sm, a, tcol + step + 1, rows - 1, scale, 2 * nseg, &issued);
   __syncthreads();
-  if (tid == 32) col_drain(sm, issued, a.status);
+  if (k >= 0) col_drain(sm, issued, k, a.status);
   if (next_norm) col_write_norm(sm, a, j, acc, scale, bad);
 }
 
