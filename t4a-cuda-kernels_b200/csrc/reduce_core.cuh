@@ -427,6 +427,66 @@ __device__ __forceinline__ void unit_rows(const T* in, T* out, const t4a_cuda_la
   }
 }
 
+// Warp-private variant of the rows path for rows of exactly L elements (L * sizeof(T) a
+// multiple of 128 bytes): each warp stages the 32 rows of its outputs (a contiguous
+// 32 L-element block) with coalesced 16-byte loads into its own shared slice, chunk c
+// of row r at slot c ^ (r mod C) (C chunks per row, so both the staging stores and
+// each lane's reads of its own row fill whole wavefronts), then lane r folds row r
+// serially: the same fold as unit_rows, with no block barrier and no index division.
+// `dst_linear`: output o lives at dst.offset + o.
+template <typename Op, typename T, int L>
+__device__ __forceinline__ void unit_warp_rows(const T* in, T* out, const t4a_cuda_layout& out_l,
+                                               const t4a_cuda_layout& in_l, long long outputs, bool dst_linear,
+                                               unsigned char* slice, Op op) {
+  constexpr int kRowBytes = L * static_cast<int>(sizeof(T));
+  constexpr int C = kRowBytes / 16;     // 16-byte chunks per row
+  constexpr int E = 16 / sizeof(T);     // elements per chunk
+  static_assert(kRowBytes % 128 == 0, "rows of whole 128-byte lines");
+  const int lane = threadIdx.x & 31;
+  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  const T* src = in + in_l.offset;
+  const long long groups = (outputs + 31) / 32;
+  for (long long g = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); g < groups;
+       g += warps) {
+    const long long o0 = g * 32;
+    const int n = outputs - o0 < 32 ? static_cast<int>(outputs - o0) : 32;
+    const uint4* gsrc = reinterpret_cast<const uint4*>(src + o0 * L);
+    uint4 v[C];
+#pragma unroll
+    for (int k = 0; k < C; ++k) {
+      const int q = lane + 32 * k;
+      if (q < n * C) v[k] = gsrc[q];
+    }
+    __syncwarp();  // the previous group's reads of the slice are done
+#pragma unroll
+    for (int k = 0; k < C; ++k) {
+      const int q = lane + 32 * k;
+      const int r = q / C, c = q % C;
+      if (q < n * C) *reinterpret_cast<uint4*>(slice + r * kRowBytes + ((c ^ (r % C)) << 4)) = v[k];
+    }
+    __syncwarp();
+    if (lane < n) {
+      const unsigned char* row = slice + lane * kRowBytes;
+      T acc;
+#pragma unroll
+      for (int c = 0; c < C; ++c) {
+        const uint4 w = *reinterpret_cast<const uint4*>(row + ((c ^ (lane % C)) << 4));
+        const T* x = reinterpret_cast<const T*>(&w);
+#pragma unroll
+        for (int j = 0; j < E; ++j) acc = (c == 0 && j == 0) ? op.seed(x[0]) : op.fold(acc, x[j]);
+      }
+      long long off;
+      if (dst_linear) {
+        off = out_l.offset + o0 + lane;
+      } else {
+        long long base;
+        output_offsets(o0 + lane, out_l, in_l, &base, &off);
+      }
+      out[off] = acc;
+    }
+  }
+}
+
 template <typename Op, typename T>
 __device__ __forceinline__ void unit_generic(const T* in, T* out, const t4a_cuda_layout& out_l,
                                              const t4a_cuda_layout& in_l, int axis, long long outputs,

@@ -35,6 +35,20 @@ __global__ void __launch_bounds__(256) k_unit_rows(T* out, const T* in, t4a_cuda
   unit_rows<Op, T>(in, out, out_l, in_l, outputs, rows, Op());
 }
 
+constexpr int kWarpRowsLen = 32;
+constexpr int kWarpRowsThreads = 256;
+
+template <typename Op, typename T>
+__global__ void __launch_bounds__(kWarpRowsThreads) k_warp_rows(T* out, const T* in, t4a_cuda_layout out_l,
+                                                                t4a_cuda_layout in_l, long long outputs,
+                                                                bool dst_linear) {
+  extern __shared__ __align__(16) unsigned char warp_slices[];
+  if constexpr ((kWarpRowsLen * sizeof(T)) % 128 == 0) {
+    unit_warp_rows<Op, T, kWarpRowsLen>(in, out, out_l, in_l, outputs, dst_linear,
+                                        warp_slices + (threadIdx.x >> 5) * kWarpRowsLen * sizeof(T) * 32, Op());
+  }
+}
+
 template <typename Op, typename T>
 __global__ void __launch_bounds__(256) k_unit(T* out, const T* in, t4a_cuda_layout out_l, t4a_cuda_layout in_l,
                                               int axis, long long outputs) {
@@ -45,6 +59,19 @@ template <typename Op, typename T>
 __global__ void __launch_bounds__(512) k_wide(T* out, const T* in, t4a_cuda_layout out_l, t4a_cuda_layout in_l,
                                               int axis, long long outputs) {
   wide_plane<Op, T>(in, out, out_l, in_l, axis, outputs, Op());
+}
+
+// The warp-rows kernel's path id (this launcher's own; the planner never returns it).
+constexpr int kPathWarpRows = 64;
+
+// Output o at dst.offset + o: the destination's strides are compact in axis order.
+bool dst_linear(const t4a_cuda_layout& l) {
+  long long expect = 1;
+  for (int d = 0; d < l.rank; ++d) {
+    if (l.extents[d] != 1 && l.strides[d] != expect) return false;
+    expect *= l.extents[d];
+  }
+  return true;
 }
 
 struct PassArgs {
@@ -72,6 +99,9 @@ void launch_path(int path, dim3 grid, dim3 block, unsigned smem, cudaStream_t st
       k_unit_rows<Op, T><<<grid, block, smem, stream>>>(dst, in, a.dst_l, a.in_l, a.outputs, rows);
       break;
     }
+    case kPathWarpRows:
+      k_warp_rows<Op, T><<<grid, block, smem, stream>>>(dst, in, a.dst_l, a.in_l, a.outputs, dst_linear(a.dst_l));
+      break;
     case kPathUnit:
       k_unit<Op, T><<<grid, block, smem, stream>>>(dst, in, a.dst_l, a.in_l, a.axis, a.outputs);
       break;
@@ -83,6 +113,28 @@ void launch_path(int path, dim3 grid, dim3 block, unsigned smem, cudaStream_t st
                                                     a.chunk, a.partials);
       break;
   }
+}
+
+// The rows path for rows of exactly kWarpRowsLen elements of 4 or 8 bytes on a
+// 16-byte-aligned base runs the warp-private kernel, with its own geometry (a
+// grid-stride walk over groups of 32 outputs).
+void prefer_warp_rows(int dtype, const void* in, int* path, dim3* grid, dim3* block, unsigned* smem,
+                      const PassArgs& a) {
+  if (*path != kPathUnitRows || a.axis != 0 || a.in_l.extents[0] != kWarpRowsLen) return;
+  const int esize = plan::dtype_size(dtype);
+  if (esize != 4 && esize != 8) return;
+  if (dtype != T4A_CUDA_F32 && dtype != T4A_CUDA_F64 && dtype != T4A_CUDA_I32 && dtype != T4A_CUDA_I64) return;
+  if (((reinterpret_cast<unsigned long long>(in) + a.in_l.offset * esize) & 15ull) != 0) return;
+  const unsigned long long groups = (static_cast<unsigned long long>(a.outputs) + 31) / 32;
+  // 8 warps of 4 KiB slices (4-byte elements) or 4 warps of 8 KiB slices: 32 KiB.
+  const unsigned warps_per_block = esize == 4 ? kWarpRowsThreads / 32 : kWarpRowsThreads / 64;
+  unsigned long long blocks = (groups + warps_per_block - 1) / warps_per_block;
+  const unsigned long long cap = 148ull * 16;
+  if (blocks > cap) blocks = cap;
+  *path = kPathWarpRows;
+  *grid = dim3(static_cast<unsigned>(blocks), 1, 1);
+  *block = dim3(warps_per_block * 32, 1, 1);
+  *smem = warps_per_block * 32 * kWarpRowsLen * esize;
 }
 
 // A 16-byte-vector path needs a 16-byte-aligned base; otherwise the same pass runs on
@@ -112,6 +164,7 @@ int run_pass(const t4a_launch* launch, void* stream, int dtype, int op, PassArgs
   dim3 block(launch->block[0], launch->block[1], launch->block[2]);
   unsigned smem = launch->shared_bytes;
   if (!fix_alignment(dtype, a.in, &path, &grid, &block, &smem, a)) return T4A_ERR_LAUNCH_LIMIT;
+  prefer_warp_rows(dtype, a.in, &path, &grid, &block, &smem, a);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (smem > 48 * 1024) {
     // Not reached by the planner's geometry (at most 32 KiB); kept explicit.

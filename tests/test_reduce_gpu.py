@@ -237,6 +237,43 @@ def raw_reduce(buf, base_elems, in_l, in_len, out_l, out_len, axis, op, dtype, e
     return take(out, out_len * esize)
 
 
+@pytest.mark.parametrize("dtype,np_dtype", [(abi.F32, np.float32), (abi.F64, np.float64), (abi.I32, np.int32),
+                                            (abi.I64, np.int64)])
+@pytest.mark.parametrize("op", [abi.SUM, abi.PROD, abi.SUM_SQUARES, abi.MAX, abi.MIN])
+def test_rows_of_32(cuda, dtype, np_dtype, op):
+    """A contiguous reduced axis of exactly 32 (the warp-private rows kernel): 315
+    outputs (not a multiple of 32), NaN and infinities in float rows."""
+    if op == abi.SUM_SQUARES and dtype in (abi.I32, abi.I64):
+        pytest.skip("sum_squares is a float reduction here")
+    rng = np.random.default_rng(int(dtype) * 10 + int(op))
+    shape = (7, 45, 32)
+    if np.issubdtype(np_dtype, np.integer):
+        arr = rng.integers(-1000, 1000, size=shape).astype(np_dtype)
+    else:
+        arr = (rng.uniform(0.9, 1.1, size=shape) if op == abi.PROD else rng.standard_normal(shape)).astype(np_dtype)
+        arr[1, 2, 5] = np.nan
+        arr[3, 4, 0] = np.inf
+        arr[5, 6, 31] = -np.inf
+    check_against_oracle(arr, 2, op, dtype)
+
+
+@pytest.mark.parametrize("base_elems", [0, 1])
+def test_rows_of_32_strided_destination_and_unaligned_base(cuda, base_elems):
+    """Rows of 32 into a transposed destination (outputs placed through their
+    coordinates), from a base aligned to 16 bytes and from one 8 bytes past it (the
+    rows path without 16-byte staging)."""
+    rng = np.random.default_rng(21 + base_elems)
+    data = rng.standard_normal(1 + 45 * 7 * 32)
+    buf = to_device(data)
+    in_l = abi.layout([32, 45, 7])
+    out_l = abi.layout([1, 45, 7], [0, 7, 1])  # transposed: output (i, j) at 7 i + j
+    sub = data[base_elems:base_elems + 45 * 7 * 32]
+    got = raw_reduce(buf, base_elems, in_l, len(sub), out_l, 45 * 7, 0, abi.SUM, abi.F64, 8)
+    want = np.zeros(45 * 7)
+    oracle.reduce(abi.F64, abi.SUM, want, out_l, np.ascontiguousarray(sub), in_l, 0)
+    assert same_bits_or_nan(want.tobytes().hex(), got, np.float64)
+
+
 @pytest.mark.parametrize("op", [abi.SUM, abi.MAX, abi.SUM_SQUARES])
 @pytest.mark.parametrize("axis", [0, 1, 2])
 def test_reversed_and_broadcast_layouts(cuda, op, axis):
