@@ -410,6 +410,18 @@ class GatherScatterWorkload(Workload):
                                                        abi.layout([N, 1]), abi.numpy_layout([N, C]), self.splan)
         if pin:
             self.ws = torch.empty(self.ws_bytes, dtype=torch.uint8, device=device)
+        # On N > 1 ranks the scatter has its exchange step: every rank adds its own
+        # update batch into a full-size partial destination and one NCCL reduce-scatter
+        # leaves it its 1/N of the destination rows (t4a_b200.dist); the gather needs no
+        # collective (each rank gathers its own batch).
+        self.sharded = pin and torch.distributed.is_available() and torch.distributed.is_initialized() \
+            and torch.distributed.get_world_size() > 1
+        if self.sharded:
+            from t4a_b200 import dist as t4dist
+            self.t4dist = t4dist
+            world = torch.distributed.get_world_size()
+            self.partial = t4dist.scatter_partial(self.dev["dest"])
+            self.shard_out = torch.empty((R // world, C), dtype=torch.float64, device=device)
         self.ops = [
             dict(tag="gather-f32-4Mx128-of-1Mx128", kind="gather", i=0,
                  bytes=N * C * 4 * 2 + N * 8),
@@ -456,16 +468,24 @@ class GatherScatterWorkload(Workload):
             t4.gather_raw(stream_handle, abi.F32, abi.I64, vp(d["gout"]), abi.numpy_layout([N, C]), N * C,
                           vp(d["table"]), abi.numpy_layout([R, C]), R * C, vp(d["gidx"]), abi.layout([N, 1]), N,
                           self.gplan)
+        elif self.sharded:
+            self.t4dist.scatter_add_rows_sharded(self.partial, d["sidx"].view(N), d["upd"], workspace=self.ws,
+                                                 out=self.shard_out)
         else:
             t4.scatter_add_raw(stream_handle, abi.F64, abi.I64, vp(d["dest"]), abi.numpy_layout([R, C]), R * C,
                                vp(d["sidx"]), abi.layout([N, 1]), N, vp(d["upd"]), abi.numpy_layout([N, C]), N * C,
                                self.splan, vp(self.ws), self.ws_bytes)
 
     def e2e_inputs(self, op):
-        keys = ["table", "gidx"] if op["kind"] == "gather" else ["dest", "sidx", "upd"]
+        if op["kind"] == "gather":
+            keys = ["table", "gidx"]
+        else:
+            keys = ["sidx", "upd"] if self.sharded else ["dest", "sidx", "upd"]
         return [(self.host[k], self.dev[k]) for k in keys]
 
     def e2e_outputs(self, op):
+        if op["kind"] != "gather" and self.sharded:
+            return [(self.shard_out, self.host["dest"][:self.shard_out.shape[0]])]
         k = "gout" if op["kind"] == "gather" else "dest"
         return [(self.dev[k], self.host[k])]
 
@@ -800,17 +820,29 @@ def main():
             print(json.dumps(line), flush=True)
         return
     import torch
-    if world > 1:
-        import datetime
-        torch.cuda.set_device(local_rank)
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    # Libraries may print to the process's stdout (NCCL's version banner at communicator
+    # set-up); send file descriptor 1 to stderr while they run, so that stdout carries
+    # the one JSON line only.
+    sys.stdout.flush()
+    saved_stdout = os.dup(1)
+    os.dup2(2, 1)
+    line = None
     try:
-        line = run_ours(args, rank, world, local_rank)
-        if rank == 0:
-            print(json.dumps(line), flush=True)
-    finally:
         if world > 1:
-            torch.distributed.destroy_process_group()
+            import datetime
+            torch.cuda.set_device(local_rank)
+            torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        try:
+            line = run_ours(args, rank, world, local_rank)
+        finally:
+            if world > 1:
+                torch.distributed.destroy_process_group()
+    finally:
+        sys.stdout.flush()
+        os.dup2(saved_stdout, 1)
+        os.close(saved_stdout)
+    if rank == 0 and line is not None:
+        print(json.dumps(line), flush=True)
 
 
 if __name__ == "__main__":
