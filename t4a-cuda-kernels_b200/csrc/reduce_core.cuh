@@ -332,6 +332,154 @@ __device__ __forceinline__ void strided_tiles(const T* __restrict__ in, T* __res
   }
 }
 
+// Staged variant of strided_tiles for 16-byte vectors (V > 1), same folds and trees.
+// Thread (tx, ty) copies the rows of its own LPT lanes, W rows of the chunk per
+// stage, with 16-byte cp.async into a thread-private slice of a D-stage ring, and folds
+// each stage from there once its own copies have landed (cp.async.wait_group), so the
+// data in flight takes no registers and needs no block barrier.  A producer cursor runs
+// D stages ahead of the fold across tile boundaries, so the next tile's loads overlap
+// this tile's lane tree.  Shared memory: D * LPT * kTileThreads * 16 bytes of ring,
+// then the kStridedSmem of the lane tree.
+struct StridedTile {
+  long long start, end, s, vi, in_q, dst_q;
+  int nk;       // stages of W rows
+  bool valid;   // the slot exists
+};
+
+__device__ __forceinline__ StridedTile strided_tile(const t4a_cuda_layout& in_l, const t4a_cuda_layout& dst_l,
+                                                    const StridedCtx& c, long long tile, int tx, int W) {
+  const long long slot_tiles = (c.slots + kSlotsPerTile - 1) / kSlotsPerTile;
+  StridedTile t;
+  t.s = tile / slot_tiles;
+  const long long slot = (tile % slot_tiles) * kSlotsPerTile + tx;
+  t.valid = slot < c.slots;
+  const long long q = t.valid ? slot / c.vectors : 0;
+  t.vi = t.valid ? slot % c.vectors : 0;
+  t.in_q = in_l.offset;
+  t.dst_q = dst_l.offset;
+  long long rest = q;
+#pragma unroll
+  for (int d = 0; d < kMaxRank; ++d) {
+    if (d < in_l.rank && d >= c.inner_r && d != c.axis) {
+      const long long e = in_l.extents[d];
+      const long long k = rest % e;
+      rest /= e;
+      t.in_q += k * in_l.strides[d];
+      t.dst_q += k * dst_l.strides[d];
+    }
+  }
+  t.start = t.s * c.chunk;
+  t.end = t.s + 1 == c.splits ? c.len : t.start + c.chunk;
+  t.nk = static_cast<int>((t.end - t.start + W - 1) / W);
+  return t;
+}
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<unsigned>(__cvta_generic_to_shared(smem))),
+               "l"(gmem)
+               : "memory");
+}
+
+template <typename Op, typename T, int V, int LPT, int D>
+__device__ __forceinline__ void strided_staged(const T* __restrict__ in, T* __restrict__ dst,
+                                               const t4a_cuda_layout& in_l, const t4a_cuda_layout& dst_l,
+                                               const StridedCtx& c, Op op) {
+  static_assert(V * sizeof(T) == 16, "16-byte vectors");
+  constexpr int W = LPT * kLaneGroups;
+  Vec<T, V>* ring = reinterpret_cast<Vec<T, V>*>(t4a_dyn_smem);  // [D][LPT][kTileThreads]
+  T* red = reinterpret_cast<T*>(t4a_dyn_smem + D * LPT * kTileThreads * 16);
+  const int tid = flat_tid();
+  const int tx = tid % kSlotsPerTile;
+  const int ty = tid / kSlotsPerTile;
+  const long long slot_tiles = (c.slots + kSlotsPerTile - 1) / kSlotsPerTile;
+  const long long tiles = slot_tiles * c.splits;
+  const long long lane0 = static_cast<long long>(ty) * LPT;
+
+  // Producer cursor: (tile, stage) of the next copies; one commit group per stage,
+  // empty once the block's tiles are exhausted.
+  long long p_tile = blockIdx.x;
+  int p_k = 0;
+  StridedTile pt{};
+  if (p_tile < tiles) pt = strided_tile(in_l, dst_l, c, p_tile, tx, W);
+  int p_slot = 0;
+  auto issue = [&]() {
+    if (p_tile < tiles) {
+      const T* base = in + pt.in_q + pt.vi * V;
+#pragma unroll
+      for (int l = 0; l < LPT; ++l) {
+        const long long row = pt.start + static_cast<long long>(p_k) * W + lane0 + l;
+        if (pt.valid && row < pt.end) cp_async16(&ring[(p_slot * LPT + l) * kTileThreads + tid], base + row * c.astride);
+      }
+      if (++p_k == pt.nk) {
+        p_k = 0;
+        p_tile += gridDim.x;
+        if (p_tile < tiles) pt = strided_tile(in_l, dst_l, c, p_tile, tx, W);
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    p_slot = p_slot + 1 == D ? 0 : p_slot + 1;
+  };
+#pragma unroll
+  for (int i = 0; i < D; ++i) issue();
+
+  int c_slot = 0;
+  for (long long tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+    const StridedTile t = strided_tile(in_l, dst_l, c, tile, tx, W);
+    Vec<T, V> acc[LPT];
+    for (int k = 0; k < t.nk; ++k) {
+      asm volatile("cp.async.wait_group %0;" ::"n"(D - 1) : "memory");
+#pragma unroll
+      for (int l = 0; l < LPT; ++l) {
+        const long long row = t.start + static_cast<long long>(k) * W + lane0 + l;
+        if (row < t.end) {
+          const Vec<T, V> x = ring[(c_slot * LPT + l) * kTileThreads + tid];
+#pragma unroll
+          for (int v = 0; v < V; ++v) acc[l].v[v] = k == 0 ? op.seed(x.v[v]) : op.fold(acc[l].v[v], x.v[v]);
+        }
+      }
+      c_slot = c_slot + 1 == D ? 0 : c_slot + 1;
+      issue();  // into the slot just folded
+    }
+#pragma unroll
+    for (int w = 1; w < LPT; w *= 2)
+#pragma unroll
+      for (int l = 0; l + w < LPT; l += 2 * w)
+#pragma unroll
+        for (int v = 0; v < V; ++v) acc[l].v[v] = op.combine(acc[l].v[v], acc[l + w].v[v]);
+    Vec<T, V> mine = acc[0];
+#pragma unroll
+    for (int w = 1; w < kLaneGroups; w *= 2) {
+      if (ty % (2 * w) == w) {
+#pragma unroll
+        for (int v = 0; v < V; ++v) red[(ty * kSlotsPerTile + tx) * V + v] = mine.v[v];
+      }
+      __syncthreads();
+      if (ty % (2 * w) == 0) {
+#pragma unroll
+        for (int v = 0; v < V; ++v) mine.v[v] = op.combine(mine.v[v], red[((ty + w) * kSlotsPerTile + tx) * V + v]);
+      }
+      __syncthreads();
+    }
+    if (ty == 0 && t.valid) {
+#pragma unroll
+      for (int v = 0; v < V; ++v) {
+        long long rest = t.vi * V + v, off = t.dst_q;
+#pragma unroll
+        for (int d = 0; d < kMaxRank; ++d) {
+          if (d < c.inner_r) {
+            const long long e = in_l.extents[d];
+            off += (rest % e) * dst_l.strides[d];
+            rest /= e;
+          }
+        }
+        if (c.partials) off += t.s * dst_l.strides[c.axis];
+        dst[off] = mine.v[v];
+      }
+    }
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+}
+
 // ---------------------------------------------------------------------------
 // One W-lane plane per cube (contiguous axis, and the general fallback).  Planes of
 // one block are consecutive cubes; every lane of a warp reaches the shuffles.

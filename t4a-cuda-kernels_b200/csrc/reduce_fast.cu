@@ -7,6 +7,8 @@
 // so both routes produce the same bits.
 #include <cuda_runtime.h>
 
+#include <atomic>
+
 #include "plan_common.h"
 #include "reduce_core.cuh"
 #include "runtime.h"
@@ -20,6 +22,23 @@ __global__ void __launch_bounds__(256) k_strided(T* dst, const T* in, t4a_cuda_l
                                                  long long chunk, bool partials) {
   constexpr int V = VecOf<T>::kLanes;
   strided_tiles<Op, T, V, 4>(in, dst, in_l, dst_l, strided_ctx(in_l, axis, splits, chunk, V, partials), Op());
+}
+
+// The staged strided pass: 4-stage cp.async ring, three blocks per SM.
+constexpr int kStagedDepth = 4;
+constexpr int kStagedBlocksPerSm = 3;
+constexpr unsigned kStagedSmem = kStagedDepth * 4 * kTileThreads * 16 + kStridedSmem;
+
+template <typename Op, typename T>
+__global__ void __launch_bounds__(256, kStagedBlocksPerSm) k_strided_staged(T* dst, const T* in, t4a_cuda_layout dst_l,
+                                                                           t4a_cuda_layout in_l, int axis,
+                                                                           long long splits, long long chunk,
+                                                                           bool partials) {
+  constexpr int V = VecOf<T>::kLanes;
+  if constexpr (V * sizeof(T) == 16) {
+    strided_staged<Op, T, V, 4, kStagedDepth>(in, dst, in_l, dst_l, strided_ctx(in_l, axis, splits, chunk, V, partials),
+                                              Op());
+  }
 }
 
 template <typename Op, typename T>
@@ -61,8 +80,9 @@ __global__ void __launch_bounds__(512) k_wide(T* out, const T* in, t4a_cuda_layo
   wide_plane<Op, T>(in, out, out_l, in_l, axis, outputs, Op());
 }
 
-// The warp-rows kernel's path id (this launcher's own; the planner never returns it).
+// This launcher's own path ids (the planner never returns them).
 constexpr int kPathWarpRows = 64;
+constexpr int kPathStridedStaged = 65;
 
 // Output o at dst.offset + o: the destination's strides are compact in axis order.
 bool dst_linear(const t4a_cuda_layout& l) {
@@ -97,6 +117,20 @@ void launch_path(int path, dim3 grid, dim3 block, unsigned smem, cudaStream_t st
     case kPathUnitRows: {
       const int rows = unit_rows_per_tile(a.in_l, a.axis, sizeof(T));
       k_unit_rows<Op, T><<<grid, block, smem, stream>>>(dst, in, a.dst_l, a.in_l, a.outputs, rows);
+      break;
+    }
+    case kPathStridedStaged: {
+      static std::atomic<unsigned long long> raised{0};
+      int dev = 0;
+      if (cudaGetDevice(&dev) == cudaSuccess) {
+        const unsigned long long bit = 1ull << (dev & 63);
+        if ((raised.load(std::memory_order_relaxed) & bit) == 0 &&
+            cudaFuncSetAttribute(k_strided_staged<Op, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) ==
+                cudaSuccess)
+          raised.fetch_or(bit);
+      }
+      k_strided_staged<Op, T><<<grid, block, smem, stream>>>(dst, in, a.dst_l, a.in_l, a.axis, a.splits, a.chunk,
+                                                             a.partials);
       break;
     }
     case kPathWarpRows:
@@ -137,6 +171,22 @@ void prefer_warp_rows(int dtype, const void* in, int* path, dim3* grid, dim3* bl
   *smem = warps_per_block * 32 * kWarpRowsLen * esize;
 }
 
+// A strided pass over 16-byte vectors with at least kStagedMinTiles tiles per resident
+// block runs the staged kernel on a grid of kStagedBlocksPerSm blocks per SM, each
+// walking many tiles, so that its copy ring runs ahead across tile boundaries; smaller
+// passes keep one tile per block.
+constexpr unsigned kStagedMinTiles = 4;
+void prefer_strided_staged(int dtype, int* path, dim3* grid, unsigned* smem) {
+  if (*path != kPathStrided || strided_vec_lanes(dtype) == 1) return;
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const unsigned cap = static_cast<unsigned>(sms * kStagedBlocksPerSm);
+  if (grid->x < kStagedMinTiles * cap) return;
+  *path = kPathStridedStaged;
+  grid->x = cap;
+  *smem = kStagedSmem;
+}
+
 // A 16-byte-vector path needs a 16-byte-aligned base; otherwise the same pass runs on
 // the per-cube path, whose geometry is recomputed here.
 bool fix_alignment(int dtype, const void* in, int* path, dim3* grid, dim3* block, unsigned* smem,
@@ -170,6 +220,7 @@ int run_pass(const t4a_launch* launch, void* stream, int dtype, int op, PassArgs
     // Not reached by the planner's geometry (at most 32 KiB); kept explicit.
     return T4A_ERR_LAUNCH_LIMIT;
   }
+  prefer_strided_staged(dtype, &path, &grid, &smem);
 #define T4A_CALL(OP, T) launch_path<OP, T>(path, grid, block, smem, s, a)
   T4A_REDUCE_SWITCH(op, dtype, T4A_CALL)
 #undef T4A_CALL
