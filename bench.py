@@ -549,7 +549,7 @@ class RrqrWorkload(Workload):
         a = np.asfortranarray(u @ v.T + 1e-10 * noise)
         self.a_host = torch.from_numpy(a.ravel(order="K").copy())  # column-major buffer
         self.steps = n
-        self.ops = [dict(tag="rrqr-f64-65536x256-256steps", i=0, launches=3 * n + 1, bytes=self.algorithmic_bytes())]
+        self.ops = [dict(tag="rrqr-f64-65536x256-256steps", i=0, launches=2 * n + 1, bytes=self.algorithmic_bytes())]
         if device is not None:
             self.host_in = [self.a_host.pin_memory()]
             self.pristine = self.a_host.to(device)

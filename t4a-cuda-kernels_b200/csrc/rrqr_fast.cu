@@ -21,10 +21,12 @@ constexpr int kFlatThreads = 256;
 constexpr int kRrqrVariant = 64;  // t4a_launch.variant of the RRQR entries
 
 // ---- kernels (this library's geometry) -----------------------------------------
-__global__ void __launch_bounds__(kFlatThreads) k_init_perm(long long* perm, long long n, long long len) {
+__global__ void __launch_bounds__(kFlatThreads) k_init_perm(long long* perm, long long n, long long len,
+                                                           unsigned* done) {
   const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
   for (long long p = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; p < len; p += stride)
     perm[p] = p % n;
+  if (done != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *done = 0;
 }
 
 template <typename T>
@@ -102,10 +104,6 @@ __global__ void __launch_bounds__(kColThreads, 2) k_col_first(FusedArgs<F> a) {
   column_first<F>(a, *reinterpret_cast<ColSmem<F>*>(smem));
 }
 template <typename F>
-__global__ void __launch_bounds__(32) k_fused_pivot(FusedArgs<F> a, long long step) {
-  fused_pivot<F>(a, step);
-}
-template <typename F>
 __global__ void __launch_bounds__(kFlatThreads) k_fused_swap(FusedArgs<F> a, long long step) {
   const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
   for (long long row = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; row < a.m; row += stride)
@@ -132,7 +130,7 @@ int allow_smem(K kernel, unsigned bytes, std::atomic<unsigned long long>& raised
 }
 
 struct FusedLayout {
-  size_t norms, rec, total;
+  size_t norms, rec, done, total;
 };
 
 FusedLayout fused_layout(long long n, int fsize) {
@@ -140,7 +138,8 @@ FusedLayout fused_layout(long long n, int fsize) {
   FusedLayout l;
   l.norms = 0;
   l.rec = up(l.norms + n * fsize);
-  l.total = up(l.rec + 64);
+  l.done = up(l.rec + 64);
+  l.total = up(l.done + 4);
   return l;
 }
 
@@ -160,18 +159,19 @@ int run_fused(cudaStream_t s, F* w, long long m, long long n, long long ld, long
   a.norms = reinterpret_cast<F*>(ws + L.norms);
   a.span = ld * (n - 1) + m;
   a.rec = reinterpret_cast<StepRecord<F>*>(ws + L.rec);
+  a.done = reinterpret_cast<unsigned*>(ws + L.done);
   static std::atomic<unsigned long long> raised_first{0}, raised_step{0};
   const unsigned smem = sizeof(ColSmem<F>);
   T4A_TRY(allow_smem(k_col_first<F>, smem, raised_first));
   T4A_TRY(allow_smem(k_col_step<F>, smem, raised_step));
   k_init_perm<<<dim3(static_cast<unsigned>((n + kFlatThreads - 1) / kFlatThreads)), dim3(kFlatThreads), 0, s>>>(
-      perm, n, n);
+      perm, n, n, a.done);
   if (steps == 0) return runtime::check_launch();
   const unsigned swap_grid = static_cast<unsigned>(m < 148ll * 8 * kFlatThreads ? (m + kFlatThreads - 1) / kFlatThreads
                                                                                 : 148 * 8);
   k_col_first<F><<<dim3(static_cast<unsigned>(n)), dim3(kColThreads), smem, s>>>(a);
+  // The first pass and every column pass end with the next step's pivot (last block).
   for (long long step = 0; step < steps; ++step) {
-    k_fused_pivot<F><<<dim3(1), dim3(32), 0, s>>>(a, step);
     k_fused_swap<F><<<dim3(swap_grid), dim3(kFlatThreads), 0, s>>>(a, step);
     const long long trailing = n - step - 1;
     if (trailing > 0)
@@ -421,7 +421,7 @@ int t4a_launch_initialize_permutation(const t4a_launch* launch, void* stream, vo
   if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
   if (launch_empty(launch) || len <= 0 || n <= 0) return T4A_OK;
   k_init_perm<<<grid_of_launch(launch), block_of_launch(launch), 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<long long*>(permutation), n, len);
+      static_cast<long long*>(permutation), n, len, nullptr);
   return runtime::check_launch();
 }
 

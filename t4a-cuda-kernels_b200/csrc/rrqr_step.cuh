@@ -2,12 +2,14 @@
 //
 // One step of the reference loop -- column_norms, select_pivot, swap_columns,
 // reflector, apply_reflector over the trailing columns (reference bench
-// examples/bench_kernels.rs:2390-2623) -- in three passes with the same arithmetic:
+// examples/bench_kernels.rs:2390-2623) -- in two launches with the same arithmetic:
 //
-//  pivot   one warp: the reference's pivot choice from the norms; the reflector's
-//          scalars (x0, alpha, denominator, coefficient) from the pivot column's norm,
-//          which equals the reflector's own norm whenever the column is finite (the
-//          same walk and the same operations); otherwise the norm is walked again.
+//  pivot   one warp of the previous column pass's last block (every block publishes
+//          its norm and draws a ticket; the one that draws the last sees them all):
+//          the reference's pivot choice from the norms, and the reflector's scalars
+//          (x0, alpha, denominator, coefficient) from the pivot column's norm, which
+//          equals the reflector's own norm whenever the column is finite (the same
+//          walk and the same operations); otherwise the norm is walked again.
 //  swap    flat over rows: column swap, permutation swap, the reflector's scaling of
 //          the new column `step` and its alpha, in one pass.
 //  column  one block per trailing column: the reference's 32-lane dot chain times the
@@ -43,6 +45,7 @@ struct FusedArgs {
   F* norms;           // n
   long long span;     // elements from w to the end of the matrix
   StepRecord<F>* rec;
+  unsigned* done;     // blocks of the running column pass that have written their norm
 };
 
 // pivot pass: one warp.
@@ -233,6 +236,7 @@ struct ColSmem {
   int bad[kColWarps];
   F dot;
   int abort;
+  int last;  // this block drew the column pass's last ticket
 };
 
 __device__ __forceinline__ unsigned col_smem(const void* p) {
@@ -553,6 +557,23 @@ __device__ __forceinline__ void col_write_norm(ColSmem<F>& sm, const FusedArgs<F
   }
 }
 
+// After this block's norm is written (by thread 0): publish it and draw a ticket; the
+// block that draws the last one sees every norm of the pass and selects the pivot of
+// `pivot_step` with its warp 0, then rearms the counter for the next pass.
+template <typename F>
+__device__ __forceinline__ void col_pivot_if_last(const FusedArgs<F>& a, long long pivot_step, ColSmem<F>& sm) {
+  if (threadIdx.x == 0) {
+    __threadfence();
+    sm.last = atomicAdd(a.done, 1u) == gridDim.x - 1 ? 1 : 0;
+  }
+  __syncthreads();
+  if (sm.last) {
+    __threadfence();
+    if (threadIdx.x < 32) fused_pivot(a, pivot_step);
+    if (threadIdx.x == 0) *a.done = 0;
+  }
+}
+
 // First pass: column j = blockIdx.x, its maximum by a walk, then its norm (step 0).
 template <typename F>
 __device__ __forceinline__ void column_first(const FusedArgs<F>& a, ColSmem<F>& sm) {
@@ -572,6 +593,7 @@ __device__ __forceinline__ void column_first(const FusedArgs<F>& a, ColSmem<F>& 
   __syncthreads();
   if (col_producer() >= 0) col_drain(sm, issued, col_producer(), a.status);
   col_write_norm(sm, a, j, acc, scale, bad);
+  col_pivot_if_last(a, 0, sm);
 }
 
 // Step pass: trailing column j = step + 1 + blockIdx.x.
@@ -684,7 +706,10 @@ __device__ __forceinline__ void column_step(const FusedArgs<F>& a, long long ste
     acc = col_norm_chain(sm, a, tcol + step + 1, rows - 1, scale, 2 * nseg, &issued);
   __syncthreads();
   if (k >= 0) col_drain(sm, issued, k, a.status);
-  if (next_norm) col_write_norm(sm, a, j, acc, scale, bad);
+  if (next_norm) {
+    col_write_norm(sm, a, j, acc, scale, bad);
+    col_pivot_if_last(a, step + 1, sm);
+  }
 }
 
 }  // namespace rrqr
