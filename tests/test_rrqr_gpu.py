@@ -453,6 +453,21 @@ def test_rrqr_loop_odd_rows_and_strides(cuda, m, n, dtype, ld):
         assert np.array_equal(np.ascontiguousarray(w_f).view(np.uint64), np.ascontiguousarray(w_o).view(np.uint64))
 
 
+@pytest.mark.parametrize("m,n,steps,dtype", [(600, 40, 13, abi.F64), (777, 33, 1, abi.F32), (2048, 64, 63, abi.F64)])
+def test_rrqr_partial_factorization(cuda, m, n, steps, dtype):
+    """Fewer steps than min(m, n): the last column pass updates the trailing columns
+    without the next step's norms and pivot; matrix, permutation, pivots and
+    coefficients equal the loop of primitives run for the same steps, bit for bit."""
+    a = config5_matrix(m, n, 6, seed=m + steps)
+    if dtype == abi.F32:
+        a = a.astype(np.float32)
+    w_p, perm_p, coeff_p, piv_p = primitives_rrqr(a, steps, dtype)
+    w_f, perm_f, coeff_f, piv_f = fused_rrqr(a, steps, dtype)
+    assert np.array_equal(perm_f, perm_p) and np.array_equal(piv_f, piv_p)
+    assert np.array_equal(coeff_f.view(np.uint8), coeff_p.view(np.uint8))
+    assert np.array_equal(w_f.view(np.uint8), w_p.view(np.uint8))
+
+
 @pytest.mark.parametrize("dtype,offset", [(abi.F64, 1), (abi.F32, 1), (abi.F32, 3)])
 def test_rrqr_loop_unaligned_base(cuda, dtype, offset):
     """A matrix that starts `offset` elements past a 16-byte boundary: the chain
