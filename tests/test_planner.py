@@ -217,3 +217,37 @@ def test_scatter_plans_nothing_when_no_window_fits():
     launch = t4.plan_scatter_add(abi.F64, abi.I64, abi.layout([6]), 6, abi.layout([2, 1]), 2,
                                  abi.layout([2, 7]), 14, plan)
     assert launch.grid[0] == 0
+
+
+def rrqr_status(dtype, layout, work_len, steps, work=0x10000, status=0x20000, ws=0x30000, ws_bytes=None,
+                perm=0x40000, coeff=0x50000, piv=0x60000):
+    """t4a_rrqr's status for arguments it rejects before any launch (addresses are
+    never dereferenced on these paths)."""
+    if ws_bytes is None:
+        n = ctypes.c_size_t(0)
+        rc = t4.lib().t4a_rrqr_workspace_bytes(dtype, ctypes.byref(layout), ctypes.byref(n))
+        ws_bytes = n.value if rc == 0 else 1 << 20
+    vp = lambda a: ctypes.c_void_p(a) if a else None  # noqa: E731
+    return t4.lib().t4a_rrqr(None, dtype, vp(work), ctypes.byref(layout), work_len, steps, vp(perm), vp(coeff),
+                             vp(piv), vp(status), vp(ws), ctypes.c_size_t(ws_bytes))
+
+
+def test_rrqr_driver_rejects_bad_arguments_before_launching():
+    good = abi.layout([600, 40])
+    n = ctypes.c_size_t(0)
+    assert t4.lib().t4a_rrqr_workspace_bytes(abi.F64, ctypes.byref(good), ctypes.byref(n)) == 0 and n.value > 0
+    assert rrqr_status(abi.F64, good, 600 * 40, 41) == 16                    # steps > min(m, n)
+    assert rrqr_status(abi.F64, good, 600 * 40, -1) == 16
+    assert rrqr_status(abi.C64, good, 600 * 40, 40) == 9                     # F32/F64 only
+    assert rrqr_status(abi.F64, abi.layout([600, 40, 2]), 48000, 40) == 1    # one matrix
+    assert rrqr_status(abi.F64, abi.layout([600, 40], [40, 1]), 24000, 40) == 20  # row stride 1
+    assert rrqr_status(abi.F64, abi.layout([600, 40], [1, 599]), 24000, 40) == 20  # columns overlap
+    assert rrqr_status(abi.F64, good, 100, 40) == 7                          # span past the buffer
+    assert rrqr_status(abi.F64, good, 600 * 40, 40, ws_bytes=16) == 65       # workspace too small
+    assert rrqr_status(abi.F64, good, 600 * 40, 40, ws=0) == 65
+    assert rrqr_status(abi.F64, good, 600 * 40, 40, work=0x10004) == 20      # not 8-byte aligned
+    assert rrqr_status(abi.F32, good, 600 * 40, 40, work=0x10002) == 20      # not 4-byte aligned
+    assert rrqr_status(abi.F64, good, 600 * 40, 40, status=0x20004) == 20    # status word alignment
+    assert rrqr_status(abi.F64, good, 600 * 40, 40, work=0) == 66            # NULL arguments
+    assert rrqr_status(abi.F64, good, 600 * 40, 40, piv=0) == 66
+    assert rrqr_status(abi.F64, abi.layout([0, 40]), 0, 0) == 0              # nothing to do
