@@ -164,6 +164,25 @@ int t4a_reduce_noalloc(void* stream, int dtype, int op, void* out, const t4a_cud
                        long long out_len, const void* in, const t4a_cuda_layout* in_layout, long long in_len,
                        unsigned axis, unsigned plane_width);
 
+/* General-rank reductions, the `_any` twins (reference cuda/src/reduce.cu:854, :902;
+ * module symbols t4a_cuda_reduce_any / t4a_cuda_reduce_partials_any in reduce.cubin):
+ * the same folds as t4a_launch_reduce / t4a_launch_reduce_partials, with the layouts'
+ * extents and strides in device memory, so any rank works.  The launchers take the
+ * kernels' argument lists; any geometry is correct, and t4a_reduce_any_geometry gives
+ * the one they are tuned for (UNIT: a thread per output; PLANE: planes of w lanes,
+ * w in {8, 16, 32}, or one block of w in {64 .. 512} per output for a direct pass).
+ * The host checks what it can without device access (layout rank and reserved field,
+ * NULL arrays, axis, split); extents and strides are the caller's, as in the reference. */
+int t4a_reduce_any_geometry(int strategy, unsigned plane_width, long long output_len, long long splits,
+                            t4a_launch* launch);
+int t4a_launch_reduce_any(const t4a_launch* launch, void* stream, void* out, const void* in, int dtype, int op,
+                          int strategy, t4a_cuda_layout_any out_layout, t4a_cuda_layout_any in_layout, int axis,
+                          long long output_len);
+int t4a_launch_reduce_partials_any(const t4a_launch* launch, void* stream, void* partials, const void* in,
+                                   int dtype, int op, t4a_cuda_layout_any partials_layout,
+                                   t4a_cuda_layout_any in_layout, int axis, long long output_len, long long splits,
+                                   long long chunk_len);
+
 
 /* ------------------------------------------------------------------------- */
 /* Strided movement (reference src/lib.rs:1465-1737, movement.cu:514-656)      */

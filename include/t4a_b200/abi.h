@@ -114,9 +114,23 @@ typedef struct {
   int vector_width;
 } t4a_cuda_transpose_config;
 
+/* General-rank layout of the `_any` entries (reference abi.cuh "Dynamic rank"): the
+ * same fields as t4a_cuda_layout with the extents and strides in caller-owned device
+ * memory, so any rank is representable; a zero-length array may be NULL. */
+typedef struct {
+  int rank;
+  int reserved;  /* must be 0 */
+  long long offset;
+  const long long* extents;  /* rank values, device memory */
+  const long long* strides;  /* rank values, device memory */
+} t4a_cuda_layout_any;
+
 #ifdef __cplusplus
 }  /* extern "C" */
 
+static_assert(sizeof(t4a_cuda_layout_any) == 32, "t4a_cuda_layout_any size");
+static_assert(alignof(t4a_cuda_layout_any) == 8, "t4a_cuda_layout_any alignment");
+static_assert(__builtin_offsetof(t4a_cuda_layout_any, extents) == 16, "layout_any.extents");
 static_assert(sizeof(t4a_cuda_layout) == 144, "t4a_cuda_layout size");
 static_assert(alignof(t4a_cuda_layout) == 8, "t4a_cuda_layout alignment");
 static_assert(__builtin_offsetof(t4a_cuda_layout, offset) == 8, "layout.offset");

@@ -70,12 +70,14 @@ __device__ __forceinline__ double square(double x) { return __fma_rn(x, x, 0.0);
 template <typename T>
 __device__ __forceinline__ T square(T x) { return Num<T>::mul(x, x); }
 
-// NaN-propagating extrema: a NaN left operand wins, then a NaN right operand,
-// otherwise the ordered extremum (fmaxf/fminf order -0.0 below +0.0).
+// NaN-propagating extrema: the ordered extremum (-0.0 below +0.0), NaN when either
+// operand is NaN.  F32 uses the one-instruction max.NaN / min.NaN (a canonical NaN);
+// F64, which has no such form, returns the NaN operand (the left one first).  Only
+// "is NaN" is part of the ABI's contract, not the payload.
 __device__ __forceinline__ float nan_max(float a, float b) {
-  const float m = fmaxf(a, b);
-  const float r = b != b ? b : m;
-  return a != a ? a : r;
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
 }
 __device__ __forceinline__ double nan_max(double a, double b) {
   const double m = fmax(a, b);
@@ -83,9 +85,9 @@ __device__ __forceinline__ double nan_max(double a, double b) {
   return a != a ? a : r;
 }
 __device__ __forceinline__ float nan_min(float a, float b) {
-  const float m = fminf(a, b);
-  const float r = b != b ? b : m;
-  return a != a ? a : r;
+  float r;
+  asm("min.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
 }
 __device__ __forceinline__ double nan_min(double a, double b) {
   const double m = fmin(a, b);

@@ -196,6 +196,49 @@ __device__ __forceinline__ void partial_offsets(long long o, const t4a_cuda_layo
   *dst_offset = off;
 }
 
+// Output decoders shared by the plane, wide and unit walks: (output, split) -> input
+// base and destination offset, for the by-value layouts (rank <= 8) and for the
+// general-rank `_any` layouts, whose arrays live in device memory (reference
+// reduce.cu:641-656, :726-745: the same walk over the operand's runtime rank).
+struct FastDecode {
+  const t4a_cuda_layout* dst;
+  const t4a_cuda_layout* in;
+  int axis;
+  bool partials;
+  __device__ __forceinline__ void operator()(long long o, long long s, long long* base, long long* off) const {
+    if (partials) {
+      partial_offsets(o, *dst, *in, axis, base, off);
+      *off += s * dst->strides[axis];
+    } else {
+      output_offsets(o, *dst, *in, base, off);
+    }
+  }
+};
+
+struct AnyDecode {
+  const t4a_cuda_layout_any* dst;
+  const t4a_cuda_layout_any* in;
+  int axis;
+  bool partials;
+  __device__ __forceinline__ void operator()(long long o, long long s, long long* in_base,
+                                             long long* dst_offset) const {
+    long long rest = o, base = in->offset, off = dst->offset;
+    for (int d = 0; d < dst->rank; ++d) {
+      if (partials && d == axis) {
+        off += s * dst->strides[d];
+        continue;
+      }
+      const long long e = dst->extents[d];
+      const long long c = rest % e;
+      rest /= e;
+      base += c * in->strides[d];
+      off += c * dst->strides[d];
+    }
+    *in_base = base;
+    *dst_offset = off;
+  }
+};
+
 // ---------------------------------------------------------------------------
 // Strided axis: one tile = 32 vector slots (V contiguous outputs each, slots run over
 // the unit-stride output run, then the outer outputs) x all W = 8*LPT lanes x one
@@ -484,18 +527,15 @@ __device__ __forceinline__ void strided_staged(const T* __restrict__ in, T* __re
 // One W-lane plane per cube (contiguous axis, and the general fallback).  Planes of
 // one block are consecutive cubes; every lane of a warp reaches the shuffles.
 // ---------------------------------------------------------------------------
-template <typename Op, typename T>
-__device__ __forceinline__ void plane_cubes(const T* in, T* dst, const t4a_cuda_layout& in_l,
-                                            const t4a_cuda_layout& dst_l, int axis, long long outputs,
-                                            long long splits, long long chunk, int W, bool partials,
-                                            bool allow_groups, Op op) {
+template <typename Op, typename T, typename Dec>
+__device__ __forceinline__ void plane_cubes_walk(const T* in, T* dst, const Dec& decode, long long astride,
+                                                 long long len, long long outputs, long long splits, long long chunk,
+                                                 int W, bool allow_groups, Op op) {
   const int tid = flat_tid();
   const int planes = block_threads() / W;
   const int plane = tid / W;
   const int lane = tid % W;
   const long long cubes = outputs * splits;
-  const long long len = in_l.extents[axis];
-  const long long astride = in_l.strides[axis];
   for (long long first = static_cast<long long>(blockIdx.x) * planes; first < cubes;
        first += static_cast<long long>(gridDim.x) * planes) {
     const long long cube = first + plane;
@@ -506,12 +546,7 @@ __device__ __forceinline__ void plane_cubes(const T* in, T* dst, const t4a_cuda_
       const long long o = cube / splits;
       const long long s = cube % splits;
       long long base;
-      if (partials) {
-        partial_offsets(o, dst_l, in_l, axis, &base, &dst_off);
-        dst_off += s * dst_l.strides[axis];
-      } else {
-        output_offsets(o, dst_l, in_l, &base, &dst_off);
-      }
+      decode(o, s, &base, &dst_off);
       const long long start = s * chunk;
       const long long end = s + 1 == splits ? len : start + chunk;
       acc = cube_lane<Op, T>(in, base, astride, start, end, W, lane, allow_groups, op);
@@ -519,6 +554,16 @@ __device__ __forceinline__ void plane_cubes(const T* in, T* dst, const t4a_cuda_
     acc = lane_tree(acc, W, op);
     if (valid && lane == 0) dst[dst_off] = acc;
   }
+}
+
+template <typename Op, typename T>
+__device__ __forceinline__ void plane_cubes(const T* in, T* dst, const t4a_cuda_layout& in_l,
+                                            const t4a_cuda_layout& dst_l, int axis, long long outputs,
+                                            long long splits, long long chunk, int W, bool partials,
+                                            bool allow_groups, Op op) {
+  const FastDecode decode{&dst_l, &in_l, axis, partials};
+  plane_cubes_walk<Op, T>(in, dst, decode, in_l.strides[axis], in_l.extents[axis], outputs, splits, chunk, W,
+                          allow_groups, op);
 }
 
 // ---------------------------------------------------------------------------
@@ -635,17 +680,14 @@ __device__ __forceinline__ void unit_warp_rows(const T* in, T* out, const t4a_cu
   }
 }
 
-template <typename Op, typename T>
-__device__ __forceinline__ void unit_generic(const T* in, T* out, const t4a_cuda_layout& out_l,
-                                             const t4a_cuda_layout& in_l, int axis, long long outputs,
-                                             Op op) {
-  const long long len = in_l.extents[axis];
-  const long long stride = in_l.strides[axis];
+template <typename Op, typename T, typename Dec>
+__device__ __forceinline__ void unit_walk(const T* in, T* out, const Dec& decode, long long len, long long stride,
+                                          long long outputs, Op op) {
   const long long threads = static_cast<long long>(gridDim.x) * block_threads();
   for (long long o = static_cast<long long>(blockIdx.x) * block_threads() + flat_tid(); o < outputs;
        o += threads) {
     long long base, off;
-    output_offsets(o, out_l, in_l, &base, &off);
+    decode(o, 0, &base, &off);
     T buf[8];
     T acc = op.seed(in[base]);
     long long i = 1;
@@ -660,24 +702,29 @@ __device__ __forceinline__ void unit_generic(const T* in, T* out, const t4a_cuda
   }
 }
 
+template <typename Op, typename T>
+__device__ __forceinline__ void unit_generic(const T* in, T* out, const t4a_cuda_layout& out_l,
+                                             const t4a_cuda_layout& in_l, int axis, long long outputs,
+                                             Op op) {
+  const FastDecode decode{&out_l, &in_l, axis, false};
+  unit_walk<Op, T>(in, out, decode, in_l.extents[axis], in_l.strides[axis], outputs, op);
+}
+
 // PLANE wider than a warp (the combine pass over many partials): one block per output;
 // blockDim.x lanes walk serially, warp trees meet in shared memory, so the result is
 // the balanced tree over all lanes.  Per-warp results: at most 16 warps of 16 bytes.
 __shared__ __align__(16) unsigned char t4a_warp_results[16 * 16];
 
-template <typename Op, typename T>
-__device__ __forceinline__ void wide_plane(const T* in, T* out, const t4a_cuda_layout& out_l,
-                                           const t4a_cuda_layout& in_l, int axis, long long outputs,
-                                           Op op) {
+template <typename Op, typename T, typename Dec>
+__device__ __forceinline__ void wide_walk(const T* in, T* out, const Dec& decode, long long len, long long stride,
+                                          long long outputs, Op op) {
   T* warp_results = reinterpret_cast<T*>(t4a_warp_results);
   const int W = blockDim.x;
   const int lane = threadIdx.x;
   const int warps = W / kWarp;
-  const long long len = in_l.extents[axis];
-  const long long stride = in_l.strides[axis];
   for (long long o = blockIdx.x; o < outputs; o += gridDim.x) {
     long long base, off;
-    output_offsets(o, out_l, in_l, &base, &off);
+    decode(o, 0, &base, &off);
     T acc = serial_walk<Op, T>(in, base, stride, 0, len, W, lane, op);
     acc = lane_tree(acc, kWarp, op);
     if ((lane & 31) == 0) warp_results[lane >> 5] = acc;
@@ -689,6 +736,14 @@ __device__ __forceinline__ void wide_plane(const T* in, T* out, const t4a_cuda_l
     }
     __syncthreads();
   }
+}
+
+template <typename Op, typename T>
+__device__ __forceinline__ void wide_plane(const T* in, T* out, const t4a_cuda_layout& out_l,
+                                           const t4a_cuda_layout& in_l, int axis, long long outputs,
+                                           Op op) {
+  const FastDecode decode{&out_l, &in_l, axis, false};
+  wide_walk<Op, T>(in, out, decode, in_l.extents[axis], in_l.strides[axis], outputs, op);
 }
 
 // ---------------------------------------------------------------------------
@@ -745,6 +800,45 @@ __device__ __forceinline__ void partials_abi_body(void* partials_p, const void* 
     return;
   }
   plane_cubes<Op, T>(in, partials, in_l, part_l, axis, outputs, splits, chunk, W, true, true, op);
+}
+
+// General-rank entries (reference reduce.cu:854-940): the same walks and trees as the
+// by-value entries (unit fold, W-lane planes, wider planes, split partials), with the
+// outputs decoded over the layouts' runtime rank.  Any launch geometry is correct: a
+// block of W = blockDim.x lanes (at most a warp: blockDim.y planes of W lanes; wider:
+// one output per block) walks outputs grid-stride.
+template <typename Op, typename T>
+__device__ __forceinline__ void reduce_any_body(void* out_p, const void* in_p, int strategy,
+                                                const t4a_cuda_layout_any& out_l, const t4a_cuda_layout_any& in_l,
+                                                int axis, long long outputs, Op op) {
+  if (axis < 0 || axis >= in_l.rank || outputs <= 0) return;
+  const T* in = static_cast<const T*>(in_p);
+  T* out = static_cast<T*>(out_p);
+  const AnyDecode decode{&out_l, &in_l, axis, false};
+  const long long len = in_l.extents[axis];
+  const long long stride = in_l.strides[axis];
+  if (strategy == T4A_CUDA_REDUCE_UNIT) {
+    unit_walk<Op, T>(in, out, decode, len, stride, outputs, op);
+    return;
+  }
+  const int W = blockDim.x;
+  if (W > kWarp) {
+    wide_walk<Op, T>(in, out, decode, len, stride, outputs, op);
+    return;
+  }
+  plane_cubes_walk<Op, T>(in, out, decode, stride, len, outputs, 1, len, W, false, op);
+}
+
+template <typename Op, typename T>
+__device__ __forceinline__ void partials_any_body(void* partials_p, const void* in_p,
+                                                  const t4a_cuda_layout_any& part_l,
+                                                  const t4a_cuda_layout_any& in_l, int axis, long long outputs,
+                                                  long long splits, long long chunk, Op op) {
+  if (axis < 0 || axis >= in_l.rank || outputs <= 0 || splits <= 0) return;
+  const int W = blockDim.x <= 32 ? static_cast<int>(blockDim.x) : kWarp;
+  const AnyDecode decode{&part_l, &in_l, axis, true};
+  plane_cubes_walk<Op, T>(static_cast<const T*>(in_p), static_cast<T*>(partials_p), decode, in_l.strides[axis],
+                          in_l.extents[axis], outputs, splits, chunk, W, true, op);
 }
 
 }  // namespace

@@ -94,6 +94,26 @@ bool dst_linear(const t4a_cuda_layout& l) {
   return true;
 }
 
+// General-rank twins: the same bodies as the exported `_any` symbols.
+template <typename Op, typename T>
+__global__ void __launch_bounds__(512) k_reduce_any(T* out, const T* in, int strategy, t4a_cuda_layout_any out_l,
+                                                    t4a_cuda_layout_any in_l, int axis, long long outputs) {
+  reduce_any_body<Op, T>(out, in, strategy, out_l, in_l, axis, outputs, Op());
+}
+template <typename Op, typename T>
+__global__ void __launch_bounds__(256) k_partials_any(T* partials, const T* in, t4a_cuda_layout_any part_l,
+                                                      t4a_cuda_layout_any in_l, int axis, long long outputs,
+                                                      long long splits, long long chunk) {
+  partials_any_body<Op, T>(partials, in, part_l, in_l, axis, outputs, splits, chunk, Op());
+}
+
+// Host checks of a general-rank layout that need no device access.
+int check_any(const t4a_cuda_layout_any& l) {
+  if (l.rank < 0 || l.reserved != 0) return T4A_ERR_RANK_OUT_OF_RANGE;
+  if (l.rank > 0 && (l.extents == nullptr || l.strides == nullptr)) return T4A_ERR_NULL_ARGUMENT;
+  return T4A_OK;
+}
+
 struct PassArgs {
   void* dst;
   const void* in;
@@ -247,6 +267,74 @@ int t4a_launch_reduce_partials(const t4a_launch* launch, void* stream, void* par
                                int axis, long long output_len, long long splits, long long chunk_len) {
   PassArgs a{partials, in, partials_layout, in_layout, axis, output_len, splits, chunk_len, true};
   return run_pass(launch, stream, dtype, op, a);
+}
+
+int t4a_reduce_any_geometry(int strategy, unsigned w, long long output_len, long long splits, t4a_launch* launch) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  if (output_len < 0 || splits < 1) return T4A_ERR_NEGATIVE_COUNT;
+  if (strategy != T4A_CUDA_REDUCE_UNIT && strategy != T4A_CUDA_REDUCE_PLANE) return T4A_ERR_UNSUPPORTED_OP;
+  const bool narrow = w == 8 || w == 16 || w == 32;
+  const bool wide = w == 64 || w == 128 || w == 256 || w == 512;
+  if (!narrow && !(wide && strategy == T4A_CUDA_REDUCE_PLANE && splits == 1)) return T4A_ERR_INVALID_PLANE_WIDTH;
+  const unsigned long long cubes = static_cast<unsigned long long>(output_len) * static_cast<unsigned long long>(splits);
+  if (cubes == 0) {
+    *launch = plan::empty_launch();
+    return T4A_OK;
+  }
+  const unsigned long long cap = 148ull * 64;
+  unsigned long long grid;
+  if (strategy == T4A_CUDA_REDUCE_UNIT) {
+    grid = plan::ceil_div(cubes, kTileThreads);
+    *launch = plan::make_launch(grid < cap ? grid : cap, kTileThreads, 1, 0, 0);
+  } else if (wide) {
+    *launch = plan::make_launch(cubes < cap ? cubes : cap, w, 1, 0, 0);
+  } else {
+    grid = plan::ceil_div(cubes, kTileThreads / w);
+    *launch = plan::make_launch(grid < cap ? grid : cap, w, kTileThreads / w, 0, 0);
+  }
+  return T4A_OK;
+}
+
+int t4a_launch_reduce_any(const t4a_launch* launch, void* stream, void* out, const void* in, int dtype, int op,
+                          int strategy, t4a_cuda_layout_any out_layout, t4a_cuda_layout_any in_layout, int axis,
+                          long long output_len) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  T4A_TRY(check_any(out_layout));
+  T4A_TRY(check_any(in_layout));
+  if (axis < 0 || axis >= in_layout.rank || out_layout.rank != in_layout.rank) return T4A_ERR_INVALID_AXIS;
+  if (launch->grid[0] == 0 || launch->grid[1] == 0 || launch->grid[2] == 0 || output_len <= 0) return T4A_OK;
+  if (out == nullptr || in == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  const dim3 grid(launch->grid[0], launch->grid[1], launch->grid[2]);
+  const dim3 block(launch->block[0], launch->block[1], launch->block[2]);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+#define T4A_CALL(OP, T)                                                                                   \
+  k_reduce_any<OP, T><<<grid, block, 0, s>>>(static_cast<T*>(out), static_cast<const T*>(in), strategy, \
+                                             out_layout, in_layout, axis, output_len)
+  T4A_REDUCE_SWITCH(op, dtype, T4A_CALL)
+#undef T4A_CALL
+  return runtime::check_launch();
+}
+
+int t4a_launch_reduce_partials_any(const t4a_launch* launch, void* stream, void* partials, const void* in,
+                                   int dtype, int op, t4a_cuda_layout_any partials_layout,
+                                   t4a_cuda_layout_any in_layout, int axis, long long output_len, long long splits,
+                                   long long chunk_len) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  T4A_TRY(check_any(partials_layout));
+  T4A_TRY(check_any(in_layout));
+  if (axis < 0 || axis >= in_layout.rank || partials_layout.rank != in_layout.rank) return T4A_ERR_INVALID_AXIS;
+  if (splits < 1 || chunk_len < 1) return T4A_ERR_INVALID_SPLIT;
+  if (launch->grid[0] == 0 || launch->grid[1] == 0 || launch->grid[2] == 0 || output_len <= 0) return T4A_OK;
+  if (partials == nullptr || in == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  const dim3 grid(launch->grid[0], launch->grid[1], launch->grid[2]);
+  const dim3 block(launch->block[0], launch->block[1], launch->block[2]);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+#define T4A_CALL(OP, T)                                                                                          \
+  k_partials_any<OP, T><<<grid, block, 0, s>>>(static_cast<T*>(partials), static_cast<const T*>(in),          \
+                                               partials_layout, in_layout, axis, output_len, splits, chunk_len)
+  T4A_REDUCE_SWITCH(op, dtype, T4A_CALL)
+#undef T4A_CALL
+  return runtime::check_launch();
 }
 
 int t4a_reduce_workspace_bytes(int dtype, int op, const t4a_cuda_layout* out, long long out_len,

@@ -345,6 +345,43 @@ def _ptr(t):
     return ctypes.c_void_p(t.data_ptr())
 
 
+def layout_any(extents, strides=None, offset=0, device="cuda"):
+    """(t4a_cuda_layout_any, keep-alive tensor) with the arrays on `device`; strides
+    default to compact (axis 0 fastest)."""
+    import torch
+    extents = list(extents)
+    if strides is None:
+        strides, acc = [], 1
+        for e in extents:
+            strides.append(acc)
+            acc *= e
+    arrays = torch.tensor(list(extents) + list(strides), dtype=torch.int64, device=device)
+    rank = len(extents)
+    lay = abi.LayoutAny(rank, 0, offset, ctypes.c_void_p(arrays.data_ptr()),
+                        ctypes.c_void_p(arrays.data_ptr() + 8 * rank))
+    return lay, arrays
+
+
+def reduce_any_geometry(strategy, plane_width, output_len, splits=1):
+    launch = Launch()
+    check(lib().t4a_reduce_any_geometry(strategy, plane_width, output_len, splits, ctypes.byref(launch)),
+          "reduce_any_geometry")
+    return launch
+
+
+def launch_reduce_any(launch, stream, out_ptr, in_ptr, dtype, op, strategy, out_layout, in_layout, axis, output_len):
+    check(lib().t4a_launch_reduce_any(ctypes.byref(launch), stream, out_ptr, in_ptr, dtype, op, strategy, out_layout,
+                                      in_layout, axis, ctypes.c_longlong(output_len)), "launch_reduce_any")
+
+
+def launch_reduce_partials_any(launch, stream, part_ptr, in_ptr, dtype, op, part_layout, in_layout, axis, output_len,
+                               splits, chunk):
+    check(lib().t4a_launch_reduce_partials_any(ctypes.byref(launch), stream, part_ptr, in_ptr, dtype, op, part_layout,
+                                               in_layout, axis, ctypes.c_longlong(output_len),
+                                               ctypes.c_longlong(splits), ctypes.c_longlong(chunk)),
+          "launch_reduce_partials_any")
+
+
 def gather_rows(table, indices, out=None, stream=None):
     """out[i, :] = table[clamp(indices[i]), :] for a row-major CUDA table [rows, cols]
     (the XLA gather of whole rows; starts clamp as the reference's)."""

@@ -40,6 +40,12 @@ class Layout(ctypes.Structure):
         return f"Layout(extents={self.extents_list()}, strides={self.strides_list()}, offset={self.offset})"
 
 
+class LayoutAny(ctypes.Structure):
+    """t4a_cuda_layout_any: extents and strides in device memory (any rank)."""
+    _fields_ = [("rank", ctypes.c_int), ("reserved", ctypes.c_int), ("offset", ctypes.c_longlong),
+                ("extents", ctypes.c_void_p), ("strides", ctypes.c_void_p)]
+
+
 class AxisValues(ctypes.Structure):
     _fields_ = [("rank", ctypes.c_int), ("reserved", ctypes.c_int), ("values", _I64x8)]
 

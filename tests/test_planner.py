@@ -251,3 +251,34 @@ def test_rrqr_driver_rejects_bad_arguments_before_launching():
     assert rrqr_status(abi.F64, good, 600 * 40, 40, work=0) == 66            # NULL arguments
     assert rrqr_status(abi.F64, good, 600 * 40, 40, piv=0) == 66
     assert rrqr_status(abi.F64, abi.layout([0, 40]), 0, 0) == 0              # nothing to do
+
+
+def test_reduce_any_geometry_and_host_checks():
+    g = t4.reduce_any_geometry(abi.UNIT, 32, 1000)
+    assert (g.block[0], g.grid[0]) == (256, 4)
+    g = t4.reduce_any_geometry(abi.PLANE, 16, 100, 3)
+    assert (g.block[0], g.block[1], g.grid[0]) == (16, 16, 19)
+    g = t4.reduce_any_geometry(abi.PLANE, 128, 70)
+    assert (g.block[0], g.grid[0]) == (128, 70)
+    assert t4.reduce_any_geometry(abi.PLANE, 32, 0).grid[0] == 0
+    for args, code in [((abi.PLANE, 128, 70, 2), 22), ((abi.PLANE, 24, 10), 22), ((abi.UNIT, 32, -1), 4),
+                       ((7, 32, 10), 25)]:
+        with pytest.raises(t4.T4AError) as err:
+            t4.reduce_any_geometry(*args)
+        assert err.value.status == code, args
+    # host-side refusals of the general-rank launchers (no device access on these paths)
+    launch = t4.reduce_any_geometry(abi.UNIT, 32, 10)
+    good = abi.LayoutAny(3, 0, 0, ctypes.c_void_p(0x1000), ctypes.c_void_p(0x2000))
+    bad_reserved = abi.LayoutAny(3, 1, 0, ctypes.c_void_p(0x1000), ctypes.c_void_p(0x2000))
+    null_arrays = abi.LayoutAny(3, 0, 0, None, None)
+    lib = t4.lib()
+    p = ctypes.c_void_p(0x3000)
+    assert lib.t4a_launch_reduce_any(ctypes.byref(launch), None, p, p, abi.F32, abi.SUM, abi.UNIT, good,
+                                     bad_reserved, 0, ctypes.c_longlong(10)) == 1
+    assert lib.t4a_launch_reduce_any(ctypes.byref(launch), None, p, p, abi.F32, abi.SUM, abi.UNIT, null_arrays,
+                                     good, 0, ctypes.c_longlong(10)) == 66
+    assert lib.t4a_launch_reduce_any(ctypes.byref(launch), None, p, p, abi.F32, abi.SUM, abi.UNIT, good, good, 3,
+                                     ctypes.c_longlong(10)) == 13
+    assert lib.t4a_launch_reduce_partials_any(ctypes.byref(launch), None, p, p, abi.F32, abi.SUM, good, good, 0,
+                                              ctypes.c_longlong(10), ctypes.c_longlong(0),
+                                              ctypes.c_longlong(1)) == 23

@@ -84,7 +84,34 @@ def run_case(route, case, module=None):
     part_l = t4.reduction_partials_layout(in_l, axis, plan.split.splits)
     part = device_bytes(part_l.count() * esize)
     stream = torch.cuda.current_stream().cuda_stream
-    if route == "launcher":
+    if route.startswith("any"):
+        # The general-rank twins, with every layout padded to rank 12 by trailing
+        # extent-1 axes (the flat output order is unchanged).
+        pad = 12 - in_l.rank
+
+        def padded(lay):
+            return t4.layout_any(lay.extents_list() + [1] * pad, lay.strides_list() + [0] * pad, lay.offset)
+        (in_any, k1), (part_any, k2), (out_any, k3) = padded(in_l), padded(part_l), padded(out_l)
+        g1 = t4.reduce_any_geometry(abi.PLANE, w, outputs, plan.split.splits)
+        width = plan.pass2.block[0] if plan.pass2.block[0] > 32 else w
+        g2 = t4.reduce_any_geometry(plan.combine_strategy, width, outputs)
+        if route == "any-launcher":
+            t4.launch_reduce_partials_any(g1, ctypes.c_void_p(stream), ctypes.c_void_p(part.data_ptr()),
+                                          ctypes.c_void_p(src.data_ptr()), dtype, op, part_any, in_any, axis, outputs,
+                                          plan.split.splits, plan.split.chunk_len)
+            t4.launch_reduce_any(g2, ctypes.c_void_p(stream), ctypes.c_void_p(out.data_ptr()),
+                                 ctypes.c_void_p(part.data_ptr()), dtype, plan.combine_op, plan.combine_strategy,
+                                 out_any, part_any, axis, outputs)
+        else:
+            module.launch("t4a_cuda_reduce_partials_any", tuple(g1.grid), tuple(g1.block), 0, launch_args(
+                ("p", part.data_ptr()), ("p", src.data_ptr()), ("i", dtype), ("i", op), ("s", part_any),
+                ("s", in_any), ("i", axis), ("l", outputs), ("l", plan.split.splits), ("l", plan.split.chunk_len)))
+            module.launch("t4a_cuda_reduce_any", tuple(g2.grid), tuple(g2.block), 0, launch_args(
+                ("p", out.data_ptr()), ("p", part.data_ptr()), ("i", dtype), ("i", plan.combine_op),
+                ("i", plan.combine_strategy), ("s", out_any), ("s", part_any), ("i", axis), ("l", outputs)))
+        torch.cuda.synchronize()
+        del k1, k2, k3
+    elif route == "launcher":
         t4.check(t4.lib().t4a_launch_reduce_partials(
             ctypes.byref(plan.pass1), ctypes.c_void_p(stream), ctypes.c_void_p(part.data_ptr()),
             ctypes.c_void_p(src.data_ptr()), dtype, op, part_l, in_l, axis, outputs, plan.split.splits,
@@ -112,14 +139,14 @@ def run_case(route, case, module=None):
     return take(out, outputs * esize), take(part, part_l.count() * esize), ftype
 
 
-ROUTES = ["launcher", "module", "module-refgeom", "reference"]
+ROUTES = ["launcher", "module", "module-refgeom", "reference", "any-launcher", "any-module"]
 
 
 @pytest.mark.parametrize("route", ROUTES)
 @pytest.mark.parametrize("shape", list(ri.SHAPES))
 def test_golden_split_reductions(cuda, route, shape):
     module = None
-    if route in ("module", "module-refgeom"):
+    if route in ("module", "module-refgeom", "any-module"):
         module = Module(OUR_CUBIN)
     elif route == "reference":
         if not os.path.exists(REF_CUBIN):
