@@ -241,6 +241,28 @@ int t4a_copy_strided(void* stream, int dtype, void* dst, const t4a_cuda_layout* 
 /* (CGatherPlan / CScatterPlan, src/lib.rs:4192-4303).                         */
 /* ------------------------------------------------------------------------- */
 
+/* General-rank movement, the `_any` twins (reference cuda/src/movement.cu:612-665;
+ * module symbols t4a_cuda_{fill_zero_view,materialize_strided,contiguous_to_view,
+ * strided_to_strided,broadcast_in_dim}_any in movement.cubin): element-wise walks over
+ * layouts whose extents and strides (and broadcast dimensions) are in device memory,
+ * so any rank works.  The launchers take the kernels' argument lists; any geometry is
+ * correct, t4a_movement_any_geometry gives the one they are tuned for.  The host checks
+ * what it can without device access (rank and reserved fields, NULL arrays, matching
+ * ranks); extents and strides are the caller's, as in the reference. */
+int t4a_movement_any_geometry(long long len, t4a_launch* launch);
+int t4a_launch_fill_zero_view_any(const t4a_launch* launch, void* stream, void* out, int dtype,
+                                  t4a_cuda_layout_any layout, long long len);
+int t4a_launch_materialize_strided_any(const t4a_launch* launch, void* stream, void* dst, const void* src, int dtype,
+                                       t4a_cuda_layout_any src_layout, long long len);
+int t4a_launch_contiguous_to_view_any(const t4a_launch* launch, void* stream, void* dst, const void* src, int dtype,
+                                      t4a_cuda_layout_any dst_layout, long long len);
+int t4a_launch_strided_to_strided_any(const t4a_launch* launch, void* stream, void* dst, const void* src, int dtype,
+                                      t4a_cuda_layout_any src_layout, t4a_cuda_layout_any dst_layout,
+                                      long long len);
+int t4a_launch_broadcast_in_dim_any(const t4a_launch* launch, void* stream, void* out, const void* in, int dtype,
+                                    t4a_cuda_layout_any out_layout, t4a_cuda_layout_any in_layout,
+                                    t4a_cuda_axis_values_any dims, long long out_len);
+
 /* plan_gather (src/lib.rs:2867): validates the maps and the derived output extents;
  * *output_len receives the output element count the launch expects. */
 int t4a_plan_gather(int dtype, int index_dtype, const t4a_cuda_layout* out, long long out_len,

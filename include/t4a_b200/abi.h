@@ -125,9 +125,17 @@ typedef struct {
   const long long* strides;  /* rank values, device memory */
 } t4a_cuda_layout_any;
 
+/* Per-axis values of the `_any` entries (broadcast dimensions), in device memory. */
+typedef struct {
+  int rank;
+  int reserved;  /* must be 0 */
+  const long long* values;  /* rank values, device memory */
+} t4a_cuda_axis_values_any;
+
 #ifdef __cplusplus
 }  /* extern "C" */
 
+static_assert(sizeof(t4a_cuda_axis_values_any) == 16, "t4a_cuda_axis_values_any size");
 static_assert(sizeof(t4a_cuda_layout_any) == 32, "t4a_cuda_layout_any size");
 static_assert(alignof(t4a_cuda_layout_any) == 8, "t4a_cuda_layout_any alignment");
 static_assert(__builtin_offsetof(t4a_cuda_layout_any, extents) == 16, "layout_any.extents");

@@ -168,3 +168,45 @@ extern "C" __global__ void __launch_bounds__(256) t4a_cuda_fill_zero_view(void* 
     default: break;
   }
 }
+
+// General-rank twins (reference cuda/src/movement.cu:612-665): element-wise walks over
+// layouts whose arrays live in device memory (movement_any.cuh).
+#include "movement_any.cuh"
+
+extern "C" __global__ void __launch_bounds__(256) t4a_cuda_fill_zero_view_any(void* out, int dtype,
+                                                                            t4a_cuda_layout_any layout,
+                                                                            long long len) {
+#define T4A_CALL(E) t4a::any::fill_zero_view<E>(out, layout, len)
+  T4A_ANY_ESIZE_SWITCH(dtype, T4A_CALL)
+#undef T4A_CALL
+}
+
+extern "C" __global__ void __launch_bounds__(256) t4a_cuda_materialize_strided_any(
+    void* dst, const void* src, int dtype, t4a_cuda_layout_any src_layout, long long len) {
+#define T4A_CALL(E) t4a::any::materialize<E>(dst, src, src_layout, len)
+  T4A_ANY_ESIZE_SWITCH(dtype, T4A_CALL)
+#undef T4A_CALL
+}
+
+extern "C" __global__ void __launch_bounds__(256) t4a_cuda_contiguous_to_view_any(
+    void* dst, const void* src, int dtype, t4a_cuda_layout_any dst_layout, long long len) {
+#define T4A_CALL(E) t4a::any::to_view<E>(dst, src, dst_layout, len)
+  T4A_ANY_ESIZE_SWITCH(dtype, T4A_CALL)
+#undef T4A_CALL
+}
+
+extern "C" __global__ void __launch_bounds__(256) t4a_cuda_strided_to_strided_any(
+    void* dst, const void* src, int dtype, t4a_cuda_layout_any src_layout, t4a_cuda_layout_any dst_layout,
+    long long len) {
+#define T4A_CALL(E) t4a::any::strided_copy<E>(dst, src, src_layout, dst_layout, len)
+  T4A_ANY_ESIZE_SWITCH(dtype, T4A_CALL)
+#undef T4A_CALL
+}
+
+extern "C" __global__ void __launch_bounds__(256) t4a_cuda_broadcast_in_dim_any(
+    void* out, const void* in, int dtype, t4a_cuda_layout_any out_layout, t4a_cuda_layout_any in_layout,
+    t4a_cuda_axis_values_any dims, long long out_len) {
+#define T4A_CALL(E) t4a::any::broadcast<E>(out, in, out_layout, in_layout, dims, out_len)
+  T4A_ANY_ESIZE_SWITCH(dtype, T4A_CALL)
+#undef T4A_CALL
+}

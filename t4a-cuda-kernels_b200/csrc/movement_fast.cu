@@ -3,6 +3,7 @@
 // the host and launch one kernel per path, compiled for that path alone.
 #include <cuda_runtime.h>
 
+#include "movement_any.cuh"
 #include "movement_core.cuh"
 #include "plan_common.h"
 #include "runtime.h"
@@ -185,6 +186,50 @@ PermPlan broadcast_plan(int dtype, const t4a_cuda_layout& out, const t4a_cuda_la
 }
 
 int check_dtype_move(int dtype) { return host_esize(dtype) ? T4A_OK : T4A_ERR_UNSUPPORTED_DTYPE; }
+
+// General-rank twins: the same bodies as the exported `_any` symbols.
+template <int E>
+__global__ void __launch_bounds__(256) k_zero_any(void* out, t4a_cuda_layout_any l, long long len) {
+  any::fill_zero_view<E>(out, l, len);
+}
+template <int E>
+__global__ void __launch_bounds__(256) k_materialize_any(void* dst, const void* src, t4a_cuda_layout_any l,
+                                                         long long len) {
+  any::materialize<E>(dst, src, l, len);
+}
+template <int E>
+__global__ void __launch_bounds__(256) k_to_view_any(void* dst, const void* src, t4a_cuda_layout_any l, long long len) {
+  any::to_view<E>(dst, src, l, len);
+}
+template <int E>
+__global__ void __launch_bounds__(256) k_strided_any(void* dst, const void* src, t4a_cuda_layout_any sl,
+                                                     t4a_cuda_layout_any dl, long long len) {
+  any::strided_copy<E>(dst, src, sl, dl, len);
+}
+template <int E>
+__global__ void __launch_bounds__(256) k_broadcast_any(void* out, const void* in, t4a_cuda_layout_any ol,
+                                                       t4a_cuda_layout_any il, t4a_cuda_axis_values_any dims,
+                                                       long long len) {
+  any::broadcast<E>(out, in, ol, il, dims, len);
+}
+
+// Host checks of a general-rank layout that need no device access.
+int check_layout_any(const t4a_cuda_layout_any& l) {
+  if (l.rank < 0 || l.reserved != 0) return T4A_ERR_RANK_OUT_OF_RANGE;
+  if (l.rank > 0 && (l.extents == nullptr || l.strides == nullptr)) return T4A_ERR_NULL_ARGUMENT;
+  return T4A_OK;
+}
+
+// Common prologue of the `_any` launchers: launch shape, count and dtype.
+int any_prologue(const t4a_launch* launch, long long len, int dtype, dim3* grid, dim3* block, bool* empty) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  if (len < 0) return T4A_ERR_NEGATIVE_COUNT;
+  if (host_esize(dtype) == 0) return T4A_ERR_UNSUPPORTED_DTYPE;
+  *empty = len == 0 || launch->grid[0] == 0 || launch->block[0] == 0;
+  *grid = dim3(launch->grid[0], launch->grid[1] ? launch->grid[1] : 1, launch->grid[2] ? launch->grid[2] : 1);
+  *block = dim3(launch->block[0], launch->block[1] ? launch->block[1] : 1, launch->block[2] ? launch->block[2] : 1);
+  return T4A_OK;
+}
 
 }  // namespace
 }  // namespace t4a
@@ -412,6 +457,101 @@ int t4a_launch_fill_zero_view(const t4a_launch* launch, void* stream, void* out,
   }
   return runtime::check_launch();
 }
+
+int t4a_movement_any_geometry(long long len, t4a_launch* launch) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  if (len < 0) return T4A_ERR_NEGATIVE_COUNT;
+  if (len == 0) {
+    *launch = plan::empty_launch();
+    return T4A_OK;
+  }
+  const unsigned long long grid = plan::ceil_div(static_cast<unsigned long long>(len), 256);
+  const unsigned long long cap = 148ull * 64;
+  *launch = plan::make_launch(grid < cap ? grid : cap, 256, 1, 0, 0);
+  return T4A_OK;
+}
+
+#define T4A_ANY_LAUNCH(KERNEL, ...)                                               \
+  switch (host_esize(dtype)) {                                                    \
+    case 1: KERNEL<1><<<grid, block, 0, s>>>(__VA_ARGS__); break;                 \
+    case 4: KERNEL<4><<<grid, block, 0, s>>>(__VA_ARGS__); break;                 \
+    case 8: KERNEL<8><<<grid, block, 0, s>>>(__VA_ARGS__); break;                 \
+    case 16: KERNEL<16><<<grid, block, 0, s>>>(__VA_ARGS__); break;               \
+    default: return T4A_ERR_UNSUPPORTED_DTYPE;                                    \
+  }
+
+int t4a_launch_fill_zero_view_any(const t4a_launch* launch, void* stream, void* out, int dtype,
+                                  t4a_cuda_layout_any layout, long long len) {
+  dim3 grid, block;
+  bool empty;
+  T4A_TRY(any_prologue(launch, len, dtype, &grid, &block, &empty));
+  T4A_TRY(check_layout_any(layout));
+  if (empty) return T4A_OK;
+  if (out == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  T4A_ANY_LAUNCH(k_zero_any, out, layout, len)
+  return runtime::check_launch();
+}
+
+int t4a_launch_materialize_strided_any(const t4a_launch* launch, void* stream, void* dst, const void* src, int dtype,
+                                       t4a_cuda_layout_any src_layout, long long len) {
+  dim3 grid, block;
+  bool empty;
+  T4A_TRY(any_prologue(launch, len, dtype, &grid, &block, &empty));
+  T4A_TRY(check_layout_any(src_layout));
+  if (empty) return T4A_OK;
+  if (dst == nullptr || src == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  T4A_ANY_LAUNCH(k_materialize_any, dst, src, src_layout, len)
+  return runtime::check_launch();
+}
+
+int t4a_launch_contiguous_to_view_any(const t4a_launch* launch, void* stream, void* dst, const void* src, int dtype,
+                                      t4a_cuda_layout_any dst_layout, long long len) {
+  dim3 grid, block;
+  bool empty;
+  T4A_TRY(any_prologue(launch, len, dtype, &grid, &block, &empty));
+  T4A_TRY(check_layout_any(dst_layout));
+  if (empty) return T4A_OK;
+  if (dst == nullptr || src == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  T4A_ANY_LAUNCH(k_to_view_any, dst, src, dst_layout, len)
+  return runtime::check_launch();
+}
+
+int t4a_launch_strided_to_strided_any(const t4a_launch* launch, void* stream, void* dst, const void* src, int dtype,
+                                      t4a_cuda_layout_any src_layout, t4a_cuda_layout_any dst_layout,
+                                      long long len) {
+  dim3 grid, block;
+  bool empty;
+  T4A_TRY(any_prologue(launch, len, dtype, &grid, &block, &empty));
+  T4A_TRY(check_layout_any(src_layout));
+  T4A_TRY(check_layout_any(dst_layout));
+  if (src_layout.rank != dst_layout.rank) return T4A_ERR_RANK_LENGTH;
+  if (empty) return T4A_OK;
+  if (dst == nullptr || src == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  T4A_ANY_LAUNCH(k_strided_any, dst, src, src_layout, dst_layout, len)
+  return runtime::check_launch();
+}
+
+int t4a_launch_broadcast_in_dim_any(const t4a_launch* launch, void* stream, void* out, const void* in, int dtype,
+                                    t4a_cuda_layout_any out_layout, t4a_cuda_layout_any in_layout,
+                                    t4a_cuda_axis_values_any dims, long long out_len) {
+  dim3 grid, block;
+  bool empty;
+  T4A_TRY(any_prologue(launch, out_len, dtype, &grid, &block, &empty));
+  T4A_TRY(check_layout_any(out_layout));
+  T4A_TRY(check_layout_any(in_layout));
+  if (dims.rank != in_layout.rank || dims.reserved != 0) return T4A_ERR_RANK_LENGTH;
+  if (dims.rank > 0 && dims.values == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  if (empty) return T4A_OK;
+  if (out == nullptr || in == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  T4A_ANY_LAUNCH(k_broadcast_any, out, in, out_layout, in_layout, dims, out_len)
+  return runtime::check_launch();
+}
+#undef T4A_ANY_LAUNCH
 
 // One call: validate and copy between two layouts of the same extents.
 int t4a_copy_strided(void* stream, int dtype, void* dst, const t4a_cuda_layout* dst_layout, long long dst_len,

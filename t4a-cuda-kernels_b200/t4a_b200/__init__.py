@@ -362,6 +362,24 @@ def layout_any(extents, strides=None, offset=0, device="cuda"):
     return lay, arrays
 
 
+def axis_values_any(values, device="cuda"):
+    """(t4a_cuda_axis_values_any, keep-alive tensor) with the values on `device`."""
+    import torch
+    arr = torch.tensor(list(values) or [0], dtype=torch.int64, device=device)
+    return abi.AxisValuesAny(len(values), 0, ctypes.c_void_p(arr.data_ptr())), arr
+
+
+def movement_any_geometry(length):
+    launch = Launch()
+    check(lib().t4a_movement_any_geometry(ctypes.c_longlong(length), ctypes.byref(launch)), "movement_any_geometry")
+    return launch
+
+
+def launch_movement_any(name, launch, stream, *args):
+    """t4a_launch_<name>_any(&launch, stream, *args): the kernel's own argument list."""
+    check(getattr(lib(), "t4a_launch_" + name + "_any")(ctypes.byref(launch), stream, *args), "launch_" + name + "_any")
+
+
 def reduce_any_geometry(strategy, plane_width, output_len, splits=1):
     launch = Launch()
     check(lib().t4a_reduce_any_geometry(strategy, plane_width, output_len, splits, ctypes.byref(launch)),

@@ -46,6 +46,11 @@ class LayoutAny(ctypes.Structure):
                 ("extents", ctypes.c_void_p), ("strides", ctypes.c_void_p)]
 
 
+class AxisValuesAny(ctypes.Structure):
+    """t4a_cuda_axis_values_any: values in device memory (any rank)."""
+    _fields_ = [("rank", ctypes.c_int), ("reserved", ctypes.c_int), ("values", ctypes.c_void_p)]
+
+
 class AxisValues(ctypes.Structure):
     _fields_ = [("rank", ctypes.c_int), ("reserved", ctypes.c_int), ("values", _I64x8)]
 

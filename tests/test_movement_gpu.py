@@ -257,3 +257,130 @@ def test_copy_exact_view_copies_and_fills(cuda):
     idx = (999 * 2000 + 2 * np.arange(1000)[:, None] - 2000 * np.arange(1000)[None, :]).reshape(-1)
     mask[idx] = True
     assert (got[mask] == 0).all() and (got[~mask] == 0xCDCDCDCD).all()
+
+
+# ---- general-rank twins (`_any`) ----------------------------------------------
+
+ANY_EXTENTS = [2, 3, 2, 2, 1, 2, 3, 2, 2, 2]  # rank 10, 576 elements
+
+
+def random_view(rng, extents):
+    """Strides and offset of a bijective view of a compact buffer: a random storage
+    order of the axes, one axis reversed (its stride negated, the offset rebased)."""
+    strides, acc = [0] * len(extents), 1
+    for d in rng.permutation(len(extents)):
+        strides[d] = acc
+        acc *= extents[d]
+    offset = 0
+    flip = int(rng.integers(len(extents)))
+    if extents[flip] > 1:
+        offset = (extents[flip] - 1) * strides[flip]
+        strides[flip] = -strides[flip]
+    return strides, offset, acc
+
+
+def view_index(extents, strides, offset):
+    """Element index of flat position f (axis 0 fastest) for every f."""
+    n = int(np.prod(extents))
+    f = np.arange(n, dtype=np.int64)
+    idx = np.full(n, offset, dtype=np.int64)
+    for e, s in zip(extents, strides):
+        idx += (f % e) * s
+        f //= e
+    return idx
+
+
+def any_launch(route, name, n, args):
+    """One `_any` entry through the library launcher, or the module symbol under this
+    library's geometry ("module") or the reference's ceil(n/256) x 256 ("refgeom")."""
+    import torch
+    if route == "launcher":
+        t4.launch_movement_any(name, t4.movement_any_geometry(n), t4.stream_handle(), *args)
+    else:
+        if route == "module":
+            g = t4.movement_any_geometry(n)
+            geom = (tuple(g.grid), tuple(g.block), 0)
+        else:
+            geom = ((max(1, (n + 255) // 256),), (256,), 0)
+        Module(OUR_CUBIN).launch("t4a_cuda_" + name + "_any", *geom, args)
+    torch.cuda.synchronize()
+
+
+ANY_ROUTES = ["launcher", "module", "refgeom"]
+
+
+@pytest.mark.parametrize("route", ANY_ROUTES)
+@pytest.mark.parametrize("dtype", [abi.F32, abi.C64, abi.BOOL])
+def test_any_twins_of_the_view_copies(cuda, route, dtype):
+    """materialize_strided, contiguous_to_view, strided_to_strided and fill_zero_view
+    over rank-10 layouts (random storage orders, a reversed axis, offsets), against the
+    index arithmetic, with sentinel-guarded destinations."""
+    es = ESIZE[dtype]
+    rng = np.random.default_rng(int(dtype) * 7 + ANY_ROUTES.index(route))
+    ext = ANY_EXTENTS
+    n = int(np.prod(ext))
+    s_str, s_off, total = random_view(rng, ext)
+    d_str, d_off, _ = random_view(rng, ext)
+    s_any, k1 = t4.layout_any(ext, s_str, s_off)
+    d_any, k2 = t4.layout_any(ext, d_str, d_off)
+    src = rng.integers(0, 256, size=total * es, dtype=np.uint8)
+    src_e = src.reshape(total, es)
+    s_idx, d_idx = view_index(ext, s_str, s_off), view_index(ext, d_str, d_off)
+    vp = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    # materialize_strided: dst[f] = src[view(f)]
+    d_src, d_dst = dev(src), sentinel(n * es)
+    any_launch(route, "materialize_strided", n, [vp(d_dst), vp(d_src), ctypes.c_int(dtype), s_any, ctypes.c_longlong(n)])
+    assert np.array_equal(take(d_dst, n * es).reshape(n, es), src_e[s_idx])
+    # contiguous_to_view: dst[view(f)] = src[f]
+    d_dst = sentinel(total * es)
+    any_launch(route, "contiguous_to_view", n, [vp(d_dst), vp(d_src), ctypes.c_int(dtype), d_any, ctypes.c_longlong(n)])
+    want = np.full((total, es), SENTINEL, dtype=np.uint8)
+    want[d_idx] = src_e[:n]
+    assert np.array_equal(take(d_dst, total * es).reshape(total, es), want)
+    # strided_to_strided: dst[dst_view(f)] = src[src_view(f)]
+    d_dst = sentinel(total * es)
+    any_launch(route, "strided_to_strided", n, [vp(d_dst), vp(d_src), ctypes.c_int(dtype), s_any, d_any,
+                                                ctypes.c_longlong(n)])
+    want = np.full((total, es), SENTINEL, dtype=np.uint8)
+    want[d_idx] = src_e[s_idx]
+    assert np.array_equal(take(d_dst, total * es).reshape(total, es), want)
+    # fill_zero_view: zeros exactly at the view
+    d_dst = sentinel(total * es)
+    any_launch(route, "fill_zero_view", n, [vp(d_dst), ctypes.c_int(dtype), d_any, ctypes.c_longlong(n)])
+    want = np.full((total, es), SENTINEL, dtype=np.uint8)
+    want[d_idx] = 0
+    assert np.array_equal(take(d_dst, total * es).reshape(total, es), want)
+    del k1, k2
+
+
+@pytest.mark.parametrize("route", ANY_ROUTES)
+@pytest.mark.parametrize("dtype", [abi.F64, abi.C64])
+def test_any_twin_of_broadcast_in_dim(cuda, route, dtype):
+    """broadcast_in_dim into a rank-10 compact destination from a rank-3 strided input
+    mapped to destination axes (1, 5, 8), one of them broadcast (input extent 1)."""
+    es = ESIZE[dtype]
+    rng = np.random.default_rng(int(dtype) + 31 * ANY_ROUTES.index(route))
+    out_ext = ANY_EXTENTS
+    n = int(np.prod(out_ext))
+    dims = [1, 5, 8]
+    in_ext = [out_ext[1], 1, out_ext[8]]
+    in_str, in_off, total = random_view(rng, in_ext)
+    out_any, k1 = t4.layout_any(out_ext)
+    in_any, k2 = t4.layout_any(in_ext, in_str, in_off)
+    av, k3 = t4.axis_values_any(dims)
+    src = rng.integers(0, 256, size=total * es, dtype=np.uint8)
+    f = np.arange(n, dtype=np.int64)
+    coords, rest = [], f.copy()
+    for e in out_ext:
+        coords.append(rest % e)
+        rest //= e
+    idx = np.full(n, in_off, dtype=np.int64)
+    for a, d in enumerate(dims):
+        if in_ext[a] != 1:
+            idx += coords[d] * in_str[a]
+    d_src, d_dst = dev(src), sentinel(n * es)
+    vp = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    any_launch(route, "broadcast_in_dim", n, [vp(d_dst), vp(d_src), ctypes.c_int(dtype), out_any, in_any, av,
+                                              ctypes.c_longlong(n)])
+    assert np.array_equal(take(d_dst, n * es).reshape(n, es), src.reshape(total, es)[idx])
+    del k1, k2, k3

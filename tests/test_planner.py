@@ -282,3 +282,28 @@ def test_reduce_any_geometry_and_host_checks():
     assert lib.t4a_launch_reduce_partials_any(ctypes.byref(launch), None, p, p, abi.F32, abi.SUM, good, good, 0,
                                               ctypes.c_longlong(10), ctypes.c_longlong(0),
                                               ctypes.c_longlong(1)) == 23
+
+
+def test_movement_any_geometry_and_host_checks():
+    g = t4.movement_any_geometry(1000)
+    assert (g.block[0], g.grid[0]) == (256, 4)
+    assert t4.movement_any_geometry(0).grid[0] == 0
+    with pytest.raises(t4.T4AError) as err:
+        t4.movement_any_geometry(-1)
+    assert err.value.status == 4
+    lib = t4.lib()
+    launch = t4.movement_any_geometry(10)
+    p = ctypes.c_void_p(0x3000)
+    good = abi.LayoutAny(3, 0, 0, ctypes.c_void_p(0x1000), ctypes.c_void_p(0x2000))
+    rank2 = abi.LayoutAny(2, 0, 0, ctypes.c_void_p(0x1000), ctypes.c_void_p(0x2000))
+    bad = abi.LayoutAny(3, 7, 0, ctypes.c_void_p(0x1000), ctypes.c_void_p(0x2000))
+    nulls = abi.LayoutAny(3, 0, 0, None, None)
+    n = ctypes.c_longlong(10)
+    assert lib.t4a_launch_materialize_strided_any(ctypes.byref(launch), None, p, p, abi.F32, bad, n) == 1
+    assert lib.t4a_launch_contiguous_to_view_any(ctypes.byref(launch), None, p, p, abi.F32, nulls, n) == 66
+    assert lib.t4a_launch_strided_to_strided_any(ctypes.byref(launch), None, p, p, abi.F32, good, rank2, n) == 2
+    assert lib.t4a_launch_fill_zero_view_any(ctypes.byref(launch), None, p, 99, good, n) == 9
+    dims = abi.AxisValuesAny(2, 0, ctypes.c_void_p(0x4000))
+    assert lib.t4a_launch_broadcast_in_dim_any(ctypes.byref(launch), None, p, p, abi.F32, good, good, dims, n) == 2
+    assert lib.t4a_launch_fill_zero_view_any(ctypes.byref(launch), None, None, abi.F32, good,
+                                             ctypes.c_longlong(0)) == 0
