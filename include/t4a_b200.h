@@ -367,6 +367,34 @@ int t4a_launch_prefix_rank(const t4a_launch* launch, void* stream, const void* r
                            t4a_cuda_layout r_layout, double rtol, double atol);
 
 
+/* General-rank RRQR primitives, the `_any` twins (reference cuda/src/rrqr.cu:930-1108;
+ * module symbols t4a_cuda_*_any in rrqr.cubin): the same bodies as the launchers above,
+ * with layouts whose extents and strides are in device memory, so any rank works.
+ * The kernels count their tasks from the layouts on the device; the grid must cover
+ * them: t4a_rrqr_any_geometry(tasks, flat) gives one task per warp for the plane
+ * entries (column_norms: batches * (n - step); select_pivot, reflector, prefix_rank:
+ * batches; apply_reflector: batches * column_count) and a grid-stride walk for the
+ * flat ones (swap_columns: rows * batches; extract_r: elements of R). */
+int t4a_rrqr_any_geometry(long long tasks, int flat, t4a_launch* launch);
+int t4a_launch_column_norms_any(const t4a_launch* launch, void* stream, const void* work, void* norms, int dtype,
+                                t4a_cuda_layout_any work_layout, t4a_cuda_layout_any norms_layout, long long step);
+int t4a_launch_select_pivot_any(const t4a_launch* launch, void* stream, const void* norms, const void* permutation,
+                                void* pivots, void* status, int dtype, t4a_cuda_layout_any norms_layout,
+                                t4a_cuda_layout_any permutation_layout, long long step);
+int t4a_launch_swap_columns_any(const t4a_launch* launch, void* stream, void* work, void* permutation,
+                                const void* pivots, int dtype, t4a_cuda_layout_any work_layout,
+                                t4a_cuda_layout_any permutation_layout, long long step);
+int t4a_launch_reflector_any(const t4a_launch* launch, void* stream, void* work, void* coeff, int dtype,
+                             t4a_cuda_layout_any work_layout, t4a_cuda_layout_any coeff_layout, long long step);
+int t4a_launch_apply_reflector_any(const t4a_launch* launch, void* stream, const void* packed, void* target,
+                                   const void* coeff, int dtype, t4a_cuda_layout_any packed_layout,
+                                   t4a_cuda_layout_any target_layout, t4a_cuda_layout_any coeff_layout,
+                                   long long step, long long first_column, long long column_count);
+int t4a_launch_extract_r_any(const t4a_launch* launch, void* stream, const void* work, void* r, int dtype,
+                             t4a_cuda_layout_any work_layout, t4a_cuda_layout_any r_layout);
+int t4a_launch_prefix_rank_any(const t4a_launch* launch, void* stream, const void* r, void* rank, void* status,
+                               int dtype, t4a_cuda_layout_any r_layout, double rtol, double atol);
+
 /* No single counterpart in the reference (its loop lives with the caller, bench
  * examples/bench_kernels.rs:2390-2623): `steps` steps of column_norms, select_pivot,
  * swap_columns, reflector and apply_reflector over the trailing columns, for one

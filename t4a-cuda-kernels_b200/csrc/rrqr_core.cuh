@@ -66,7 +66,10 @@ __device__ __forceinline__ bool not_finite(F v) {
 }
 
 // Offset of batch `batch` over the layout's axes first..rank-1 (axis `first` fastest).
-__device__ __forceinline__ long long batch_offset(long long batch, const t4a_cuda_layout& l, int first) {
+// L is t4a_cuda_layout or the general-rank t4a_cuda_layout_any (arrays in device
+// memory); every body below reads either through the same field names.
+template <typename L>
+__device__ __forceinline__ long long batch_offset(long long batch, const L& l, int first) {
   long long off = 0;
   for (int ax = first; ax < l.rank; ++ax) {
     const long long e = l.extents[ax];
@@ -76,7 +79,8 @@ __device__ __forceinline__ long long batch_offset(long long batch, const t4a_cud
   return off;
 }
 
-__device__ __forceinline__ long long batch_count(const t4a_cuda_layout& l, int first) {
+template <typename L>
+__device__ __forceinline__ long long batch_count(const L& l, int first) {
   long long n = 1;
   for (int ax = first; ax < l.rank; ++ax) n *= l.extents[ax];
   return n;
@@ -117,9 +121,9 @@ __device__ __forceinline__ F column_norm(const T* w, long long base, long long r
 }
 
 // column_norms (reference rrqr.cu:144-190): one warp per (batch, column >= step).
-template <typename T>
-__device__ __forceinline__ void column_norms_task(const T* w, typename RealOf<T>::F* norms, const t4a_cuda_layout& wl,
-                                                  const t4a_cuda_layout& nl, long long step, long long task) {
+template <typename T, typename L>
+__device__ __forceinline__ void column_norms_task(const T* w, typename RealOf<T>::F* norms, const L& wl, const L& nl,
+                                                  long long step, long long task) {
   using F = typename RealOf<T>::F;
   const long long trailing = wl.extents[1] - step;
   const long long batch = task / trailing;
@@ -133,10 +137,10 @@ __device__ __forceinline__ void column_norms_task(const T* w, typename RealOf<T>
 }
 
 // select_pivot (reference rrqr.cu:197-239): one warp per batch.
-template <typename F>
+template <typename F, typename L>
 __device__ __forceinline__ void select_pivot_task(const F* norms, const long long* perm, long long* pivots,
-                                                  long long* status, const t4a_cuda_layout& nl,
-                                                  const t4a_cuda_layout& pl, long long step, long long batch) {
+                                                  long long* status, const L& nl, const L& pl, long long step,
+                                                  long long batch) {
   const long long columns = nl.extents[0];
   const int lane = threadIdx.x & 31;
   const long long nb = nl.offset + batch_offset(batch, nl, 1);
@@ -166,10 +170,9 @@ __device__ __forceinline__ void select_pivot_task(const F* norms, const long lon
 }
 
 // swap_columns (reference rrqr.cu:244-284): element (row, batch) of a flat walk.
-template <typename T>
-__device__ __forceinline__ void swap_columns_elem(T* w, long long* perm, const long long* pivots,
-                                                  const t4a_cuda_layout& wl, const t4a_cuda_layout& pl,
-                                                  long long step, long long pos) {
+template <typename T, typename L>
+__device__ __forceinline__ void swap_columns_elem(T* w, long long* perm, const long long* pivots, const L& wl,
+                                                  const L& pl, long long step, long long pos) {
   const long long rows = wl.extents[0];
   const long long row = pos % rows;
   const long long batch = pos / rows;
@@ -332,9 +335,9 @@ __device__ __forceinline__ void apply_task(const T* packed, T* target, const T* 
 }
 
 // prefix_rank (reference rrqr.cu:476-509): one warp per batch.
-template <typename T>
-__device__ __forceinline__ void prefix_rank_task(const T* r, long long* rank, long long* status,
-                                                 const t4a_cuda_layout& rl, typename RealOf<T>::F rtol,
+template <typename T, typename L>
+__device__ __forceinline__ void prefix_rank_task(const T* r, long long* rank, long long* status, const L& rl,
+                                                 typename RealOf<T>::F rtol,
                                                  typename RealOf<T>::F atol, long long batch) {
   using F = typename RealOf<T>::F;
   const long long k = rl.extents[0];
@@ -359,9 +362,8 @@ __device__ __forceinline__ void prefix_rank_task(const T* r, long long* rank, lo
 }
 
 // extract_r (reference rrqr.cu:449-470): element `flat` of R.
-template <typename T>
-__device__ __forceinline__ void extract_r_elem(const T* w, T* r, const t4a_cuda_layout& wl, const t4a_cuda_layout& rl,
-                                               long long flat) {
+template <typename T, typename L>
+__device__ __forceinline__ void extract_r_elem(const T* w, T* r, const L& wl, const L& rl, long long flat) {
   const long long row = flat % rl.extents[0];
   const long long column = (flat / rl.extents[0]) % rl.extents[1];
   const long long batch = flat / (rl.extents[0] * rl.extents[1]);

@@ -7,6 +7,7 @@
 
 #include "plan_common.h"
 #include "rrqr_core.cuh"
+#include "rrqr_entries.cuh"
 #include "rrqr_step.cuh"
 #include "runtime.h"
 
@@ -95,6 +96,49 @@ __global__ void __launch_bounds__(kTaskThreads) k_prefix_rank(const T* r, long l
   using F = typename RealOf<T>::F;
   const long long batch = warp_task();
   if (batch < tasks) prefix_rank_task<T>(r, rank, status, rl, static_cast<F>(rtol), static_cast<F>(atol), batch);
+}
+
+// ---- general-rank kernels: the module's `_any` entry bodies ------------------------
+__global__ void __launch_bounds__(kTaskThreads) k_norms_any(const void* w, void* norms, int dtype,
+                                                           t4a_cuda_layout_any wl, t4a_cuda_layout_any nl,
+                                                           long long step) {
+  entry::column_norms_entry(w, norms, dtype, wl, nl, step);
+}
+__global__ void __launch_bounds__(kTaskThreads) k_pivot_any(const void* norms, const void* perm, void* pivots,
+                                                           void* status, int dtype, t4a_cuda_layout_any nl,
+                                                           t4a_cuda_layout_any pl, long long step) {
+  entry::select_pivot_entry(norms, perm, pivots, status, dtype, nl, pl, step);
+}
+__global__ void __launch_bounds__(kFlatThreads) k_swap_any(void* w, void* perm, const void* pivots, int dtype,
+                                                          t4a_cuda_layout_any wl, t4a_cuda_layout_any pl,
+                                                          long long step) {
+  entry::swap_entry(w, perm, pivots, dtype, wl, pl, step);
+}
+__global__ void __launch_bounds__(kTaskThreads) k_reflector_any(void* w, void* coeff, int dtype,
+                                                               t4a_cuda_layout_any wl, t4a_cuda_layout_any cl,
+                                                               long long step) {
+  entry::reflector_entry(w, coeff, dtype, wl, cl, step);
+}
+__global__ void __launch_bounds__(kTaskThreads) k_apply_any(const void* packed, void* target, const void* coeff,
+                                                           int dtype, t4a_cuda_layout_any pl, t4a_cuda_layout_any tl,
+                                                           t4a_cuda_layout_any cl, long long step,
+                                                           long long first_column, long long column_count) {
+  entry::apply_entry(packed, target, coeff, dtype, pl, tl, cl, step, first_column, column_count);
+}
+__global__ void __launch_bounds__(kFlatThreads) k_extract_r_any(const void* w, void* r, int dtype,
+                                                               t4a_cuda_layout_any wl, t4a_cuda_layout_any rl) {
+  entry::extract_entry(w, r, dtype, wl, rl);
+}
+__global__ void __launch_bounds__(kTaskThreads) k_prefix_rank_any(const void* r, void* rank, void* status, int dtype,
+                                                                 t4a_cuda_layout_any rl, double rtol, double atol) {
+  entry::prefix_rank_entry(r, rank, status, dtype, rl, rtol, atol);
+}
+
+// Host checks of a general-rank layout that need no device access.
+int check_rrqr_any(const t4a_cuda_layout_any& l, int min_rank) {
+  if (l.rank < min_rank || l.reserved != 0) return T4A_ERR_RANK_OUT_OF_RANGE;
+  if (l.extents == nullptr || l.strides == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  return T4A_OK;
 }
 
 // ---- fused step driver kernels ---------------------------------------------------
@@ -600,6 +644,106 @@ int t4a_launch_prefix_rank(const t4a_launch* launch, void* stream, const void* r
 }
 
 // ---- whole factorization (fused steps) ----------------------------------------------
+
+int t4a_rrqr_any_geometry(long long tasks, int flat, t4a_launch* launch) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  if (tasks < 0) return T4A_ERR_NEGATIVE_COUNT;
+  if (tasks == 0) {
+    *launch = plan::empty_launch();
+    return T4A_OK;
+  }
+  if (flat) {
+    unsigned long long grid = plan::ceil_div(static_cast<unsigned long long>(tasks), kFlatThreads);
+    if (grid > 148ull * 64) grid = 148ull * 64;
+    *launch = plan::make_launch(grid, kFlatThreads, 1, 0, 0);
+  } else {
+    *launch = plan::make_launch(plan::ceil_div(static_cast<unsigned long long>(tasks), kTaskWarps), kTaskThreads, 1,
+                                0, 0);
+  }
+  return T4A_OK;
+}
+
+#define T4A_ANY_PROLOGUE                                        \
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;          \
+  if (launch_empty(launch)) return T4A_OK;                      \
+  const dim3 g = grid_of_launch(launch), b = block_of_launch(launch); \
+  cudaStream_t s = static_cast<cudaStream_t>(stream)
+
+int t4a_launch_column_norms_any(const t4a_launch* launch, void* stream, const void* work, void* norms, int dtype,
+                                t4a_cuda_layout_any work_layout, t4a_cuda_layout_any norms_layout, long long step) {
+  T4A_TRY(check_algebra(dtype));
+  T4A_TRY(check_rrqr_any(work_layout, 2));
+  T4A_TRY(check_rrqr_any(norms_layout, 1));
+  T4A_ANY_PROLOGUE;
+  k_norms_any<<<g, b, 0, s>>>(work, norms, dtype, work_layout, norms_layout, step);
+  return runtime::check_launch();
+}
+
+int t4a_launch_select_pivot_any(const t4a_launch* launch, void* stream, const void* norms, const void* permutation,
+                                void* pivots, void* status, int dtype, t4a_cuda_layout_any norms_layout,
+                                t4a_cuda_layout_any permutation_layout, long long step) {
+  if (dtype != T4A_CUDA_F32 && dtype != T4A_CUDA_F64) return T4A_ERR_UNSUPPORTED_DTYPE;
+  T4A_TRY(check_rrqr_any(norms_layout, 1));
+  T4A_TRY(check_rrqr_any(permutation_layout, 1));
+  T4A_ANY_PROLOGUE;
+  k_pivot_any<<<g, b, 0, s>>>(norms, permutation, pivots, status, dtype, norms_layout, permutation_layout, step);
+  return runtime::check_launch();
+}
+
+int t4a_launch_swap_columns_any(const t4a_launch* launch, void* stream, void* work, void* permutation,
+                                const void* pivots, int dtype, t4a_cuda_layout_any work_layout,
+                                t4a_cuda_layout_any permutation_layout, long long step) {
+  T4A_TRY(check_numeric(dtype));
+  T4A_TRY(check_rrqr_any(work_layout, 2));
+  T4A_TRY(check_rrqr_any(permutation_layout, 1));
+  T4A_ANY_PROLOGUE;
+  k_swap_any<<<g, b, 0, s>>>(work, permutation, pivots, dtype, work_layout, permutation_layout, step);
+  return runtime::check_launch();
+}
+
+int t4a_launch_reflector_any(const t4a_launch* launch, void* stream, void* work, void* coeff, int dtype,
+                             t4a_cuda_layout_any work_layout, t4a_cuda_layout_any coeff_layout, long long step) {
+  T4A_TRY(check_algebra(dtype));
+  T4A_TRY(check_rrqr_any(work_layout, 2));
+  T4A_TRY(check_rrqr_any(coeff_layout, 1));
+  T4A_ANY_PROLOGUE;
+  k_reflector_any<<<g, b, 0, s>>>(work, coeff, dtype, work_layout, coeff_layout, step);
+  return runtime::check_launch();
+}
+
+int t4a_launch_apply_reflector_any(const t4a_launch* launch, void* stream, const void* packed, void* target,
+                                   const void* coeff, int dtype, t4a_cuda_layout_any packed_layout,
+                                   t4a_cuda_layout_any target_layout, t4a_cuda_layout_any coeff_layout,
+                                   long long step, long long first_column, long long column_count) {
+  T4A_TRY(check_algebra(dtype));
+  T4A_TRY(check_rrqr_any(packed_layout, 2));
+  T4A_TRY(check_rrqr_any(target_layout, 2));
+  T4A_TRY(check_rrqr_any(coeff_layout, 1));
+  T4A_ANY_PROLOGUE;
+  k_apply_any<<<g, b, 0, s>>>(packed, target, coeff, dtype, packed_layout, target_layout, coeff_layout, step,
+                              first_column, column_count);
+  return runtime::check_launch();
+}
+
+int t4a_launch_extract_r_any(const t4a_launch* launch, void* stream, const void* work, void* r, int dtype,
+                             t4a_cuda_layout_any work_layout, t4a_cuda_layout_any r_layout) {
+  T4A_TRY(check_algebra(dtype));
+  T4A_TRY(check_rrqr_any(work_layout, 2));
+  T4A_TRY(check_rrqr_any(r_layout, 2));
+  T4A_ANY_PROLOGUE;
+  k_extract_r_any<<<g, b, 0, s>>>(work, r, dtype, work_layout, r_layout);
+  return runtime::check_launch();
+}
+
+int t4a_launch_prefix_rank_any(const t4a_launch* launch, void* stream, const void* r, void* rank, void* status,
+                               int dtype, t4a_cuda_layout_any r_layout, double rtol, double atol) {
+  T4A_TRY(check_algebra(dtype));
+  T4A_TRY(check_rrqr_any(r_layout, 2));
+  T4A_ANY_PROLOGUE;
+  k_prefix_rank_any<<<g, b, 0, s>>>(r, rank, status, dtype, r_layout, rtol, atol);
+  return runtime::check_launch();
+}
+#undef T4A_ANY_PROLOGUE
 
 int t4a_rrqr_workspace_bytes(int dtype, const t4a_cuda_layout* work, size_t* bytes) {
   if (work == nullptr || bytes == nullptr) return T4A_ERR_NULL_ARGUMENT;

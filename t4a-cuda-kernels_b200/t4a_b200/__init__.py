@@ -451,6 +451,13 @@ def launch_rrqr(name, launch, stream, *args):
     check(getattr(lib(), "t4a_launch_" + name)(ctypes.byref(launch), stream, *args), "launch_" + name)
 
 
+def rrqr_any_geometry(tasks, flat):
+    launch = Launch()
+    check(lib().t4a_rrqr_any_geometry(ctypes.c_longlong(tasks), int(bool(flat)), ctypes.byref(launch)),
+          "rrqr_any_geometry")
+    return launch
+
+
 def rrqr_workspace_bytes(dtype, work_layout):
     n = ctypes.c_size_t(0)
     check(lib().t4a_rrqr_workspace_bytes(dtype, ctypes.byref(work_layout), ctypes.byref(n)), "rrqr_workspace_bytes")

@@ -307,3 +307,37 @@ def test_movement_any_geometry_and_host_checks():
     assert lib.t4a_launch_broadcast_in_dim_any(ctypes.byref(launch), None, p, p, abi.F32, good, good, dims, n) == 2
     assert lib.t4a_launch_fill_zero_view_any(ctypes.byref(launch), None, None, abi.F32, good,
                                              ctypes.c_longlong(0)) == 0
+
+
+def test_rrqr_any_geometry_and_host_checks():
+    g = t4.rrqr_any_geometry(20, False)
+    assert (g.block[0], g.grid[0]) == (256, 3)  # eight tasks (warps) per block
+    g = t4.rrqr_any_geometry(1000, True)
+    assert (g.block[0], g.grid[0]) == (256, 4)
+    assert t4.rrqr_any_geometry(10 ** 12, True).grid[0] == 148 * 64
+    assert t4.rrqr_any_geometry(0, True).grid[0] == 0
+    with pytest.raises(t4.T4AError) as err:
+        t4.rrqr_any_geometry(-1, False)
+    assert err.value.status == 4
+    lib = t4.lib()
+    launch = t4.rrqr_any_geometry(4, False)
+    lp = ctypes.byref(launch)
+    p = ctypes.c_void_p(0x3000)
+    mat = abi.LayoutAny(2, 0, 0, ctypes.c_void_p(0x1000), ctypes.c_void_p(0x2000))
+    vec = abi.LayoutAny(1, 0, 0, ctypes.c_void_p(0x1000), ctypes.c_void_p(0x2000))
+    bad = abi.LayoutAny(2, 7, 0, ctypes.c_void_p(0x1000), ctypes.c_void_p(0x2000))
+    nulls = abi.LayoutAny(2, 0, 0, None, None)
+    st = ctypes.c_longlong(0)
+    assert lib.t4a_launch_column_norms_any(lp, None, p, p, abi.F64, vec, vec, st) == 1  # work needs rank 2
+    assert lib.t4a_launch_column_norms_any(lp, None, p, p, abi.I32, mat, vec, st) == 9
+    assert lib.t4a_launch_select_pivot_any(lp, None, p, p, p, p, abi.C64, vec, vec, st) == 9
+    assert lib.t4a_launch_swap_columns_any(lp, None, p, p, p, abi.F64, nulls, vec, st) == 66
+    assert lib.t4a_launch_reflector_any(lp, None, p, p, abi.F64, bad, vec, st) == 1
+    assert lib.t4a_launch_apply_reflector_any(lp, None, p, p, p, abi.F64, mat, vec, vec, st, st, st) == 1
+    assert lib.t4a_launch_extract_r_any(lp, None, p, p, abi.F64, mat, vec) == 1
+    assert lib.t4a_launch_prefix_rank_any(lp, None, p, p, p, abi.F64, vec, ctypes.c_double(0.0),
+                                          ctypes.c_double(0.0)) == 1
+    assert lib.t4a_launch_prefix_rank_any(None, None, p, p, p, abi.F64, mat, ctypes.c_double(0.0),
+                                          ctypes.c_double(0.0)) == 66
+    empty = t4.rrqr_any_geometry(0, True)
+    assert lib.t4a_launch_extract_r_any(ctypes.byref(empty), None, p, p, abi.F64, mat, mat) == 0

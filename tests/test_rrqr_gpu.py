@@ -513,3 +513,105 @@ def test_rrqr_loop_special_values(cuda):
     assert np.array_equal(coeff_f.view(np.uint64), coeff_o.view(np.uint64))
     assert np.array_equal(np.asarray(w_p, order="F").view(np.uint64), np.asarray(w_o, order="F").view(np.uint64))
     assert np.array_equal(np.asarray(w_f, order="F").view(np.uint64), np.asarray(w_o, order="F").view(np.uint64))
+
+
+# ---- general-rank twins (`_any`) ----------------------------------------------
+
+def rrqr_loop(dtype, mats, steps, mode):
+    """The reference bench's loop of primitives over a batch of matrices ([m, n, B]
+    layouts, batch axis last), then extract_r and prefix_rank.  mode "fast": this
+    library's launchers with the planners' geometry; "any-launcher" / "any-module":
+    the general-rank twins (launchers / module symbols) on the same layouts padded to
+    rank 9-10 with trailing extent-1 axes, on t4a_rrqr_any_geometry."""
+    import torch
+    B = len(mats)
+    m, n = mats[0].shape[1], mats[0].shape[0]
+    es = np.dtype(NP[dtype]).itemsize
+    rdt = np.float32 if dtype in (abi.F32, abi.C32) else np.float64
+    work = np.concatenate([mt.ravel() for mt in mats])
+    d_w = dev(work)
+    d_norms = dev(np.zeros(n * B, rdt))
+    d_perm = dev(np.zeros(n * B, np.int64))
+    d_piv = dev(np.zeros(B, np.int64))
+    d_st = dev(np.zeros(B, np.int64))
+    d_coeff = dev(np.zeros(steps * B, NP[dtype]))
+    d_packed = dev(np.zeros(m * B, NP[dtype]))
+    k = min(m, n)
+    d_r = dev(np.zeros(k * n * B, NP[dtype]))
+    d_rank, d_rst = dev(np.zeros(B, np.int64)), dev(np.zeros(B, np.int64))
+    shapes = {"w": ([m, n, B], [1, m, m * n]), "v": ([n, B], [1, n]), "c": ([steps, B], [1, steps]),
+              "p": ([m, n, B], [1, 0, m]), "r": ([k, n, B], [1, k, k * n])}
+    keep = []
+
+    def lay(key):
+        ext, st = shapes[key]
+        if mode == "fast":
+            return abi.layout(ext, st)
+        pad = 10 - len(ext) if key in ("w", "p", "r") else 9 - len(ext)
+        la, arr = t4.layout_any(ext + [1] * pad, st + [0] * pad)
+        keep.append(arr)
+        return la
+    wl, vl, cl, pk, rl = lay("w"), lay("v"), lay("c"), lay("p"), lay("r")
+    fl = {"w": abi.layout(*shapes["w"]), "v": abi.layout(*shapes["v"]), "c": abi.layout(*shapes["c"]),
+          "p": abi.layout(*shapes["p"]), "r": abi.layout(*shapes["r"])}
+    s = t4.stream_handle()
+
+    def run(name, plan_args, tasks, is_flat, args):
+        if mode == "fast":
+            t4.launch_rrqr(name, t4.plan_rrqr(name, *plan_args), s, *args)
+        else:
+            g = t4.rrqr_any_geometry(tasks, is_flat)
+            if mode == "any-launcher":
+                t4.launch_rrqr(name + "_any", g, s, *args)
+            elif g.grid[0] > 0:
+                module(OUR_CUBIN).launch("t4a_cuda_" + name + "_any", tuple(g.grid), tuple(g.block), 0, list(args))
+    t4.launch_rrqr("initialize_permutation", t4.plan_rrqr("initialize_permutation", n, n * B), s, vp(d_perm),
+                   ctypes.c_longlong(n), ctypes.c_longlong(n * B))
+    span = m * n * B
+    for step in range(steps):
+        st = ctypes.c_longlong(step)
+        run("column_norms", (dtype, fl["w"], span, fl["v"], n * B, step), B * (n - step), False,
+            [vp(d_w), vp(d_norms), ctypes.c_int(dtype), wl, vl, st])
+        pdt = abi.F32 if rdt == np.float32 else abi.F64
+        run("select_pivot", (pdt, fl["v"], n * B, fl["v"], n * B, B, B, step), B, False,
+            [vp(d_norms), vp(d_perm), vp(d_piv), vp(d_st), ctypes.c_int(pdt), vl, vl, st])
+        run("swap_columns", (dtype, fl["w"], span, fl["v"], n * B, B, step), m * B, True,
+            [vp(d_w), vp(d_perm), vp(d_piv), ctypes.c_int(dtype), wl, vl, st])
+        run("reflector", (dtype, fl["w"], span, fl["c"], steps * B, step), B, False,
+            [vp(d_w), vp(d_coeff), ctypes.c_int(dtype), wl, cl, st])
+        if n - step - 1 > 0:
+            wv = d_w[:span * es].view(torch.uint8)
+            for b in range(B):
+                src = wv[(b * m * n + step * m) * es:(b * m * n + step * m + m) * es]
+                d_packed[b * m * es:(b + 1) * m * es].copy_(src)
+            run("apply_reflector", (dtype, fl["p"], m * B, fl["w"], span, fl["c"], steps * B, step, step + 1,
+                                    n - step - 1), B * (n - step - 1), False,
+                [vp(d_packed), vp(d_w), vp(d_coeff), ctypes.c_int(dtype), pk, wl, cl, st,
+                 ctypes.c_longlong(step + 1), ctypes.c_longlong(n - step - 1)])
+    run("extract_r", (dtype, fl["w"], span, fl["r"], k * n * B), k * n * B, True,
+        [vp(d_w), vp(d_r), ctypes.c_int(dtype), wl, rl])
+    run("prefix_rank", (dtype, fl["r"], k * n * B, B, B, 1e-8, 0.0), B, False,
+        [vp(d_r), vp(d_rank), vp(d_rst), ctypes.c_int(dtype), rl, ctypes.c_double(1e-8), ctypes.c_double(0.0)])
+    torch.cuda.synchronize()
+    out = (host(d_w, span * es, NP[dtype]), host(d_perm, n * B * 8, np.int64), host(d_coeff, steps * B * es, NP[dtype]),
+           host(d_piv, B * 8, np.int64), host(d_r, k * n * B * es, NP[dtype]), host(d_rank, B * 8, np.int64))
+    del keep
+    return out
+
+
+@pytest.mark.parametrize("mode", ["any-launcher", "any-module"])
+@pytest.mark.parametrize("dtype", [abi.F64, abi.F32, abi.C64])
+def test_any_twins_match_the_fast_primitives(cuda, mode, dtype):
+    """Two batched matrices, rank-10 layouts: the general-rank twins give the fast
+    primitives' results (bit for bit for F32/F64; complex within 1e-12 relative to the
+    column scale, as the complex product's contraction may differ between kernels)."""
+    rng = np.random.default_rng(60 + int(dtype))
+    m, n, steps = 300, 24, 20
+    mats = [rand_matrix(rng, dtype, m, n), rand_matrix(rng, dtype, m, n, shift=0.5)]
+    fast = rrqr_loop(dtype, mats, steps, "fast")
+    got = rrqr_loop(dtype, mats, steps, mode)
+    for name, a, b in zip(["work", "perm", "coeff", "pivots", "R", "rank"], got, fast):
+        if name in ("perm", "pivots", "rank") or dtype in (abi.F32, abi.F64):
+            assert np.array_equal(np.asarray(a).view(np.uint8), np.asarray(b).view(np.uint8)), name
+        else:
+            assert same(dtype, a, b), name
