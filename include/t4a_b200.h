@@ -310,6 +310,27 @@ int t4a_scatter_add(void* stream, int dtype, int index_dtype, void* out, const t
                     long long updates_len, const t4a_cuda_scatter_plan* plan, void* workspace,
                     size_t workspace_bytes);
 
+/* General-rank gather / scatter_add, the `_any` twins (reference
+ * cuda/src/gather_scatter.cu:587, :619; module symbols t4a_cuda_gather_any and
+ * t4a_cuda_scatter_add_any in gather_scatter.cubin): element-wise walks over layouts
+ * and maps in device memory, with the kernels' argument lists (layouts and plans by
+ * value).  Any geometry is correct; t4a_gather_scatter_any_geometry(elements) gives
+ * the one they are tuned for (elements = output_len / update_len).  The host checks
+ * dtypes, ranks, the maps' counts, null arrays and the index tensor's rank; the
+ * kernels check the maps' values (axes in range, distinct window positions) and that
+ * the count fits the walked layout, and a block that finds them malformed does
+ * nothing.  Elements are accessed as wide as the buffers' bases allow, so complex64
+ * needs 4-byte and complex128 8-byte alignment only. */
+int t4a_gather_scatter_any_geometry(long long elements, t4a_launch* launch);
+int t4a_launch_gather_any(const t4a_launch* launch, void* stream, void* out, const void* operand,
+                          const void* indices, int dtype, int index_dtype, t4a_cuda_layout_any out_layout,
+                          t4a_cuda_layout_any operand_layout, t4a_cuda_layout_any indices_layout,
+                          t4a_cuda_gather_plan_any plan, long long output_len);
+int t4a_launch_scatter_add_any(const t4a_launch* launch, void* stream, void* out, const void* indices,
+                               const void* updates, int dtype, int index_dtype, t4a_cuda_layout_any out_layout,
+                               t4a_cuda_layout_any indices_layout, t4a_cuda_layout_any updates_layout,
+                               t4a_cuda_scatter_plan_any plan, long long update_len);
+
 
 /* ------------------------------------------------------------------------- */
 /* RRQR primitives (reference src/lib.rs:2460-2774, rrqr.cu:513-705).          */

@@ -132,9 +132,45 @@ typedef struct {
   const long long* values;  /* rank values, device memory */
 } t4a_cuda_axis_values_any;
 
+/* Gather dimension maps of the `_any` entries: the fields of t4a_cuda_gather_plan with
+ * the maps in caller-owned device memory (window_dims / offset_dims: window_rank
+ * values; start_index_map: start_map_len; slice_sizes: operand_rank). */
+typedef struct {
+  int operand_rank;
+  int out_rank;
+  int index_vector_dim;
+  int window_rank;
+  int start_map_len;
+  int reserved;  /* must be 0 */
+  const long long* window_dims;
+  const long long* offset_dims;
+  const long long* start_index_map;
+  const long long* slice_sizes;
+} t4a_cuda_gather_plan_any;
+
+/* Additive-scatter dimension maps of the `_any` entries (window_dims /
+ * update_window_dims: window_rank values; scatter_dims: scatter_map_len), device
+ * memory. */
+typedef struct {
+  int operand_rank;
+  int updates_rank;
+  int index_vector_dim;
+  int window_rank;
+  int scatter_map_len;
+  int reserved;  /* must be 0 */
+  const long long* window_dims;
+  const long long* update_window_dims;
+  const long long* scatter_dims;
+} t4a_cuda_scatter_plan_any;
+
 #ifdef __cplusplus
 }  /* extern "C" */
 
+static_assert(sizeof(t4a_cuda_gather_plan_any) == 56, "t4a_cuda_gather_plan_any size");
+static_assert(__builtin_offsetof(t4a_cuda_gather_plan_any, window_dims) == 24, "gather_any.window_dims");
+static_assert(__builtin_offsetof(t4a_cuda_gather_plan_any, slice_sizes) == 48, "gather_any.slice_sizes");
+static_assert(sizeof(t4a_cuda_scatter_plan_any) == 48, "t4a_cuda_scatter_plan_any size");
+static_assert(__builtin_offsetof(t4a_cuda_scatter_plan_any, scatter_dims) == 40, "scatter_any.scatter_dims");
 static_assert(sizeof(t4a_cuda_axis_values_any) == 16, "t4a_cuda_axis_values_any size");
 static_assert(sizeof(t4a_cuda_layout_any) == 32, "t4a_cuda_layout_any size");
 static_assert(alignof(t4a_cuda_layout_any) == 8, "t4a_cuda_layout_any alignment");

@@ -139,3 +139,23 @@ extern "C" __global__ void __launch_bounds__(512) t4a_cuda_scatter_add(
     default: break;
   }
 }
+
+// ---- general-rank twins (`_any`, reference cuda/src/gather_scatter.cu:587, :619) ----
+// Element-wise walks over layouts and maps in device memory (gather_scatter_any.cuh).
+#include "gather_scatter_any.cuh"
+
+extern "C" __global__ void __launch_bounds__(256) t4a_cuda_gather_any(
+    void* out, const void* operand, const void* indices, int dtype, int index_dtype, t4a_cuda_layout_any out_layout,
+    t4a_cuda_layout_any operand_layout, t4a_cuda_layout_any indices_layout, t4a_cuda_gather_plan_any plan,
+    long long output_len) {
+  t4a::any::gather_entry(out, operand, indices, dtype, index_dtype, out_layout, operand_layout, indices_layout, plan,
+                         output_len);
+}
+
+extern "C" __global__ void __launch_bounds__(256) t4a_cuda_scatter_add_any(
+    void* out, const void* indices, const void* updates, int dtype, int index_dtype, t4a_cuda_layout_any out_layout,
+    t4a_cuda_layout_any indices_layout, t4a_cuda_layout_any updates_layout, t4a_cuda_scatter_plan_any plan,
+    long long update_len) {
+  t4a::any::scatter_entry(out, indices, updates, dtype, index_dtype, out_layout, indices_layout, updates_layout, plan,
+                          update_len);
+}

@@ -503,3 +503,118 @@ int t4a_scatter_add(void* stream, int dtype, int index_dtype, void* out, const t
 }
 
 }  // extern "C"
+
+// ---- general-rank twins (`_any`) ------------------------------------------------
+// The same bodies as the exported t4a_cuda_gather_any / t4a_cuda_scatter_add_any
+// (gather_scatter_any.cuh).  The maps live in device memory, so the host checks what it
+// can without reading them; each block checks the maps before it walks.
+#include "gather_scatter_any.cuh"
+
+namespace t4a {
+namespace {
+
+__global__ void __launch_bounds__(256) k_gather_any(void* out, const void* operand, const void* indices, int dtype,
+                                                    int index_dtype, t4a_cuda_layout_any ol, t4a_cuda_layout_any al,
+                                                    t4a_cuda_layout_any il, t4a_cuda_gather_plan_any g,
+                                                    long long len) {
+  any::gather_entry(out, operand, indices, dtype, index_dtype, ol, al, il, g, len);
+}
+
+__global__ void __launch_bounds__(256) k_scatter_add_any(void* out, const void* indices, const void* updates,
+                                                         int dtype, int index_dtype, t4a_cuda_layout_any ol,
+                                                         t4a_cuda_layout_any il, t4a_cuda_layout_any ul,
+                                                         t4a_cuda_scatter_plan_any g, long long len) {
+  any::scatter_entry(out, indices, updates, dtype, index_dtype, ol, il, ul, g, len);
+}
+
+int check_layout_any_gs(const t4a_cuda_layout_any& l) {
+  if (l.rank < 0 || l.reserved != 0) return T4A_ERR_RANK_OUT_OF_RANGE;
+  if (l.rank > 0 && (l.extents == nullptr || l.strides == nullptr)) return T4A_ERR_NULL_ARGUMENT;
+  return T4A_OK;
+}
+
+// The maps' counts against the layouts' ranks, and the index tensor's rank.
+int check_maps_any(int plan_rank_a, int layout_rank_a, int plan_rank_b, int layout_rank_b, int window_rank,
+                   int map_len, int reserved, int index_vector_dim, int walked_rank, int index_rank,
+                   const void* const* arrays, const bool* needed, int n_arrays) {
+  if (reserved != 0 || window_rank < 0 || map_len < 0) return T4A_ERR_RANK_OUT_OF_RANGE;
+  if (plan_rank_a != layout_rank_a || plan_rank_b != layout_rank_b) return T4A_ERR_RANK_LENGTH;
+  if (window_rank > layout_rank_a || window_rank > layout_rank_b) return T4A_ERR_RANK_OUT_OF_RANGE;
+  for (int i = 0; i < n_arrays; ++i)
+    if (needed[i] && arrays[i] == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  if (index_vector_dim < 0 || index_vector_dim > index_rank) return T4A_ERR_INVALID_AXIS;
+  if (walked_rank - window_rank + (index_vector_dim < index_rank ? 1 : 0) != index_rank)
+    return T4A_ERR_INDEX_VECTOR_MISMATCH;
+  return T4A_OK;
+}
+
+dim3 dim_of(const unsigned* v) { return dim3(v[0], v[1] ? v[1] : 1, v[2] ? v[2] : 1); }
+
+}  // namespace
+}  // namespace t4a
+
+extern "C" {
+
+int t4a_gather_scatter_any_geometry(long long elements, t4a_launch* launch) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  if (elements < 0) return T4A_ERR_NEGATIVE_COUNT;
+  if (elements == 0) {
+    *launch = plan::empty_launch();
+    return T4A_OK;
+  }
+  const unsigned long long grid = plan::ceil_div(static_cast<unsigned long long>(elements), 256);
+  const unsigned long long cap = 148ull * 64;
+  *launch = plan::make_launch(grid < cap ? grid : cap, 256, 1, 0, 0);
+  return T4A_OK;
+}
+
+int t4a_launch_gather_any(const t4a_launch* launch, void* stream, void* out, const void* operand,
+                          const void* indices, int dtype, int index_dtype, t4a_cuda_layout_any out_layout,
+                          t4a_cuda_layout_any operand_layout, t4a_cuda_layout_any indices_layout,
+                          t4a_cuda_gather_plan_any plan, long long output_len) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  if (output_len < 0) return T4A_ERR_NEGATIVE_COUNT;
+  if (dtype_size(dtype) == 0) return T4A_ERR_UNSUPPORTED_DTYPE;
+  T4A_TRY(require_index_dtype(index_dtype));
+  T4A_TRY(check_layout_any_gs(out_layout));
+  T4A_TRY(check_layout_any_gs(operand_layout));
+  T4A_TRY(check_layout_any_gs(indices_layout));
+  const void* arrays[] = {plan.window_dims, plan.offset_dims, plan.start_index_map, plan.slice_sizes};
+  const bool needed[] = {plan.window_rank > 0, plan.window_rank > 0, plan.start_map_len > 0, plan.start_map_len > 0};
+  T4A_TRY(check_maps_any(plan.operand_rank, operand_layout.rank, plan.out_rank, out_layout.rank, plan.window_rank,
+                         plan.start_map_len, plan.reserved, plan.index_vector_dim, out_layout.rank,
+                         indices_layout.rank, arrays, needed, 4));
+  if (output_len == 0 || launch->grid[0] == 0 || launch->block[0] == 0) return T4A_OK;
+  if (out == nullptr || operand == nullptr || (plan.start_map_len > 0 && indices == nullptr))
+    return T4A_ERR_NULL_ARGUMENT;
+  k_gather_any<<<dim_of(launch->grid), dim_of(launch->block), 0, static_cast<cudaStream_t>(stream)>>>(
+      out, operand, indices, dtype, index_dtype, out_layout, operand_layout, indices_layout, plan, output_len);
+  return runtime::check_launch();
+}
+
+int t4a_launch_scatter_add_any(const t4a_launch* launch, void* stream, void* out, const void* indices,
+                               const void* updates, int dtype, int index_dtype, t4a_cuda_layout_any out_layout,
+                               t4a_cuda_layout_any indices_layout, t4a_cuda_layout_any updates_layout,
+                               t4a_cuda_scatter_plan_any plan, long long update_len) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  if (update_len < 0) return T4A_ERR_NEGATIVE_COUNT;
+  if (dtype != T4A_CUDA_F32 && dtype != T4A_CUDA_F64 && dtype != T4A_CUDA_C32 && dtype != T4A_CUDA_C64)
+    return T4A_ERR_UNSUPPORTED_DTYPE;
+  T4A_TRY(require_index_dtype(index_dtype));
+  T4A_TRY(check_layout_any_gs(out_layout));
+  T4A_TRY(check_layout_any_gs(indices_layout));
+  T4A_TRY(check_layout_any_gs(updates_layout));
+  const void* arrays[] = {plan.window_dims, plan.update_window_dims, plan.scatter_dims};
+  const bool needed[] = {plan.window_rank > 0, plan.window_rank > 0, plan.scatter_map_len > 0};
+  T4A_TRY(check_maps_any(plan.operand_rank, out_layout.rank, plan.updates_rank, updates_layout.rank,
+                         plan.window_rank, plan.scatter_map_len, plan.reserved, plan.index_vector_dim,
+                         updates_layout.rank, indices_layout.rank, arrays, needed, 3));
+  if (update_len == 0 || launch->grid[0] == 0 || launch->block[0] == 0) return T4A_OK;
+  if (out == nullptr || updates == nullptr || (plan.scatter_map_len > 0 && indices == nullptr))
+    return T4A_ERR_NULL_ARGUMENT;
+  k_scatter_add_any<<<dim_of(launch->grid), dim_of(launch->block), 0, static_cast<cudaStream_t>(stream)>>>(
+      out, indices, updates, dtype, index_dtype, out_layout, indices_layout, updates_layout, plan, update_len);
+  return runtime::check_launch();
+}
+
+}  // extern "C"

@@ -131,22 +131,6 @@ extern "C" __global__ void __launch_bounds__(256) t4a_cuda_broadcast_in_dim(
   run_plan(p, out, in);
 }
 
-namespace t4a {
-namespace {
-template <int B>
-__device__ __forceinline__ void zero_fill(void* out, const t4a_cuda_layout* l, long long len) {
-  using E = typename Elem<B>::T;
-  E* o = static_cast<E*>(out);
-  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
-  for (long long f = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; f < len; f += stride) {
-    const long long at = l == nullptr ? f : decode_offset(f, *l, l->strides, l->offset);
-    E z;
-    memset(&z, 0, sizeof(E));
-    o[at] = z;
-  }
-}
-}  // namespace
-}  // namespace t4a
 
 extern "C" __global__ void __launch_bounds__(256) t4a_cuda_fill_zero(void* out, int dtype, long long len) {
   switch (move_esize(dtype)) {
@@ -176,37 +160,37 @@ extern "C" __global__ void __launch_bounds__(256) t4a_cuda_fill_zero_view(void* 
 extern "C" __global__ void __launch_bounds__(256) t4a_cuda_fill_zero_view_any(void* out, int dtype,
                                                                             t4a_cuda_layout_any layout,
                                                                             long long len) {
-#define T4A_CALL(E) t4a::any::fill_zero_view<E>(out, layout, len)
-  T4A_ANY_ESIZE_SWITCH(dtype, T4A_CALL)
+#define T4A_CALL(E, A) t4a::any::fill_zero_view<E, A>(out, layout, len)
+  T4A_ANY_ESIZE_SWITCH(dtype, T4A_ANY_BITS(out), T4A_CALL)
 #undef T4A_CALL
 }
 
 extern "C" __global__ void __launch_bounds__(256) t4a_cuda_materialize_strided_any(
     void* dst, const void* src, int dtype, t4a_cuda_layout_any src_layout, long long len) {
-#define T4A_CALL(E) t4a::any::materialize<E>(dst, src, src_layout, len)
-  T4A_ANY_ESIZE_SWITCH(dtype, T4A_CALL)
+#define T4A_CALL(E, A) t4a::any::materialize<E, A>(dst, src, src_layout, len)
+  T4A_ANY_ESIZE_SWITCH(dtype, T4A_ANY_BITS(dst) | T4A_ANY_BITS(src), T4A_CALL)
 #undef T4A_CALL
 }
 
 extern "C" __global__ void __launch_bounds__(256) t4a_cuda_contiguous_to_view_any(
     void* dst, const void* src, int dtype, t4a_cuda_layout_any dst_layout, long long len) {
-#define T4A_CALL(E) t4a::any::to_view<E>(dst, src, dst_layout, len)
-  T4A_ANY_ESIZE_SWITCH(dtype, T4A_CALL)
+#define T4A_CALL(E, A) t4a::any::to_view<E, A>(dst, src, dst_layout, len)
+  T4A_ANY_ESIZE_SWITCH(dtype, T4A_ANY_BITS(dst) | T4A_ANY_BITS(src), T4A_CALL)
 #undef T4A_CALL
 }
 
 extern "C" __global__ void __launch_bounds__(256) t4a_cuda_strided_to_strided_any(
     void* dst, const void* src, int dtype, t4a_cuda_layout_any src_layout, t4a_cuda_layout_any dst_layout,
     long long len) {
-#define T4A_CALL(E) t4a::any::strided_copy<E>(dst, src, src_layout, dst_layout, len)
-  T4A_ANY_ESIZE_SWITCH(dtype, T4A_CALL)
+#define T4A_CALL(E, A) t4a::any::strided_copy<E, A>(dst, src, src_layout, dst_layout, len)
+  T4A_ANY_ESIZE_SWITCH(dtype, T4A_ANY_BITS(dst) | T4A_ANY_BITS(src), T4A_CALL)
 #undef T4A_CALL
 }
 
 extern "C" __global__ void __launch_bounds__(256) t4a_cuda_broadcast_in_dim_any(
     void* out, const void* in, int dtype, t4a_cuda_layout_any out_layout, t4a_cuda_layout_any in_layout,
     t4a_cuda_axis_values_any dims, long long out_len) {
-#define T4A_CALL(E) t4a::any::broadcast<E>(out, in, out_layout, in_layout, dims, out_len)
-  T4A_ANY_ESIZE_SWITCH(dtype, T4A_CALL)
+#define T4A_CALL(E, A) t4a::any::broadcast<E, A>(out, in, out_layout, in_layout, dims, out_len)
+  T4A_ANY_ESIZE_SWITCH(dtype, T4A_ANY_BITS(out) | T4A_ANY_BITS(in), T4A_CALL)
 #undef T4A_CALL
 }

@@ -10,7 +10,8 @@
 //                        the coordinate taken as 0 on an input axis of extent 1
 // where view(f) decodes the flat index f (axis 0 fastest) over the layout's extents
 // into offset + sum of coordinate * stride.  Elements move as raw bytes of the
-// dtype's size.
+// dtype's size, in accesses as wide as the buffers' bases allow (complex64 and
+// complex128 are only 4- and 8-byte aligned in the ABI).
 #pragma once
 
 #include "common.cuh"
@@ -18,8 +19,8 @@
 namespace t4a {
 namespace any {
 
-template <int E>
-struct alignas(E) Elem {
+template <int E, int A>
+struct alignas(A) Elem {
   unsigned char b[E];
 };
 
@@ -43,38 +44,38 @@ __device__ __forceinline__ long long flat_first() {
 }
 __device__ __forceinline__ long long flat_step() { return static_cast<long long>(gridDim.x) * blockDim.x; }
 
-template <int E>
+template <int E, int A>
 __device__ __forceinline__ void fill_zero_view(void* out, const t4a_cuda_layout_any& l, long long len) {
-  Elem<E> z;
+  Elem<E, A> z;
 #pragma unroll
   for (int i = 0; i < E; ++i) z.b[i] = 0;
   for (long long f = flat_first(); f < len; f += flat_step())
-    static_cast<Elem<E>*>(out)[view_of(f, l.rank, l.extents, l.strides, l.offset)] = z;
+    static_cast<Elem<E, A>*>(out)[view_of(f, l.rank, l.extents, l.strides, l.offset)] = z;
 }
 
-template <int E>
+template <int E, int A>
 __device__ __forceinline__ void materialize(void* dst, const void* src, const t4a_cuda_layout_any& l, long long len) {
   for (long long f = flat_first(); f < len; f += flat_step())
-    static_cast<Elem<E>*>(dst)[f] = static_cast<const Elem<E>*>(src)[view_of(f, l.rank, l.extents, l.strides, l.offset)];
+    static_cast<Elem<E, A>*>(dst)[f] = static_cast<const Elem<E, A>*>(src)[view_of(f, l.rank, l.extents, l.strides, l.offset)];
 }
 
-template <int E>
+template <int E, int A>
 __device__ __forceinline__ void to_view(void* dst, const void* src, const t4a_cuda_layout_any& l, long long len) {
   for (long long f = flat_first(); f < len; f += flat_step())
-    static_cast<Elem<E>*>(dst)[view_of(f, l.rank, l.extents, l.strides, l.offset)] = static_cast<const Elem<E>*>(src)[f];
+    static_cast<Elem<E, A>*>(dst)[view_of(f, l.rank, l.extents, l.strides, l.offset)] = static_cast<const Elem<E, A>*>(src)[f];
 }
 
-template <int E>
+template <int E, int A>
 __device__ __forceinline__ void strided_copy(void* dst, const void* src, const t4a_cuda_layout_any& sl,
                                              const t4a_cuda_layout_any& dl, long long len) {
   for (long long f = flat_first(); f < len; f += flat_step()) {
     const long long si = view_of(f, sl.rank, sl.extents, sl.strides, sl.offset);
     const long long di = view_of(f, sl.rank, sl.extents, dl.strides, dl.offset);
-    static_cast<Elem<E>*>(dst)[di] = static_cast<const Elem<E>*>(src)[si];
+    static_cast<Elem<E, A>*>(dst)[di] = static_cast<const Elem<E, A>*>(src)[si];
   }
 }
 
-template <int E>
+template <int E, int A>
 __device__ __forceinline__ void broadcast(void* out, const void* in, const t4a_cuda_layout_any& ol,
                                           const t4a_cuda_layout_any& il, const t4a_cuda_axis_values_any& dims,
                                           long long len) {
@@ -84,7 +85,7 @@ __device__ __forceinline__ void broadcast(void* out, const void* in, const t4a_c
       if (il.extents[a] != 1)
         index += compact_coordinate(f, ol.extents, static_cast<int>(dims.values[a])) * il.strides[a];
     }
-    static_cast<Elem<E>*>(out)[f] = static_cast<const Elem<E>*>(in)[index];
+    static_cast<Elem<E, A>*>(out)[f] = static_cast<const Elem<E, A>*>(in)[index];
   }
 }
 
@@ -104,12 +105,22 @@ __device__ __forceinline__ int elem_bytes(int dtype) {
 }  // namespace any
 }  // namespace t4a
 
-// Calls CALL(E) for the dtype's element size E (unknown dtypes do nothing).
-#define T4A_ANY_ESIZE_SWITCH(DTYPE, CALL)         \
-  switch (t4a::any::elem_bytes(DTYPE)) {          \
-    case 1: CALL(1); break;                       \
-    case 4: CALL(4); break;                       \
-    case 8: CALL(8); break;                       \
-    case 16: CALL(16); break;                     \
-    default: break;                               \
+// Calls CALL(E, A) for the dtype's element size E and the widest access A <= E that
+// every element reaches, given BITS = the OR of the buffers' base addresses (unknown
+// dtypes do nothing).
+#define T4A_ANY_ESIZE_SWITCH(DTYPE, BITS, CALL)                        \
+  switch (t4a::any::elem_bytes(DTYPE)) {                               \
+    case 1: CALL(1, 1); break;                                         \
+    case 4: CALL(4, 4); break;                                         \
+    case 8:                                                            \
+      if (((BITS) & 7ull) == 0) CALL(8, 8); else CALL(8, 4);           \
+      break;                                                           \
+    case 16:                                                           \
+      if (((BITS) & 15ull) == 0) CALL(16, 16);                         \
+      else if (((BITS) & 7ull) == 0) CALL(16, 8);                      \
+      else CALL(16, 4);                                                \
+      break;                                                           \
+    default: break;                                                    \
   }
+
+#define T4A_ANY_BITS(P) reinterpret_cast<unsigned long long>(P)

@@ -36,6 +36,37 @@ struct Elem<16> {
   using T = Bytes16;
 };
 
+// complex64 elements are only 4-byte aligned in the ABI: an 8-byte element walk whose
+// bases are off 8 bytes moves each element as two 4-byte words.
+struct alignas(4) Words8 {
+  unsigned lo, hi;
+};
+__host__ __device__ __forceinline__ bool off8(const void* a, const void* b) {
+  return ((reinterpret_cast<unsigned long long>(a) | reinterpret_cast<unsigned long long>(b)) & 7ull) != 0;
+}
+
+// out[view(f)] = 0 for f < len; the view is the identity when `l` is null.
+template <typename E>
+__device__ __forceinline__ void zero_walk(void* out, const t4a_cuda_layout* l, long long len) {
+  E* o = static_cast<E*>(out);
+  E z;
+  memset(&z, 0, sizeof(E));
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long f = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; f < len; f += stride)
+    o[l == nullptr ? f : decode_offset(f, *l, l->strides, l->offset)] = z;
+}
+
+template <int B>
+__device__ __forceinline__ void zero_fill(void* out, const t4a_cuda_layout* l, long long len) {
+  if constexpr (B == 8) {
+    if (off8(out, out)) {
+      zero_walk<Words8>(out, l, len);
+      return;
+    }
+  }
+  zero_walk<typename Elem<B>::T>(out, l, len);
+}
+
 extern __shared__ __align__(16) unsigned char t4a_move_smem[];
 
 // One 16-byte vector of `V` elements (V * sizeof(E) == 16), or a single element.
@@ -417,6 +448,12 @@ __device__ __forceinline__ void perm_rows_any(const PermPlan& p, E* dst, const E
 
 template <int B>
 __device__ __forceinline__ void perm_run(const PermPlan& p, void* dst_p, const void* src_p, bool smem_ok) {
+  if constexpr (B == 8) {
+    if (off8(dst_p, src_p)) {
+      if (p.kind != kPermEmpty) perm_generic<Words8>(p, static_cast<Words8*>(dst_p), static_cast<const Words8*>(src_p));
+      return;
+    }
+  }
   using E = typename Elem<B>::T;
   E* dst = static_cast<E*>(dst_p);
   const E* src = static_cast<const E*>(src_p);

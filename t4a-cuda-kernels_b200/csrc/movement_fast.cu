@@ -52,14 +52,7 @@ __global__ void __launch_bounds__(256) k_generic(PermPlan p, void* dst, const vo
 
 template <int B>
 __global__ void __launch_bounds__(256) k_zero(void* out, t4a_cuda_layout l, long long len, bool view) {
-  using E = typename Elem<B>::T;
-  E* o = static_cast<E*>(out);
-  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
-  for (long long f = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; f < len; f += stride) {
-    E z;
-    memset(&z, 0, sizeof(E));
-    o[view ? decode_offset(f, l, l.strides, l.offset) : f] = z;
-  }
+  zero_fill<B>(out, view ? &l : nullptr, len);
 }
 
 int host_esize(int dtype) { return plan::dtype_size(dtype); }
@@ -91,8 +84,18 @@ int perm_geometry(const PermPlan& p, t4a_launch* launch) {
   return T4A_OK;
 }
 
+__global__ void __launch_bounds__(256) k_generic_words8(PermPlan p, void* dst, const void* src) {
+  perm_generic<Words8>(p, static_cast<Words8*>(dst), static_cast<const Words8*>(src));
+}
+
 template <int B>
 int launch_plan_sized(const PermPlan& p, void* dst, const void* src, dim3 grid, unsigned smem, cudaStream_t s) {
+  if constexpr (B == 8) {
+    if (off8(dst, src)) {
+      k_generic_words8<<<grid, dim3(kPermThreads), 0, s>>>(p, dst, src);
+      return runtime::check_launch();
+    }
+  }
   constexpr int VV = B >= 16 ? 1 : 16 / B;
   const bool src_al = (reinterpret_cast<unsigned long long>(src) & 15ull) == 0;
   const bool dst_al = (reinterpret_cast<unsigned long long>(dst) & 15ull) == 0;
@@ -188,29 +191,29 @@ PermPlan broadcast_plan(int dtype, const t4a_cuda_layout& out, const t4a_cuda_la
 int check_dtype_move(int dtype) { return host_esize(dtype) ? T4A_OK : T4A_ERR_UNSUPPORTED_DTYPE; }
 
 // General-rank twins: the same bodies as the exported `_any` symbols.
-template <int E>
+template <int E, int A>
 __global__ void __launch_bounds__(256) k_zero_any(void* out, t4a_cuda_layout_any l, long long len) {
-  any::fill_zero_view<E>(out, l, len);
+  any::fill_zero_view<E, A>(out, l, len);
 }
-template <int E>
+template <int E, int A>
 __global__ void __launch_bounds__(256) k_materialize_any(void* dst, const void* src, t4a_cuda_layout_any l,
                                                          long long len) {
-  any::materialize<E>(dst, src, l, len);
+  any::materialize<E, A>(dst, src, l, len);
 }
-template <int E>
+template <int E, int A>
 __global__ void __launch_bounds__(256) k_to_view_any(void* dst, const void* src, t4a_cuda_layout_any l, long long len) {
-  any::to_view<E>(dst, src, l, len);
+  any::to_view<E, A>(dst, src, l, len);
 }
-template <int E>
+template <int E, int A>
 __global__ void __launch_bounds__(256) k_strided_any(void* dst, const void* src, t4a_cuda_layout_any sl,
                                                      t4a_cuda_layout_any dl, long long len) {
-  any::strided_copy<E>(dst, src, sl, dl, len);
+  any::strided_copy<E, A>(dst, src, sl, dl, len);
 }
-template <int E>
+template <int E, int A>
 __global__ void __launch_bounds__(256) k_broadcast_any(void* out, const void* in, t4a_cuda_layout_any ol,
                                                        t4a_cuda_layout_any il, t4a_cuda_axis_values_any dims,
                                                        long long len) {
-  any::broadcast<E>(out, in, ol, il, dims, len);
+  any::broadcast<E, A>(out, in, ol, il, dims, len);
 }
 
 // Host checks of a general-rank layout that need no device access.
@@ -471,13 +474,22 @@ int t4a_movement_any_geometry(long long len, t4a_launch* launch) {
   return T4A_OK;
 }
 
-#define T4A_ANY_LAUNCH(KERNEL, ...)                                               \
-  switch (host_esize(dtype)) {                                                    \
-    case 1: KERNEL<1><<<grid, block, 0, s>>>(__VA_ARGS__); break;                 \
-    case 4: KERNEL<4><<<grid, block, 0, s>>>(__VA_ARGS__); break;                 \
-    case 8: KERNEL<8><<<grid, block, 0, s>>>(__VA_ARGS__); break;                 \
-    case 16: KERNEL<16><<<grid, block, 0, s>>>(__VA_ARGS__); break;               \
-    default: return T4A_ERR_UNSUPPORTED_DTYPE;                                    \
+// Launches KERNEL<E, A> for the dtype's element size E and the widest access A that
+// the buffers' bases (BITS, their OR) allow.
+#define T4A_ANY_LAUNCH(BITS, KERNEL, ...)                                           \
+  switch (host_esize(dtype)) {                                                      \
+    case 1: KERNEL<1, 1><<<grid, block, 0, s>>>(__VA_ARGS__); break;                \
+    case 4: KERNEL<4, 4><<<grid, block, 0, s>>>(__VA_ARGS__); break;                \
+    case 8:                                                                         \
+      if (((BITS) & 7ull) == 0) KERNEL<8, 8><<<grid, block, 0, s>>>(__VA_ARGS__);   \
+      else KERNEL<8, 4><<<grid, block, 0, s>>>(__VA_ARGS__);                        \
+      break;                                                                        \
+    case 16:                                                                        \
+      if (((BITS) & 15ull) == 0) KERNEL<16, 16><<<grid, block, 0, s>>>(__VA_ARGS__); \
+      else if (((BITS) & 7ull) == 0) KERNEL<16, 8><<<grid, block, 0, s>>>(__VA_ARGS__); \
+      else KERNEL<16, 4><<<grid, block, 0, s>>>(__VA_ARGS__);                       \
+      break;                                                                        \
+    default: return T4A_ERR_UNSUPPORTED_DTYPE;                                      \
   }
 
 int t4a_launch_fill_zero_view_any(const t4a_launch* launch, void* stream, void* out, int dtype,
@@ -489,7 +501,7 @@ int t4a_launch_fill_zero_view_any(const t4a_launch* launch, void* stream, void* 
   if (empty) return T4A_OK;
   if (out == nullptr) return T4A_ERR_NULL_ARGUMENT;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  T4A_ANY_LAUNCH(k_zero_any, out, layout, len)
+  T4A_ANY_LAUNCH(T4A_ANY_BITS(out), k_zero_any, out, layout, len)
   return runtime::check_launch();
 }
 
@@ -502,7 +514,7 @@ int t4a_launch_materialize_strided_any(const t4a_launch* launch, void* stream, v
   if (empty) return T4A_OK;
   if (dst == nullptr || src == nullptr) return T4A_ERR_NULL_ARGUMENT;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  T4A_ANY_LAUNCH(k_materialize_any, dst, src, src_layout, len)
+  T4A_ANY_LAUNCH(T4A_ANY_BITS(dst) | T4A_ANY_BITS(src), k_materialize_any, dst, src, src_layout, len)
   return runtime::check_launch();
 }
 
@@ -515,7 +527,7 @@ int t4a_launch_contiguous_to_view_any(const t4a_launch* launch, void* stream, vo
   if (empty) return T4A_OK;
   if (dst == nullptr || src == nullptr) return T4A_ERR_NULL_ARGUMENT;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  T4A_ANY_LAUNCH(k_to_view_any, dst, src, dst_layout, len)
+  T4A_ANY_LAUNCH(T4A_ANY_BITS(dst) | T4A_ANY_BITS(src), k_to_view_any, dst, src, dst_layout, len)
   return runtime::check_launch();
 }
 
@@ -531,7 +543,7 @@ int t4a_launch_strided_to_strided_any(const t4a_launch* launch, void* stream, vo
   if (empty) return T4A_OK;
   if (dst == nullptr || src == nullptr) return T4A_ERR_NULL_ARGUMENT;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  T4A_ANY_LAUNCH(k_strided_any, dst, src, src_layout, dst_layout, len)
+  T4A_ANY_LAUNCH(T4A_ANY_BITS(dst) | T4A_ANY_BITS(src), k_strided_any, dst, src, src_layout, dst_layout, len)
   return runtime::check_launch();
 }
 
@@ -548,7 +560,7 @@ int t4a_launch_broadcast_in_dim_any(const t4a_launch* launch, void* stream, void
   if (empty) return T4A_OK;
   if (out == nullptr || in == nullptr) return T4A_ERR_NULL_ARGUMENT;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  T4A_ANY_LAUNCH(k_broadcast_any, out, in, out_layout, in_layout, dims, out_len)
+  T4A_ANY_LAUNCH(T4A_ANY_BITS(out) | T4A_ANY_BITS(in), k_broadcast_any, out, in, out_layout, in_layout, dims, out_len)
   return runtime::check_launch();
 }
 #undef T4A_ANY_LAUNCH

@@ -369,6 +369,38 @@ def axis_values_any(values, device="cuda"):
     return abi.AxisValuesAny(len(values), 0, ctypes.c_void_p(arr.data_ptr())), arr
 
 
+def gather_plan_any(window_dims, offset_dims, start_index_map, slice_sizes, index_vector_dim, out_rank,
+                    device="cuda"):
+    """(t4a_cuda_gather_plan_any, keep-alive tensor): the gather maps in device memory."""
+    import torch
+    vals = list(window_dims) + list(offset_dims) + list(start_index_map) + list(slice_sizes)
+    arr = torch.tensor(vals or [0], dtype=torch.int64, device=device)
+    base, w, k = arr.data_ptr(), len(window_dims), len(start_index_map)
+    plan = abi.GatherPlanAny(len(slice_sizes), out_rank, index_vector_dim, w, k, 0, ctypes.c_void_p(base),
+                             ctypes.c_void_p(base + 8 * w), ctypes.c_void_p(base + 16 * w),
+                             ctypes.c_void_p(base + 16 * w + 8 * k))
+    return plan, arr
+
+
+def scatter_plan_any(window_dims, update_window_dims, scatter_dims, index_vector_dim, operand_rank, updates_rank,
+                     device="cuda"):
+    """(t4a_cuda_scatter_plan_any, keep-alive tensor): the scatter maps in device memory."""
+    import torch
+    vals = list(window_dims) + list(update_window_dims) + list(scatter_dims)
+    arr = torch.tensor(vals or [0], dtype=torch.int64, device=device)
+    base, w = arr.data_ptr(), len(window_dims)
+    plan = abi.ScatterPlanAny(operand_rank, updates_rank, index_vector_dim, w, len(scatter_dims), 0,
+                              ctypes.c_void_p(base), ctypes.c_void_p(base + 8 * w), ctypes.c_void_p(base + 16 * w))
+    return plan, arr
+
+
+def gather_scatter_any_geometry(elements):
+    launch = Launch()
+    check(lib().t4a_gather_scatter_any_geometry(ctypes.c_longlong(elements), ctypes.byref(launch)),
+          "gather_scatter_any_geometry")
+    return launch
+
+
 def movement_any_geometry(length):
     launch = Launch()
     check(lib().t4a_movement_any_geometry(ctypes.c_longlong(length), ctypes.byref(launch)), "movement_any_geometry")

@@ -51,6 +51,24 @@ class AxisValuesAny(ctypes.Structure):
     _fields_ = [("rank", ctypes.c_int), ("reserved", ctypes.c_int), ("values", ctypes.c_void_p)]
 
 
+class GatherPlanAny(ctypes.Structure):
+    """t4a_cuda_gather_plan_any: the gather maps in device memory (any rank)."""
+    _fields_ = [("operand_rank", ctypes.c_int), ("out_rank", ctypes.c_int),
+                ("index_vector_dim", ctypes.c_int), ("window_rank", ctypes.c_int),
+                ("start_map_len", ctypes.c_int), ("reserved", ctypes.c_int),
+                ("window_dims", ctypes.c_void_p), ("offset_dims", ctypes.c_void_p),
+                ("start_index_map", ctypes.c_void_p), ("slice_sizes", ctypes.c_void_p)]
+
+
+class ScatterPlanAny(ctypes.Structure):
+    """t4a_cuda_scatter_plan_any: the scatter maps in device memory (any rank)."""
+    _fields_ = [("operand_rank", ctypes.c_int), ("updates_rank", ctypes.c_int),
+                ("index_vector_dim", ctypes.c_int), ("window_rank", ctypes.c_int),
+                ("scatter_map_len", ctypes.c_int), ("reserved", ctypes.c_int),
+                ("window_dims", ctypes.c_void_p), ("update_window_dims", ctypes.c_void_p),
+                ("scatter_dims", ctypes.c_void_p)]
+
+
 class AxisValues(ctypes.Structure):
     _fields_ = [("rank", ctypes.c_int), ("reserved", ctypes.c_int), ("values", _I64x8)]
 
@@ -80,6 +98,8 @@ assert ctypes.sizeof(Layout) == 144 and Layout.offset.offset == 8 and Layout.str
 assert ctypes.sizeof(AxisValues) == 72
 assert ctypes.sizeof(GatherPlan) == 280 and GatherPlan.window_dims.offset == 24
 assert ctypes.sizeof(ScatterPlan) == 216 and ScatterPlan.window_dims.offset == 24
+assert ctypes.sizeof(GatherPlanAny) == 56 and GatherPlanAny.slice_sizes.offset == 48
+assert ctypes.sizeof(ScatterPlanAny) == 48 and ScatterPlanAny.scatter_dims.offset == 40
 assert ctypes.sizeof(TransposeConfig) == 16
 
 

@@ -553,3 +553,145 @@ def test_config4_full_size_properties(cuda):
     assert sel.shape[0] > 100_000
     row_err = (dest[hot] - sel.sum(dim=0)).abs()
     assert bool((row_err <= 1e-12 * sel.abs().sum(dim=0)).all())
+
+
+# ---- general-rank twins (`_any`) ------------------------------------------------
+
+ANY_ROUTES = ["launcher", "module", "refgeom"]
+
+
+def any_layout(l, pad=0):
+    """A by-value layout as t4a_cuda_layout_any, with `pad` trailing extent-1 axes."""
+    return t4.layout_any(l.extents_list() + [1] * pad, l.strides_list() + [0] * pad, l.offset)
+
+
+def any_launch(route, name, n, args):
+    import torch
+    if route == "launcher":
+        t4.launch_movement_any(name, t4.gather_scatter_any_geometry(n), t4.stream_handle(), *args)
+    elif n > 0:
+        if route == "module":
+            g = t4.gather_scatter_any_geometry(n)
+            geom = (tuple(g.grid), tuple(g.block), 0)
+        else:
+            geom = ((max(1, (n + 255) // 256),), (256,), 0)
+        module(OUR_CUBIN).launch("t4a_cuda_" + name + "_any", *geom, args)
+    torch.cuda.synchronize()
+
+
+def gather_any(case, route, pad):
+    """Case `case` through t4a_cuda_gather_any; `pad` extent-1 operand axes become
+    window axes of slice 1 on as many new trailing output axes (rank up to 4 + pad)."""
+    import torch
+    p = case.plan
+    w, k = p.window_rank, p.start_map_len
+    r, out_rank = p.operand_rank, p.out_rank
+    win = list(p.window_dims[:w]) + list(range(r, r + pad))
+    offs = list(p.offset_dims[:w]) + list(range(out_rank, out_rank + pad))
+    slices = list(p.slice_sizes[:r]) + [1] * pad
+    plan, keep_p = t4.gather_plan_any(win, offs, list(p.start_index_map[:k]), slices, p.index_vector_dim,
+                                      out_rank + pad)
+    ol, k1 = any_layout(case.out_l, pad)
+    al, k2 = any_layout(case.operand_l, pad)
+    il, k3 = any_layout(case.indices_l)
+    n = case.out_l.count()
+    d_op = dev(case.operand)
+    d_idx = dev(case.indices.view(np.uint8)) if case.indices.size else torch.zeros(16, dtype=torch.uint8,
+                                                                                     device="cuda")
+    d_out = sentinel(case.out_elems * case.es)
+    any_launch(route, "gather", n, [vptr(d_out), vptr(d_op), vptr(d_idx), ctypes.c_int(case.dtype),
+                                    ctypes.c_int(case.index_dtype), ol, al, il, plan, ctypes.c_longlong(n)])
+    del keep_p, k1, k2, k3
+    return take(d_out, case.out_elems * case.es)
+
+
+def scatter_any(case, route, pad):
+    """Case `case` through t4a_cuda_scatter_add_any; `pad` extent-1 destination axes
+    become window axes fed by as many new trailing extent-1 update axes."""
+    import torch
+    p = case.plan
+    w, k = p.window_rank, p.scatter_map_len
+    r, ur = p.operand_rank, p.updates_rank
+    plan, keep_p = t4.scatter_plan_any(list(p.window_dims[:w]) + list(range(r, r + pad)),
+                                       list(p.update_window_dims[:w]) + list(range(ur, ur + pad)),
+                                       list(p.scatter_dims[:k]), p.index_vector_dim, r + pad, ur + pad)
+    ol, k1 = any_layout(case.dest_l, pad)
+    il, k2 = any_layout(case.indices_l)
+    ul, k3 = any_layout(case.updates_l, pad)
+    n = case.updates_l.count()
+    d_out = sentinel(case.dest.nbytes)
+    d_out[:case.dest.nbytes] = dev(case.dest.view(np.uint8))
+    d_upd = dev(case.updates.view(np.uint8)) if case.updates.size else torch.zeros(16, dtype=torch.uint8,
+                                                                                     device="cuda")
+    d_idx = dev(case.indices.view(np.uint8)) if case.indices.size else torch.zeros(16, dtype=torch.uint8,
+                                                                                     device="cuda")
+    any_launch(route, "scatter_add", n, [vptr(d_out), vptr(d_idx), vptr(d_upd), ctypes.c_int(case.dtype),
+                                         ctypes.c_int(case.index_dtype), ol, il, ul, plan, ctypes.c_longlong(n)])
+    del keep_p, k1, k2, k3
+    return take(d_out, case.dest.nbytes).view(case.comp)
+
+
+@pytest.mark.parametrize("route", ANY_ROUTES)
+@pytest.mark.parametrize("dtype", [abi.BOOL, abi.F64, abi.C32, abi.C64])
+@pytest.mark.parametrize("index_dtype", [abi.I64, abi.F32])
+def test_gather_any_random_plans(cuda, route, dtype, index_dtype):
+    """The general-rank gather equals the oracle bit for bit on random plans, as given
+    (rank <= 4) and padded with extent-1 window axes to rank 9-12."""
+    rng = np.random.default_rng(3000 + 10 * dtype + index_dtype + 100 * ANY_ROUTES.index(route))
+    for i in range(12):
+        case = random_gather(rng, dtype, index_dtype)
+        want = case.oracle()
+        for pad in (0, 8):
+            got = gather_any(case, route, pad)
+            assert np.array_equal(want, got), (i, pad)
+
+
+@pytest.mark.parametrize("route", ANY_ROUTES)
+@pytest.mark.parametrize("dtype", [abi.F32, abi.F64, abi.C32, abi.C64])
+@pytest.mark.parametrize("index_dtype", [abi.I32, abi.F64])
+def test_scatter_add_any_random_plans(cuda, route, dtype, index_dtype):
+    """The general-rank scatter_add equals the oracle (within the atomics' rounding) on
+    random plans, including windows that do not fit, as given and padded to rank 9-11."""
+    rng = np.random.default_rng(4000 + 10 * dtype + index_dtype + 100 * ANY_ROUTES.index(route))
+    tol, atol = TOL[dtype]
+    for i in range(12):
+        case = random_scatter(rng, dtype, index_dtype)
+        want = case._oracle(case.dest, case.updates)
+        mag = case._oracle(np.abs(case.dest), np.abs(case.updates))
+        for pad in (0, 8):
+            got = scatter_any(case, route, pad)
+            ok = (got == want) | (np.abs(got - want) <= tol * mag + atol)
+            assert ok.all(), (i, pad, np.flatnonzero(~ok)[:8])
+
+
+def test_any_twins_on_config4_rows(cuda):
+    """BASELINE config 4's row gather and Zipf scatter_add (reduced row counts) through
+    the general-rank twins, against the fast entries."""
+    import torch
+    rng = np.random.default_rng(5)
+    rows, cols, n = 4096, 128, 20000
+    table = torch.from_numpy(rng.standard_normal((rows, cols)).astype(np.float32)).cuda()
+    gidx = torch.from_numpy(rng.integers(0, rows, n)).cuda()
+    want = t4.gather_rows(table, gidx)
+    plan, kp = t4.gather_plan_any([0], [0], [1], [cols, 1], 1, 2)
+    ol, k1 = t4.layout_any([cols, n], [1, cols])
+    al, k2 = t4.layout_any([cols, rows], [1, cols])
+    il, k3 = t4.layout_any([n, 1])
+    out = torch.empty((n, cols), dtype=torch.float32, device="cuda")
+    any_launch("launcher", "gather", n * cols, [vptr(out), vptr(table), vptr(gidx), ctypes.c_int(abi.F32),
+                                                ctypes.c_int(abi.I64), ol, al, il, plan, ctypes.c_longlong(n * cols)])
+    assert torch.equal(out, want)
+    dest = torch.from_numpy(rng.standard_normal((rows, cols))).cuda()
+    sidx = torch.from_numpy(zipf_rows(rng, n, rows)).cuda()
+    upd = torch.from_numpy(rng.standard_normal((n, cols))).cuda()
+    want = t4.scatter_add_rows(dest.clone(), sidx, upd)
+    splan_any, kq = t4.scatter_plan_any([0], [0], [1], 1, 2, 2)
+    dl, k4 = t4.layout_any([cols, rows], [1, cols])
+    sl, k5 = t4.layout_any([n, 1])
+    ul, k6 = t4.layout_any([cols, n], [1, cols])
+    got = dest.clone()
+    any_launch("launcher", "scatter_add", n * cols, [vptr(got), vptr(sidx), vptr(upd), ctypes.c_int(abi.F64),
+                                                     ctypes.c_int(abi.I64), dl, sl, ul, splan_any,
+                                                     ctypes.c_longlong(n * cols)])
+    assert torch.allclose(got, want, rtol=0, atol=1e-12 * float(want.abs().max()))
+    del kp, kq, k1, k2, k3, k4, k5, k6

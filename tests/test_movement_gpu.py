@@ -57,11 +57,13 @@ def span_of(l):
     return hi + 1
 
 
-def gpu_copy(route, dtype, src_bytes, src_l, dst_l, dst_nbytes, module=None):
+def gpu_copy(route, dtype, src_bytes, src_l, dst_l, dst_nbytes, module=None, base=0):
+    """strided_to_strided by `route`; `base` shifts both device buffers by that many
+    bytes from the allocation's (256-byte aligned) start."""
     import torch
     es = ESIZE[dtype]
-    src = dev(src_bytes)
-    dst = sentinel(dst_nbytes)
+    src = dev(np.concatenate([np.zeros(base, np.uint8), src_bytes]))[base:]
+    dst = sentinel(dst_nbytes + base)[base:]
     src_len, dst_len = len(src_bytes) // es, dst_nbytes // es
     n = src_l.count()
     if route == "launcher":
@@ -310,12 +312,21 @@ ANY_ROUTES = ["launcher", "module", "refgeom"]
 
 
 @pytest.mark.parametrize("route", ANY_ROUTES)
-@pytest.mark.parametrize("dtype", [abi.F32, abi.C64, abi.BOOL])
-def test_any_twins_of_the_view_copies(cuda, route, dtype):
+@pytest.mark.parametrize("dtype,base", [(abi.F32, 0), (abi.C64, 0), (abi.BOOL, 0), (abi.C32, 4), (abi.C64, 8)])
+def test_any_twins_of_the_view_copies(cuda, route, dtype, base):
     """materialize_strided, contiguous_to_view, strided_to_strided and fill_zero_view
     over rank-10 layouts (random storage orders, a reversed axis, offsets), against the
-    index arithmetic, with sentinel-guarded destinations."""
+    index arithmetic, with sentinel-guarded destinations.  `base` shifts every buffer
+    off the allocation's alignment: complex64 is 4-byte and complex128 8-byte aligned in
+    the ABI."""
+    import torch
     es = ESIZE[dtype]
+
+    def dev(buf):
+        return globals()["dev"](np.concatenate([np.zeros(base, np.uint8), buf]))[base:]
+
+    def sentinel(nbytes):
+        return globals()["sentinel"](nbytes + base)[base:]
     rng = np.random.default_rng(int(dtype) * 7 + ANY_ROUTES.index(route))
     ext = ANY_EXTENTS
     n = int(np.prod(ext))
@@ -384,3 +395,36 @@ def test_any_twin_of_broadcast_in_dim(cuda, route, dtype):
                                               ctypes.c_longlong(n)])
     assert np.array_equal(take(d_dst, n * es).reshape(n, es), src.reshape(total, es)[idx])
     del k1, k2, k3
+
+
+@pytest.mark.parametrize("route", ["launcher", "module", "module-refgeom"])
+def test_complex64_bases_off_8_bytes(cuda, route):
+    """complex64 buffers 4 bytes off an 8-byte boundary (legal: the ABI's complex64 is
+    4-byte aligned) through the by-value entries: permutations, a reversal and fills."""
+    import torch
+    rng = np.random.default_rng(77)
+    es = ESIZE[abi.C32]
+    mod = Module(OUR_CUBIN) if route != "launcher" else None
+    for shape, perm in [((64, 48), (1, 0)), ((6, 5, 7), (2, 0, 1)), ((300,), (0,))]:
+        src_l, out_shape = permuted_view(shape, perm)
+        n = src_l.count()
+        src = rng.integers(0, 256, size=n * es, dtype=np.uint8)
+        dst_l = abi.layout(src_l.extents_list())
+        want = oracle_copy(abi.C32, src, src_l, dst_l, n * es)
+        got = gpu_copy(route, abi.C32, src, src_l, dst_l, n * es, module=mod, base=4)
+        assert np.array_equal(want, got), (shape, perm)
+    # fill_zero_view of every other element of a 4-off buffer
+    n = 257
+    view = abi.layout([n], [2], 1)
+    d = sentinel(2 * n * es + 4)[4:]
+    if route == "launcher":
+        launch = t4.Launch()
+        t4.check(t4.lib().t4a_plan_fill_zero_view(abi.C32, ctypes.byref(view), 2 * n, ctypes.byref(launch)))
+        t4.check(t4.lib().t4a_launch_fill_zero_view(ctypes.byref(launch), t4.stream_handle(),
+                                                    ctypes.c_void_p(d.data_ptr()), abi.C32, view, n))
+    else:
+        mod.launch("t4a_cuda_fill_zero_view", (2,), (256,), 0,
+                   [ctypes.c_void_p(d.data_ptr()), ctypes.c_int(abi.C32), view, ctypes.c_longlong(n)])
+    torch.cuda.synchronize()
+    got = take(d, 2 * n * es).reshape(2 * n, es)
+    assert (got[1::2] == 0).all() and (got[0::2] == SENTINEL).all()

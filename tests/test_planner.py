@@ -341,3 +341,61 @@ def test_rrqr_any_geometry_and_host_checks():
                                           ctypes.c_double(0.0)) == 66
     empty = t4.rrqr_any_geometry(0, True)
     assert lib.t4a_launch_extract_r_any(ctypes.byref(empty), None, p, p, abi.F64, mat, mat) == 0
+
+
+def test_gather_scatter_any_geometry_and_host_checks():
+    g = t4.gather_scatter_any_geometry(1000)
+    assert (g.block[0], g.grid[0]) == (256, 4)
+    assert t4.gather_scatter_any_geometry(10 ** 12).grid[0] == 148 * 64
+    assert t4.gather_scatter_any_geometry(0).grid[0] == 0
+    with pytest.raises(t4.T4AError) as err:
+        t4.gather_scatter_any_geometry(-5)
+    assert err.value.status == 4
+    lib = t4.lib()
+    lp = ctypes.byref(t4.gather_scatter_any_geometry(10))
+    p = ctypes.c_void_p(0x3000)
+    a = ctypes.c_void_p(0x1000)
+
+    def lay(rank, reserved=0, arrays=True):
+        return abi.LayoutAny(rank, reserved, 0, a if arrays else None, a if arrays else None)
+
+    def gplan(operand_rank, out_rank, ivd, window_rank, start_len, reserved=0, arrays=True):
+        x = a if arrays else None
+        return abi.GatherPlanAny(operand_rank, out_rank, ivd, window_rank, start_len, reserved, x, x, x, x)
+
+    def splan(operand_rank, updates_rank, ivd, window_rank, map_len, reserved=0):
+        return abi.ScatterPlanAny(operand_rank, updates_rank, ivd, window_rank, map_len, reserved, a, a, a)
+
+    n = ctypes.c_longlong(10)
+    # Row gather: operand [cols, rows], out [cols, n], indices [n, 1] (vector axis 1).
+    good = (lay(2), lay(2), lay(2), gplan(2, 2, 1, 1, 1))
+    assert lib.t4a_launch_gather_any(lp, None, p, p, p, abi.F32, abi.I64, *good, ctypes.c_longlong(0)) == 0
+    assert lib.t4a_launch_gather_any(lp, None, p, p, p, 99, abi.I64, *good, n) == 9
+    assert lib.t4a_launch_gather_any(lp, None, p, p, p, abi.F32, abi.C32, *good, n) == 9
+    assert lib.t4a_launch_gather_any(lp, None, p, p, p, abi.F32, abi.I64, *good, ctypes.c_longlong(-1)) == 4
+    assert lib.t4a_launch_gather_any(lp, None, p, p, p, abi.F32, abi.I64, lay(2, 3), lay(2), lay(2),
+                                     gplan(2, 2, 1, 1, 1), n) == 1
+    assert lib.t4a_launch_gather_any(lp, None, p, p, p, abi.F32, abi.I64, lay(2), lay(2, arrays=False), lay(2),
+                                     gplan(2, 2, 1, 1, 1), n) == 66
+    assert lib.t4a_launch_gather_any(lp, None, p, p, p, abi.F32, abi.I64, lay(2), lay(2), lay(2),
+                                     gplan(3, 2, 1, 1, 1), n) == 2  # operand rank differs from the plan's
+    assert lib.t4a_launch_gather_any(lp, None, p, p, p, abi.F32, abi.I64, lay(2), lay(2), lay(2),
+                                     gplan(2, 2, 1, 1, 1, reserved=1), n) == 1
+    assert lib.t4a_launch_gather_any(lp, None, p, p, p, abi.F32, abi.I64, lay(2), lay(2), lay(2),
+                                     gplan(2, 2, 1, 1, 1, arrays=False), n) == 66
+    assert lib.t4a_launch_gather_any(lp, None, p, p, p, abi.F32, abi.I64, lay(2), lay(2), lay(2),
+                                     gplan(2, 2, 3, 1, 1), n) == 13  # index_vector_dim past the indices
+    assert lib.t4a_launch_gather_any(lp, None, p, p, p, abi.F32, abi.I64, lay(2), lay(2), lay(3),
+                                     gplan(2, 2, 1, 1, 1), n) == 24  # index rank does not match
+    assert lib.t4a_launch_gather_any(lp, None, None, p, p, abi.F32, abi.I64, *good, n) == 66
+    # Row scatter: destination [cols, rows], updates [cols, n], indices [n, 1].
+    sgood = (lay(2), lay(2), lay(2), splan(2, 2, 1, 1, 1))
+    assert lib.t4a_launch_scatter_add_any(lp, None, p, p, p, abi.F64, abi.I32, *sgood, ctypes.c_longlong(0)) == 0
+    assert lib.t4a_launch_scatter_add_any(lp, None, p, p, p, abi.I32, abi.I32, *sgood, n) == 9
+    assert lib.t4a_launch_scatter_add_any(lp, None, p, p, p, abi.F64, abi.I32, lay(2), lay(2), lay(2),
+                                          splan(2, 3, 1, 1, 1), n) == 2
+    assert lib.t4a_launch_scatter_add_any(lp, None, p, p, p, abi.F64, abi.I32, lay(2), lay(3), lay(2),
+                                          splan(2, 2, 1, 1, 1), n) == 24
+    assert lib.t4a_launch_scatter_add_any(lp, None, p, p, p, abi.F64, abi.I32, lay(2), lay(2), lay(2),
+                                          splan(2, 2, 1, 3, 1), n) == 1  # window wider than the ranks
+    assert lib.t4a_launch_scatter_add_any(None, None, p, p, p, abi.F64, abi.I32, *sgood, n) == 66
