@@ -416,6 +416,27 @@ int t4a_launch_extract_r_any(const t4a_launch* launch, void* stream, const void*
 int t4a_launch_prefix_rank_any(const t4a_launch* launch, void* stream, const void* r, void* rank, void* status,
                                int dtype, t4a_cuda_layout_any r_layout, double rtol, double atol);
 
+/* RRQR epilogue: the shifted identity Q formation starts from (reference
+ * linalg_aux.cu:506, :960; plan_identity_shifted src/lib.rs:2158; module symbols
+ * t4a_cuda_identity_shifted / _any in linalg_aux.cubin): out(i, j, ..) = 1 where
+ * i == start + j, else 0, for F32/F64/I32/I64/C32/C64.  The `_any` launcher takes a
+ * geometry from t4a_rrqr_any_geometry(elements, 1). */
+int t4a_plan_identity_shifted(int dtype, const t4a_cuda_layout* out, long long out_len, long long start,
+                              t4a_launch* launch);
+int t4a_launch_identity_shifted(const t4a_launch* launch, void* stream, void* out, int dtype,
+                                t4a_cuda_layout out_layout, long long start);
+int t4a_launch_identity_shifted_any(const t4a_launch* launch, void* stream, void* out, int dtype,
+                                    t4a_cuda_layout_any out_layout, long long start);
+/* No single counterpart in the reference (its bench drives the same steps,
+ * examples/bench_kernels.rs:2560-2590): Q formation after a factorization,
+ * q = identity_shifted(start 0), then apply_reflector for step = k-1 .. 0 over all k
+ * columns of q (k = q's columns) with the reflectors of `work` and `coeff`.  Every
+ * step is planned before the first launch, so an invalid argument launches nothing.
+ * Results equal that loop of primitives bit for bit. */
+int t4a_rrqr_form_q(void* stream, int dtype, const void* work, const t4a_cuda_layout* work_layout,
+                    long long work_len, const void* coeff, const t4a_cuda_layout* coeff_layout, long long coeff_len,
+                    void* q, const t4a_cuda_layout* q_layout, long long q_len);
+
 /* No single counterpart in the reference (its loop lives with the caller, bench
  * examples/bench_kernels.rs:2390-2623): `steps` steps of column_norms, select_pivot,
  * swap_columns, reflector and apply_reflector over the trailing columns, for one

@@ -67,6 +67,7 @@ def _declare(l):
         "t4a_oracle_reflector": (I, [I, P, P, L, L, LL]),
         "t4a_oracle_apply_reflector": (I, [I, P, P, P, L, L, L, LL, LL, LL, I]),
         "t4a_oracle_extract_r": (I, [I, P, P, L, L]),
+        "t4a_oracle_identity_shifted": (I, [I, P, L, LL]),
         "t4a_oracle_prefix_rank": (I, [I, P, LP, LP, L, D, D]),
         "t4a_oracle_rrqr_f64": (LL, [P, LL, LL, LL, LP, P, D, D, I]),
     }

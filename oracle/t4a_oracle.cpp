@@ -1093,6 +1093,30 @@ int t4a_oracle_apply_reflector(int dtype, const void* packed, void* target, cons
   }
 }
 
+// Restates linalg_aux.cu:200-211: the element at flat position f (axis 0 fastest) holds
+// one exactly when its row equals start + its column.
+int t4a_oracle_identity_shifted(int dtype, void* out, const t4a_cuda_layout* l, long long start) {
+  const int es = dtype_size(dtype);
+  if (!es || l->rank < 2 || dtype == T4A_CUDA_BOOL) return -1;
+  const long long len = element_count(*l);
+  for (long long f = 0; f < len; ++f) {
+    const long long row = f % l->extents[0];
+    const long long col = (f / l->extents[0]) % l->extents[1];
+    const long long batch = f / (l->extents[0] * l->extents[1]);
+    char* dst = (char*)out + (l->offset + row * l->strides[0] + col * l->strides[1] + batch_offset(batch, *l, 2)) * es;
+    std::memset(dst, 0, es);
+    if (row != start + col) continue;
+    switch (dtype) {
+      case T4A_CUDA_F32: case T4A_CUDA_C32: { const float one = 1.0f; std::memcpy(dst, &one, 4); break; }
+      case T4A_CUDA_F64: case T4A_CUDA_C64: { const double one = 1.0; std::memcpy(dst, &one, 8); break; }
+      case T4A_CUDA_I32: { const int one = 1; std::memcpy(dst, &one, 4); break; }
+      case T4A_CUDA_I64: { const long long one = 1; std::memcpy(dst, &one, 8); break; }
+      default: return -1;
+    }
+  }
+  return 0;
+}
+
 int t4a_oracle_extract_r(int dtype, const void* work, void* r, const t4a_cuda_layout* w,
                          const t4a_cuda_layout* rl) {
   const int es = dtype_size(dtype);

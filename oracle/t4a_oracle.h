@@ -104,6 +104,10 @@ int t4a_oracle_extract_r(int dtype, const void* work, void* r,
 int t4a_oracle_prefix_rank(int dtype, const void* r, long long* rank, long long* status,
                            const t4a_cuda_layout* r_layout, double rtol, double atol);
 
+/* identity_shifted (reference cuda/src/linalg_aux.cu:200-211): out(i, j, ..) = 1
+ * where i == start + j, else 0, over every element of a rank >= 2 layout. */
+int t4a_oracle_identity_shifted(int dtype, void* out, const t4a_cuda_layout* out_layout, long long start);
+
 /* Whole tall-skinny RRQR loop as the reference bench drives it
  * (examples/bench_kernels.rs:2390-2623): work is an m x n column-major F64
  * matrix, updated in place; perm/coeff receive n entries; returns the rank. */

@@ -4,7 +4,7 @@
 
 Objects go to <repo>/_build/; the library and the modules to
 t4a-cuda-kernels_b200/t4a_b200/lib/.  The modules are one cubin per kernel family
-(reduce, movement, gather_scatter, rrqr), like the reference's per-file modules,
+(reduce, movement, gather_scatter, rrqr, linalg_aux), like the reference's per-file modules,
 exporting the reference's `extern "C" __global__` symbols.  A source is rebuilt when it, or any header
 of csrc/ or include/, is newer than its object.
 """
@@ -24,7 +24,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC = os.environ.get("NVCC", "nvcc")
 COMMON = ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC", "-I", os.path.join(ROOT, "include")]
 # Translation units that export the reference's __global__ symbols (the module).
-MODULE_TUS = ["reduce_abi.cu", "movement_abi.cu", "gather_scatter_abi.cu", "rrqr_abi.cu"]
+MODULE_TUS = ["reduce_abi.cu", "movement_abi.cu", "gather_scatter_abi.cu", "rrqr_abi.cu", "linalg_aux_abi.cu"]
 
 
 def headers(src=None):

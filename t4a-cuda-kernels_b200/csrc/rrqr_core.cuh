@@ -374,5 +374,22 @@ __device__ __forceinline__ void extract_r_elem(const T* w, T* r, const L& wl, co
   r[rl.offset + row * rl.strides[0] + column * rl.strides[1] + batch_offset(batch, rl, 2)] = value;
 }
 
+template <typename T> __device__ __forceinline__ T unit_of() { return T(1); }
+template <> __device__ __forceinline__ c32 unit_of<c32>() { return {1.0f, 0.0f}; }
+template <> __device__ __forceinline__ c64 unit_of<c64>() { return {1.0, 0.0}; }
+
+// out(i, j, batch) = 1 where i == start + j, else 0 (reference linalg_aux.cu:200-211):
+// the identity that Q formation starts from, shifted down by `start` rows.
+template <typename T, typename L>
+__device__ __forceinline__ void identity_shifted_elem(T* out, const L& l, long long start, long long flat) {
+  const long long row = flat % l.extents[0];
+  const long long column = (flat / l.extents[0]) % l.extents[1];
+  const long long batch = flat / (l.extents[0] * l.extents[1]);
+  T value;
+  memset(&value, 0, sizeof(T));
+  if (row == start + column) value = unit_of<T>();
+  out[l.offset + row * l.strides[0] + column * l.strides[1] + batch_offset(batch, l, 2)] = value;
+}
+
 }  // namespace rrqr
 }  // namespace t4a

@@ -186,6 +186,28 @@ __device__ __forceinline__ void prefix_rank_entry(const void* r, void* rank, voi
   }
 }
 
+template <typename T, typename L>
+__device__ __forceinline__ void identity_walk(void* out, const L& l, long long start) {
+  long long len = 1;
+  for (int ax = 0; ax < l.rank; ++ax) len *= l.extents[ax];
+  for (long long f = flat_begin(); f < len; f += flat_stride())
+    identity_shifted_elem<T>(static_cast<T*>(out), l, start, f);
+}
+
+template <typename L>
+__device__ __forceinline__ void identity_entry(void* out, int dtype, const L& l, long long start) {
+  if (l.rank < 2) return;
+  switch (dtype) {
+    case T4A_CUDA_F32: identity_walk<float>(out, l, start); break;
+    case T4A_CUDA_F64: identity_walk<double>(out, l, start); break;
+    case T4A_CUDA_I32: identity_walk<int>(out, l, start); break;
+    case T4A_CUDA_I64: identity_walk<long long>(out, l, start); break;
+    case T4A_CUDA_C32: identity_walk<c32>(out, l, start); break;
+    case T4A_CUDA_C64: identity_walk<c64>(out, l, start); break;
+    default: break;
+  }
+}
+
 }  // namespace entry
 }  // namespace rrqr
 }  // namespace t4a

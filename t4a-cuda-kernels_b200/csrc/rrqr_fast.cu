@@ -134,6 +134,14 @@ __global__ void __launch_bounds__(kTaskThreads) k_prefix_rank_any(const void* r,
   entry::prefix_rank_entry(r, rank, status, dtype, rl, rtol, atol);
 }
 
+__global__ void __launch_bounds__(kFlatThreads) k_identity(void* out, int dtype, t4a_cuda_layout l, long long start) {
+  entry::identity_entry(out, dtype, l, start);
+}
+__global__ void __launch_bounds__(kFlatThreads) k_identity_any(void* out, int dtype, t4a_cuda_layout_any l,
+                                                               long long start) {
+  entry::identity_entry(out, dtype, l, start);
+}
+
 // Host checks of a general-rank layout that need no device access.
 int check_rrqr_any(const t4a_cuda_layout_any& l, int min_rank) {
   if (l.rank < min_rank || l.reserved != 0) return T4A_ERR_RANK_OUT_OF_RANGE;
@@ -788,6 +796,76 @@ int t4a_rrqr(void* stream, int dtype, void* work, const t4a_cuda_layout* work_la
                              static_cast<double*>(coeff), piv, st, ws);
   return run_fused<float>(s, static_cast<float*>(work) + work_layout->offset, m, n, ld, steps, perm,
                           static_cast<float*>(coeff), piv, st, ws);
+}
+
+// plan_identity_shifted (src/lib.rs:2158): out(i, j, ..) = (i == start + j).
+int t4a_plan_identity_shifted(int dtype, const t4a_cuda_layout* out, long long out_len, long long start,
+                              t4a_launch* launch) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  T4A_TRY(check_layout(out));
+  T4A_TRY(check_numeric(dtype));
+  T4A_TRY(require_destination(*out));
+  T4A_TRY(require_matrix(*out));
+  if (start < 0) return T4A_ERR_NEGATIVE_COUNT;
+  long long end = 0;
+  if (__builtin_add_overflow(start, out->extents[1], &end)) return T4A_ERR_OVERFLOW;
+  long long len = 0;
+  T4A_TRY(element_count(*out, &len));
+  T4A_TRY(check_span(*out, out_len, dtype_size(dtype)));
+  return flat_geometry(len, launch);
+}
+
+int t4a_launch_identity_shifted(const t4a_launch* launch, void* stream, void* out, int dtype,
+                                t4a_cuda_layout out_layout, long long start) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  T4A_TRY(check_numeric(dtype));
+  if (out_layout.rank < 2 || out_layout.rank > T4A_CUDA_MAX_RANK) return T4A_ERR_RANK_OUT_OF_RANGE;
+  if (launch_empty(launch)) return T4A_OK;
+  if (out == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  k_identity<<<grid_of_launch(launch), block_of_launch(launch), 0, static_cast<cudaStream_t>(stream)>>>(
+      out, dtype, out_layout, start);
+  return runtime::check_launch();
+}
+
+int t4a_launch_identity_shifted_any(const t4a_launch* launch, void* stream, void* out, int dtype,
+                                    t4a_cuda_layout_any out_layout, long long start) {
+  if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  T4A_TRY(check_numeric(dtype));
+  T4A_TRY(check_rrqr_any(out_layout, 2));
+  if (launch_empty(launch)) return T4A_OK;
+  if (out == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  k_identity_any<<<grid_of_launch(launch), block_of_launch(launch), 0, static_cast<cudaStream_t>(stream)>>>(
+      out, dtype, out_layout, start);
+  return runtime::check_launch();
+}
+
+// Q formation of the RRQR epilogue as the reference bench drives it
+// (examples/bench_kernels.rs:2560-2590): q = identity_shifted(start 0), then
+// apply_reflector for step = k-1 .. 0 over all k columns of q, the reflectors read from
+// the factorized `work` and `coeff`; k = the columns of q.
+int t4a_rrqr_form_q(void* stream, int dtype, const void* work, const t4a_cuda_layout* work_layout,
+                    long long work_len, const void* coeff, const t4a_cuda_layout* coeff_layout, long long coeff_len,
+                    void* q, const t4a_cuda_layout* q_layout, long long q_len) {
+  if (work_layout == nullptr || coeff_layout == nullptr || q_layout == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  T4A_TRY(check_algebra(dtype));
+  t4a_launch l;
+  T4A_TRY(t4a_plan_identity_shifted(dtype, q_layout, q_len, 0, &l));
+  const long long k = q_layout->extents[1];
+  for (long long step = k - 1; step >= 0; --step) {
+    t4a_launch a;
+    T4A_TRY(t4a_plan_apply_reflector(dtype, work_layout, work_len, q_layout, q_len, coeff_layout, coeff_len, step, 0,
+                                     k, &a));
+  }
+  if (q == nullptr || (k > 0 && (work == nullptr || coeff == nullptr))) return T4A_ERR_NULL_ARGUMENT;
+  T4A_TRY(t4a_launch_identity_shifted(&l, stream, q, dtype, *q_layout, 0));
+  for (long long step = k - 1; step >= 0; --step) {
+    t4a_launch a;
+    T4A_TRY(t4a_plan_apply_reflector(dtype, work_layout, work_len, q_layout, q_len, coeff_layout, coeff_len, step, 0,
+                                     k, &a));
+    T4A_TRY(t4a_launch_apply_reflector(&a, stream, work, q, coeff, dtype, *work_layout, *q_layout, *coeff_layout,
+                                       step, 0, k));
+  }
+  return T4A_OK;
 }
 
 }  // extern "C"

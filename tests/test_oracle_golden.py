@@ -7,6 +7,9 @@ regenerated bit for bit (tests/golden/reduce_inputs.py).  The oracle must reprod
 every plan, every NaN-free partials buffer and every final output; NaN payloads are
 not part of the ABI contract, so a final that differs only in the payload of a NaN
 component passes.
+
+identity_shifted is pinned to the reference's own test cases
+(tests/gpu_linalg_aux.rs:1153-1185) restated as expectations.
 """
 import os
 
@@ -49,3 +52,39 @@ def test_oracle_reproduces_golden(shape):
     assert not partial_bad, partial_bad[:5]
     assert not bad, bad[:5]
     assert exact > 0
+
+
+# identity_shifted: the reference's own cases (tests/gpu_linalg_aux.rs:1153-1185, its
+# expectation: the element at flat position f of the layout holds one exactly when
+# row(f) == start + column(f)), written into a sentinel-filled buffer so that the
+# holes of the strided layout must stay untouched.
+@pytest.mark.parametrize("dtype,extents,strides,offset,start", [
+    ("F64", [4, 3], [1, 5], 1, 0),
+    ("F64", [3, 2], [1, 3], 0, 2),
+    ("F32", [3, 2], [1, 3], 0, 2),
+    ("I32", [3, 2], [1, 3], 0, 0),
+    ("I64", [3, 2], [1, 3], 0, 1),
+    ("C32", [5, 3, 2], [1, 5, 15], 0, 1),
+    ("C64", [4, 4, 3], [2, 8, 40], 1, 0),
+])
+def test_oracle_identity_shifted_reference_cases(dtype, extents, strides, offset, start):
+    import ctypes
+    from t4a_b200 import abi
+    tag = getattr(abi, dtype)
+    npdt = {"F32": np.float32, "F64": np.float64, "I32": np.int32, "I64": np.int64, "C32": np.complex64,
+            "C64": np.complex128}[dtype]
+    span = offset + sum((e - 1) * s for e, s in zip(extents, strides)) + 1
+    sentinel = np.full(span, 7, dtype=npdt)
+    want = sentinel.copy()
+    count = int(np.prod(extents))
+    for f in range(count):
+        row, col, rest = f % extents[0], (f // extents[0]) % extents[1], f // (extents[0] * extents[1])
+        at = offset + row * strides[0] + col * strides[1]
+        for e, s in zip(extents[2:], strides[2:]):
+            at += (rest % e) * s
+            rest //= e
+        want[at] = 1 if row == start + col else 0
+    got = sentinel.copy()
+    lay = abi.layout(extents, strides, offset)
+    assert oracle.lib().t4a_oracle_identity_shifted(tag, oracle.ptr(got), ctypes.byref(lay), start) == 0
+    assert np.array_equal(got.view(np.uint8), want.view(np.uint8))

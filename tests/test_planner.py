@@ -399,3 +399,29 @@ def test_gather_scatter_any_geometry_and_host_checks():
     assert lib.t4a_launch_scatter_add_any(lp, None, p, p, p, abi.F64, abi.I32, lay(2), lay(2), lay(2),
                                           splan(2, 2, 1, 3, 1), n) == 1  # window wider than the ranks
     assert lib.t4a_launch_scatter_add_any(None, None, p, p, p, abi.F64, abi.I32, *sgood, n) == 66
+
+
+def test_plan_identity_shifted_validation():
+    """plan_identity_shifted (reference src/lib.rs:2158): numeric dtypes, a matrix
+    destination without aliasing, start >= 0 and a span that covers the layout."""
+    lib = t4.lib()
+    launch = t4.Launch()
+    lp = ctypes.byref(launch)
+    lay = abi.layout([4, 3], [1, 5], 1)
+    assert lib.t4a_plan_identity_shifted(abi.F64, ctypes.byref(lay), 15, 0, lp) == 0
+    assert (launch.grid[0], launch.block[0]) == (1, 256)
+    assert lib.t4a_plan_identity_shifted(abi.F64, ctypes.byref(lay), 14, 0, lp) == 7  # span too short
+    assert lib.t4a_plan_identity_shifted(abi.F64, ctypes.byref(lay), 15, -1, lp) == 4
+    assert lib.t4a_plan_identity_shifted(abi.BOOL, ctypes.byref(lay), 15, 0, lp) == 9
+    assert lib.t4a_plan_identity_shifted(abi.F64, ctypes.byref(abi.layout([4])), 4, 0, lp) == 1
+    assert lib.t4a_plan_identity_shifted(abi.F64, ctypes.byref(abi.layout([4, 3], [1, 0])), 4, 0, lp) == 8
+    assert lib.t4a_plan_identity_shifted(abi.I32, ctypes.byref(abi.layout([4, 3])), 12, 2 ** 63 - 2, lp) == 5
+    assert lib.t4a_plan_identity_shifted(abi.C64, ctypes.byref(abi.layout([0, 3], [1, 4])), 0, 0, lp) == 0
+    assert launch.grid[0] == 0
+    # Q formation plans every step before launching: a bad coefficient span launches nothing.
+    wl, ql, cl = abi.layout([10, 4]), abi.layout([10, 4]), abi.layout([4])
+    p = ctypes.c_void_p(0x1000)
+    assert lib.t4a_rrqr_form_q(None, abi.F64, p, ctypes.byref(wl), 40, p, ctypes.byref(cl), 3, p,
+                               ctypes.byref(ql), 40) == 7
+    assert lib.t4a_rrqr_form_q(None, abi.I32, p, ctypes.byref(wl), 40, p, ctypes.byref(cl), 4, p,
+                               ctypes.byref(ql), 40) == 9

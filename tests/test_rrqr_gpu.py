@@ -29,6 +29,8 @@ pytestmark = pytest.mark.gpu
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 OUR_CUBIN = os.path.join(ROOT, "t4a-cuda-kernels_b200", "t4a_b200", "lib", "rrqr.cubin")
 REF_CUBIN = os.path.join(ROOT, "oracle", "_ref", "rrqr.cubin")
+OUR_LINALG = os.path.join(ROOT, "t4a-cuda-kernels_b200", "t4a_b200", "lib", "linalg_aux.cubin")
+REF_LINALG = os.path.join(ROOT, "oracle", "_ref", "linalg_aux.cubin")
 SENTINEL, GUARD = 0xCD, 256
 THREADS = os.cpu_count() or 4
 NP = {abi.F32: np.float32, abi.F64: np.float64, abi.C32: np.complex64, abi.C64: np.complex128,
@@ -615,3 +617,112 @@ def test_any_twins_match_the_fast_primitives(cuda, mode, dtype):
             assert np.array_equal(np.asarray(a).view(np.uint8), np.asarray(b).view(np.uint8)), name
         else:
             assert same(dtype, a, b), name
+
+
+# ---- RRQR epilogue: identity_shifted and Q formation ---------------------------------
+
+IDENTITY_CASES = [  # the reference's own cases (tests/gpu_linalg_aux.rs:1153-1185), then batched ones
+    (abi.F64, [4, 3], [1, 5], 1, 0), (abi.F64, [3, 2], [1, 3], 0, 2), (abi.F32, [3, 2], [1, 3], 0, 2),
+    (abi.I32, [3, 2], [1, 3], 0, 0), (abi.I64, [3, 2], [1, 3], 0, 1), (abi.C32, [5, 3, 2], [1, 5, 15], 0, 1),
+    (abi.C64, [4, 4, 3], [2, 8, 40], 1, 0), (abi.F64, [1000, 300], [1, 1003], 5, 0),
+]
+
+
+@pytest.mark.parametrize("route", ["launcher", "module", "module-refgeom", "reference", "any-launcher", "any-module"])
+def test_identity_shifted(cuda, route):
+    """Every route writes the oracle's shifted identity bit for bit and leaves the
+    strided layout's holes untouched; `_any` routes run the layouts padded to rank 10."""
+    import torch
+    for dtype, ext, st, off, start in IDENTITY_CASES:
+        es = np.dtype(NP[dtype]).itemsize
+        span = off + sum((e - 1) * x for e, x in zip(ext, st)) + 1
+        lay = abi.layout(ext, st, off)
+        want = np.full(span, 7, NP[dtype])
+        assert oracle.lib().t4a_oracle_identity_shifted(dtype, oracle.ptr(want), ctypes.byref(lay), start) == 0
+        d = dev(np.full(span, 7, NP[dtype]))
+        count = int(np.prod(ext))
+        args = [vp(d), ctypes.c_int(dtype), lay, ctypes.c_longlong(start)]
+        if route == "launcher":
+            t4.launch_rrqr("identity_shifted", t4.plan_rrqr("identity_shifted", dtype, lay, span, start),
+                           t4.stream_handle(), *args)
+        elif route in ("module", "module-refgeom", "reference"):
+            plan = t4.plan_rrqr("identity_shifted", dtype, lay, span, start)
+            geom = (tuple(plan.grid), tuple(plan.block), 0) if route == "module" else flat(count)
+            module(REF_LINALG if route == "reference" else OUR_LINALG).launch("t4a_cuda_identity_shifted", *geom,
+                                                                               args)
+        else:
+            pad = 10 - len(ext)
+            la, keep = t4.layout_any(ext + [1] * pad, st + [0] * pad, off)
+            g = t4.rrqr_any_geometry(count, True)
+            any_args = [vp(d), ctypes.c_int(dtype), la, ctypes.c_longlong(start)]
+            if route == "any-launcher":
+                t4.launch_rrqr("identity_shifted_any", g, t4.stream_handle(), *any_args)
+            else:
+                module(OUR_LINALG).launch("t4a_cuda_identity_shifted_any", tuple(g.grid), tuple(g.block), 0,
+                                          any_args)
+        torch.cuda.synchronize()
+        got = host(d, span * es, NP[dtype])
+        assert np.array_equal(got.view(np.uint8), want.view(np.uint8)), (route, dtype, ext, start)
+
+
+def oracle_form_q(work, coeff, dtype, k):
+    """The reference bench's Q formation on the oracle: identity, then apply_reflector
+    for step = k-1 .. 0 over all k columns (work: column-major [m, n] host array)."""
+    m, n = work.shape
+    w = np.asfortranarray(work)
+    q = np.zeros((m, k), NP[dtype], order="F")
+    wl, ql, cl = abi.layout([m, n]), abi.layout([m, k]), abi.layout([k])
+    assert oracle.lib().t4a_oracle_identity_shifted(dtype, oracle.ptr(q.ravel(order="K")), ctypes.byref(ql), 0) == 0
+    c = np.ascontiguousarray(coeff[:k])
+    for step in range(k - 1, -1, -1):
+        assert oracle.lib().t4a_oracle_apply_reflector(dtype, oracle.ptr(w.ravel(order="K")),
+                                                       oracle.ptr(q.ravel(order="K")), oracle.ptr(c),
+                                                       ctypes.byref(wl), ctypes.byref(ql), ctypes.byref(cl), step, 0,
+                                                       k, THREADS) == 0
+    return q
+
+
+@pytest.mark.parametrize("dtype", [abi.F64, abi.F32])
+@pytest.mark.parametrize("m,n,k", [(300, 24, 24), (517, 40, 13)])
+def test_form_q_matches_the_oracle(cuda, dtype, m, n, k):
+    """t4a_rrqr_form_q after the fused factorization equals the oracle's loop bit for
+    bit, and Q is orthonormal with Q R = A P on the factorized columns."""
+    import torch
+    rng = np.random.default_rng(m + n + k + dtype)
+    a = np.asfortranarray(rng.standard_normal((m, n)).astype(NP[dtype]))
+    tdt = torch.float64 if dtype == abi.F64 else torch.float32
+    d_w = to_strided(a, m, tdt)
+    t = torch.as_strided(d_w, (m, n), (1, m))
+    perm, coeff, _, status = t4.rrqr(t, k)
+    q = t4.rrqr_form_q(t, coeff[:k])
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    work = from_strided(d_w, m, n, m)
+    want = oracle_form_q(work, coeff.cpu().numpy(), dtype, k)
+    got = q.cpu().numpy()
+    assert np.array_equal(np.ascontiguousarray(got).view(np.uint8), np.ascontiguousarray(want).view(np.uint8))
+    eps = 1e-12 if dtype == abi.F64 else 2e-5
+    q64 = got.astype(np.float64)
+    assert np.abs(q64.T @ q64 - np.eye(k)).max() < eps * m
+    r = np.triu(work[:k, :].astype(np.float64))
+    ap = a.astype(np.float64)[:, perm.cpu().numpy()]
+    assert np.abs(q64 @ r - ap)[:, :k].max() < eps * m * np.abs(a).max()
+
+
+def test_form_q_config5_properties(cuda):
+    """BASELINE config 5 at full size (m 65536, 256 reflectors): the Q formation's Q is
+    orthonormal and Q R equals A P, checked on the GPU in F64."""
+    import torch
+    m, n, rank = 65536, 256, 64
+    a = config5_matrix(m, n, rank, seed=10)
+    d_w = to_strided(a, m, torch.float64)
+    t = torch.as_strided(d_w, (m, n), (1, m))
+    perm, coeff, _, status = t4.rrqr(t, n)
+    q = t4.rrqr_form_q(t, coeff)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    eye = torch.eye(n, dtype=torch.float64, device="cuda")
+    assert float((q.T @ q - eye).abs().max()) < 1e-12
+    r = torch.triu(t[:n, :])
+    ap = torch.from_numpy(np.ascontiguousarray(a)).cuda()[:, perm]
+    assert float((q @ r - ap).abs().max()) < 1e-12 * float(ap.abs().max()) * 100
