@@ -375,47 +375,13 @@ __device__ __forceinline__ void strided_tiles(const T* __restrict__ in, T* __res
   }
 }
 
-// Staged variant of strided_tiles for 16-byte vectors (V > 1), same folds and trees.
-// Thread (tx, ty) copies the rows of its own LPT lanes, W rows of the chunk per
-// stage, with 16-byte cp.async into a thread-private slice of a D-stage ring, and folds
-// each stage from there once its own copies have landed (cp.async.wait_group), so the
-// data in flight takes no registers and needs no block barrier.  A producer cursor runs
-// D stages ahead of the fold across tile boundaries, so the next tile's loads overlap
-// this tile's lane tree.  Shared memory: D * LPT * kTileThreads * 16 bytes of ring,
-// then the kStridedSmem of the lane tree.
+// One (slot, split) unit of the staged strided pass: rows [start, end) of the chunk,
+// the slot's input and destination bases, and its stage count.
 struct StridedTile {
   long long start, end, s, vi, in_q, dst_q;
   int nk;       // stages of W rows
   bool valid;   // the slot exists
 };
-
-__device__ __forceinline__ StridedTile strided_tile(const t4a_cuda_layout& in_l, const t4a_cuda_layout& dst_l,
-                                                    const StridedCtx& c, long long tile, int tx, int W) {
-  const long long slot_tiles = (c.slots + kSlotsPerTile - 1) / kSlotsPerTile;
-  StridedTile t;
-  t.s = tile / slot_tiles;
-  const long long slot = (tile % slot_tiles) * kSlotsPerTile + tx;
-  t.valid = slot < c.slots;
-  const long long q = t.valid ? slot / c.vectors : 0;
-  t.vi = t.valid ? slot % c.vectors : 0;
-  t.in_q = in_l.offset;
-  t.dst_q = dst_l.offset;
-  long long rest = q;
-#pragma unroll
-  for (int d = 0; d < kMaxRank; ++d) {
-    if (d < in_l.rank && d >= c.inner_r && d != c.axis) {
-      const long long e = in_l.extents[d];
-      const long long k = rest % e;
-      rest /= e;
-      t.in_q += k * in_l.strides[d];
-      t.dst_q += k * dst_l.strides[d];
-    }
-  }
-  t.start = t.s * c.chunk;
-  t.end = t.s + 1 == c.splits ? c.len : t.start + c.chunk;
-  t.nk = static_cast<int>((t.end - t.start + W - 1) / W);
-  return t;
-}
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(static_cast<unsigned>(__cvta_generic_to_shared(smem))),
@@ -423,40 +389,81 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
                : "memory");
 }
 
+// Staged variant of strided_tiles for 16-byte vectors (V > 1): the same lanes, folds
+// and tree, with every warp working on its own units so that no block barrier is needed.  A unit is kWarpSlots
+// consecutive vector slots of one split; lane = ty * kWarpSlots + tx holds slot tx and
+// the plane lanes [ty * LPT, ty * LPT + LPT) (LPT * 32 / kWarpSlots == 32 plane lanes).
+// Each thread copies its LPT rows of a stage with 16-byte cp.async into its own slice
+// of a D-stage ring and folds them once its own copies have landed; a producer cursor
+// runs D stages ahead across the warp's units.  The plane tree pairs lanes at distances
+// 1, 2, 4 inside the thread, then 8 and 16 across threads by shuffles, each pair
+// combined as (lower, higher), the order of strided_tiles' tree.  Every lane must own
+// at least one row (chunk >= 32): the host takes this path only then.
+// Shared memory: D * LPT * blockDim * 16 bytes.
+constexpr int kWarpSlots = 8;
+
 template <typename Op, typename T, int V, int LPT, int D>
-__device__ __forceinline__ void strided_staged(const T* __restrict__ in, T* __restrict__ dst,
-                                               const t4a_cuda_layout& in_l, const t4a_cuda_layout& dst_l,
-                                               const StridedCtx& c, Op op) {
+__device__ __forceinline__ void strided_warp_staged(const T* __restrict__ in, T* __restrict__ dst,
+                                                    const t4a_cuda_layout& in_l, const t4a_cuda_layout& dst_l,
+                                                    const StridedCtx& c, Op op) {
   static_assert(V * sizeof(T) == 16, "16-byte vectors");
-  constexpr int W = LPT * kLaneGroups;
-  Vec<T, V>* ring = reinterpret_cast<Vec<T, V>*>(t4a_dyn_smem);  // [D][LPT][kTileThreads]
-  T* red = reinterpret_cast<T*>(t4a_dyn_smem + D * LPT * kTileThreads * 16);
+  static_assert(LPT * (32 / kWarpSlots) == 32, "LPT lanes per thread cover the 32-lane plane");
+  constexpr int W = 32;
+  const int nthreads = block_threads();
+  Vec<T, V>* ring = reinterpret_cast<Vec<T, V>*>(t4a_dyn_smem);  // [D][LPT][nthreads]
   const int tid = flat_tid();
-  const int tx = tid % kSlotsPerTile;
-  const int ty = tid / kSlotsPerTile;
-  const long long slot_tiles = (c.slots + kSlotsPerTile - 1) / kSlotsPerTile;
-  const long long tiles = slot_tiles * c.splits;
+  const int lane = tid & 31;
+  const int tx = lane % kWarpSlots;
+  const int ty = lane / kWarpSlots;
+  const long long gw = static_cast<long long>(blockIdx.x) * (nthreads >> 5) + (tid >> 5);
+  const long long nw = static_cast<long long>(gridDim.x) * (nthreads >> 5);
+  const long long slot_units = (c.slots + kWarpSlots - 1) / kWarpSlots;
+  const long long units = slot_units * c.splits;
   const long long lane0 = static_cast<long long>(ty) * LPT;
 
-  // Producer cursor: (tile, stage) of the next copies; one commit group per stage,
-  // empty once the block's tiles are exhausted.
-  long long p_tile = blockIdx.x;
+  auto unit_of = [&](long long u) {
+    StridedTile t;
+    t.s = u / slot_units;
+    const long long slot = (u % slot_units) * kWarpSlots + tx;
+    t.valid = slot < c.slots;
+    const long long q = t.valid ? slot / c.vectors : 0;
+    t.vi = t.valid ? slot % c.vectors : 0;
+    t.in_q = in_l.offset;
+    t.dst_q = dst_l.offset;
+    long long rest = q;
+#pragma unroll
+    for (int d = 0; d < kMaxRank; ++d) {
+      if (d < in_l.rank && d >= c.inner_r && d != c.axis) {
+        const long long e = in_l.extents[d];
+        const long long k = rest % e;
+        rest /= e;
+        t.in_q += k * in_l.strides[d];
+        t.dst_q += k * dst_l.strides[d];
+      }
+    }
+    t.start = t.s * c.chunk;
+    t.end = t.s + 1 == c.splits ? c.len : t.start + c.chunk;
+    t.nk = static_cast<int>((t.end - t.start + W - 1) / W);
+    return t;
+  };
+
+  long long p_unit = gw;
   int p_k = 0;
   StridedTile pt{};
-  if (p_tile < tiles) pt = strided_tile(in_l, dst_l, c, p_tile, tx, W);
+  if (p_unit < units) pt = unit_of(p_unit);
   int p_slot = 0;
   auto issue = [&]() {
-    if (p_tile < tiles) {
+    if (p_unit < units) {
       const T* base = in + pt.in_q + pt.vi * V;
 #pragma unroll
       for (int l = 0; l < LPT; ++l) {
         const long long row = pt.start + static_cast<long long>(p_k) * W + lane0 + l;
-        if (pt.valid && row < pt.end) cp_async16(&ring[(p_slot * LPT + l) * kTileThreads + tid], base + row * c.astride);
+        if (pt.valid && row < pt.end) cp_async16(&ring[(p_slot * LPT + l) * nthreads + tid], base + row * c.astride);
       }
       if (++p_k == pt.nk) {
         p_k = 0;
-        p_tile += gridDim.x;
-        if (p_tile < tiles) pt = strided_tile(in_l, dst_l, c, p_tile, tx, W);
+        p_unit += nw;
+        if (p_unit < units) pt = unit_of(p_unit);
       }
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
@@ -466,8 +473,8 @@ __device__ __forceinline__ void strided_staged(const T* __restrict__ in, T* __re
   for (int i = 0; i < D; ++i) issue();
 
   int c_slot = 0;
-  for (long long tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
-    const StridedTile t = strided_tile(in_l, dst_l, c, tile, tx, W);
+  for (long long u = gw; u < units; u += nw) {
+    const StridedTile t = unit_of(u);
     Vec<T, V> acc[LPT];
     for (int k = 0; k < t.nk; ++k) {
       asm volatile("cp.async.wait_group %0;" ::"n"(D - 1) : "memory");
@@ -475,7 +482,7 @@ __device__ __forceinline__ void strided_staged(const T* __restrict__ in, T* __re
       for (int l = 0; l < LPT; ++l) {
         const long long row = t.start + static_cast<long long>(k) * W + lane0 + l;
         if (row < t.end) {
-          const Vec<T, V> x = ring[(c_slot * LPT + l) * kTileThreads + tid];
+          const Vec<T, V> x = ring[(c_slot * LPT + l) * nthreads + tid];
 #pragma unroll
           for (int v = 0; v < V; ++v) acc[l].v[v] = k == 0 ? op.seed(x.v[v]) : op.fold(acc[l].v[v], x.v[v]);
         }
@@ -491,17 +498,13 @@ __device__ __forceinline__ void strided_staged(const T* __restrict__ in, T* __re
         for (int v = 0; v < V; ++v) acc[l].v[v] = op.combine(acc[l].v[v], acc[l + w].v[v]);
     Vec<T, V> mine = acc[0];
 #pragma unroll
-    for (int w = 1; w < kLaneGroups; w *= 2) {
-      if (ty % (2 * w) == w) {
+    for (int w = 1; w < 32 / kWarpSlots; w *= 2) {
+      const bool upper = (ty & w) != 0;
 #pragma unroll
-        for (int v = 0; v < V; ++v) red[(ty * kSlotsPerTile + tx) * V + v] = mine.v[v];
+      for (int v = 0; v < V; ++v) {
+        const T other = shfl_xor<T>(mine.v[v], w * kWarpSlots, 0xffffffffu);
+        if (!upper) mine.v[v] = op.combine(mine.v[v], other);
       }
-      __syncthreads();
-      if (ty % (2 * w) == 0) {
-#pragma unroll
-        for (int v = 0; v < V; ++v) mine.v[v] = op.combine(mine.v[v], red[((ty + w) * kSlotsPerTile + tx) * V + v]);
-      }
-      __syncthreads();
     }
     if (ty == 0 && t.valid) {
 #pragma unroll
@@ -520,7 +523,7 @@ __device__ __forceinline__ void strided_staged(const T* __restrict__ in, T* __re
       }
     }
   }
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
 // ---------------------------------------------------------------------------

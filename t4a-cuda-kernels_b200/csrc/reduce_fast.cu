@@ -24,10 +24,12 @@ __global__ void __launch_bounds__(256) k_strided(T* dst, const T* in, t4a_cuda_l
   strided_tiles<Op, T, V, 4>(in, dst, in_l, dst_l, strided_ctx(in_l, axis, splits, chunk, V, partials), Op());
 }
 
-// The staged strided pass: 4-stage cp.async ring, three blocks per SM.
-constexpr int kStagedDepth = 4;
-constexpr int kStagedBlocksPerSm = 3;
-constexpr unsigned kStagedSmem = kStagedDepth * 4 * kTileThreads * 16 + kStridedSmem;
+// The staged strided pass: warp units, 8 plane lanes per thread, a 2-stage cp.async
+// ring per thread, two blocks per SM.
+constexpr int kStagedLanes = 8;
+constexpr int kStagedDepth = 3;
+constexpr int kStagedBlocksPerSm = 2;
+constexpr unsigned kStagedSmem = kStagedDepth * kStagedLanes * kTileThreads * 16;
 
 template <typename Op, typename T>
 __global__ void __launch_bounds__(256, kStagedBlocksPerSm) k_strided_staged(T* dst, const T* in, t4a_cuda_layout dst_l,
@@ -36,8 +38,8 @@ __global__ void __launch_bounds__(256, kStagedBlocksPerSm) k_strided_staged(T* d
                                                                            bool partials) {
   constexpr int V = VecOf<T>::kLanes;
   if constexpr (V * sizeof(T) == 16) {
-    strided_staged<Op, T, V, 4, kStagedDepth>(in, dst, in_l, dst_l, strided_ctx(in_l, axis, splits, chunk, V, partials),
-                                              Op());
+    strided_warp_staged<Op, T, V, kStagedLanes, kStagedDepth>(
+        in, dst, in_l, dst_l, strided_ctx(in_l, axis, splits, chunk, V, partials), Op());
   }
 }
 
@@ -192,12 +194,15 @@ void prefer_warp_rows(int dtype, const void* in, int* path, dim3* grid, dim3* bl
 }
 
 // A strided pass over 16-byte vectors with at least kStagedMinTiles tiles per resident
-// block runs the staged kernel on a grid of kStagedBlocksPerSm blocks per SM, each
-// walking many tiles, so that its copy ring runs ahead across tile boundaries; smaller
-// passes keep one tile per block.
+// block runs the staged kernel on a grid of kStagedBlocksPerSm blocks per SM, each warp
+// walking many units, so that its copy ring runs ahead across unit boundaries; smaller
+// passes keep one tile per block.  The staged kernel needs every plane lane to own a
+// row: chunks of at least 32 rows.
 constexpr unsigned kStagedMinTiles = 4;
-void prefer_strided_staged(int dtype, int* path, dim3* grid, unsigned* smem) {
+void prefer_strided_staged(int dtype, int* path, dim3* grid, unsigned* smem, const PassArgs& a) {
   if (*path != kPathStrided || strided_vec_lanes(dtype) == 1) return;
+  const long long shortest = a.splits > 1 ? a.chunk : a.in_l.extents[a.axis];
+  if (shortest < 32) return;
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const unsigned cap = static_cast<unsigned>(sms * kStagedBlocksPerSm);
@@ -240,7 +245,7 @@ int run_pass(const t4a_launch* launch, void* stream, int dtype, int op, PassArgs
     // Not reached by the planner's geometry (at most 32 KiB); kept explicit.
     return T4A_ERR_LAUNCH_LIMIT;
   }
-  prefer_strided_staged(dtype, &path, &grid, &smem);
+  prefer_strided_staged(dtype, &path, &grid, &smem, a);
 #define T4A_CALL(OP, T) launch_path<OP, T>(path, grid, block, smem, s, a)
   T4A_REDUCE_SWITCH(op, dtype, T4A_CALL)
 #undef T4A_CALL
