@@ -198,7 +198,7 @@ __device__ __forceinline__ bool quotient_safe(const ScaledQuotient<F>& s, F a) {
 // p mod 3, which reuses a stage once its consumer has released it on the stage's
 // `empty` mbarrier (warp 0 for chain segments, the helper warps 4-11 for update
 // segments).  One warp's bulk copies are served one after another (about 55 GB/s of
-// 16 KB copies from L2), so three producers keep three streams going per block.  The
+// 16 KB copies from L2, more for larger ones), so three producers keep three streams going per block.  The
 // update's segments (v and t, last first) follow the dot's in the same ring, so their
 // copies start while the dot chain finishes; the helpers compute and store them.  For
 // the norm, the helpers turn each landed segment into scaled magnitudes in place and
@@ -215,8 +215,11 @@ constexpr int kColProducers = 3;                     // divides kColStages
 constexpr int kColHelperWarp0 = 1 + kColProducers;  // first helper warp
 constexpr int kColThreads = 32 * kColHelperWarp0 + kColHelpers;
 constexpr int kColWarps = kColThreads / 32;
-constexpr int kColStages = 6;
-constexpr int kColStageBytes = 16384;
+// Three 32 KB stages (96 KB, two blocks per SM).  Each stage boundary costs the chain a
+// fixed hand-off (wait, abort vote, release, a restarted load pipeline), so fewer and
+// larger stages beat a deeper ring of small ones.
+constexpr int kColStages = 3;
+constexpr int kColStageBytes = 32768;
 constexpr unsigned kColWaitLimit = 1u << 20;  // try_wait rounds before giving up
 constexpr unsigned kColSuspendNs = 1000;
 
