@@ -695,3 +695,57 @@ def test_any_twins_on_config4_rows(cuda):
                                                      ctypes.c_longlong(n * cols)])
     assert torch.allclose(got, want, rtol=0, atol=1e-12 * float(want.abs().max()))
     del kp, kq, k1, k2, k3, k4, k5, k6
+
+
+@pytest.mark.parametrize("route", ["launcher", "module"])
+def test_any_twins_leave_malformed_maps_untouched(cuda, route):
+    """The kernels check the device-resident maps before walking: a repeated offset
+    dimension, a window axis past the operand's rank, or a count beyond the walked
+    layout's extents makes every block return, so the destination keeps its sentinel."""
+    import torch
+    rows, cols, n = 64, 8, 16
+    table = dev(np.arange(rows * cols, dtype=np.float32).view(np.uint8))
+    idx = dev(np.arange(n, dtype=np.int64).view(np.uint8))
+    ol, k1 = t4.layout_any([cols, n], [1, cols])
+    al, k2 = t4.layout_any([cols, rows], [1, cols])
+    il, k3 = t4.layout_any([n, 1])
+    bad_plans = [
+        t4.gather_plan_any([0, 1], [0, 0], [1], [cols, 1], 1, 2),  # offset dimension repeated
+        t4.gather_plan_any([5], [0], [1], [cols, 1], 1, 2),        # window axis past the operand
+    ]
+    good, kg = t4.gather_plan_any([0], [0], [1], [cols, 1], 1, 2)
+    cases = [(p, n * cols) for p, _ in bad_plans] + [(good, n * cols + 1)]  # last: count beyond the extents
+    for plan, count in cases:
+        out = sentinel(n * cols * 4)
+        args = [vptr(out), vptr(table), vptr(idx), ctypes.c_int(abi.F32), ctypes.c_int(abi.I64), ol, al, il, plan,
+                ctypes.c_longlong(count)]
+        if route == "launcher":
+            try:
+                t4.launch_movement_any("gather", t4.gather_scatter_any_geometry(count), t4.stream_handle(), *args)
+            except t4.T4AError:
+                pass  # refused on the host: nothing launched
+        else:
+            g = t4.gather_scatter_any_geometry(count)
+            module(OUR_CUBIN).launch("t4a_cuda_gather_any", tuple(g.grid), tuple(g.block), 0, args)
+        torch.cuda.synchronize()
+        assert (take(out, n * cols * 4) == SENTINEL).all()
+    # scatter: update window wider than the updates' rank is refused on the host; a
+    # repeated update window dimension is refused by the kernel.
+    dest = dev(np.zeros(rows * cols, np.float64).view(np.uint8))
+    upd = dev(np.ones(n * cols, np.float64).view(np.uint8))
+    dl, k4 = t4.layout_any([cols, rows], [1, cols])
+    ul, k5 = t4.layout_any([cols, n], [1, cols])
+    splan, ks = t4.scatter_plan_any([0, 1], [0, 0], [1], 1, 2, 2)
+    args = [vptr(dest), vptr(idx), vptr(upd), ctypes.c_int(abi.F64), ctypes.c_int(abi.I64), dl, il, ul, splan,
+            ctypes.c_longlong(n * cols)]
+    g = t4.gather_scatter_any_geometry(n * cols)
+    if route == "launcher":
+        try:
+            t4.launch_movement_any("scatter_add", g, t4.stream_handle(), *args)
+        except t4.T4AError:
+            pass
+    else:
+        module(OUR_CUBIN).launch("t4a_cuda_scatter_add_any", tuple(g.grid), tuple(g.block), 0, args)
+    torch.cuda.synchronize()
+    assert (take(dest, rows * cols * 8).view(np.float64) == 0).all()
+    del k1, k2, k3, k4, k5, kg, ks, bad_plans
