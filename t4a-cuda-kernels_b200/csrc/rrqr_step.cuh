@@ -215,9 +215,9 @@ constexpr int kColProducers = 3;                     // divides kColStages
 constexpr int kColHelperWarp0 = 1 + kColProducers;  // first helper warp
 constexpr int kColThreads = 32 * kColHelperWarp0 + kColHelpers;
 constexpr int kColWarps = kColThreads / 32;
-// Three 32 KB stages (96 KB, two blocks per SM).  Each stage boundary costs the chain a
-// fixed hand-off (wait, abort vote, release, a restarted load pipeline), so fewer and
-// larger stages beat a deeper ring of small ones.
+// Three 32 KB stages (96 KB, two blocks per SM).  A bulk copy costs its issuing warp
+// about the same time whatever its size, so fewer and larger stages beat a deeper ring
+// of small ones.
 constexpr int kColStages = 3;
 constexpr int kColStageBytes = 32768;
 constexpr unsigned kColWaitLimit = 1u << 20;  // try_wait rounds before giving up
