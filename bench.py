@@ -585,6 +585,45 @@ class RrqrWorkload(Workload):
     def host_arrays(self):
         return [self.a_host.numpy()], [None]
 
+    def measure_epilogue(self, stream, stream_handle, args):
+        """The reference bench's Q formation after the factorization
+        (examples/bench_kernels.rs:2560-2590) through t4a_rrqr_form_q: identity_shifted,
+        then apply_reflector for step = n-1 .. 0 over all n columns of Q [m, n].  Timed
+        with CUDA events on the launching stream after 3 untimed runs, `args.steps`
+        runs, L2 not flushed (Q alone is 134 MB).  Algorithmic bytes: the identity's
+        writes 8 m n, then per step s the reflector's rows 8 (m - s) and Q's rows read
+        and written 16 n (m - s)."""
+        import torch
+        t4, abi = self.t4, self.abi
+        m, n = self.M, self.N
+        q = torch.empty((n, m), dtype=torch.float64, device=self.device).t()
+        wl_, ql, cl = abi.layout([m, n]), abi.layout([m, n], [1, m]), abi.layout([n])
+        vp = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+
+        qstatus = torch.zeros(1, dtype=torch.int64, device=self.device)
+
+        def form_q():
+            t4.check(t4.lib().t4a_rrqr_form_q(stream_handle, abi.F64, vp(self.work), ctypes.byref(wl_), m * n,
+                                              vp(self.coeff), ctypes.byref(cl), n, vp(q), ctypes.byref(ql), m * n,
+                                              vp(qstatus)),
+                     "rrqr_form_q")
+        for _ in range(3):
+            form_q()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            form_q()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        if int(qstatus.item()) != 0:
+            raise RuntimeError(f"Q formation status {int(qstatus.item())}: a bounded wait ran out")
+        nbytes = 8 * m * n + sum(8 * (m - s) + 16 * n * (m - s) for s in range(n))
+        return {"what": "Q formation (identity_shifted + 256 reflector passes over Q's columns), t4a_rrqr_form_q",
+                "ms": round(ms, 3), "bytes": nbytes, "gbs": round(nbytes / (ms / 1e3) / 1e9, 1),
+                "launches": n + 1, "status": int(qstatus.item())}
+
     def cpu_sample(self):
         return f"one full {self.name} factorization"
 
@@ -732,6 +771,9 @@ def run_ours(args, rank, world, local_rank):
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         e2e_ms = t.item()
     e2e_value = wl.units() * world * args.steps / (e2e_ms / 1e3) / 1e9
+    # A workload may time a follow-on stage of the path separately (RRQR: the Q
+    # formation that follows the factorization in the reference bench).
+    epilogue = wl.measure_epilogue(stream, sh, args) if hasattr(wl, "measure_epilogue") else None
 
     # Roofline of the dominant kernel (longest total time).
     peak, peak_kind = read_peaks()
@@ -774,6 +816,8 @@ def run_ours(args, rank, world, local_rank):
         "clocks": sampler.summary(),
         "wall_s_timed_region": round(wall, 3),
     }
+    if epilogue is not None:
+        line["epilogue"] = epilogue
     if rank == 0 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(wl, args)
     return line

@@ -12,8 +12,8 @@
  *     caller's stream and exactly the argument list of the kernel symbol it stands
  *     for (docs/abi/c-kernel-abi.md entry tables), and launches it.
  *
- * The modules lib/{reduce,movement,gather_scatter,rrqr}.cubin built beside the
- * library export the same
+ * The modules lib/{reduce,movement,gather_scatter,rrqr,linalg_aux}.cubin built beside
+ * the library export the same
  * `extern "C" __global__` symbols as the reference (t4a_cuda_reduce, ...), for
  * callers that load kernels by name.
  *
@@ -432,10 +432,14 @@ int t4a_launch_identity_shifted_any(const t4a_launch* launch, void* stream, void
  * q = identity_shifted(start 0), then apply_reflector for step = k-1 .. 0 over all k
  * columns of q (k = q's columns) with the reflectors of `work` and `coeff`.  Every
  * step is planned before the first launch, so an invalid argument launches nothing.
- * Results equal that loop of primitives bit for bit. */
+ * Results equal that loop of primitives bit for bit.  F32/F64 column-major matrices
+ * (row stride 1) with contiguous coefficients, naturally aligned, and a non-NULL
+ * `status` (device, one long long the caller zeroes) take the column pass: one block
+ * per column of q per step, status bit 1 set if a bounded wait ran out.  Everything
+ * else runs the primitives' launches. */
 int t4a_rrqr_form_q(void* stream, int dtype, const void* work, const t4a_cuda_layout* work_layout,
                     long long work_len, const void* coeff, const t4a_cuda_layout* coeff_layout, long long coeff_len,
-                    void* q, const t4a_cuda_layout* q_layout, long long q_len);
+                    void* q, const t4a_cuda_layout* q_layout, long long q_len, long long* status);
 
 /* No single counterpart in the reference (its loop lives with the caller, bench
  * examples/bench_kernels.rs:2390-2623): `steps` steps of column_norms, select_pivot,

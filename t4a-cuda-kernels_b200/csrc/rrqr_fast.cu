@@ -167,6 +167,14 @@ __global__ void __launch_bounds__(kColThreads, 2) k_col_step(FusedArgs<F> a, lon
   column_step<F>(a, step, next_norm != 0, *reinterpret_cast<ColSmem<F>*>(smem));
 }
 
+// Q formation pass for reflector `step`: one block per column of Q.
+template <typename F>
+__global__ void __launch_bounds__(kColThreads, 2) k_q_step(FusedArgs<F> a, long long step, F* q, long long qld,
+                                                          long long qcols, long long q_span) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  column_q<F>(a, step, q, qld, qcols, q_span, *reinterpret_cast<ColSmem<F>*>(smem));
+}
+
 // Raises a kernel's dynamic shared memory limit once on each device.
 template <typename K>
 int allow_smem(K kernel, unsigned bytes, std::atomic<unsigned long long>& raised) {
@@ -230,6 +238,27 @@ int run_fused(cudaStream_t s, F* w, long long m, long long n, long long ld, long
       k_col_step<F><<<dim3(static_cast<unsigned>(trailing)), dim3(kColThreads), smem, s>>>(a, step,
                                                                                         step + 1 < steps ? 1 : 0);
   }
+  return runtime::check_launch();
+}
+
+// Q formation through the column pass: identity, then for step = k-1 .. 0 one block per
+// column of Q applies reflector `step` (dot and update phases, the primitives' bits).
+template <typename F>
+int run_form_q(cudaStream_t s, const F* w, long long m, long long ld, long long w_span, const F* coeff, F* q,
+               long long qld, long long k, long long q_span, long long* status) {
+  FusedArgs<F> a{};
+  a.w = const_cast<F*>(w);
+  a.m = m;
+  a.n = k;
+  a.ld = ld;
+  a.coeff = const_cast<F*>(coeff);
+  a.status = status;
+  a.span = w_span;
+  static std::atomic<unsigned long long> raised{0};
+  const unsigned smem = sizeof(ColSmem<F>);
+  T4A_TRY(allow_smem(k_q_step<F>, smem, raised));
+  for (long long step = k - 1; step >= 0; --step)
+    k_q_step<F><<<dim3(static_cast<unsigned>(k)), dim3(kColThreads), smem, s>>>(a, step, q, qld, k, q_span);
   return runtime::check_launch();
 }
 
@@ -845,7 +874,7 @@ int t4a_launch_identity_shifted_any(const t4a_launch* launch, void* stream, void
 // the factorized `work` and `coeff`; k = the columns of q.
 int t4a_rrqr_form_q(void* stream, int dtype, const void* work, const t4a_cuda_layout* work_layout,
                     long long work_len, const void* coeff, const t4a_cuda_layout* coeff_layout, long long coeff_len,
-                    void* q, const t4a_cuda_layout* q_layout, long long q_len) {
+                    void* q, const t4a_cuda_layout* q_layout, long long q_len, long long* status) {
   if (work_layout == nullptr || coeff_layout == nullptr || q_layout == nullptr) return T4A_ERR_NULL_ARGUMENT;
   T4A_TRY(check_algebra(dtype));
   t4a_launch l;
@@ -858,6 +887,30 @@ int t4a_rrqr_form_q(void* stream, int dtype, const void* work, const t4a_cuda_la
   }
   if (q == nullptr || (k > 0 && (work == nullptr || coeff == nullptr))) return T4A_ERR_NULL_ARGUMENT;
   T4A_TRY(t4a_launch_identity_shifted(&l, stream, q, dtype, *q_layout, 0));
+  // The column-pass route: F32/F64 column-major matrices (row stride 1), contiguous
+  // coefficients, naturally aligned buffers and a status word.
+  const int es = dtype_size(dtype);
+  const auto aligned = [es](const void* p, long long off) {
+    return ((reinterpret_cast<unsigned long long>(p) + static_cast<unsigned long long>(off) * es) % es) == 0;
+  };
+  if ((dtype == T4A_CUDA_F32 || dtype == T4A_CUDA_F64) && status != nullptr && k > 0 && work_layout->rank == 2 &&
+      q_layout->rank == 2 && work_layout->strides[0] == 1 && q_layout->strides[0] == 1 &&
+      work_layout->strides[1] > 0 && q_layout->strides[1] > 0 && coeff_layout->rank == 1 &&
+      (coeff_layout->strides[0] == 1 || coeff_layout->extents[0] <= 1) && aligned(work, work_layout->offset) &&
+      aligned(q, q_layout->offset) && aligned(coeff, coeff_layout->offset) &&
+      (reinterpret_cast<unsigned long long>(status) & 7ull) == 0) {
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const long long m = work_layout->extents[0];
+    if (dtype == T4A_CUDA_F64)
+      return run_form_q<double>(s, static_cast<const double*>(work) + work_layout->offset, m, work_layout->strides[1],
+                                work_len - work_layout->offset, static_cast<const double*>(coeff) + coeff_layout->offset,
+                                static_cast<double*>(q) + q_layout->offset, q_layout->strides[1], k,
+                                q_len - q_layout->offset, status);
+    return run_form_q<float>(s, static_cast<const float*>(work) + work_layout->offset, m, work_layout->strides[1],
+                             work_len - work_layout->offset, static_cast<const float*>(coeff) + coeff_layout->offset,
+                             static_cast<float*>(q) + q_layout->offset, q_layout->strides[1], k,
+                             q_len - q_layout->offset, status);
+  }
   for (long long step = k - 1; step >= 0; --step) {
     t4a_launch a;
     T4A_TRY(t4a_plan_apply_reflector(dtype, work_layout, work_len, q_layout, q_len, coeff_layout, coeff_len, step, 0,

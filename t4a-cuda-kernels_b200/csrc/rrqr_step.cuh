@@ -289,6 +289,8 @@ struct ColStream {
   int seg;     // elements per segment
   int sh;      // slot of element 0 (address of base modulo 16, in elements)
   int region;  // first slot of this operand within a stage
+  const F* lo;  // the operand's buffer: aligned copies never leave [lo, hi)
+  const F* hi;
 };
 
 // Producer index of this thread (lane 0 of warps 1 .. kColProducers), or -1.
@@ -314,18 +316,17 @@ __device__ __forceinline__ bool col_aborted(ColSmem<F>& sm) {
 // Producer: ring position p holds segment g of every operand.  Waits (bounded) until
 // warp 0 has released the stage's previous use, then issues the bulk copies.
 template <typename F, int Ops>
-__device__ __forceinline__ bool col_issue(ColSmem<F>& sm, const ColStream<F>* ops, long long p, long long g,
-                                          const F* span_lo, const F* span_hi) {
+__device__ __forceinline__ bool col_issue(ColSmem<F>& sm, const ColStream<F>* ops, long long p, long long g) {
   constexpr unsigned long long es = sizeof(F);
   const int st = ring_stage(p);
   if (p >= kColStages && !col_wait(&sm.empty[st], ring_parity(p - kColStages))) return false;
-  const unsigned long long w0 = (reinterpret_cast<unsigned long long>(span_lo) + 15) & ~15ull;
-  const unsigned long long w1 = reinterpret_cast<unsigned long long>(span_hi) & ~15ull;
   unsigned long long c0[Ops], c1[Ops], g0[Ops];
   unsigned tx = 0;
   bool edges = false;
 #pragma unroll
   for (int o = 0; o < Ops; ++o) {
+    const unsigned long long w0 = (reinterpret_cast<unsigned long long>(ops[o].lo) + 15) & ~15ull;
+    const unsigned long long w1 = reinterpret_cast<unsigned long long>(ops[o].hi) & ~15ull;
     const long long e0 = g * ops[o].seg;
     const long long e1 = ops[o].rows < e0 + ops[o].seg ? ops[o].rows : e0 + ops[o].seg;
     g0[o] = reinterpret_cast<unsigned long long>(ops[o].base + e0);
@@ -443,11 +444,13 @@ __device__ __forceinline__ F col_norm_chain(ColSmem<F>& sm, const FusedArgs<F>& 
   op.seg = S::kSeg1;
   op.sh = slot_shift(base);
   op.region = 0;
+  op.lo = a.w;
+  op.hi = a.w + a.span;
   F acc = F(0);
   const int k = col_producer();
   if (k >= 0) {
     for (long long p = col_first_position(p0, k); p < p0 + nseg && !col_aborted(sm); p += kColProducers) {
-      if (!col_issue<F, 1>(sm, &op, p, p - p0, a.w, a.w + a.span)) {
+      if (!col_issue<F, 1>(sm, &op, p, p - p0)) {
         col_fail(sm, a.status);
         break;
       }
@@ -599,17 +602,18 @@ __device__ __forceinline__ void column_first(const FusedArgs<F>& a, ColSmem<F>& 
   col_pivot_if_last(a, 0, sm);
 }
 
-// Step pass: trailing column j = step + 1 + blockIdx.x.
+// The dot and update phases of a column pass: t -= v * (coeff[step] * dot(v, t)) over
+// rows [step, m) of the target column `tcol`, the reflector read from `vcol` (its row
+// `step` is the implicit 1).  v lies in [vlo, vhi), t in [tlo, thi).  Returns the
+// positions this thread issued as a producer (for col_drain); the helpers' maximum of
+// the updated rows below `step` goes to local_max / invalid.
 template <typename F>
-__device__ __forceinline__ void column_step(const FusedArgs<F>& a, long long step, bool next_norm, ColSmem<F>& sm) {
+__device__ __forceinline__ long long col_dot_update(const FusedArgs<F>& a, long long step, const F* vcol, F* tcol,
+                                                    const F* vlo, const F* vhi, const F* tlo, const F* thi,
+                                                    ColSmem<F>& sm, F* local_max_out, bool* invalid_out) {
   using S = ColSmem<F>;
-  const long long j = step + 1 + blockIdx.x;
-  if (j >= a.n) return;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const F* vcol = a.w + step * a.ld;
-  F* tcol = a.w + j * a.ld;
   const long long rows = a.m - step;
-  col_init(sm);
   long long issued = 0;
   // Ring positions [0, nseg): the dot's segments; [nseg, 2 nseg): the update's, last
   // segment first; then the norm's.
@@ -624,13 +628,17 @@ __device__ __forceinline__ void column_step(const FusedArgs<F>& a, long long ste
     ops[o].sh = slot_shift(ops[o].base);
     ops[o].region = o * S::kRegion2;
   }
+  ops[0].lo = vlo;
+  ops[0].hi = vhi;
+  ops[1].lo = tlo;
+  ops[1].hi = thi;
   F local_max = F(0);
   bool invalid = false;
   const int k = col_producer();
   if (k >= 0) {
     for (long long p = k; p < 2 * nseg && !col_aborted(sm); p += kColProducers) {
       const long long g = p < nseg ? p : 2 * nseg - 1 - p;
-      if (!col_issue<F, 2>(sm, ops, p, g, a.w, a.w + a.span)) {
+      if (!col_issue<F, 2>(sm, ops, p, g)) {
         col_fail(sm, a.status);
         break;
       }
@@ -700,6 +708,25 @@ __device__ __forceinline__ void column_step(const FusedArgs<F>& a, long long ste
     }
     col_fence_global();
   }
+  *local_max_out = local_max;
+  *invalid_out = invalid;
+  return issued;
+}
+
+// Step pass: trailing column j = step + 1 + blockIdx.x.
+template <typename F>
+__device__ __forceinline__ void column_step(const FusedArgs<F>& a, long long step, bool next_norm, ColSmem<F>& sm) {
+  const long long j = step + 1 + blockIdx.x;
+  if (j >= a.n) return;
+  const int k = col_producer();
+  F* tcol = a.w + j * a.ld;
+  const long long rows = a.m - step;
+  const long long nseg = (rows + ColSmem<F>::kSeg2 - 1) / ColSmem<F>::kSeg2;
+  col_init(sm);
+  F local_max;
+  bool invalid;
+  long long issued = col_dot_update(a, step, a.w + step * a.ld, tcol, a.w, a.w + a.span, a.w, a.w + a.span, sm,
+                                    &local_max, &invalid);
   F scale;
   bool bad;
   col_block_max(sm, local_max, invalid, &scale, &bad);
@@ -713,6 +740,24 @@ __device__ __forceinline__ void column_step(const FusedArgs<F>& a, long long ste
     col_write_norm(sm, a, j, acc, scale, bad);
     col_pivot_if_last(a, step + 1, sm);
   }
+}
+
+// Q formation pass: the dot and update phases of reflector `step` (a column of a.w,
+// coefficient a.coeff[step]) applied to column j = blockIdx.x of Q (q, column stride
+// qld, q_span elements); the same arithmetic as apply_reflector over Q's columns.
+template <typename F>
+__device__ __forceinline__ void column_q(const FusedArgs<F>& a, long long step, F* q, long long qld, long long qcols,
+                                         long long q_span, ColSmem<F>& sm) {
+  const long long j = blockIdx.x;
+  if (j >= qcols) return;
+  const int k = col_producer();
+  col_init(sm);
+  F local_max;
+  bool invalid;
+  const long long issued = col_dot_update(a, step, a.w + step * a.ld, q + j * qld, a.w, a.w + a.span, q, q + q_span,
+                                          sm, &local_max, &invalid);
+  __syncthreads();
+  if (k >= 0) col_drain(sm, issued, k, a.status);
 }
 
 }  // namespace rrqr

@@ -123,7 +123,7 @@ def _declare(l):
         "t4a_launch_prefix_rank": (I, [ctypes.POINTER(Launch), P, P, P, P, I, LB, ctypes.c_double, ctypes.c_double]),
         "t4a_rrqr_workspace_bytes": (I, [I, LP, ctypes.POINTER(SZ)]),
         "t4a_rrqr": (I, [P, I, P, LP, LL, LL, P, P, P, P, P, SZ]),
-        "t4a_rrqr_form_q": (I, [P, I, P, LP, LL, P, LP, LL, P, LP, LL]),
+        "t4a_rrqr_form_q": (I, [P, I, P, LP, LL, P, LP, LL, P, LP, LL, P]),
         "t4a_plan_identity_shifted": (I, [I, LP, LL, LL, ctypes.POINTER(Launch)]),
         "t4a_launch_identity_shifted": (I, [ctypes.POINTER(Launch), P, P, I, LB, LL]),
         "t4a_scatter_add": (I, [P, I, I, P, LP, LL, P, LP, LL, P, LP, LL, ctypes.POINTER(abi.ScatterPlan), P, SZ]),
@@ -493,22 +493,26 @@ def rrqr_any_geometry(tasks, flat):
     return launch
 
 
-def rrqr_form_q(work, coeff, k=None, q=None, stream=None):
+def rrqr_form_q(work, coeff, k=None, q=None, stream=None, status=None):
     """Q formation after rrqr(work): q [m, k] (column-major, k default the coefficients
     given) = identity_shifted(0), then apply_reflector for step = k-1 .. 0 over all k
-    columns with the reflectors in `work` and `coeff` (the reference bench's epilogue)."""
+    columns with the reflectors in `work` and `coeff` (the reference bench's epilogue).
+    Returns (q, status); status bit 1 means a bounded wait of the column pass ran out."""
     import torch
     m, n = work.shape
     k = coeff.numel() if k is None else k
     if q is None:
         q = torch.empty((k, m), dtype=work.dtype, device=work.device).t()
+    if status is None:
+        status = torch.zeros(1, dtype=torch.int64, device=work.device)
     wl = abi.layout([m, n], [work.stride(0), work.stride(1)])
     ql = abi.layout([m, k], [q.stride(0), q.stride(1)])
     cl = abi.layout([coeff.numel()])
     check(lib().t4a_rrqr_form_q(stream_handle(stream), torch_dtype_tag(work), _ptr(work), ctypes.byref(wl), span(work),
-                                _ptr(coeff), ctypes.byref(cl), coeff.numel(), _ptr(q), ctypes.byref(ql), span(q)),
+                                _ptr(coeff), ctypes.byref(cl), coeff.numel(), _ptr(q), ctypes.byref(ql), span(q),
+                                _ptr(status)),
           "rrqr_form_q")
-    return q
+    return q, status
 
 
 def rrqr_workspace_bytes(dtype, work_layout):

@@ -422,6 +422,6 @@ def test_plan_identity_shifted_validation():
     wl, ql, cl = abi.layout([10, 4]), abi.layout([10, 4]), abi.layout([4])
     p = ctypes.c_void_p(0x1000)
     assert lib.t4a_rrqr_form_q(None, abi.F64, p, ctypes.byref(wl), 40, p, ctypes.byref(cl), 3, p,
-                               ctypes.byref(ql), 40) == 7
+                               ctypes.byref(ql), 40, None) == 7
     assert lib.t4a_rrqr_form_q(None, abi.I32, p, ctypes.byref(wl), 40, p, ctypes.byref(cl), 4, p,
-                               ctypes.byref(ql), 40) == 9
+                               ctypes.byref(ql), 40, None) == 9

@@ -694,9 +694,9 @@ def test_form_q_matches_the_oracle(cuda, dtype, m, n, k):
     d_w = to_strided(a, m, tdt)
     t = torch.as_strided(d_w, (m, n), (1, m))
     perm, coeff, _, status = t4.rrqr(t, k)
-    q = t4.rrqr_form_q(t, coeff[:k])
+    q, qst = t4.rrqr_form_q(t, coeff[:k])
     torch.cuda.synchronize()
-    assert int(status.item()) == 0
+    assert int(status.item()) == 0 and int(qst.item()) == 0
     work = from_strided(d_w, m, n, m)
     want = oracle_form_q(work, coeff.cpu().numpy(), dtype, k)
     got = q.cpu().numpy()
@@ -718,9 +718,9 @@ def test_form_q_config5_properties(cuda):
     d_w = to_strided(a, m, torch.float64)
     t = torch.as_strided(d_w, (m, n), (1, m))
     perm, coeff, _, status = t4.rrqr(t, n)
-    q = t4.rrqr_form_q(t, coeff)
+    q, qst = t4.rrqr_form_q(t, coeff)
     torch.cuda.synchronize()
-    assert int(status.item()) == 0
+    assert int(status.item()) == 0 and int(qst.item()) == 0
     eye = torch.eye(n, dtype=torch.float64, device="cuda")
     assert float((q.T @ q - eye).abs().max()) < 1e-12
     r = torch.triu(t[:n, :])
