@@ -17,6 +17,10 @@
 //          step's scaled sum-of-squares norm chain of the updated column, whose
 //          maximum the update found (a maximum is exact in any order).
 // Step 0's norms run the column pass's norm chain after a walk for the maximum.
+//
+// Q formation (column_q) reuses the column pass's dot and update phases
+// (col_dot_update): reflector `step` of the factorized matrix applied to one column of
+// Q per block, the same arithmetic as apply_reflector over Q's columns.
 #pragma once
 
 #include "rrqr_core.cuh"
