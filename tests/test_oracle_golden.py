@@ -88,3 +88,28 @@ def test_oracle_identity_shifted_reference_cases(dtype, extents, strides, offset
     lay = abi.layout(extents, strides, offset)
     assert oracle.lib().t4a_oracle_identity_shifted(tag, oracle.ptr(got), ctypes.byref(lay), start) == 0
     assert np.array_equal(got.view(np.uint8), want.view(np.uint8))
+
+
+def test_oracle_q_formation_is_orthonormal():
+    """The oracle's own epilogue, which the GPU Q-formation tests compare against:
+    after its RRQR loop (t4a_oracle_rrqr_f64), the identity and apply_reflector for
+    step = k-1 .. 0 give an orthonormal Q with Q R = A P on the factorized columns."""
+    import ctypes
+    from t4a_b200 import abi
+    rng = np.random.default_rng(7)
+    m, n = 120, 16
+    a = np.asfortranarray(rng.standard_normal((m, n)))
+    work = a.copy(order="F")
+    perm, coeff = np.zeros(n, np.int64), np.zeros(n)
+    oracle.lib().t4a_oracle_rrqr_f64(oracle.ptr(work.ravel(order="K")), m, n, n, oracle.lptr(perm),
+                                     oracle.ptr(coeff), 1e-8, 0.0, 1)
+    q = np.zeros((m, n), order="F")
+    wl, ql, cl = abi.layout([m, n]), abi.layout([m, n]), abi.layout([n])
+    assert oracle.lib().t4a_oracle_identity_shifted(abi.F64, oracle.ptr(q.ravel(order="K")), ctypes.byref(ql), 0) == 0
+    for step in range(n - 1, -1, -1):
+        assert oracle.lib().t4a_oracle_apply_reflector(abi.F64, oracle.ptr(work.ravel(order="K")),
+                                                       oracle.ptr(q.ravel(order="K")), oracle.ptr(coeff),
+                                                       ctypes.byref(wl), ctypes.byref(ql), ctypes.byref(cl), step, 0,
+                                                       n, 1) == 0
+    assert np.abs(q.T @ q - np.eye(n)).max() < 1e-12
+    assert np.abs(q @ np.triu(work[:n, :]) - a[:, perm]).max() < 1e-12 * np.abs(a).max() * m
