@@ -282,19 +282,42 @@ template <typename F>
 __device__ __forceinline__ void apply_real(const F* packed, F* target, const F* coeff, long long pb, long long tb,
                                            long long ci, long long step, long long rows, long long prs,
                                            long long trs) {
+  // Batches of kApplyBatch rows per lane: every load of a batch is issued before the
+  // batch is folded, so a lane keeps that many global loads in flight instead of
+  // waiting on each; the fold order (rows step + lane + 32 k, ascending) is unchanged.
+  constexpr int kApplyBatch = 16;
   const int lane = threadIdx.x & 31;
   F dot = F(0);
-#pragma unroll 4
-  for (long long row = step + lane; row < rows; row += kPlane) {
-    const F v = row == step ? F(1) : packed[pb + row * prs];
-    dot = fused(v, target[tb + row * trs], dot);
+  for (long long row0 = step + lane; row0 < rows; row0 += kApplyBatch * kPlane) {
+    F vb[kApplyBatch], xb[kApplyBatch];
+#pragma unroll
+    for (int b = 0; b < kApplyBatch; ++b) {
+      const long long row = row0 + static_cast<long long>(b) * kPlane;
+      if (row < rows) {
+        vb[b] = row == step ? F(1) : packed[pb + row * prs];
+        xb[b] = target[tb + row * trs];
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < kApplyBatch; ++b)
+      if (row0 + static_cast<long long>(b) * kPlane < rows) dot = fused(vb[b], xb[b], dot);
   }
   dot = plane_sum(dot) * coeff[ci];
-#pragma unroll 4
-  for (long long row = step + lane; row < rows; row += kPlane) {
-    const F v = row == step ? F(1) : packed[pb + row * prs];
-    F& t = target[tb + row * trs];
-    t = fused(-v, dot, t);
+  for (long long row0 = step + lane; row0 < rows; row0 += kApplyBatch * kPlane) {
+    F vb[kApplyBatch], xb[kApplyBatch];
+#pragma unroll
+    for (int b = 0; b < kApplyBatch; ++b) {
+      const long long row = row0 + static_cast<long long>(b) * kPlane;
+      if (row < rows) {
+        vb[b] = row == step ? F(1) : packed[pb + row * prs];
+        xb[b] = target[tb + row * trs];
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < kApplyBatch; ++b) {
+      const long long row = row0 + static_cast<long long>(b) * kPlane;
+      if (row < rows) target[tb + row * trs] = fused(-vb[b], dot, xb[b]);
+    }
   }
 }
 
