@@ -93,27 +93,51 @@ __device__ __forceinline__ long long warp_task() {
 
 // Max-scaled 2-norm of rows [step, rows) of one column (all lanes return it);
 // `bad` = a non-finite magnitude was seen (the reflector's walk ignores it).
-template <typename T, typename F, bool kCheck>
+template <typename T, typename F, bool kCheck, int kNormBatch = 16>
 __device__ __forceinline__ F column_norm(const T* w, long long base, long long rs, long long step, long long rows,
                                          int lane, bool* bad) {
+  // Both walks take batches of kNormBatch rows per lane, every load of a batch issued
+  // before any is used, so a lane keeps that many global loads in flight; the sum of
+  // squares still folds rows step + lane + 32 k in ascending order.  (The fused pivot's
+  // rarely taken re-walk uses batches of 1, which keeps its kernels' registers.)
   F local_max = F(0);
   bool invalid = false;
-#pragma unroll 4
-  for (long long row = step + lane; row < rows; row += kPlane) {
-    const F value = mag(w[base + row * rs]);
-    if (kCheck && not_finite(value)) {
-      invalid = true;
-    } else if (value > local_max) {
-      local_max = value;
+  for (long long row0 = step + lane; row0 < rows; row0 += kNormBatch * kPlane) {
+    T xb[kNormBatch];
+#pragma unroll
+    for (int b = 0; b < kNormBatch; ++b) {
+      const long long row = row0 + static_cast<long long>(b) * kPlane;
+      if (row < rows) xb[b] = w[base + row * rs];
+    }
+#pragma unroll
+    for (int b = 0; b < kNormBatch; ++b) {
+      if (row0 + static_cast<long long>(b) * kPlane < rows) {
+        const F value = mag(xb[b]);
+        if (kCheck && not_finite(value)) {
+          invalid = true;
+        } else if (value > local_max) {
+          local_max = value;
+        }
+      }
     }
   }
   const F scale = plane_max(local_max);
   F local_sum = F(0);
   if (scale > F(0)) {
-#pragma unroll 4
-    for (long long row = step + lane; row < rows; row += kPlane) {
-      const F scaled = mag(w[base + row * rs]) / scale;
-      local_sum = fused(scaled, scaled, local_sum);
+    for (long long row0 = step + lane; row0 < rows; row0 += kNormBatch * kPlane) {
+      T xb[kNormBatch];
+#pragma unroll
+      for (int b = 0; b < kNormBatch; ++b) {
+        const long long row = row0 + static_cast<long long>(b) * kPlane;
+        if (row < rows) xb[b] = w[base + row * rs];
+      }
+#pragma unroll
+      for (int b = 0; b < kNormBatch; ++b) {
+        if (row0 + static_cast<long long>(b) * kPlane < rows) {
+          const F scaled = mag(xb[b]) / scale;
+          local_sum = fused(scaled, scaled, local_sum);
+        }
+      }
     }
   }
   if (kCheck) *bad = __any_sync(kFull, invalid);

@@ -79,7 +79,7 @@ __device__ __forceinline__ void fused_pivot(const FusedArgs<F>& a, long long ste
   F norm = a.norms[pivot];
   if (!(norm >= F(0))) {
     // Non-finite column: the reflector's own walk (it does not skip non-finite values).
-    norm = column_norm<F, F, false>(a.w, pivot * a.ld, 1, step, a.m, lane, nullptr);
+    norm = column_norm<F, F, false, 1>(a.w, pivot * a.ld, 1, step, a.m, lane, nullptr);
   }
   const F x0 = a.w[pivot * a.ld + step];
   if (lane == 0) {
