@@ -452,6 +452,14 @@ int t4a_rrqr_form_q(void* stream, int dtype, const void* work, const t4a_cuda_la
  * caller zeroes it).  work and status must be naturally aligned
  * (T4A_ERR_INVALID_STRIDE otherwise).  The workspace holds the norms and per-step
  * scalars (t4a_rrqr_workspace_bytes). */
+/* F32/F64 column_norms, reflector and apply_reflector over columns of unit row stride
+ * and at least 2048 rows from the step are planned on this library's column engine
+ * (t4a_launch.variant 66: one block of 384 threads per task, the same bits as the warp
+ * entries, which also run correctly under that geometry).  Their waits on bulk copies
+ * are bounded; one that runs out leaves the task's outputs unwritten and sets bit 1 of
+ * a device word that this call returns and clears (reference: no counterpart, the
+ * reference's primitives have no staged copies).  Synchronizes the current device. */
+int t4a_rrqr_primitive_faults(unsigned long long* faults);
 int t4a_rrqr_workspace_bytes(int dtype, const t4a_cuda_layout* work, size_t* bytes);
 int t4a_rrqr(void* stream, int dtype, void* work, const t4a_cuda_layout* work_layout, long long work_len,
              long long steps, void* permutation, void* coeff, void* pivots, void* status, void* workspace,

@@ -30,107 +30,42 @@ __global__ void __launch_bounds__(kFlatThreads) k_init_perm(long long* perm, lon
   if (done != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *done = 0;
 }
 
-template <typename T>
-__global__ void __launch_bounds__(kTaskThreads) k_column_norms(const T* w, typename RealOf<T>::F* norms,
-                                                               t4a_cuda_layout wl, t4a_cuda_layout nl, long long step,
-                                                               long long tasks) {
-  const long long task = warp_task();
-  if (task < tasks) column_norms_task<T>(w, norms, wl, nl, step, task);
-}
-
-template <typename F>
-__global__ void __launch_bounds__(kTaskThreads) k_select_pivot(const F* norms, const long long* perm,
-                                                               long long* pivots, long long* status,
-                                                               t4a_cuda_layout nl, t4a_cuda_layout pl,
-                                                               long long step, long long tasks) {
-  const long long batch = warp_task();
-  if (batch < tasks) select_pivot_task<F>(norms, perm, pivots, status, nl, pl, step, batch);
-}
-
-template <typename T>
-__global__ void __launch_bounds__(kFlatThreads) k_swap(T* w, long long* perm, const long long* pivots,
-                                                       t4a_cuda_layout wl, t4a_cuda_layout pl, long long step,
-                                                       long long len) {
-  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
-  for (long long p = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; p < len; p += stride)
-    swap_columns_elem<T>(w, perm, pivots, wl, pl, step, p);
-}
-
-template <typename T>
-__global__ void __launch_bounds__(kTaskThreads) k_reflector(T* w, T* coeff, t4a_cuda_layout wl, t4a_cuda_layout cl,
-                                                            long long step, long long tasks) {
-  const long long batch = warp_task();
-  if (batch >= tasks) return;
-  const long long base = wl.offset + step * wl.strides[1] + batch_offset(batch, wl, 2);
-  const long long ci = cl.offset + step * cl.strides[0] + batch_offset(batch, cl, 1);
-  reflector_task<T>(w, coeff, base, wl.strides[0], ci, step, wl.extents[0]);
-}
-
-template <typename T>
-__global__ void __launch_bounds__(kTaskThreads) k_apply(const T* packed, T* target, const T* coeff,
-                                                        t4a_cuda_layout pl, t4a_cuda_layout tl, t4a_cuda_layout cl,
-                                                        long long step, long long first_column,
-                                                        long long column_count, long long tasks) {
-  const long long task = warp_task();
-  if (task >= tasks) return;
-  const long long batch = task / column_count;
-  const long long column = first_column + task % column_count;
-  const long long pb = pl.offset + step * pl.strides[1] + batch_offset(batch, pl, 2);
-  const long long tb = tl.offset + column * tl.strides[1] + batch_offset(batch, tl, 2);
-  const long long ci = cl.offset + step * cl.strides[0] + batch_offset(batch, cl, 1);
-  apply_task<T>(packed, target, coeff, pb, tb, ci, step, pl.extents[0], pl.strides[0], tl.strides[0]);
-}
-
-template <typename T>
-__global__ void __launch_bounds__(kFlatThreads) k_extract_r(const T* w, T* r, t4a_cuda_layout wl, t4a_cuda_layout rl,
-                                                            long long len) {
-  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
-  for (long long f = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; f < len; f += stride)
-    extract_r_elem<T>(w, r, wl, rl, f);
-}
-
-template <typename T>
-__global__ void __launch_bounds__(kTaskThreads) k_prefix_rank(const T* r, long long* rank, long long* status,
-                                                              t4a_cuda_layout rl, double rtol, double atol,
-                                                              long long tasks) {
-  using F = typename RealOf<T>::F;
-  const long long batch = warp_task();
-  if (batch < tasks) prefix_rank_task<T>(r, rank, status, rl, static_cast<F>(rtol), static_cast<F>(atol), batch);
-}
-
-// ---- general-rank kernels: the module's `_any` entry bodies ------------------------
-__global__ void __launch_bounds__(kTaskThreads) k_norms_any(const void* w, void* norms, int dtype,
-                                                           t4a_cuda_layout_any wl, t4a_cuda_layout_any nl,
-                                                           long long step) {
+// The primitives' kernels, templated on the layout type: t4a_cuda_layout for the
+// launchers of the by-value entries, t4a_cuda_layout_any for the general-rank twins.
+// Both run the module's entry bodies (rrqr_entries.cuh).
+template <typename L>
+__global__ void __launch_bounds__(kTaskThreads) k_norms(const void* w, void* norms, int dtype, L wl, L nl,
+                                                        long long step) {
   entry::column_norms_entry(w, norms, dtype, wl, nl, step);
 }
-__global__ void __launch_bounds__(kTaskThreads) k_pivot_any(const void* norms, const void* perm, void* pivots,
-                                                           void* status, int dtype, t4a_cuda_layout_any nl,
-                                                           t4a_cuda_layout_any pl, long long step) {
+template <typename L>
+__global__ void __launch_bounds__(kTaskThreads) k_pivot(const void* norms, const void* perm, void* pivots,
+                                                        void* status, int dtype, L nl, L pl, long long step) {
   entry::select_pivot_entry(norms, perm, pivots, status, dtype, nl, pl, step);
 }
-__global__ void __launch_bounds__(kFlatThreads) k_swap_any(void* w, void* perm, const void* pivots, int dtype,
-                                                          t4a_cuda_layout_any wl, t4a_cuda_layout_any pl,
-                                                          long long step) {
+template <typename L>
+__global__ void __launch_bounds__(kFlatThreads) k_swap(void* w, void* perm, const void* pivots, int dtype, L wl, L pl,
+                                                       long long step) {
   entry::swap_entry(w, perm, pivots, dtype, wl, pl, step);
 }
-__global__ void __launch_bounds__(kTaskThreads) k_reflector_any(void* w, void* coeff, int dtype,
-                                                               t4a_cuda_layout_any wl, t4a_cuda_layout_any cl,
-                                                               long long step) {
+template <typename L>
+__global__ void __launch_bounds__(kTaskThreads) k_reflector(void* w, void* coeff, int dtype, L wl, L cl,
+                                                            long long step) {
   entry::reflector_entry(w, coeff, dtype, wl, cl, step);
 }
-__global__ void __launch_bounds__(kTaskThreads) k_apply_any(const void* packed, void* target, const void* coeff,
-                                                           int dtype, t4a_cuda_layout_any pl, t4a_cuda_layout_any tl,
-                                                           t4a_cuda_layout_any cl, long long step,
-                                                           long long first_column, long long column_count) {
+template <typename L>
+__global__ void __launch_bounds__(kTaskThreads) k_apply(const void* packed, void* target, const void* coeff,
+                                                        int dtype, L pl, L tl, L cl, long long step,
+                                                        long long first_column, long long column_count) {
   entry::apply_entry(packed, target, coeff, dtype, pl, tl, cl, step, first_column, column_count);
 }
-__global__ void __launch_bounds__(kFlatThreads) k_extract_r_any(const void* w, void* r, int dtype,
-                                                               t4a_cuda_layout_any wl, t4a_cuda_layout_any rl) {
+template <typename L>
+__global__ void __launch_bounds__(kFlatThreads) k_extract_r(const void* w, void* r, int dtype, L wl, L rl) {
   entry::extract_entry(w, r, dtype, wl, rl);
 }
-__global__ void __launch_bounds__(kTaskThreads) k_prefix_rank_any(const void* r, void* rank, void* status, int dtype,
-                                                                 t4a_cuda_layout_any rl, double rtol, double atol) {
+template <typename L>
+__global__ void __launch_bounds__(kTaskThreads) k_prefix_rank(const void* r, void* rank, void* status, int dtype,
+                                                              L rl, double rtol, double atol) {
   entry::prefix_rank_entry(r, rank, status, dtype, rl, rtol, atol);
 }
 
@@ -170,9 +105,57 @@ __global__ void __launch_bounds__(kColThreads, 2) k_col_step(FusedArgs<F> a, lon
 // Q formation pass for reflector `step`: one block per column of Q.
 template <typename F>
 __global__ void __launch_bounds__(kColThreads, 2) k_q_step(FusedArgs<F> a, long long step, F* q, long long qld,
-                                                          long long qcols, long long q_span) {
+                                                          long long qcols) {
   extern __shared__ __align__(128) unsigned char smem[];
-  column_q<F>(a, step, q, qld, qcols, q_span, *reinterpret_cast<ColSmem<F>*>(smem));
+  column_q<F>(a, step, q, qld, qcols, *reinterpret_cast<ColSmem<F>*>(smem));
+}
+
+// ---- the primitives on the column engine -------------------------------------------
+// F32/F64 columns with unit row stride and at least kEngineRows rows from `step` run one
+// block per task on the column engine instead of one warp per task; the results are
+// the same bits.  A bounded wait that runs out sets bit 1 of g_engine_faults (read and
+// cleared by t4a_rrqr_primitive_faults) and leaves that task's outputs unwritten.
+constexpr int kRrqrEngineVariant = kRrqrVariant + 2;
+constexpr long long kEngineRows = 2048;
+
+__device__ unsigned long long g_engine_faults;
+
+__device__ __forceinline__ long long* engine_faults() { return reinterpret_cast<long long*>(&g_engine_faults); }
+
+template <typename F>
+__global__ void __launch_bounds__(kColThreads, 2) k_eng_norms(const F* w, F* norms, t4a_cuda_layout wl,
+                                                             t4a_cuda_layout nl, long long step) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const long long width = wl.extents[1] - step;
+  const long long b = blockIdx.x / width;
+  const long long col = step + (blockIdx.x - b * width);
+  engine_norms_task<F>(w + wl.offset + col * wl.strides[1] + batch_base(wl, 2, b), step, wl.extents[0],
+                       norms + nl.offset + col * nl.strides[0] + batch_base(nl, 1, b), engine_faults(),
+                       *reinterpret_cast<ColSmem<F>*>(smem));
+}
+
+template <typename F>
+__global__ void __launch_bounds__(kColThreads, 2) k_eng_reflector(F* w, F* coeff, t4a_cuda_layout wl,
+                                                                 t4a_cuda_layout cl, long long step) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const long long b = blockIdx.x;
+  engine_reflect_task<F>(w + wl.offset + step * wl.strides[1] + batch_base(wl, 2, b), step, wl.extents[0],
+                         coeff + cl.offset + step * cl.strides[0] + batch_base(cl, 1, b), engine_faults(),
+                         *reinterpret_cast<ColSmem<F>*>(smem));
+}
+
+template <typename F>
+__global__ void __launch_bounds__(kColThreads, 2) k_eng_apply(const F* packed, F* target, const F* coeff,
+                                                             t4a_cuda_layout pl, t4a_cuda_layout tl,
+                                                             t4a_cuda_layout cl, long long step,
+                                                             long long first_column, long long column_count) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const long long b = blockIdx.x / column_count;
+  const long long col = first_column + (blockIdx.x - b * column_count);
+  const F* v = packed + pl.offset + step * pl.strides[1] + batch_base(pl, 2, b) + step;
+  F* t = target + tl.offset + col * tl.strides[1] + batch_base(tl, 2, b) + step;
+  const F c = coeff[cl.offset + step * cl.strides[0] + batch_base(cl, 1, b)];
+  engine_apply_task<F>(v, t, pl.extents[0] - step, c, engine_faults(), *reinterpret_cast<ColSmem<F>*>(smem));
 }
 
 // Raises a kernel's dynamic shared memory limit once on each device.
@@ -217,7 +200,6 @@ int run_fused(cudaStream_t s, F* w, long long m, long long n, long long ld, long
   a.pivots = pivots;
   a.status = status;
   a.norms = reinterpret_cast<F*>(ws + L.norms);
-  a.span = ld * (n - 1) + m;
   a.rec = reinterpret_cast<StepRecord<F>*>(ws + L.rec);
   a.done = reinterpret_cast<unsigned*>(ws + L.done);
   static std::atomic<unsigned long long> raised_first{0}, raised_step{0};
@@ -253,12 +235,11 @@ int run_form_q(cudaStream_t s, const F* w, long long m, long long ld, long long 
   a.ld = ld;
   a.coeff = const_cast<F*>(coeff);
   a.status = status;
-  a.span = w_span;
   static std::atomic<unsigned long long> raised{0};
   const unsigned smem = sizeof(ColSmem<F>);
   T4A_TRY(allow_smem(k_q_step<F>, smem, raised));
   for (long long step = k - 1; step >= 0; --step)
-    k_q_step<F><<<dim3(static_cast<unsigned>(k)), dim3(kColThreads), smem, s>>>(a, step, q, qld, k, q_span);
+    k_q_step<F><<<dim3(static_cast<unsigned>(k)), dim3(kColThreads), smem, s>>>(a, step, q, qld, k);
   return runtime::check_launch();
 }
 
@@ -330,6 +311,41 @@ int flat_geometry(long long len, t4a_launch* launch) {
   return T4A_OK;
 }
 
+// One block per task on the column engine (F32/F64, unit row stride, at least
+// kEngineRows rows from the step).  The module's warp entries run correctly under this
+// geometry too (one task per warp; the extra warps return).
+bool engine_eligible(int dtype, long long rows, long long row_stride) {
+  return (dtype == T4A_CUDA_F32 || dtype == T4A_CUDA_F64) && row_stride == 1 && rows >= kEngineRows;
+}
+
+int task_geometry(int dtype, long long tasks, long long rows, long long row_stride, t4a_launch* launch) {
+  if (tasks > 0 && tasks <= 0x7fffffffll && engine_eligible(dtype, rows, row_stride)) {
+    *launch = plan::make_launch(static_cast<unsigned long long>(tasks), kColThreads, 1, 0, kRrqrEngineVariant);
+    return T4A_OK;
+  }
+  return plane_geometry(tasks, launch);
+}
+
+// The engine path at launch: the planned variant, and a layout and pointers that still
+// qualify (the launchers take layouts by value).
+template <typename F>
+bool engine_runs(const t4a_launch* launch, const void* p, const void* q, long long rows, long long s0,
+                 long long s1) {
+  const auto a = [](const void* x) { return reinterpret_cast<unsigned long long>(x) % sizeof(F) == 0; };
+  return launch->variant == kRrqrEngineVariant && s0 == 1 && s1 == 1 && rows >= kEngineRows && a(p) && a(q);
+}
+
+// Launches a column-engine kernel: one block of kColThreads per planned task, with the
+// engine's shared memory (its limit raised once per device and kernel).
+template <typename F, typename... KArgs, typename... Args>
+int launch_engine(void (*kernel)(KArgs...), const t4a_launch* launch, cudaStream_t s, Args... args) {
+  static std::atomic<unsigned long long> raised{0};
+  const unsigned smem = sizeof(ColSmem<F>);
+  T4A_TRY(allow_smem(kernel, smem, raised));
+  kernel<<<dim3(launch->grid[0]), dim3(kColThreads), smem, s>>>(args...);
+  return runtime::check_launch();
+}
+
 dim3 grid_of_launch(const t4a_launch* l) { return dim3(l->grid[0], l->grid[1] ? l->grid[1] : 1, l->grid[2] ? l->grid[2] : 1); }
 dim3 block_of_launch(const t4a_launch* l) { return dim3(l->block[0], l->block[1] ? l->block[1] : 1, l->block[2] ? l->block[2] : 1); }
 bool launch_empty(const t4a_launch* l) { return l->grid[0] == 0 || l->block[0] == 0; }
@@ -366,7 +382,7 @@ int t4a_plan_column_norms(int dtype, const t4a_cuda_layout* work, long long work
   long long batches = 0, tasks = 0;
   T4A_TRY(batches_of(*work, 2, &batches));
   if (mul_overflows(batches, cols - step, &tasks)) return T4A_ERR_OVERFLOW;
-  return plane_geometry(tasks, launch);
+  return task_geometry(dtype, tasks, rows - step, work->strides[0], launch);
 }
 
 int t4a_plan_select_pivot(int dtype, const t4a_cuda_layout* norms, long long norms_len,
@@ -427,7 +443,7 @@ int t4a_plan_reflector(int dtype, const t4a_cuda_layout* work, long long work_le
   T4A_TRY(check_span(*coeff, coeff_len, dtype_size(dtype)));
   long long batches = 0;
   T4A_TRY(batches_of(*work, 2, &batches));
-  return plane_geometry(batches, launch);
+  return task_geometry(dtype, batches, work->extents[0] - step, work->strides[0], launch);
 }
 
 int t4a_plan_apply_reflector(int dtype, const t4a_cuda_layout* packed, long long packed_len,
@@ -456,7 +472,8 @@ int t4a_plan_apply_reflector(int dtype, const t4a_cuda_layout* packed, long long
   long long batches = 0, tasks = 0;
   T4A_TRY(batches_of(*packed, 2, &batches));
   if (mul_overflows(batches, column_count, &tasks)) return T4A_ERR_OVERFLOW;
-  return plane_geometry(tasks, launch);
+  return task_geometry(dtype, tasks, packed->extents[0] - step,
+                       packed->strides[0] == 1 && target->strides[0] == 1 ? 1 : 0, launch);
 }
 
 int t4a_plan_extract_r(int dtype, const t4a_cuda_layout* work, long long work_len, const t4a_cuda_layout* r,
@@ -510,30 +527,17 @@ int t4a_launch_column_norms(const t4a_launch* launch, void* stream, const void* 
                             t4a_cuda_layout work_layout, t4a_cuda_layout norms_layout, long long step) {
   if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
   if (launch_empty(launch)) return T4A_OK;
-  long long batches = 1;
-  for (int ax = 2; ax < work_layout.rank; ++ax) batches *= work_layout.extents[ax];
-  const long long tasks = batches * (work_layout.extents[1] - step);
-  const dim3 g = grid_of_launch(launch), b = block_of_launch(launch);
+  T4A_TRY(check_algebra(dtype));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  switch (dtype) {
-    case T4A_CUDA_F32:
-      k_column_norms<float><<<g, b, 0, s>>>(static_cast<const float*>(work), static_cast<float*>(norms), work_layout,
-                                            norms_layout, step, tasks);
-      break;
-    case T4A_CUDA_F64:
-      k_column_norms<double><<<g, b, 0, s>>>(static_cast<const double*>(work), static_cast<double*>(norms),
-                                             work_layout, norms_layout, step, tasks);
-      break;
-    case T4A_CUDA_C32:
-      k_column_norms<c32><<<g, b, 0, s>>>(static_cast<const c32*>(work), static_cast<float*>(norms), work_layout,
-                                          norms_layout, step, tasks);
-      break;
-    case T4A_CUDA_C64:
-      k_column_norms<c64><<<g, b, 0, s>>>(static_cast<const c64*>(work), static_cast<double*>(norms), work_layout,
-                                          norms_layout, step, tasks);
-      break;
-    default: return T4A_ERR_UNSUPPORTED_DTYPE;
-  }
+  const long long rows = work_layout.extents[0] - step;
+  if (dtype == T4A_CUDA_F64 && engine_runs<double>(launch, work, norms, rows, work_layout.strides[0], 1))
+    return launch_engine<double>(k_eng_norms<double>, launch, s, static_cast<const double*>(work),
+                         static_cast<double*>(norms), work_layout, norms_layout, step);
+  if (dtype == T4A_CUDA_F32 && engine_runs<float>(launch, work, norms, rows, work_layout.strides[0], 1))
+    return launch_engine<float>(k_eng_norms<float>, launch, s, static_cast<const float*>(work), static_cast<float*>(norms),
+                         work_layout, norms_layout, step);
+  k_norms<t4a_cuda_layout><<<grid_of_launch(launch), block_of_launch(launch), 0, s>>>(work, norms, dtype, work_layout,
+                                                                                     norms_layout, step);
   return runtime::check_launch();
 }
 
@@ -542,24 +546,9 @@ int t4a_launch_select_pivot(const t4a_launch* launch, void* stream, const void* 
                             t4a_cuda_layout permutation_layout, long long step) {
   if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
   if (launch_empty(launch)) return T4A_OK;
-  long long batches = 1;
-  for (int ax = 1; ax < norms_layout.rank; ++ax) batches *= norms_layout.extents[ax];
-  const dim3 g = grid_of_launch(launch), b = block_of_launch(launch);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  auto* piv = static_cast<long long*>(pivots);
-  auto* st = static_cast<long long*>(status);
-  const auto* perm = static_cast<const long long*>(permutation);
-  switch (dtype) {
-    case T4A_CUDA_F32:
-      k_select_pivot<float><<<g, b, 0, s>>>(static_cast<const float*>(norms), perm, piv, st, norms_layout,
-                                            permutation_layout, step, batches);
-      break;
-    case T4A_CUDA_F64:
-      k_select_pivot<double><<<g, b, 0, s>>>(static_cast<const double*>(norms), perm, piv, st, norms_layout,
-                                             permutation_layout, step, batches);
-      break;
-    default: return T4A_ERR_UNSUPPORTED_DTYPE;
-  }
+  if (dtype != T4A_CUDA_F32 && dtype != T4A_CUDA_F64) return T4A_ERR_UNSUPPORTED_DTYPE;
+  k_pivot<t4a_cuda_layout><<<grid_of_launch(launch), block_of_launch(launch), 0, static_cast<cudaStream_t>(stream)>>>(
+      norms, permutation, pivots, status, dtype, norms_layout, permutation_layout, step);
   return runtime::check_launch();
 }
 
@@ -568,25 +557,9 @@ int t4a_launch_swap_columns(const t4a_launch* launch, void* stream, void* work, 
                             t4a_cuda_layout permutation_layout, long long step) {
   if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
   if (launch_empty(launch)) return T4A_OK;
-  long long batches = 1;
-  for (int ax = 2; ax < work_layout.rank; ++ax) batches *= work_layout.extents[ax];
-  const long long len = work_layout.extents[0] * batches;
-  const dim3 g = grid_of_launch(launch), b = block_of_launch(launch);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  auto* perm = static_cast<long long*>(permutation);
-  const auto* piv = static_cast<const long long*>(pivots);
-#define T4A_SWAP(T) \
-  k_swap<T><<<g, b, 0, s>>>(static_cast<T*>(work), perm, piv, work_layout, permutation_layout, step, len)
-  switch (dtype) {
-    case T4A_CUDA_F32: T4A_SWAP(float); break;
-    case T4A_CUDA_F64: T4A_SWAP(double); break;
-    case T4A_CUDA_I32: T4A_SWAP(int); break;
-    case T4A_CUDA_I64: T4A_SWAP(long long); break;
-    case T4A_CUDA_C32: T4A_SWAP(c32); break;
-    case T4A_CUDA_C64: T4A_SWAP(c64); break;
-    default: return T4A_ERR_UNSUPPORTED_DTYPE;
-  }
-#undef T4A_SWAP
+  T4A_TRY(check_numeric(dtype));
+  k_swap<t4a_cuda_layout><<<grid_of_launch(launch), block_of_launch(launch), 0, static_cast<cudaStream_t>(stream)>>>(
+      work, permutation, pivots, dtype, work_layout, permutation_layout, step);
   return runtime::check_launch();
 }
 
@@ -594,20 +567,18 @@ int t4a_launch_reflector(const t4a_launch* launch, void* stream, void* work, voi
                          t4a_cuda_layout work_layout, t4a_cuda_layout coeff_layout, long long step) {
   if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
   if (launch_empty(launch)) return T4A_OK;
-  long long batches = 1;
-  for (int ax = 2; ax < work_layout.rank; ++ax) batches *= work_layout.extents[ax];
-  const dim3 g = grid_of_launch(launch), b = block_of_launch(launch);
+  T4A_TRY(check_algebra(dtype));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-#define T4A_REFL(T) \
-  k_reflector<T><<<g, b, 0, s>>>(static_cast<T*>(work), static_cast<T*>(coeff), work_layout, coeff_layout, step, batches)
-  switch (dtype) {
-    case T4A_CUDA_F32: T4A_REFL(float); break;
-    case T4A_CUDA_F64: T4A_REFL(double); break;
-    case T4A_CUDA_C32: T4A_REFL(c32); break;
-    case T4A_CUDA_C64: T4A_REFL(c64); break;
-    default: return T4A_ERR_UNSUPPORTED_DTYPE;
-  }
-#undef T4A_REFL
+  const long long rows = work_layout.extents[0] - step;
+  if (dtype == T4A_CUDA_F64 && engine_runs<double>(launch, work, coeff, rows, work_layout.strides[0], 1))
+    return launch_engine<double>(k_eng_reflector<double>, launch, s, static_cast<double*>(work), static_cast<double*>(coeff),
+                         work_layout, coeff_layout, step);
+  if (dtype == T4A_CUDA_F32 && engine_runs<float>(launch, work, coeff, rows, work_layout.strides[0], 1))
+    return launch_engine<float>(k_eng_reflector<float>, launch, s, static_cast<float*>(work), static_cast<float*>(coeff),
+                         work_layout, coeff_layout, step);
+  k_reflector<t4a_cuda_layout><<<grid_of_launch(launch), block_of_launch(launch), 0, s>>>(work, coeff, dtype,
+                                                                                         work_layout, coeff_layout,
+                                                                                         step);
   return runtime::check_launch();
 }
 
@@ -617,22 +588,21 @@ int t4a_launch_apply_reflector(const t4a_launch* launch, void* stream, const voi
                                long long first_column, long long column_count) {
   if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
   if (launch_empty(launch) || column_count <= 0) return T4A_OK;
-  long long batches = 1;
-  for (int ax = 2; ax < packed_layout.rank; ++ax) batches *= packed_layout.extents[ax];
-  const long long tasks = batches * column_count;
-  const dim3 g = grid_of_launch(launch), b = block_of_launch(launch);
+  T4A_TRY(check_algebra(dtype));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-#define T4A_APPLY(T)                                                                                               \
-  k_apply<T><<<g, b, 0, s>>>(static_cast<const T*>(packed), static_cast<T*>(target), static_cast<const T*>(coeff), \
-                             packed_layout, target_layout, coeff_layout, step, first_column, column_count, tasks)
-  switch (dtype) {
-    case T4A_CUDA_F32: T4A_APPLY(float); break;
-    case T4A_CUDA_F64: T4A_APPLY(double); break;
-    case T4A_CUDA_C32: T4A_APPLY(c32); break;
-    case T4A_CUDA_C64: T4A_APPLY(c64); break;
-    default: return T4A_ERR_UNSUPPORTED_DTYPE;
-  }
-#undef T4A_APPLY
+  const long long rows = packed_layout.extents[0] - step;
+  if (dtype == T4A_CUDA_F64 &&
+      engine_runs<double>(launch, packed, target, rows, packed_layout.strides[0], target_layout.strides[0]))
+    return launch_engine<double>(k_eng_apply<double>, launch, s, static_cast<const double*>(packed),
+                         static_cast<double*>(target), static_cast<const double*>(coeff), packed_layout, target_layout,
+                         coeff_layout, step, first_column, column_count);
+  if (dtype == T4A_CUDA_F32 &&
+      engine_runs<float>(launch, packed, target, rows, packed_layout.strides[0], target_layout.strides[0]))
+    return launch_engine<float>(k_eng_apply<float>, launch, s, static_cast<const float*>(packed), static_cast<float*>(target),
+                         static_cast<const float*>(coeff), packed_layout, target_layout, coeff_layout, step,
+                         first_column, column_count);
+  k_apply<t4a_cuda_layout><<<grid_of_launch(launch), block_of_launch(launch), 0, s>>>(
+      packed, target, coeff, dtype, packed_layout, target_layout, coeff_layout, step, first_column, column_count);
   return runtime::check_launch();
 }
 
@@ -640,20 +610,9 @@ int t4a_launch_extract_r(const t4a_launch* launch, void* stream, const void* wor
                          t4a_cuda_layout work_layout, t4a_cuda_layout r_layout) {
   if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
   if (launch_empty(launch)) return T4A_OK;
-  long long len = 1;
-  for (int ax = 0; ax < r_layout.rank; ++ax) len *= r_layout.extents[ax];
-  const dim3 g = grid_of_launch(launch), b = block_of_launch(launch);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-#define T4A_EXTRACT(T) \
-  k_extract_r<T><<<g, b, 0, s>>>(static_cast<const T*>(work), static_cast<T*>(r), work_layout, r_layout, len)
-  switch (dtype) {
-    case T4A_CUDA_F32: T4A_EXTRACT(float); break;
-    case T4A_CUDA_F64: T4A_EXTRACT(double); break;
-    case T4A_CUDA_C32: T4A_EXTRACT(c32); break;
-    case T4A_CUDA_C64: T4A_EXTRACT(c64); break;
-    default: return T4A_ERR_UNSUPPORTED_DTYPE;
-  }
-#undef T4A_EXTRACT
+  T4A_TRY(check_algebra(dtype));
+  k_extract_r<t4a_cuda_layout><<<grid_of_launch(launch), block_of_launch(launch), 0,
+                                 static_cast<cudaStream_t>(stream)>>>(work, r, dtype, work_layout, r_layout);
   return runtime::check_launch();
 }
 
@@ -661,22 +620,9 @@ int t4a_launch_prefix_rank(const t4a_launch* launch, void* stream, const void* r
                            t4a_cuda_layout r_layout, double rtol, double atol) {
   if (launch == nullptr) return T4A_ERR_NULL_ARGUMENT;
   if (launch_empty(launch)) return T4A_OK;
-  long long batches = 1;
-  for (int ax = 2; ax < r_layout.rank; ++ax) batches *= r_layout.extents[ax];
-  const dim3 g = grid_of_launch(launch), b = block_of_launch(launch);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  auto* rk = static_cast<long long*>(rank);
-  auto* st = static_cast<long long*>(status);
-#define T4A_RANK(T) \
-  k_prefix_rank<T><<<g, b, 0, s>>>(static_cast<const T*>(r), rk, st, r_layout, rtol, atol, batches)
-  switch (dtype) {
-    case T4A_CUDA_F32: T4A_RANK(float); break;
-    case T4A_CUDA_F64: T4A_RANK(double); break;
-    case T4A_CUDA_C32: T4A_RANK(c32); break;
-    case T4A_CUDA_C64: T4A_RANK(c64); break;
-    default: return T4A_ERR_UNSUPPORTED_DTYPE;
-  }
-#undef T4A_RANK
+  T4A_TRY(check_algebra(dtype));
+  k_prefix_rank<t4a_cuda_layout><<<grid_of_launch(launch), block_of_launch(launch), 0,
+                                   static_cast<cudaStream_t>(stream)>>>(r, rank, status, dtype, r_layout, rtol, atol);
   return runtime::check_launch();
 }
 
@@ -712,7 +658,7 @@ int t4a_launch_column_norms_any(const t4a_launch* launch, void* stream, const vo
   T4A_TRY(check_rrqr_any(work_layout, 2));
   T4A_TRY(check_rrqr_any(norms_layout, 1));
   T4A_ANY_PROLOGUE;
-  k_norms_any<<<g, b, 0, s>>>(work, norms, dtype, work_layout, norms_layout, step);
+  k_norms<t4a_cuda_layout_any><<<g, b, 0, s>>>(work, norms, dtype, work_layout, norms_layout, step);
   return runtime::check_launch();
 }
 
@@ -723,7 +669,7 @@ int t4a_launch_select_pivot_any(const t4a_launch* launch, void* stream, const vo
   T4A_TRY(check_rrqr_any(norms_layout, 1));
   T4A_TRY(check_rrqr_any(permutation_layout, 1));
   T4A_ANY_PROLOGUE;
-  k_pivot_any<<<g, b, 0, s>>>(norms, permutation, pivots, status, dtype, norms_layout, permutation_layout, step);
+  k_pivot<t4a_cuda_layout_any><<<g, b, 0, s>>>(norms, permutation, pivots, status, dtype, norms_layout, permutation_layout, step);
   return runtime::check_launch();
 }
 
@@ -734,7 +680,7 @@ int t4a_launch_swap_columns_any(const t4a_launch* launch, void* stream, void* wo
   T4A_TRY(check_rrqr_any(work_layout, 2));
   T4A_TRY(check_rrqr_any(permutation_layout, 1));
   T4A_ANY_PROLOGUE;
-  k_swap_any<<<g, b, 0, s>>>(work, permutation, pivots, dtype, work_layout, permutation_layout, step);
+  k_swap<t4a_cuda_layout_any><<<g, b, 0, s>>>(work, permutation, pivots, dtype, work_layout, permutation_layout, step);
   return runtime::check_launch();
 }
 
@@ -744,7 +690,7 @@ int t4a_launch_reflector_any(const t4a_launch* launch, void* stream, void* work,
   T4A_TRY(check_rrqr_any(work_layout, 2));
   T4A_TRY(check_rrqr_any(coeff_layout, 1));
   T4A_ANY_PROLOGUE;
-  k_reflector_any<<<g, b, 0, s>>>(work, coeff, dtype, work_layout, coeff_layout, step);
+  k_reflector<t4a_cuda_layout_any><<<g, b, 0, s>>>(work, coeff, dtype, work_layout, coeff_layout, step);
   return runtime::check_launch();
 }
 
@@ -757,7 +703,7 @@ int t4a_launch_apply_reflector_any(const t4a_launch* launch, void* stream, const
   T4A_TRY(check_rrqr_any(target_layout, 2));
   T4A_TRY(check_rrqr_any(coeff_layout, 1));
   T4A_ANY_PROLOGUE;
-  k_apply_any<<<g, b, 0, s>>>(packed, target, coeff, dtype, packed_layout, target_layout, coeff_layout, step,
+  k_apply<t4a_cuda_layout_any><<<g, b, 0, s>>>(packed, target, coeff, dtype, packed_layout, target_layout, coeff_layout, step,
                               first_column, column_count);
   return runtime::check_launch();
 }
@@ -768,7 +714,7 @@ int t4a_launch_extract_r_any(const t4a_launch* launch, void* stream, const void*
   T4A_TRY(check_rrqr_any(work_layout, 2));
   T4A_TRY(check_rrqr_any(r_layout, 2));
   T4A_ANY_PROLOGUE;
-  k_extract_r_any<<<g, b, 0, s>>>(work, r, dtype, work_layout, r_layout);
+  k_extract_r<t4a_cuda_layout_any><<<g, b, 0, s>>>(work, r, dtype, work_layout, r_layout);
   return runtime::check_launch();
 }
 
@@ -777,7 +723,7 @@ int t4a_launch_prefix_rank_any(const t4a_launch* launch, void* stream, const voi
   T4A_TRY(check_algebra(dtype));
   T4A_TRY(check_rrqr_any(r_layout, 2));
   T4A_ANY_PROLOGUE;
-  k_prefix_rank_any<<<g, b, 0, s>>>(r, rank, status, dtype, r_layout, rtol, atol);
+  k_prefix_rank<t4a_cuda_layout_any><<<g, b, 0, s>>>(r, rank, status, dtype, r_layout, rtol, atol);
   return runtime::check_launch();
 }
 #undef T4A_ANY_PROLOGUE
@@ -917,6 +863,21 @@ int t4a_rrqr_form_q(void* stream, int dtype, const void* work, const t4a_cuda_la
                                      k, &a));
     T4A_TRY(t4a_launch_apply_reflector(&a, stream, work, q, coeff, dtype, *work_layout, *q_layout, *coeff_layout,
                                        step, 0, k));
+  }
+  return T4A_OK;
+}
+
+// Faults of the column-engine primitives since the last call (bit 1: a bounded wait ran
+// out and a task's outputs were left unwritten); reading clears them.  Synchronizes the
+// current device.
+int t4a_rrqr_primitive_faults(unsigned long long* faults) {
+  if (faults == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  unsigned long long zero = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(faults, g_engine_faults, sizeof(zero));
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_engine_faults, &zero, sizeof(zero));
+  if (e != cudaSuccess) {
+    runtime::last_error() = static_cast<int>(e);
+    return T4A_ERR_CUDA;
   }
   return T4A_OK;
 }

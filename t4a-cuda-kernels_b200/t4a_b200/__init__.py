@@ -122,6 +122,7 @@ def _declare(l):
         "t4a_launch_extract_r": (I, [ctypes.POINTER(Launch), P, P, P, I, LB, LB]),
         "t4a_launch_prefix_rank": (I, [ctypes.POINTER(Launch), P, P, P, P, I, LB, ctypes.c_double, ctypes.c_double]),
         "t4a_rrqr_workspace_bytes": (I, [I, LP, ctypes.POINTER(SZ)]),
+        "t4a_rrqr_primitive_faults": (I, [ctypes.POINTER(ctypes.c_ulonglong)]),
         "t4a_rrqr": (I, [P, I, P, LP, LL, LL, P, P, P, P, P, SZ]),
         "t4a_rrqr_form_q": (I, [P, I, P, LP, LL, P, LP, LL, P, LP, LL, P]),
         "t4a_plan_identity_shifted": (I, [I, LP, LL, LL, ctypes.POINTER(Launch)]),
@@ -513,6 +514,14 @@ def rrqr_form_q(work, coeff, k=None, q=None, stream=None, status=None):
                                 _ptr(status)),
           "rrqr_form_q")
     return q, status
+
+
+def rrqr_primitive_faults():
+    """Faults of the column-engine primitives since the last call (bit 1: a bounded wait
+    ran out and a task's outputs were left unwritten); reading clears them."""
+    f = ctypes.c_ulonglong(0)
+    check(lib().t4a_rrqr_primitive_faults(ctypes.byref(f)), "rrqr_primitive_faults")
+    return f.value
 
 
 def rrqr_workspace_bytes(dtype, work_layout):
