@@ -1,26 +1,53 @@
 """Benchmark of the t4a_b200 hot path on B200 (one JSON line on stdout, rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--op NAME]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--op all|movement|reduce|gather|rrqr] [--only TAGS] [--no-cpu-baseline]
 
-Headline workload ("Permutation movement"): one step is
-  * F32 [64,64,64,64] materialized in permutation (3,1,0,2),
-  * C64 [16]^6 materialized in permutation (5,0,4,1,3,2),
-  * F32 [64,64,64,64] with axis 2 reversed (negated stride, rebased offset),
-through the library's strided-copy entry (t4a_copy_strided / the strided_to_strided
-plan).  Inputs are seeded normal(0,1) values (synthetic; no dataset is involved).
-`value` is the algorithmic HBM traffic (each element read once and written once)
-per second of kernel time, summed over all ranks; each rank copies its own full
-workload (weak scaling, no collective: the movement ops shard by independent
-tensors).  L2 is flushed before every op (a 256 MiB read, outside the timed events),
-so every kernel streams from HBM and starts without another kernel's dirty lines.
+One step runs every operation of the BASELINE configurations once, back to back on one
+stream (the default `--op all`):
+  config 1  F64 [256,1024,64] uniform(-1,1): sum and max over NumPy axis 1;
+  config 2  F32 [64]^4 permuted (3,1,0,2), C64 [16]^6 permuted (5,0,4,1,3,2), F32 [64]^4
+            with axis 2 reversed (strided_to_strided);
+  config 3  F32 [4096,4096,32] normal: sum, sum_squares and max over each NumPy axis;
+            C64 [8192,8192] sum over axis 1 (split reductions: partials + combine);
+  config 4  gather of 4,194,304 rows of an F32 [1048576,128] table by uniform I64
+            indices; scatter_add of F64 [4194304,128] updates into [1048576,128] with
+            Zipf(1.1) indices;
+  config 5  F64 RRQR of [65536,256] = U V^T + 1e-10 N, 256 steps (t4a_rrqr).
+Inputs are seeded synthetic values (SplitMix64 streams; NumPy generators for config 5);
+no dataset is involved.
 
-`--op` selects another BASELINE config as the workload (reduce; gather = gather and
-scatter_add; rrqr) for the secondary lines; the driver's runs use the default.
+`value` is algorithmic HBM bytes (each logical input element read once, each output
+element written once; workspace excluded) over kernel time: the sum over ops of the
+bytes of the whole job (all ranks) divided by the max over ranks of the summed CUDA-event
+time of the ops.  Timing is steady state: the ops of a step run back to back with no L2
+flush; a step touches about 12 GB, so every op starts with its inputs evicted from L2 by
+the ops before it and pays for the write-back of the previous op's dirty lines.  A
+second, shorter pass flushes L2 (a 256 MiB read) before every op and reports each op's
+cold figure beside the steady one.
 
-`--impl reference` times the reference path's CPU implementation on this box's host
-cores: the reference library has no CPU path of its own (its Rust crate only plans),
-so the arm runs the C++ restatement under oracle/ (the same semantics, the same
-inputs), multi-threaded over the host cores, on a bounded sample per step.
+At `--gpus N` (torchrun, one rank per GPU) every op is sharded (strong scaling: the
+global problem stays the same):
+  reductions  slabs of a non-reduced axis, one per rank, resident on that rank;
+  movement    destination slabs along its slowest axis, each written from the strided
+              view of the (replicated) source that feeds it;
+  gather      index batches, table replicated;
+  scatter_add update batches into per-rank partial destinations, then an NCCL
+              reduce-scatter of the partials inside the timed op;
+  RRQR        row blocks, with the per-step exchange of column norms and reflector dots.
+Before timing, every rank checks its shard against the single-GPU result of the same
+library (computed on that rank from the full input): bit for bit for reductions,
+movement and gather; for scatter_add (atomic, so its summation order is not fixed)
+within the bound on reordering a sum of n terms, 2 (n - 1) 2^-53 sum|x| per element; for
+RRQR the pivots over the rank-revealing prefix and the factorization residual.  A
+mismatch exits non-zero.
+
+`e2e` is the same bytes through the public C ABI with this rank's inputs copied from
+pinned host memory every step and each op's results copied back, on three streams as a
+caller pipelines them.  `cpu_baseline` (rank 0, N=1) and `--impl reference` time the
+path's CPU implementation on this box's host cores: the reference library has no CPU
+path of its own (its Rust crate only plans), so both run the C++ restatement under
+oracle/ on a bounded sample of every op.
 """
 import argparse
 import ctypes
@@ -35,6 +62,9 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "t4a-cuda-kernels_b200"))
 
+MIB = 1 << 20
+METRIC = "achieved HBM GB/s (% of B200 peak) per op at 1/2/4/8 GPUs vs CPU baseline"
+
 
 def _oracle():
     """The CPU restatement (oracle/), used only by the CPU-baseline leg and --impl reference."""
@@ -42,8 +72,6 @@ def _oracle():
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
     return oracle
-
-MIB = 1 << 20
 
 
 def read_peaks():
@@ -56,14 +84,17 @@ def read_peaks():
         return 6650.0, "fallback"
 
 
-def profile_traffic(kernel_tag):
-    """Per-launch DRAM bytes of a kernel from a committed ncu summary, or None."""
-    for name in sorted(os.listdir(os.path.join(ROOT, "profiles"))) if os.path.isdir(os.path.join(ROOT, "profiles")) else []:
+def profile_traffic(tag):
+    """Per-launch DRAM bytes of an op from a committed ncu summary, or None."""
+    pdir = os.path.join(ROOT, "profiles")
+    if not os.path.isdir(pdir):
+        return None
+    for name in sorted(os.listdir(pdir)):
         if not name.endswith((".md", ".txt")):
             continue
-        with open(os.path.join(ROOT, "profiles", name)) as fh:
+        with open(os.path.join(pdir, name)) as fh:
             for line in fh:
-                if line.startswith(f"traffic_per_launch[{kernel_tag}]"):
+                if line.startswith(f"traffic_per_launch[{tag}]"):
                     try:
                         return int(line.split("=")[1].split()[0])
                     except (IndexError, ValueError):
@@ -121,27 +152,9 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------
-# Workloads.  Each builds its device inputs and returns a list of ops; an op is
-# (tag, algorithmic bytes, launch(stream), host_inputs, device_inputs, device_outputs).
+# Seeded inputs (counter-based SplitMix64, so any slice of a stream is generated
+# directly).  torch int64 arithmetic wraps like uint64.
 # ---------------------------------------------------------------------------
-
-def gen_device():
-    """A GPU to generate inputs on when one is visible (the reference arm times only host
-    work), else None."""
-    import torch
-    return torch.device("cuda", 0) if torch.cuda.is_available() else None
-
-
-def _splitmix_bits(seed, start, count):
-    """Draws start+1 .. start+count of a SplitMix64 stream from state `seed` (counter-based)."""
-    import numpy as np
-    with np.errstate(over="ignore"):
-        k = np.arange(start + 1, start + count + 1, dtype=np.uint64)
-        z = np.uint64(seed) + k * np.uint64(0x9E3779B97F4A7C15)
-        z = (z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
-        z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
-        return z ^ (z >> np.uint64(31))
-
 
 def _srl(z, n):
     """Logical right shift of an int64 tensor holding uint64 bits."""
@@ -152,7 +165,7 @@ def _i64(x):
     return x - (1 << 64) if x >= 1 << 63 else x
 
 
-def _splitmix_bits_torch(seed, start, count, device):
+def _splitmix_bits(seed, start, count, device):
     import torch
     k = torch.arange(start + 1, start + count + 1, dtype=torch.int64, device=device)
     z = _i64(seed) + k * _i64(0x9E3779B97F4A7C15)
@@ -161,92 +174,296 @@ def _splitmix_bits_torch(seed, start, count, device):
     return z ^ _srl(z, 31)
 
 
-def gen_normal(seed, count, np_dtype, device=None, chunk=1 << 24):
-    """Seeded normal(0,1) values: Box-Muller over a SplitMix64 stream (draws 2i, 2i+1
-    make value i).  On `device` when given (torch int64 arithmetic wraps like uint64),
-    else with NumPy; both produce the same values.  Returns a CPU torch tensor."""
-    import numpy as np
+def gen_normal(seed, count, dtype, device, start=0, chunk=1 << 24):
+    """Values start .. start+count-1 of the seeded normal(0,1) stream: Box-Muller over
+    SplitMix64 (draws 2i, 2i+1 make value i)."""
+    import math
     import torch
-    if device is None or not torch.cuda.is_available():
-        out = np.empty(count, dtype=np_dtype)
-        for lo in range(0, count, chunk):
-            n = min(chunk, count - lo)
-            z = _splitmix_bits(seed, 2 * lo, 2 * n)
-            u = ((z >> np.uint64(11)).astype(np.float64) + 0.5) * (1.0 / (1 << 53))
-            out[lo:lo + n] = np.sqrt(-2.0 * np.log(u[0::2])) * np.cos(2 * np.pi * u[1::2])
-        return torch.from_numpy(out)
-    tdt = {np.float32: torch.float32, np.float64: torch.float64}[np_dtype]
-    out = torch.empty(count, dtype=tdt)
+    out = torch.empty(count, dtype=dtype, device=device)
     for lo in range(0, count, chunk):
         n = min(chunk, count - lo)
-        z = _splitmix_bits_torch(seed, 2 * lo, 2 * n, device)
+        z = _splitmix_bits(seed, 2 * (start + lo), 2 * n, device)
         u = (_srl(z, 11).double() + 0.5) * (1.0 / (1 << 53))
-        v = torch.sqrt(-2.0 * torch.log(u[0::2])) * torch.cos(2 * np.pi * u[1::2])
-        out[lo:lo + n] = v.to(tdt).cpu()
+        out[lo:lo + n] = (torch.sqrt(-2.0 * torch.log(u[0::2])) * torch.cos(2 * math.pi * u[1::2])).to(dtype)
     return out
 
 
-def gen_uniform(seed, count, np_dtype, device=None, chunk=1 << 24):
-    """Seeded uniform(-1,1) values on a 2^-52 grid: (next >> 11) * 2^-52 - 1."""
-    import numpy as np
+def gen_uniform(seed, count, dtype, device, start=0, chunk=1 << 24):
+    """Values of the seeded uniform(-1,1) stream on a 2^-52 grid: (next >> 11) 2^-52 - 1."""
     import torch
-    if device is None or not torch.cuda.is_available():
-        out = np.empty(count, dtype=np_dtype)
-        for lo in range(0, count, chunk):
-            n = min(chunk, count - lo)
-            z = _splitmix_bits(seed, lo, n)
-            out[lo:lo + n] = (z >> np.uint64(11)).astype(np.float64) * (1.0 / (1 << 52)) - 1.0
-        return torch.from_numpy(out)
-    tdt = {np.float32: torch.float32, np.float64: torch.float64}[np_dtype]
-    out = torch.empty(count, dtype=tdt)
+    out = torch.empty(count, dtype=dtype, device=device)
     for lo in range(0, count, chunk):
         n = min(chunk, count - lo)
-        z = _splitmix_bits_torch(seed, lo, n, device)
-        out[lo:lo + n] = (_srl(z, 11).double() * (1.0 / (1 << 52)) - 1.0).to(tdt).cpu()
+        z = _splitmix_bits(seed, start + lo, n, device)
+        out[lo:lo + n] = (_srl(z, 11).double() * (1.0 / (1 << 52)) - 1.0).to(dtype)
     return out
 
 
-class Workload:
-    """Shared defaults: one input tensor (host_in[i] -> dev_in[i]) and one output
-    (dev_out[j] -> host_out[j]) per op; the CPU leg runs the whole step."""
-
-    def e2e_inputs(self, op):
-        return [(self.host_in[op["i"]], self.dev_in[op["i"]])]
-
-    def e2e_outputs(self, op):
-        j = op.get("j", op["i"])
-        return [(self.dev_out[j], self.host_out[j])]
-
-    def cpu_units(self):
-        return self.units()
-
-    def cpu_sample(self):
-        return f"the full {self.name} step"
+def gen_complex(seed, count, device, start=0):
+    """complex128 values: real parts from stream `seed`, imaginary from `seed + 1000`."""
+    import torch
+    return torch.complex(gen_normal(seed, count, torch.float64, device, start),
+                         gen_normal(seed + 1000, count, torch.float64, device, start))
 
 
-class MovementWorkload(Workload):
-    name = "config2-permutation-movement"
-    dtype = "f32,c64"
+def gen_rows_uniform(seed, n, rows, device, start=0):
+    import torch
+    z = _splitmix_bits(seed, start, n, device)
+    u = _srl(z, 11).double() * (1.0 / (1 << 53))
+    return (u * rows).to(torch.int64)
 
-    def __init__(self, device=None):
-        import numpy as np
-        import torch
+
+def gen_rows_zipf(seed, n, rows, s, device, start=0):
+    """Zipf(s) ranks 1..rows by inverse CDF (row = rank - 1)."""
+    import torch
+    w = torch.arange(1, rows + 1, dtype=torch.float64, device=device) ** -s
+    cdf = torch.cumsum(w, 0)
+    cdf /= cdf[-1].clone()
+    z = _splitmix_bits(seed, start, n, device)
+    u = _srl(z, 11).double() * (1.0 / (1 << 53))
+    return torch.clamp(torch.searchsorted(cdf, u, right=True), max=rows - 1).to(torch.int64)
+
+
+def gen_device():
+    """A GPU to generate inputs on when one is visible, else the CPU."""
+    import torch
+    return torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu")
+
+
+def pinned(t):
+    """A pinned host copy of a tensor (plain host copy without a GPU)."""
+    import torch
+    h = torch.empty(t.shape, dtype=t.dtype, pin_memory=torch.cuda.is_available())
+    h.copy_(t)
+    return h
+
+
+def vp(t):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def numpy_view(t):
+    """NumPy array over a host tensor (complex tensors as their float pairs)."""
+    import torch
+    if t.is_complex():
+        return torch.view_as_real(t).numpy()
+    return t.numpy()
+
+
+class CheckFailed(RuntimeError):
+    pass
+
+
+def same_bits(got, want, what):
+    import torch
+    g, w = got.contiguous(), want.contiguous()
+    if g.shape != w.shape:
+        raise CheckFailed(f"{what}: shape {tuple(g.shape)} != {tuple(w.shape)}")
+    if g.is_complex():
+        g, w = torch.view_as_real(g), torch.view_as_real(w)
+    ib = {1: torch.uint8, 4: torch.int32, 8: torch.int64}[g.element_size()]
+    if not torch.equal(g.view(ib), w.view(ib)):
+        bad = int((g.view(ib) != w.view(ib)).sum())
+        raise CheckFailed(f"{what}: {bad} elements differ from the single-GPU result")
+
+
+def close_rel(got, want, tol, what):
+    import torch
+    err = ((got - want).abs() / torch.clamp(want.abs(), min=1.0)).max().item()
+    if not err <= tol:
+        raise CheckFailed(f"{what}: relative error {err:.3e} > {tol:.0e}")
+    return err
+
+
+# ---------------------------------------------------------------------------
+# Configurations.  Each holds this rank's device inputs and outputs and a list of
+# ops; an op is a dict with
+#   tag, config, bytes (whole job), local_bytes (this rank), launches,
+#   run(stream_handle), inputs / outputs (names in self.dev / self.host),
+#   optional prepare() (untimed, before the op), cpu(threads) -> sample bytes.
+# setup() builds the rank's shards; check() compares them with the single-GPU result.
+# ---------------------------------------------------------------------------
+
+class Config:
+    """Shared machinery: device tensors in self.dev, pinned host copies in self.host."""
+
+    def __init__(self, rank, world, device, host_only=False):
         import t4a_b200 as t4
         from t4a_b200 import abi
         self.t4, self.abi = t4, abi
-        self.device = device
-        gdev = device if device is not None else gen_device()
-        a = gen_normal(2, 64 ** 4, np.float32, gdev)
-        b = torch.stack([gen_normal(3, 16 ** 6, np.float64, gdev), gen_normal(3 + 1000, 16 ** 6, np.float64, gdev)],
-                        dim=1).reshape(-1)  # interleaved (re, im)
-        c = gen_normal(4, 64 ** 4, np.float32, gdev)
-        pin = device is not None
-        host = [a, b, c]
-        self.host_in = [h.pin_memory() for h in host] if pin else host
-        self.host_out = [torch.empty_like(h).pin_memory() if pin else torch.empty_like(h) for h in host]
-        if device is not None:
-            self.dev_in = [h.to(device) for h in self.host_in]
-            self.dev_out = [torch.empty_like(d) for d in self.dev_in]
+        self.rank, self.world, self.device = rank, world, device
+        self.host_only = host_only
+        self.dev, self.host, self.ops, self.expect = {}, {}, [], {}
+        self.checks = {}
+
+    def keep(self, name, t, host=True):
+        """Registers a tensor: on the device (unless host_only) and, for e2e or the CPU
+        leg, as a pinned host copy."""
+        if not self.host_only:
+            self.dev[name] = t if t.device.type == "cuda" else t.to(self.device)
+        if host:
+            self.host[name] = pinned(t)
+
+    def shard(self, n):
+        from t4a_b200 import dist as t4dist
+        return t4dist.shard_range(n, self.world, self.rank)
+
+    def group_bytes(self):
+        return sum(op["bytes"] for op in self.ops)
+
+    def after_timing(self):
+        """Checks of status words after the timed steps (none by default)."""
+
+
+class ReduceConfigs(Config):
+    """single-axis reductions through t4a_reduce
+    (a direct pass, or pass 1 into the caller's partials workspace plus the combine pass).
+
+    Sharding: axis-1 and axis-2 reductions of the F32 tensor, the C64 reduction and the
+    config-1 reductions shard NumPy axis 0; axis-0 reductions of the F32 tensor shard
+    axis 1.  Every rank holds its slabs (a compact copy made once) and reduces them."""
+
+    name = "reduce"
+
+    def setup(self):
+        import torch
+        t4, abi = self.t4, self.abi
+        gdev = gen_device()
+        n0 = 4096
+        a0, a1 = self.shard(n0)
+        specs = []
+        # config 1
+        full1 = gen_uniform(0, 256 * 1024 * 64, torch.float64, gdev).reshape(256, 1024, 64)
+        c0, c1 = self.shard(256)
+        self.keep("c1", full1[c0:c1].contiguous())
+        specs += [("sum-f64-256x1024x64-axis1", 1, "c1", full1, (c0, c1), 0, 1, abi.SUM),
+                  ("max-f64-256x1024x64-axis1", 1, "c1", full1, (c0, c1), 0, 1, abi.MAX)]
+        # config 3 F32
+        big = gen_normal(4, n0 * 4096 * 32, torch.float32, gdev).reshape(n0, 4096, 32)
+        self.keep("x_rows", big[a0:a1].contiguous())  # axis-0 slab: reduced over axes 1 and 2
+        b0, b1 = self.shard(4096)
+        if self.world == 1:
+            self.dev.setdefault("x_cols", self.dev.get("x_rows"))
+            self.host["x_cols"] = self.host["x_rows"]
+        else:
+            self.keep("x_cols", big[:, b0:b1].contiguous())  # axis-1 slab: reduced over axis 0
+        for ax in (0, 1, 2):
+            for op, tag in ((abi.SUM, "sum"), (abi.SUM_SQUARES, "sumsq"), (abi.MAX, "max")):
+                if ax == 0:
+                    specs.append((f"{tag}-f32-4096x4096x32-axis0", 3, "x_cols", big, (b0, b1), 1, 0, op))
+                else:
+                    specs.append((f"{tag}-f32-4096x4096x32-axis{ax}", 3, "x_rows", big, (a0, a1), 0, ax, op))
+        # config 3 C64
+        cplx = gen_complex(5, 8192 * 8192, gdev).reshape(8192, 8192)
+        z0, z1 = self.shard(8192)
+        self.keep("z", cplx[z0:z1].contiguous())
+        specs.append(("sum-c64-8192x8192-axis1", 3, "z", cplx, (z0, z1), 0, 1, abi.SUM))
+        need_ws = 16
+        for j, (tag, cfg, name, full, (s0, s1), shard_axis, ax, op) in enumerate(specs):
+            local = self.dev.get(name) if not self.host_only else self.host[name]
+            shape = list(local.shape)
+            oshape = list(shape)
+            oshape[ax] = 1
+            gshape = list(full.shape)
+            gshape[ax] = 1
+            dt = t4.torch_dtype_tag(local)
+            in_l, out_l = abi.numpy_layout(shape), abi.numpy_layout(oshape)
+            n_out = 1
+            for e in oshape:
+                n_out *= e
+            ref_axis = len(shape) - 1 - ax
+            ws = t4.reduce_workspace_bytes(dt, op, out_l, n_out, in_l, local.numel(), ref_axis)
+            need_ws = max(need_ws, ws)
+            es = local.element_size()
+            out_name = f"out{j}"
+            if not self.host_only:
+                self.dev[out_name] = torch.empty(oshape, dtype=local.dtype, device=self.device)
+                # the single-GPU result of the whole tensor, this rank's slab of it
+                want = t4.reduce(full.to(self.device) if full.device != self.device else full, ax, op)
+                self.expect[out_name] = want.narrow(shard_axis, s0, s1 - s0).clone()
+            self.host[out_name] = pinned(torch.empty(oshape, dtype=local.dtype))
+            gl = full.numel()
+            gout = 1
+            for e in gshape:
+                gout *= e
+            self.ops.append(dict(tag=tag, config=cfg, bytes=(gl + gout) * es, local_bytes=(local.numel() + n_out) * es,
+                                 launches=2 if ws else 1, inputs=[name], outputs=[out_name], dtype=dt, op=op,
+                                 in_l=in_l, out_l=out_l, n_in=local.numel(), n_out=n_out, axis=ref_axis, ws=ws,
+                                 src=name, dst=out_name, full_shape=list(full.shape), np_axis=ax))
+        del big, cplx, full1
+        if not self.host_only:
+            self.workspace = torch.empty(need_ws, dtype=torch.uint8, device=self.device)
+        for op in self.ops:
+            op["run"] = self._runner(op)
+            op["cpu"] = self._cpu(op)
+
+    def _runner(self, op):
+        def run(sh):
+            self.t4.reduce_raw(sh, op["dtype"], op["op"], vp(self.dev[op["dst"]]), op["out_l"], op["n_out"],
+                               vp(self.dev[op["src"]]), op["in_l"], op["n_in"], op["axis"], 32,
+                               vp(self.workspace), op["ws"])
+        return run
+
+    def _cpu(self, op):
+        """The oracle on a slab of the op: the whole op for config 1, 1/16 of the rows of
+        a non-reduced axis for config 3 (axis-0 reductions: 256 of the 4096 columns of
+        NumPy axis 1, a strided view)."""
+        def cpu(threads):
+            oracle = _oracle()
+            abi = self.abi
+            src = self.host[op["src"]]
+            dst = self.host[op["dst"]]
+            shape = list(src.shape)
+            es = src.element_size()
+            ax = op["np_axis"]
+            if op["config"] == 1:
+                in_l, out_l, nbytes = op["in_l"], op["out_l"], (op["n_in"] + op["n_out"]) * es
+            else:
+                cut = 1 if ax == 0 else 0
+                keep = shape[cut] // 16
+                sub = list(shape)
+                sub[cut] = keep
+                st, s = [], 1
+                for e in reversed(shape):
+                    st.insert(0, s)
+                    s *= e
+                in_l = abi.numpy_layout(sub, st)
+                osub = list(sub)
+                osub[ax] = 1
+                out_l = abi.numpy_layout(osub)
+                n_in = 1
+                for e in sub:
+                    n_in *= e
+                nbytes = (n_in + n_in // sub[ax]) * es
+            rc = oracle.lib().t4a_oracle_reduce_threaded(op["dtype"], op["op"], oracle.ptr(numpy_view(dst)),
+                                                         ctypes.byref(out_l), oracle.ptr(numpy_view(src)),
+                                                         ctypes.byref(in_l), op["axis"], 32, threads)
+            assert rc == 0
+            return nbytes
+        return cpu
+
+    def check(self):
+        for op in self.ops:
+            op["run"](self.t4.stream_handle())
+            same_bits(self.dev[op["dst"]], self.expect[op["dst"]], op["tag"])
+
+
+class MovementConfig(Config):
+    """permutations and a reversal through the strided-copy entry.
+
+    Sharding: the destination is split along its slowest axis; every rank writes its
+    contiguous slab from the matching strided view of the source (replicated)."""
+
+    name = "movement"
+
+    def setup(self):
+        import torch
+        from t4a_b200 import dist as t4dist
+        abi = self.abi
+        gdev = gen_device()
+        a = gen_normal(2, 64 ** 4, torch.float32, gdev)
+        b = gen_complex(3, 16 ** 6, gdev).view(torch.float64)  # interleaved (re, im) pairs
+        c = gen_normal(4, 64 ** 4, torch.float32, gdev)
 
         def perm_layout(shape, perm):
             st, s = [], 1
@@ -255,509 +472,595 @@ class MovementWorkload(Workload):
                 s *= e
             return abi.numpy_layout([shape[p] for p in perm], [st[p] for p in perm])
 
-        self.ops = []
         specs = [
-            ("perm-f32-64^4", abi.F32, perm_layout([64] * 4, (3, 1, 0, 2)), 64 ** 4, 4),
-            ("perm-c64-16^6", abi.C64, perm_layout([16] * 6, (5, 0, 4, 1, 3, 2)), 16 ** 6, 16),
-            ("reverse-f32-64^4", abi.F32, abi.numpy_layout([64] * 4, [64 ** 3, 64 ** 2, -64, 1], 63 * 64), 64 ** 4, 4),
+            ("perm-f32-64^4", abi.F32, a, perm_layout([64] * 4, (3, 1, 0, 2)), 4),
+            ("perm-c64-16^6", abi.C64, b, perm_layout([16] * 6, (5, 0, 4, 1, 3, 2)), 16),
+            ("reverse-f32-64^4", abi.F32, c, abi.numpy_layout([64] * 4, [64 ** 3, 64 ** 2, -64, 1], 63 * 64), 4),
         ]
-        for i, (tag, dt, src_l, n, es) in enumerate(specs):
-            dst_l = abi.layout(src_l.extents_list())
-            self.ops.append(dict(tag=tag, dtype=dt, src_l=src_l, dst_l=dst_l, n=n, bytes=2 * n * es, i=i))
+        for i, (tag, dt, src, full_l, es) in enumerate(specs):
+            n_full = full_l.count()
+            src_l, dst_l, start = t4dist.movement_slab(full_l, self.world, self.rank)
+            n_local = dst_l.count()
+            name, out = f"src{i}", f"dst{i}"
+            self.keep(name, src)
+            flat_len = src.numel() * src.element_size() // es
+            if not self.host_only:
+                self.dev[out] = torch.empty(n_local * es // src.element_size(), dtype=src.dtype, device=self.device)
+                # single-GPU result of the whole permutation, this rank's slab
+                whole = torch.empty_like(self.dev[name])
+                self.t4.copy_strided_raw(self.t4.stream_handle(), dt, vp(whole), abi.layout(full_l.extents_list()),
+                                         n_full, vp(self.dev[name]), full_l, flat_len)
+                per_row = n_full // full_l.extents[full_l.rank - 1]
+                lo = start * per_row * es // src.element_size()
+                self.expect[out] = whole[lo:lo + n_local * es // src.element_size()].clone()
+            self.host[out] = pinned(torch.empty(n_local * es // src.element_size(), dtype=src.dtype))
+            self.ops.append(dict(tag=tag, config=2, bytes=2 * n_full * es, local_bytes=2 * n_local * es, launches=1,
+                                 inputs=[name], outputs=[out], dtype=dt, src_l=src_l, dst_l=dst_l, n=n_local,
+                                 flat_len=flat_len, src=name, dst=out, full_l=full_l, n_full=n_full, es=es))
+        for op in self.ops:
+            op["run"] = self._runner(op)
+            op["cpu"] = self._cpu(op)
 
-    def units(self):
-        return sum(op["bytes"] for op in self.ops)
+    def _runner(self, op):
+        def run(sh):
+            self.t4.copy_strided_raw(sh, op["dtype"], vp(self.dev[op["dst"]]), op["dst_l"], op["n"],
+                                     vp(self.dev[op["src"]]), op["src_l"], op["flat_len"])
+        return run
 
-    def run_op(self, op, stream_handle, dev_in=None, dev_out=None):
-        i = op["i"]
-        src = (dev_in or self.dev_in)[i]
-        dst = (dev_out or self.dev_out)[i]
-        self.t4.copy_strided_raw(stream_handle, op["dtype"], ctypes.c_void_p(dst.data_ptr()), op["dst_l"], op["n"],
-                                 ctypes.c_void_p(src.data_ptr()), op["src_l"], op["n"])
+    def _cpu(self, op):
+        def cpu(threads):
+            oracle = _oracle()
+            rc = oracle.lib().t4a_oracle_strided_to_strided(op["dtype"], oracle.ptr(numpy_view(self.host[op["dst"]])),
+                                                            oracle.ptr(numpy_view(self.host[op["src"]])),
+                                                            ctypes.byref(op["src_l"]), ctypes.byref(op["dst_l"]),
+                                                            threads)
+            assert rc == 0
+            return 2 * op["n"] * op["es"]
+        return cpu
 
-    def cpu_op(self, op, threads, srcs, dsts):
-        oracle = _oracle()
-        host_src, host_dst = srcs[op["i"]], dsts[op["i"]]
-        rc = oracle.lib().t4a_oracle_strided_to_strided(op["dtype"], oracle.ptr(host_dst), oracle.ptr(host_src),
-                                                        ctypes.byref(op["src_l"]), ctypes.byref(op["dst_l"]), threads)
-        assert rc == 0
-
-    def host_arrays(self):
-        return [h.numpy() for h in self.host_in], [h.numpy() for h in self.host_out]
-
-
-
-class ReduceWorkload(Workload):
-    """BASELINE configs[2] (and configs[0]): single-axis reductions.
-
-    F32 [4096,4096,32] normal(0,1): sum, sum_squares and max over each NumPy axis; C64
-    [8192,8192] sum over axis 1; F64 [256,1024,64] uniform(-1,1) sum and max over axis 1.
-    Each op is one whole reduction (t4a_reduce: pass 1 + combine, or a direct pass)."""
-
-    name = "config3-reduction-sweep+config1"
-    dtype = "f32,f64,c64"
-
-    def __init__(self, device=None):
-        import numpy as np
-        import torch
-        import t4a_b200 as t4
-        from t4a_b200 import abi
-        self.t4, self.abi = t4, abi
-        self.device = device
-        gdev = device if device is not None else gen_device()
-        big = gen_normal(4, 4096 * 4096 * 32, np.float32, gdev).reshape(4096, 4096, 32)
-        c = torch.complex(gen_normal(5, 8192 * 8192, np.float64, gdev),
-                          gen_normal(5 + 1000, 8192 * 8192, np.float64, gdev)).reshape(8192, 8192)
-        u = gen_uniform(0, 256 * 1024 * 64, np.float64, gdev).reshape(256, 1024, 64)
-        self.host_in = [big, c, u]
-        if device is not None:
-            self.host_in = [h.pin_memory() for h in self.host_in]
-            self.dev_in = [h.to(device) for h in self.host_in]
-        specs = []
-        for ax in (0, 1, 2):
-            for op, tag in ((abi.SUM, "sum"), (abi.SUM_SQUARES, "sumsq"), (abi.MAX, "max")):
-                specs.append((f"{tag}-f32-4096x4096x32-axis{ax}", 0, ax, op))
-        specs.append(("sum-c64-8192x8192-axis1", 1, 1, abi.SUM))
-        specs.append(("sum-f64-256x1024x64-axis1", 2, 1, abi.SUM))
-        specs.append(("max-f64-256x1024x64-axis1", 2, 1, abi.MAX))
-        self.ops = []
-        self.dev_out, self.host_out, self.workspace = [], [], None
-        need_ws = 0
-        for j, (tag, i, ax, op) in enumerate(specs):
-            x = self.host_in[i]
-            shape = list(x.shape)
-            oshape = list(shape)
-            oshape[ax] = 1
-            dt = t4.torch_dtype_tag(x)
-            in_l = abi.numpy_layout(shape)
-            out_l = abi.numpy_layout(oshape)
-            n_out = int(np.prod(oshape))
-            ws = t4.reduce_workspace_bytes(dt, op, out_l, n_out, in_l, x.numel(), len(shape) - 1 - ax)
-            need_ws = max(need_ws, ws)
-            esize = x.element_size()
-            self.ops.append(dict(tag=tag, i=i, j=j, op=op, dtype=dt, in_l=in_l, out_l=out_l, n_in=x.numel(),
-                                 n_out=n_out, axis=len(shape) - 1 - ax, ws=ws, np_axis=ax,
-                                 bytes=(x.numel() + n_out) * esize, launches=2 if ws else 1))
-            self.host_out.append(torch.empty(oshape, dtype=x.dtype).pin_memory() if device is not None
-                                 else torch.empty(oshape, dtype=x.dtype))
-            if device is not None:
-                self.dev_out.append(torch.empty(oshape, dtype=x.dtype, device=device))
-        if device is not None:
-            self.workspace = torch.empty(max(need_ws, 16), dtype=torch.uint8, device=device)
-
-    def units(self):
-        return sum(op["bytes"] for op in self.ops)
-
-    def run_op(self, op, stream_handle, dev_in=None, dev_out=None):
-        src = (dev_in or self.dev_in)[op["i"]]
-        dst = (dev_out or self.dev_out)[op["j"]]
-        self.t4.reduce_raw(stream_handle, op["dtype"], op["op"], ctypes.c_void_p(dst.data_ptr()), op["out_l"],
-                           op["n_out"], ctypes.c_void_p(src.data_ptr()), op["in_l"], op["n_in"], op["axis"], 32,
-                           ctypes.c_void_p(self.workspace.data_ptr()), op["ws"])
-
-    def cpu_op(self, op, threads, srcs, dsts):
-        oracle = _oracle()
-        host_src, host_dst = srcs[op["i"]], dsts[op["j"]]
-        rc = oracle.lib().t4a_oracle_reduce_threaded(op["dtype"], op["op"], oracle.ptr(host_dst),
-                                                     ctypes.byref(op["out_l"]), oracle.ptr(host_src),
-                                                     ctypes.byref(op["in_l"]), op["axis"], 32, threads)
-        assert rc == 0
-
-    def host_arrays(self):
-        srcs = [h.numpy() for h in self.host_in]
-        outs = [h.numpy() for h in self.host_out]
-        return srcs, outs
+    def check(self):
+        for op in self.ops:
+            op["run"](self.t4.stream_handle())
+            same_bits(self.dev[op["dst"]], self.expect[op["dst"]], op["tag"])
 
 
-class GatherScatterWorkload(Workload):
+class GatherScatterConfig(Config):
     """XLA gather of 4,194,304 rows from an F32 table
-    [1,048,576,128] with I64 indices uniform in [0, 1048576) (seeds 6, 7), and
-    scatter_add of F64 updates [4,194,304,128] normal(0,1) (seed 8) into a
-    [1,048,576,128] destination with Zipf(s=1.1) row indices (seed 9; inverse CDF over
-    ranks 1..1048576, row = rank - 1).  Algorithmic bytes: gather = output + gathered
-    rows + indices; scatter = updates + indices + destination read and write.  The
-    destination is zeroed once; the caller's operand copy (copy_exact) is not part of
-    the timed scatter op.  The CPU leg runs the oracle on the first 262,144 index rows
-    of each op."""
+    [1048576,128] with I64 indices uniform in [0, 1048576) (seeds 6, 7), and scatter_add
+    of F64 updates [4194304,128] normal(0,1) (seed 8) into a zeroed [1048576,128]
+    destination with Zipf(s=1.1) row indices (seed 9).  Algorithmic bytes: gather =
+    output + gathered rows + indices; scatter = updates + indices + destination read
+    and write.
 
-    name = "config4-gather-scatter"
-    dtype = "f32 (gather), f64 (scatter); i64 indices"
-    ROWS, COLS, N, SAMPLE = 1 << 20, 128, 1 << 22, 1 << 18
+    Sharding: index batches (rows shard_range of the 4M); the table is replicated.
+    scatter_add adds each rank's batch into its full-size partial destination, then one
+    NCCL reduce-scatter inside the timed op leaves each rank 1/N of the rows."""
 
-    def __init__(self, device=None):
-        import numpy as np
+    name = "gather"
+    ROWS, COLS, N = 1 << 20, 128, 1 << 22
+    SAMPLE = 1 << 18
+
+    def setup(self):
         import torch
-        import t4a_b200 as t4
-        from t4a_b200 import abi
-        self.t4, self.abi = t4, abi
-        self.device = device
-        gdev = device if device is not None else gen_device()
+        t4, abi = self.t4, self.abi
         R, C, N = self.ROWS, self.COLS, self.N
-        table = gen_normal(6, R * C, np.float32, gdev).reshape(R, C)
-        gidx = self._uniform_rows(7, N, R, gdev)
-        upd = gen_normal(8, N * C, np.float64, gdev).reshape(N, C)
-        sidx = self._zipf_rows(9, N, R, 1.1, gdev)
-        dest0 = torch.zeros((R, C), dtype=torch.float64)
-        pin = device is not None
-        self.host = {"table": table, "gidx": gidx, "upd": upd, "sidx": sidx, "dest": dest0,
-                     "gout": torch.empty((N, C), dtype=torch.float32)}
-        if pin:
-            self.host = {k: v.pin_memory() for k, v in self.host.items()}
-            self.dev = {k: v.to(device) for k, v in self.host.items()}
+        gdev = gen_device()
+        lo, hi = self.shard(N)
+        n = hi - lo
+        self.lo, self.n = lo, n
+        table = gen_normal(6, R * C, torch.float32, gdev).reshape(R, C)
+        self.keep("table", table)
+        gidx_full = gen_rows_uniform(7, N, R, gdev)
+        self.keep("gidx", gidx_full[lo:hi].contiguous())
+        upd = gen_normal(8, n * C, torch.float64, gdev, start=lo * C).reshape(n, C)
+        sidx_full = gen_rows_zipf(9, N, R, 1.1, gdev)
+        self.keep("upd", upd)
+        self.keep("sidx", sidx_full[lo:hi].contiguous())
+        self.sharded = self.world > 1
         self.gplan = abi.gather_plan([0], [0], [1], [C, 1], 1, 2)
         self.splan = abi.scatter_plan([0], [0], [1], 1, 2, 2)
-        self.ws_bytes = t4.scatter_add_workspace_bytes(abi.F64, abi.I64, abi.numpy_layout([R, C]),
-                                                       abi.layout([N, 1]), abi.numpy_layout([N, C]), self.splan)
-        if pin:
-            self.ws = torch.empty(self.ws_bytes, dtype=torch.uint8, device=device)
-        # On N > 1 ranks the scatter has its exchange step: every rank adds its own
-        # update batch into a full-size partial destination and one NCCL reduce-scatter
-        # leaves it its 1/N of the destination rows (t4a_b200.dist); the gather needs no
-        # collective (each rank gathers its own batch).
-        self.sharded = pin and torch.distributed.is_available() and torch.distributed.is_initialized() \
-            and torch.distributed.get_world_size() > 1
-        if self.sharded:
-            from t4a_b200 import dist as t4dist
-            self.t4dist = t4dist
-            world = torch.distributed.get_world_size()
-            self.partial = t4dist.scatter_partial(self.dev["dest"])
-            self.shard_out = torch.empty((R // world, C), dtype=torch.float64, device=device)
+        own = R // self.world
+        if not self.host_only:
+            d = self.dev
+            d["gout"] = torch.empty((n, C), dtype=torch.float32, device=self.device)
+            d["dest"] = torch.zeros((R, C), dtype=torch.float64, device=self.device)  # the partial when sharded
+            self.ws_bytes = t4.scatter_add_workspace_bytes(abi.F64, abi.I64, abi.numpy_layout([R, C]),
+                                                           abi.layout([n, 1]), abi.numpy_layout([n, C]), self.splan)
+            self.ws = torch.empty(max(self.ws_bytes, 16), dtype=torch.uint8, device=self.device)
+            if self.sharded:
+                d["shard_out"] = torch.empty((own, C), dtype=torch.float64, device=self.device)
+            # single-GPU results of the whole ops (this rank's rows)
+            full_gout = torch.empty((N, C), dtype=torch.float32, device=self.device)
+            t4.gather_raw(t4.stream_handle(), abi.F32, abi.I64, vp(full_gout), abi.numpy_layout([N, C]), N * C,
+                          vp(d["table"]), abi.numpy_layout([R, C]), R * C, vp(gidx_full.to(self.device)),
+                          abi.layout([N, 1]), N, self.gplan)
+            self.expect["gout"] = full_gout[lo:hi].clone()
+            del full_gout
+            full_upd = gen_normal(8, N * C, torch.float64, self.device).reshape(N, C)
+            full_dest = torch.zeros((R, C), dtype=torch.float64, device=self.device)
+            d_sidx = sidx_full.to(self.device)
+            t4.scatter_add_rows(full_dest, d_sidx, full_upd)
+            rows = slice(self.rank * own, (self.rank + 1) * own)
+            self.expect["dest"] = full_dest[rows].clone()
+            # Two summation orders of the same n terms differ by at most 2 (n - 1) u sum|x|
+            # (u = 2^-53, recursive summation): the per-element bound for the check.
+            absum = torch.zeros((R, C), dtype=torch.float64, device=self.device).index_add_(0, d_sidx, full_upd.abs())
+            count = torch.zeros(R, dtype=torch.float64, device=self.device).index_add_(
+                0, d_sidx, torch.ones(N, dtype=torch.float64, device=self.device))
+            self.expect["dest_bound"] = (2.0 * torch.clamp(count - 1, min=0) * 2.0 ** -53)[rows, None] * absum[rows]
+            del full_upd, full_dest, absum, count
+        self.host["gout"] = pinned(torch.empty((n, C), dtype=torch.float32))
+        self.host["dest"] = pinned(torch.empty((own, C), dtype=torch.float64))
         self.ops = [
-            dict(tag="gather-f32-4Mx128-of-1Mx128", kind="gather", i=0,
-                 bytes=N * C * 4 * 2 + N * 8),
-            dict(tag="scatter-add-f64-4Mx128-zipf-into-1Mx128", kind="scatter", i=1, launches=2,
-                 bytes=N * C * 8 + N * 8 + 2 * R * C * 8),
+            dict(tag="gather-f32-4Mx128-of-1Mx128", config=4, kind="gather", launches=1,
+                 bytes=N * C * 4 * 2 + N * 8, local_bytes=n * C * 4 * 2 + n * 8,
+                 inputs=["table", "gidx"], outputs=["gout"]),
+            dict(tag="scatter-add-f64-4Mx128-zipf-into-1Mx128", config=4, kind="scatter", launches=2,
+                 bytes=N * C * 8 + N * 8 + 2 * R * C * 8, local_bytes=n * C * 8 + n * 8 + 2 * R * C * 8,
+                 inputs=["sidx", "upd"], outputs=["shard_out" if self.sharded else "dest"]),
         ]
+        if self.sharded:
+            self.host["shard_out"] = self.host.pop("dest")
+        for op in self.ops:
+            op["run"] = self._runner(op)
+            op["cpu"] = self._cpu(op)
 
-    @staticmethod
-    def _uniform_rows(seed, n, rows, gdev):
-        import numpy as np
-        import torch
-        if gdev is None:
-            z = _splitmix_bits(seed, 0, n)
-            u = (z >> np.uint64(11)).astype(np.float64) * (1.0 / (1 << 53))
-            return torch.from_numpy((u * rows).astype(np.int64))
-        z = _splitmix_bits_torch(seed, 0, n, gdev)
-        u = _srl(z, 11).double() * (1.0 / (1 << 53))
-        return (u * rows).to(torch.int64).cpu()
-
-    @staticmethod
-    def _zipf_rows(seed, n, rows, s, gdev):
-        import numpy as np
-        import torch
-        w = np.arange(1, rows + 1, dtype=np.float64) ** -s
-        cdf = np.cumsum(w)
-        cdf /= cdf[-1]
-        if gdev is None:
-            z = _splitmix_bits(seed, 0, n)
-            u = (z >> np.uint64(11)).astype(np.float64) * (1.0 / (1 << 53))
-            return torch.from_numpy(np.minimum(np.searchsorted(cdf, u, side="right"), rows - 1).astype(np.int64))
-        z = _splitmix_bits_torch(seed, 0, n, gdev)
-        u = _srl(z, 11).double() * (1.0 / (1 << 53))
-        r = torch.searchsorted(torch.from_numpy(cdf).to(gdev), u, right=True)
-        return torch.clamp(r, max=rows - 1).to(torch.int64).cpu()
-
-    def units(self):
-        return sum(op["bytes"] for op in self.ops)
-
-    def run_op(self, op, stream_handle, dev_in=None, dev_out=None):
+    def _runner(self, op):
         t4, abi, d = self.t4, self.abi, self.dev
-        R, C, N = self.ROWS, self.COLS, self.N
-        vp = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
-        if op["kind"] == "gather":
-            t4.gather_raw(stream_handle, abi.F32, abi.I64, vp(d["gout"]), abi.numpy_layout([N, C]), N * C,
-                          vp(d["table"]), abi.numpy_layout([R, C]), R * C, vp(d["gidx"]), abi.layout([N, 1]), N,
-                          self.gplan)
-        elif self.sharded:
-            self.t4dist.scatter_add_rows_sharded(self.partial, d["sidx"].view(N), d["upd"], workspace=self.ws,
-                                                 out=self.shard_out)
-        else:
-            t4.scatter_add_raw(stream_handle, abi.F64, abi.I64, vp(d["dest"]), abi.numpy_layout([R, C]), R * C,
-                               vp(d["sidx"]), abi.layout([N, 1]), N, vp(d["upd"]), abi.numpy_layout([N, C]), N * C,
-                               self.splan, vp(self.ws), self.ws_bytes)
+        R, C, n = self.ROWS, self.COLS, self.n
 
-    def e2e_inputs(self, op):
-        if op["kind"] == "gather":
-            keys = ["table", "gidx"]
-        else:
-            keys = ["sidx", "upd"] if self.sharded else ["dest", "sidx", "upd"]
-        return [(self.host[k], self.dev[k]) for k in keys]
+        def run(sh):
+            if op["kind"] == "gather":
+                t4.gather_raw(sh, abi.F32, abi.I64, vp(d["gout"]), abi.numpy_layout([n, C]), n * C, vp(d["table"]),
+                              abi.numpy_layout([R, C]), R * C, vp(d["gidx"]), abi.layout([n, 1]), n, self.gplan)
+                return
+            t4.scatter_add_raw(sh, abi.F64, abi.I64, vp(d["dest"]), abi.numpy_layout([R, C]), R * C, vp(d["sidx"]),
+                               abi.layout([n, 1]), n, vp(d["upd"]), abi.numpy_layout([n, C]), n * C, self.splan,
+                               vp(self.ws), self.ws_bytes)
+            if self.sharded:
+                import torch.distributed as tdist
+                tdist.reduce_scatter_tensor(d["shard_out"], d["dest"], op=tdist.ReduceOp.SUM)
+        return run
 
-    def e2e_outputs(self, op):
-        if op["kind"] != "gather" and self.sharded:
-            return [(self.shard_out, self.host["dest"][:self.shard_out.shape[0]])]
-        k = "gout" if op["kind"] == "gather" else "dest"
-        return [(self.dev[k], self.host[k])]
-
-    def host_arrays(self):
-        return self.host, None
-
-    def cpu_units(self):
-        return sum(op["bytes"] for op in self.ops) * self.SAMPLE // self.N
-
-    def cpu_sample(self):
-        return f"the first {self.SAMPLE} of {self.N} index rows of each {self.name} op"
-
-    def cpu_op(self, op, threads, srcs, dsts):
-        oracle = _oracle()
-        abi = self.abi
-        R, C, S = self.ROWS, self.COLS, self.SAMPLE
-        h = srcs
-        if op["kind"] == "gather":
-            rc = oracle.lib().t4a_oracle_gather(abi.F32, abi.I64, oracle.ptr(h["gout"].numpy()),
-                                                oracle.ptr(h["table"].numpy()), oracle.ptr(h["gidx"].numpy()),
-                                                ctypes.byref(abi.numpy_layout([S, C])),
-                                                ctypes.byref(abi.numpy_layout([R, C])),
-                                                ctypes.byref(abi.layout([S, 1])), ctypes.byref(self.gplan), threads)
-        else:
-            rc = oracle.lib().t4a_oracle_scatter_add(abi.F64, abi.I64, oracle.ptr(h["dest"].numpy()),
+    def _cpu(self, op):
+        """The oracle on the first SAMPLE index rows of the op."""
+        def cpu(threads):
+            oracle = _oracle()
+            abi = self.abi
+            R, C, S = self.ROWS, self.COLS, self.SAMPLE
+            h = self.host
+            if op["kind"] == "gather":
+                rc = oracle.lib().t4a_oracle_gather(abi.F32, abi.I64, oracle.ptr(h["gout"].numpy()),
+                                                    oracle.ptr(h["table"].numpy()), oracle.ptr(h["gidx"].numpy()),
+                                                    ctypes.byref(abi.numpy_layout([S, C])),
+                                                    ctypes.byref(abi.numpy_layout([R, C])),
+                                                    ctypes.byref(abi.layout([S, 1])), ctypes.byref(self.gplan),
+                                                    threads)
+                assert rc == 0
+                return S * C * 4 * 2 + S * 8
+            if "cpu_dest" not in h:
+                import torch
+                h["cpu_dest"] = torch.zeros((R, C), dtype=torch.float64)
+            rc = oracle.lib().t4a_oracle_scatter_add(abi.F64, abi.I64, oracle.ptr(h["cpu_dest"].numpy()),
                                                      oracle.ptr(h["sidx"].numpy()), oracle.ptr(h["upd"].numpy()),
                                                      ctypes.byref(abi.numpy_layout([R, C])),
                                                      ctypes.byref(abi.layout([S, 1])),
                                                      ctypes.byref(abi.numpy_layout([S, C])),
                                                      ctypes.byref(self.splan), threads)
-        assert rc == 0
+            assert rc == 0
+            return S * C * 8 + S * 8 + 2 * R * C * 8 * S // self.N
+        return cpu
+
+    def after_timing(self):
+        status = int(self.ws[:4].view(__import__("torch").int32).item())
+        self.checks["scatter_status"] = status
+        if status != 0:
+            raise CheckFailed(f"scatter_add status {status}: a bounded wait of the fold ran out")
+
+    def reset_scatter(self):
+        """Untimed: the destination (rank 0) or partial (others) back to zeros."""
+        self.dev["dest"].zero_()
+
+    def check(self):
+        import torch
+        self.ops[0]["run"](self.t4.stream_handle())
+        same_bits(self.dev["gout"], self.expect["gout"], "gather")
+        self.reset_scatter()
+        scatter = self.ops[1]
+        scatter["run"](self.t4.stream_handle())
+        got = self.dev["shard_out"] if self.sharded else self.dev["dest"]
+        want, bound = self.expect["dest"], self.expect["dest_bound"]
+        err = (got - want).abs()
+        excess = (err - bound).max().item()
+        self.checks["scatter_max_abs_err"] = err.max().item()
+        self.checks["scatter_max_rel_err"] = (err / torch.clamp(want.abs(), min=1.0)).max().item()
+        if excess > 0:
+            raise CheckFailed(f"{scatter['tag']}: an element differs from the single-GPU sum by more than the "
+                              f"reordering bound 2 (n-1) 2^-53 sum|x| (excess {excess:.3e})")
+        self.reset_scatter()
 
 
-
-class RrqrWorkload(Workload):
+class RrqrConfig(Config):
     """tall-skinny F64 RRQR of A = U V^T + 1e-10 N, U [65536,64],
-    V [256,64], N [65536,256] normal(0,1) (NumPy generators seeded 10, 11, 12): 256
+    V [256,64], N [65536,256] normal(0,1) (NumPy generators seeded 10, 11, 12), 256
     steps of column_norms -> select_pivot -> swap_columns -> reflector ->
-    apply_reflector (t4a_rrqr, bit-identical to that loop of primitives).  Algorithmic
+    apply_reflector.  One GPU: the fused driver t4a_rrqr (bit-identical to that loop of
+    primitives).  N GPUs: row blocks of m/N rows with the per-step exchange of the
+    column norms and reflector dots (t4a_b200.dist.rrqr_rows_sharded).  Algorithmic
     bytes per factorization: sum over steps s of norms 8(m-s)(n-s) + apply
-    16(m-s)(n-s-1) + swap 32m + reflector 16(m-s).  Each step restores A from a
-    pristine device copy outside the timed events; in the end-to-end leg the timed
-    host-to-device copy of A is the restore."""
+    16(m-s)(n-s-1) + swap 32m + reflector 16(m-s).  A is restored from a pristine device
+    copy before every factorization, outside the op's events; in the end-to-end leg the
+    timed host-to-device copy of A is the restore."""
 
-    name = "config5-rrqr-65536x256-f64"
-    dtype = "f64"
-    e2e_restores = True
+    name = "rrqr"
     M, N, RANK = 65536, 256, 64
+    CPU_STEPS = 16
 
-    def __init__(self, device=None):
+    @classmethod
+    def step_bytes(cls, s):
+        m, n = cls.M, cls.N
+        return 8 * (m - s) * (n - s) + 16 * (m - s) * (n - s - 1) + 32 * m + 16 * (m - s)
+
+    def setup(self):
         import numpy as np
         import torch
-        import t4a_b200 as t4
-        from t4a_b200 import abi
-        self.t4, self.abi = t4, abi
-        self.device = device
+        t4, abi = self.t4, self.abi
         m, n, k = self.M, self.N, self.RANK
         u = np.random.default_rng(10).standard_normal((m, k))
         v = np.random.default_rng(11).standard_normal((n, k))
         noise = np.random.default_rng(12).standard_normal((m, n))
-        a = np.asfortranarray(u @ v.T + 1e-10 * noise)
-        self.a_host = torch.from_numpy(a.ravel(order="K").copy())  # column-major buffer
-        self.steps = n
-        self.ops = [dict(tag="rrqr-f64-65536x256-256steps", i=0, launches=2 * n + 1, bytes=self.algorithmic_bytes())]
-        if device is not None:
-            self.host_in = [self.a_host.pin_memory()]
-            self.pristine = self.a_host.to(device)
-            self.work = torch.empty_like(self.pristine)
-            self.dev_in = [self.work]
-            self.perm = torch.empty(n, dtype=torch.int64, device=device)
-            self.coeff = torch.empty(n, dtype=torch.float64, device=device)
-            self.pivots = torch.empty(n, dtype=torch.int64, device=device)
-            self.status = torch.zeros(1, dtype=torch.int64, device=device)
-            self.layout = abi.layout([m, n])
-            self.ws = torch.empty(t4.rrqr_workspace_bytes(abi.F64, self.layout), dtype=torch.uint8, device=device)
-            self.dev_out = [self.pivots]
-            self.host_out = [torch.empty(n, dtype=torch.int64).pin_memory()]
+        a = torch.from_numpy(np.asfortranarray(u @ v.T + 1e-10 * noise).ravel(order="K").copy())  # column-major
+        from t4a_b200 import dist as t4dist
+        # Row sharding needs the library's sharded driver; without it every rank runs the
+        # whole factorization (replicas), which the op's tag says.
+        self.sharded = self.world > 1 and hasattr(t4dist, "RrqrRowsSharded")
+        self.replicated = self.world > 1 and not self.sharded
+        r0, r1 = self.shard(m) if self.sharded else (0, m)
+        self.rows = r1 - r0
+        self.r0 = r0
+        local = a.view(n, m)[:, r0:r1].contiguous().view(-1)  # this rank's rows, column-major
+        self.keep("a", local)
+        self.a_full = a
+        bytes_all = sum(self.step_bytes(s) for s in range(n))
+        if not self.host_only:
+            d = self.dev
+            d["pristine"] = d["a"].clone()
+            d["perm"] = torch.empty(n, dtype=torch.int64, device=self.device)
+            d["coeff"] = torch.empty(n, dtype=torch.float64, device=self.device)
+            d["pivots"] = torch.empty(n, dtype=torch.int64, device=self.device)
+            d["status"] = torch.zeros(1, dtype=torch.int64, device=self.device)
+            if self.sharded:
+                from t4a_b200 import dist as t4dist
+                self.driver = t4dist.RrqrRowsSharded(d["a"], m, n, r0, n)
+            else:
+                self.layout = abi.layout([m, n])
+                self.ws = torch.empty(t4.rrqr_workspace_bytes(abi.F64, self.layout), dtype=torch.uint8,
+                                      device=self.device)
+        for name in ("perm", "coeff", "pivots"):
+            self.host[name] = pinned(torch.empty(n, dtype=torch.float64 if name == "coeff" else torch.int64))
+        tag = "rrqr-f64-65536x256-256steps" + ("-replicated" if self.replicated else "")
+        self.ops = [dict(tag=tag, config=5, bytes=bytes_all,
+                         local_bytes=bytes_all * self.rows // m, inputs=["a"], outputs=["a", "perm", "coeff", "pivots"],
+                         launches=None, e2e_restores=True)]
+        op = self.ops[0]
+        op["run"] = self._run
+        op["prepare"] = self._prepare
+        op["cpu"] = self._cpu
+        op["launches"] = self.driver.launches if (self.sharded and not self.host_only) else 2 * n + 1
 
-    def algorithmic_bytes(self):
-        m, n = self.M, self.N
-        return sum(8 * (m - s) * (n - s) + 16 * (m - s) * (n - s - 1) + 32 * m + 16 * (m - s) for s in range(n))
+    def _prepare(self):
+        self.dev["a"].copy_(self.dev["pristine"])
 
-    def units(self):
-        return sum(op["bytes"] for op in self.ops)
+    def after_timing(self):
+        status = int(self.dev["status"].item())
+        self.checks["rrqr_status"] = status
+        if status != 0:
+            raise CheckFailed(f"RRQR status {status} after the timed factorizations")
 
-    def prepare(self, op):
-        """Untimed: restore A before a factorization."""
-        self.work.copy_(self.pristine)
+    def _run(self, sh):
+        t4, abi, d = self.t4, self.abi, self.dev
+        if self.sharded:
+            self.driver.run(sh, d["perm"], d["coeff"], d["pivots"], d["status"])
+            return
+        t4.check(t4.lib().t4a_rrqr(sh, abi.F64, vp(d["a"]), ctypes.byref(self.layout), self.M * self.N, self.N,
+                                   vp(d["perm"]), vp(d["coeff"]), vp(d["pivots"]), vp(d["status"]), vp(self.ws),
+                                   self.ws.numel()), "rrqr")
 
-    def run_op(self, op, stream_handle, dev_in=None, dev_out=None):
-        t4, abi = self.t4, self.abi
-        vp = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
-        t4.check(t4.lib().t4a_rrqr(stream_handle, abi.F64, vp(self.work), ctypes.byref(self.layout),
-                                   self.M * self.N, self.steps, vp(self.perm), vp(self.coeff), vp(self.pivots),
-                                   vp(self.status), vp(self.ws), self.ws.numel()), "rrqr")
-
-    def host_arrays(self):
-        return [self.a_host.numpy()], [None]
-
-    def measure_epilogue(self, stream, stream_handle, args):
-        """The reference bench's Q formation after the factorization
-        (examples/bench_kernels.rs:2560-2590) through t4a_rrqr_form_q: identity_shifted,
-        then apply_reflector for step = n-1 .. 0 over all n columns of Q [m, n].  Timed
-        with CUDA events on the launching stream after 3 untimed runs, `args.steps`
-        runs, L2 not flushed (Q alone is 134 MB).  Algorithmic bytes: the identity's
-        writes 8 m n, then per step s the reflector's rows 8 (m - s) and Q's rows read
-        and written 16 n (m - s)."""
-        import torch
-        t4, abi = self.t4, self.abi
-        m, n = self.M, self.N
-        q = torch.empty((n, m), dtype=torch.float64, device=self.device).t()
-        wl_, ql, cl = abi.layout([m, n]), abi.layout([m, n], [1, m]), abi.layout([n])
-        vp = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
-
-        qstatus = torch.zeros(1, dtype=torch.int64, device=self.device)
-
-        def form_q():
-            t4.check(t4.lib().t4a_rrqr_form_q(stream_handle, abi.F64, vp(self.work), ctypes.byref(wl_), m * n,
-                                              vp(self.coeff), ctypes.byref(cl), n, vp(q), ctypes.byref(ql), m * n,
-                                              vp(qstatus)),
-                     "rrqr_form_q")
-        for _ in range(3):
-            form_q()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(args.steps):
-            form_q()
-        e1.record(stream)
-        torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1) / args.steps
-        if int(qstatus.item()) != 0:
-            raise RuntimeError(f"Q formation status {int(qstatus.item())}: a bounded wait ran out")
-        nbytes = 8 * m * n + sum(8 * (m - s) + 16 * n * (m - s) for s in range(n))
-        return {"what": "Q formation (identity_shifted + 256 reflector passes over Q's columns), t4a_rrqr_form_q",
-                "ms": round(ms, 3), "bytes": nbytes, "gbs": round(nbytes / (ms / 1e3) / 1e9, 1),
-                "launches": n + 1, "status": int(qstatus.item())}
-
-    def cpu_sample(self):
-        return f"one full {self.name} factorization"
-
-    def cpu_op(self, op, threads, srcs, dsts):
+    def _cpu(self, threads):
+        """The oracle's factorization loop for the first CPU_STEPS steps."""
         import numpy as np
         oracle = _oracle()
-        work = srcs[0].copy()
+        work = self.a_full.numpy().copy()
         perm = np.zeros(self.N, np.int64)
         coeff = np.zeros(self.N)
-        oracle.lib().t4a_oracle_rrqr_f64(oracle.ptr(work), self.M, self.N, self.steps, oracle.lptr(perm),
+        oracle.lib().t4a_oracle_rrqr_f64(oracle.ptr(work), self.M, self.N, self.CPU_STEPS, oracle.lptr(perm),
                                          oracle.ptr(coeff), 1e-8, 0.0, threads)
+        return sum(self.step_bytes(s) for s in range(self.CPU_STEPS))
+
+    def check(self):
+        """One GPU: status 0 and the rank-revealing prefix (prefix_rank of R is 64).
+        Sharded: pivots over the first 64 steps equal the single-GPU driver's, and the
+        gathered factorization satisfies |Q R - A P| <= 1e-8 |A|."""
+        import torch
+        t4, abi, d = self.t4, self.abi, self.dev
+        m, n = self.M, self.N
+        self._prepare()
+        self._run(t4.stream_handle())
+        torch.cuda.synchronize()
+        if int(d["status"].item()) != 0:
+            raise CheckFailed(f"RRQR status {int(d['status'].item())}")
+        if self.sharded:
+            import torch.distributed as tdist
+            from t4a_b200 import dist as t4dist
+            work = t4dist.gather_rows_colmajor(d["a"], m, n, self.r0)
+            ref_a = self.a_full.to(self.device)
+            ref_layout = abi.layout([m, n])
+            ref_ws = torch.empty(t4.rrqr_workspace_bytes(abi.F64, ref_layout), dtype=torch.uint8, device=self.device)
+            rp, rc_, rv, rs = (torch.empty(n, dtype=torch.int64, device=self.device),
+                               torch.empty(n, dtype=torch.float64, device=self.device),
+                               torch.empty(n, dtype=torch.int64, device=self.device),
+                               torch.zeros(1, dtype=torch.int64, device=self.device))
+            t4.check(t4.lib().t4a_rrqr(t4.stream_handle(), abi.F64, vp(ref_a), ctypes.byref(ref_layout), m * n, n,
+                                       vp(rp), vp(rc_), vp(rv), vp(rs), vp(ref_ws), ref_ws.numel()), "rrqr")
+            piv, ref_piv = d["pivots"].cpu(), rv.cpu()
+            diverge = next((i for i in range(n) if int(piv[i]) != int(ref_piv[i])), n)
+            self.checks["rrqr_first_pivot_divergence"] = diverge
+            if diverge < self.RANK:
+                raise CheckFailed(f"RRQR pivots differ from the single-GPU driver at step {diverge} < {self.RANK}")
+            resid = t4dist.rrqr_residual(work, d["coeff"], d["perm"], self.a_full.to(self.device), m, n)
+            self.checks["rrqr_residual_rel"] = resid
+            if not resid <= 1e-8:
+                raise CheckFailed(f"RRQR residual |QR - AP| / |A| = {resid:.3e} > 1e-8")
+            tdist.barrier()
+        else:
+            rank = torch.zeros(1, dtype=torch.int64, device=self.device)
+            st = torch.zeros(1, dtype=torch.int64, device=self.device)
+            rl = abi.layout([n, n], [1, m])
+            launch = t4.plan_rrqr("prefix_rank", abi.F64, rl, m * n, 1, 1, 1e-8, 0.0)
+            t4.launch_rrqr("prefix_rank", launch, t4.stream_handle(), vp(d["a"]), vp(rank), vp(st), abi.F64, rl,
+                           1e-8, 0.0)
+            self.checks["rrqr_prefix_rank"] = int(rank.item())
+            if int(rank.item()) != self.RANK or int(st.item()) != 0:
+                raise CheckFailed(f"RRQR prefix rank {int(rank.item())} (status {int(st.item())}), expected 64")
 
 
-WORKLOADS = {"movement": MovementWorkload, "reduce": ReduceWorkload, "gather": GatherScatterWorkload,
-             "rrqr": RrqrWorkload}
+CONFIGS = {"reduce": ReduceConfigs, "movement": MovementConfig, "gather": GatherScatterConfig, "rrqr": RrqrConfig}
+ORDER = ["reduce", "movement", "gather", "rrqr"]
 
 
-def torch_int64():
-    import torch
-    return torch.int64
+def build_configs(args, rank, world, device, host_only=False):
+    names = ORDER if args.op == "all" else [args.op]
+    groups = []
+    for name in names:
+        g = CONFIGS[name](rank, world, device, host_only)
+        g.setup()
+        if args.only:
+            keep = set(args.only.split(","))
+            g.ops = [op for op in g.ops if op["tag"] in keep]
+        if g.ops:
+            groups.append(g)
+    return groups
 
 
-def flush_l2(buf):
-    """Evict the working set from L2 by reading a buffer larger than L2 (clean lines, so
-    nothing is written back during the next timed op)."""
-    buf.sum(dtype=torch_int64())
+def workload_config(groups, world):
+    """The `config` object of the JSON line (identical in both arms)."""
+    ops = [op for g in groups for op in g.ops]
+    return {"workload": "BASELINE configs 1-5: " + ", ".join(sorted({g.name for g in groups})) if len(groups) > 1
+            else f"BASELINE {groups[0].name}",
+            "ops": [op["tag"] for op in ops],
+            "bytes_per_step": sum(op["bytes"] for op in ops),
+            "parallelism": f"sharded x{world}" if world > 1 else "1 gpu",
+            "l2": "steady state: ops back to back, each op's inputs evicted by the ~12 GB step; "
+                  "a flushed pass (256 MiB read before every op) is reported per op",
+            "timing": "CUDA events per op on the launching stream, max over ranks"}
+
+
+def dtype_string(groups):
+    names = {"reduce": "f32,f64,c64", "movement": "f32,c64", "gather": "f32,f64,i64", "rrqr": "f64"}
+    return ";".join(names[g.name] for g in groups)
 
 
 def run_ours(args, rank, world, local_rank):
     import torch
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
-    wl = WORKLOADS[args.op](device)
-    if args.only:
-        keep = set(args.only.split(","))
-        wl.ops = [op for op in wl.ops if op["tag"] in keep]
-    t4 = wl.t4
-    stream = torch.cuda.current_stream()
-    sh = ctypes.c_void_p(stream.cuda_stream)
-    flush = torch.ones(256 * MIB, dtype=torch.uint8, device=device)
-    dist = world > 1
+    dist_on = world > 1
 
     def barrier():
-        if dist:
+        if dist_on:
             torch.distributed.barrier()
 
-    prepare = getattr(wl, "prepare", None)
-    for _ in range(args.warmup):
-        for op in wl.ops:
-            if prepare:
-                prepare(op)
-            wl.run_op(op, sh)
-        flush_l2(flush)
+    groups = build_configs(args, rank, world, device)
+    ops = [(g, op) for g in groups for op in g.ops]
+    stream = torch.cuda.current_stream()
+    sh = ctypes.c_void_p(stream.cuda_stream)
     torch.cuda.synchronize()
 
-    # Timed region: K steps, CUDA events around every op on the launching stream.
-    events = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in wl.ops]
+    # Every rank checks its shards against the single-GPU result before timing.
+    checks = {}
+    if not args.no_check:
+        for g in groups:
+            g.check()
+            checks.update(g.checks)
+        torch.cuda.synchronize()
+    for g in groups:
+        g.expect.clear()
+    torch.cuda.empty_cache()
+    barrier()
+
+    def one_step(events=None, flush=None):
+        for j, (g, op) in enumerate(ops):
+            if op.get("prepare"):
+                op["prepare"]()
+            if flush is not None:
+                flush.sum(dtype=torch.int64)
+            if events is not None:
+                events[j][0].record(stream)
+            op["run"](sh)
+            if events is not None:
+                events[j][1].record(stream)
+
+    for _ in range(args.warmup):
+        one_step()
+    torch.cuda.synchronize()
+    barrier()
+
+    # Timed region: K steady-state steps.
+    events = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in ops]
               for _ in range(args.steps)]
+    r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     sampler = ClockSampler(local_rank)
     barrier()
     torch.cuda.synchronize()
     wall0 = time.perf_counter()
     with sampler:
-        # Hold the stream with a bounded sleep kernel while the timed steps are enqueued,
-        # so each event pair brackets GPU work only, not the host's launch latency.
+        # Hold the stream with a bounded sleep kernel while the first steps are enqueued,
+        # so each event pair brackets GPU work, not the host's launch latency.
         torch.cuda._sleep(int(2e8))
+        r0.record(stream)
         for k in range(args.steps):
-            for j, op in enumerate(wl.ops):
-                if prepare:
-                    prepare(op)
-                flush_l2(flush)
-                events[k][j][0].record(stream)
-                wl.run_op(op, sh)
-                events[k][j][1].record(stream)
+            one_step(events[k])
+        r1.record(stream)
         torch.cuda.synchronize()
     barrier()
     wall = time.perf_counter() - wall0
-    per_op_ms = [[events[k][j][0].elapsed_time(events[k][j][1]) for k in range(args.steps)] for j in range(len(wl.ops))]
-    kernel_ms = sum(sum(x) for x in per_op_ms)
-    step_ms = kernel_ms / args.steps
-    if dist:
-        t = torch.tensor([kernel_ms], device=device, dtype=torch.float64)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        kernel_ms = t.item()
-        step_ms = kernel_ms / args.steps
-    value = wl.units() * world * args.steps / (kernel_ms / 1e3) / 1e9
+    per_op = [[events[k][j][0].elapsed_time(events[k][j][1]) for k in range(args.steps)] for j in range(len(ops))]
+    totals = [sum(x) for x in per_op]
+    stats = torch.tensor([sum(totals), r0.elapsed_time(r1)] + totals, device=device, dtype=torch.float64)
+    if dist_on:
+        torch.distributed.all_reduce(stats, op=torch.distributed.ReduceOp.MAX)
+    kernel_ms, region_ms = stats[0].item(), stats[1].item()
+    totals_max = stats[2:].tolist()
+    job_bytes = sum(op["bytes"] for _, op in ops)
+    value = job_bytes * args.steps / (kernel_ms / 1e3) / 1e9
 
-    # End to end through the public API: pinned host inputs -> device -> op -> host.
-    e2e_ms = None
-    h2d = sum(h.numel() * h.element_size() for op in wl.ops for h, _ in wl.e2e_inputs(op))
-    d2h = sum(h.numel() * h.element_size() for op in wl.ops for _, h in wl.e2e_outputs(op))
-    # Three streams, as a caller pipelines host data through the library: host->device
-    # copies on s_in, the ops on the launching stream, device->host copies on s_out, so
-    # one op's result copy overlaps the next op's input copy (PCIe is full duplex).  A
-    # copy into a device input waits for the last op that read that buffer; an op waits
-    # for its input copies and for the last copy out of its output buffers.
+    # Status words of the timed steps: a bounded wait that ran out fails the run.
+    for g in groups:
+        g.after_timing()
+
+    # Cold pass: L2 flushed (256 MiB read) before every op.
+    flush = torch.ones(256 * MIB, dtype=torch.uint8, device=device)
+    cold_steps = min(args.steps, 3)
+    cold_events = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in ops]
+                   for _ in range(cold_steps)]
+    barrier()
+    torch.cuda.synchronize()
+    for k in range(cold_steps):
+        one_step(cold_events[k], flush)
+    torch.cuda.synchronize()
+    cold = torch.tensor([sum(cold_events[k][j][0].elapsed_time(cold_events[k][j][1]) for k in range(cold_steps))
+                         for j in range(len(ops))], device=device, dtype=torch.float64)
+    if dist_on:
+        torch.distributed.all_reduce(cold, op=torch.distributed.ReduceOp.MAX)
+    cold = cold.tolist()
+    del flush
+
+    e2e = measure_e2e(args, groups, ops, stream, sh, device, world, barrier)
+
+    peak, peak_kind = read_peaks()
+    ops_detail = {}
+    for j, (g, op) in enumerate(ops):
+        ms = totals_max[j] / args.steps
+        cms = cold[j] / cold_steps
+        ops_detail[op["tag"]] = {
+            "config": op["config"], "bytes": op["bytes"], "us": round(1e3 * ms, 2),
+            "gbs": round(op["bytes"] / (ms / 1e3) / 1e9, 1), "frac": round(op["bytes"] / (ms / 1e3) / 1e9 / peak, 3),
+            "us_flushed": round(1e3 * cms, 2),
+            "frac_flushed": round(op["bytes"] / (cms / 1e3) / 1e9 / peak, 3)}
+    dom = max(range(len(ops)), key=lambda j: totals_max[j])
+    dom_op = ops[dom][1]
+    dom_ms = totals_max[dom] / args.steps
+    achieved = dom_op["bytes"] / (dom_ms / 1e3) / 1e9
+    line = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(region_ms / args.steps, 4),
+        "higher_is_better": True,
+        "scaling": "strong" if world > 1 else "weak",
+        "vs_baseline": None,
+        "dtype": dtype_string(groups),
+        "data": "synthetic (seeded SplitMix64 normal/uniform/Zipf streams; NumPy generators for RRQR)",
+        "config": workload_config(groups, world),
+        "roofline": {"bound": "hbm", "kernel": dom_op["tag"], "achieved": round(achieved, 1), "peak": peak,
+                     "peak_kind": f"{peak_kind} hbm_gbs", "unit": "GB/s", "frac": round(achieved / peak, 4),
+                     "traffic": profile_traffic(dom_op["tag"]) if world == 1 else None,
+                     "unit_of_launch": "one whole op (RRQR: one 256-step factorization)"},
+        "ops": ops_detail,
+        "e2e": e2e,
+        "gpu_launches": sum(op["launches"] for _, op in ops) * args.steps,
+        "clocks": sampler.summary(),
+        "checks": dict(checks, passed=not args.no_check, against="single-GPU result of the same library"),
+        "kernel_ms_per_step": round(kernel_ms / args.steps, 4),
+        "wall_s_timed_region": round(wall, 3),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(groups, args)
+    return line
+
+
+def measure_e2e(args, groups, ops, stream, sh, device, world, barrier):
+    """Same ops through the C ABI from pinned host memory: every input tensor of a step is
+    copied in before its first op, every op's outputs are copied out after it, on three
+    streams (host-to-device copies, the ops, device-to-host copies) with buffer-level
+    events, as a caller pipelines host data through the library."""
+    import torch
     s_in = torch.cuda.Stream(device=device)
     s_out = torch.cuda.Stream(device=device)
+    h2d = d2h = 0
+    for g in groups:
+        names_in = []
+        for op in g.ops:
+            for nm in op["inputs"]:
+                if nm not in names_in:
+                    names_in.append(nm)
+        h2d += sum(g.host[nm].numel() * g.host[nm].element_size() for nm in names_in)
+        d2h += sum(g.host[nm].numel() * g.host[nm].element_size() for op in g.ops for nm in op["outputs"])
     barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     s_in.wait_event(e0)
     s_out.wait_event(e0)
-    read_done, copied_out = {}, {}  # device buffer -> event: last op that read it / last copy out of it
+    read_done, copied_out = {}, {}
     for _ in range(args.steps):
-        for op in wl.ops:
-            ins, outs = wl.e2e_inputs(op), wl.e2e_outputs(op)
-            with torch.cuda.stream(s_in):
-                for h, d in ins:
-                    if d.data_ptr() in read_done:
-                        s_in.wait_event(read_done[d.data_ptr()])
-                    d.copy_(h, non_blocking=True)
-                arrived = torch.cuda.Event()
-                arrived.record(s_in)
-            stream.wait_event(arrived)
-            for d, _ in outs:
-                if d.data_ptr() in copied_out:
-                    stream.wait_event(copied_out[d.data_ptr()])
-            if prepare and not getattr(wl, "e2e_restores", False):
-                prepare(op)
-            wl.run_op(op, sh)
-            done = torch.cuda.Event()
-            done.record(stream)
-            for _, d in ins:
-                read_done[d.data_ptr()] = done
-            s_out.wait_event(done)
-            with torch.cuda.stream(s_out):
-                for d, h in outs:
-                    h.copy_(d, non_blocking=True)
-                out_done = torch.cuda.Event()
-                out_done.record(s_out)
-            for d, _ in outs:
-                copied_out[d.data_ptr()] = out_done
+        for g in groups:
+            copied = set()
+            for op in g.ops:
+                with torch.cuda.stream(s_in):
+                    for nm in op["inputs"]:
+                        if nm in copied:
+                            continue
+                        d = g.dev[nm]
+                        if d.data_ptr() in read_done:
+                            s_in.wait_event(read_done[d.data_ptr()])
+                        d.copy_(g.host[nm], non_blocking=True)
+                        copied.add(nm)
+                    arrived = torch.cuda.Event()
+                    arrived.record(s_in)
+                stream.wait_event(arrived)
+                for nm in op["outputs"]:
+                    d = g.dev[nm]
+                    if d.data_ptr() in copied_out:
+                        stream.wait_event(copied_out[d.data_ptr()])
+                if op.get("prepare") and not op.get("e2e_restores"):
+                    op["prepare"]()
+                op["run"](sh)
+                done = torch.cuda.Event()
+                done.record(stream)
+                for nm in op["inputs"]:
+                    read_done[g.dev[nm].data_ptr()] = done
+                s_out.wait_event(done)
+                with torch.cuda.stream(s_out):
+                    for nm in op["outputs"]:
+                        g.host[nm].copy_(g.dev[nm], non_blocking=True)
+                    out_done = torch.cuda.Event()
+                    out_done.record(s_out)
+                for nm in op["outputs"]:
+                    copied_out[g.dev[nm].data_ptr()] = out_done
     tail_in, tail_out = torch.cuda.Event(), torch.cuda.Event()
     tail_in.record(s_in)
     tail_out.record(s_out)
@@ -765,62 +1068,14 @@ def run_ours(args, rank, world, local_rank):
     stream.wait_event(tail_out)
     e1.record(stream)
     torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
-    if dist:
-        t = torch.tensor([e2e_ms], device=device, dtype=torch.float64)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        e2e_ms = t.item()
-    e2e_value = wl.units() * world * args.steps / (e2e_ms / 1e3) / 1e9
-    # A workload may time a follow-on stage of the path separately (RRQR: the Q
-    # formation that follows the factorization in the reference bench).
-    epilogue = wl.measure_epilogue(stream, sh, args) if hasattr(wl, "measure_epilogue") else None
-
-    # Roofline of the dominant kernel (longest total time).
-    peak, peak_kind = read_peaks()
-    totals = [sum(x) for x in per_op_ms]
-    dom = max(range(len(wl.ops)), key=lambda j: totals[j])
-    dom_op = wl.ops[dom]
-    dom_ms = totals[dom] / args.steps
-    achieved = dom_op["bytes"] / (dom_ms / 1e3) / 1e9
-    traffic = profile_traffic(dom_op["tag"])
-    ops_detail = {wl.ops[j]["tag"]: {"bytes": wl.ops[j]["bytes"], "us": round(1e3 * totals[j] / args.steps, 2),
-                                     "gbs": round(wl.ops[j]["bytes"] / (totals[j] / args.steps / 1e3) / 1e9, 1),
-                                     "frac_of_measured": round(wl.ops[j]["bytes"] / (totals[j] / args.steps / 1e3)
-                                                               / 1e9 / peak, 3)}
-                  for j in range(len(wl.ops))}
-
-    line = {
-        "metric": "achieved HBM GB/s (% of B200 peak) per op at 1/2/4/8 GPUs vs CPU baseline",
-        "value": round(value, 2),
-        "unit": "GB/s",
-        "n_gpus": world,
-        "steps": args.steps,
-        "warmup": args.warmup,
-        "ms_per_step": round(step_ms, 4),
-        "higher_is_better": True,
-        "scaling": "weak",
-        "vs_baseline": None,
-        "dtype": wl.dtype,
-        "data": "synthetic (seeded normal(0,1), SplitMix64 Box-Muller)",
-        "config": {"workload": wl.name, "ops": [op["tag"] for op in wl.ops],
-                   "bytes_per_step_per_gpu": wl.units(), "l2": "flushed before every op (256 MiB read, untimed)",
-                   "parallelism": f"replicas x{world}" if world > 1 else "1 gpu",
-                   "timing": "CUDA events per op on the launching stream, max over ranks"},
-        "roofline": {"bound": "hbm", "kernel": dom_op["tag"], "achieved": round(achieved, 1), "peak": peak,
-                     "peak_kind": f"{peak_kind} hbm_gbs", "unit": "GB/s", "frac": round(achieved / peak, 4),
-                     "traffic": traffic},
-        "ops": ops_detail,
-        "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "ms_per_step": round(e2e_ms / args.steps, 3)},
-        "gpu_launches": sum(op.get("launches", 1) for op in wl.ops) * args.steps,
-        "clocks": sampler.summary(),
-        "wall_s_timed_region": round(wall, 3),
-    }
-    if epilogue is not None:
-        line["epilogue"] = epilogue
-    if rank == 0 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(wl, args)
-    return line
+    ms = torch.tensor([e0.elapsed_time(e1)], device=device, dtype=torch.float64)
+    if world > 1:
+        torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
+    ms = ms.item()
+    job_bytes = sum(op["bytes"] for g in groups for op in g.ops)
+    return {"value": round(job_bytes * args.steps / (ms / 1e3) / 1e9, 2), "unit": "GB/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms / args.steps, 3),
+            "per_rank": world > 1}
 
 
 def host_threads():
@@ -830,50 +1085,72 @@ def host_threads():
         return os.cpu_count() or 1
 
 
-def cpu_baseline(wl, args, repeats=1):
-    """The oracle port over every host core on the same workload (one full step)."""
-    import numpy as np
+def cpu_sample_text(groups):
+    parts = []
+    for g in groups:
+        if g.name == "reduce":
+            parts.append("config 1 whole, config 3 on 1/16 of a non-reduced axis")
+        elif g.name == "movement":
+            parts.append("config 2 whole")
+        elif g.name == "gather":
+            parts.append(f"config 4 on the first {GatherScatterConfig.SAMPLE} of {GatherScatterConfig.N} index rows")
+        elif g.name == "rrqr":
+            parts.append(f"config 5's first {RrqrConfig.CPU_STEPS} of {RrqrConfig.N} factorization steps")
+    return "; ".join(parts)
+
+
+def cpu_step(groups, threads):
+    nbytes = 0
+    for g in groups:
+        for op in g.ops:
+            nbytes += op["cpu"](threads)
+    return nbytes
+
+
+def cpu_baseline(groups, args, steps=3):
+    """The oracle port over every host core on a bounded sample of every op, `steps` times."""
     threads = host_threads()
-    srcs, dsts = wl.host_arrays()
+    cpu_step(groups, threads)  # warm-up (page faults of the output buffers)
     t0 = time.perf_counter()
-    n = 0
-    while True:
-        for op in wl.ops:
-            wl.cpu_op(op, threads, srcs, dsts)
-        n += 1
-        if time.perf_counter() - t0 > 2.0 or n >= repeats:
-            break
+    nbytes = 0
+    for _ in range(steps):
+        nbytes += cpu_step(groups, threads)
     dt = time.perf_counter() - t0
-    return {"value": round(wl.cpu_units() * n / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"{n} step(s) of {wl.cpu_sample()} ({wl.cpu_units() / MIB:.0f} MiB algorithmic), {dt:.2f} s"}
+    return {"value": round(nbytes / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{steps} steps of: {cpu_sample_text(groups)} "
+                      f"({nbytes / steps / MIB:.0f} MiB algorithmic per step), {dt:.2f} s"}
 
 
 def run_reference(args, rank, world):
     """CPU implementation of the path on the host cores (see module docstring)."""
-    import torch
     if rank != 0:
         return None
-    wl = WORKLOADS[args.op](None)
+    import torch
+    device = gen_device()
+    groups = build_configs(args, 0, 1, device, host_only=True)
+    if torch.cuda.is_available():
+        torch.cuda.empty_cache()
     threads = host_threads()
-    srcs, dsts = wl.host_arrays()
     for _ in range(max(0, min(args.warmup, 1))):
-        for op in wl.ops:
-            wl.cpu_op(op, threads, srcs, dsts)
+        cpu_step(groups, threads)
     t0 = time.perf_counter()
+    nbytes = 0
     for _ in range(args.steps):
-        for op in wl.ops:
-            wl.cpu_op(op, threads, srcs, dsts)
+        nbytes += cpu_step(groups, threads)
     dt = time.perf_counter() - t0
-    value = wl.cpu_units() * args.steps / dt / 1e9
+    value = nbytes / dt / 1e9
     return {
         "impl": "reference",
-        "metric": "achieved HBM GB/s (% of B200 peak) per op at 1/2/4/8 GPUs vs CPU baseline",
+        "metric": METRIC,
         "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(1e3 * dt / args.steps, 3), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic (seeded normal(0,1))",
-        "config": {"workload": wl.name, "ops": [op["tag"] for op in wl.ops], "bytes_per_step": wl.units()},
+        "ms_per_step": round(1e3 * dt / args.steps, 3), "higher_is_better": True,
+        "scaling": "strong" if world > 1 else "weak",
+        "vs_baseline": None, "dtype": dtype_string(groups),
+        "data": "synthetic (seeded SplitMix64 normal/uniform/Zipf streams; NumPy generators for RRQR)",
+        "config": workload_config(groups, world),
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": f"{args.steps} steps of {wl.cpu_sample()} on the host cores"},
+                         "sample": f"{args.steps} steps of: {cpu_sample_text(groups)} "
+                                   f"({nbytes / args.steps / MIB:.0f} MiB algorithmic per step)"},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
@@ -884,9 +1161,10 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--op", default="movement", choices=sorted(WORKLOADS))
+    ap.add_argument("--op", default="all", choices=["all"] + ORDER)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", default=None, help="comma-separated op tags of the workload to run (profiling)")
+    ap.add_argument("--no-check", action="store_true", help="skip the per-rank check against the single-GPU result")
+    ap.add_argument("--only", default=None, help="comma-separated op tags to run (profiling)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
 
@@ -906,13 +1184,17 @@ def main():
     saved_stdout = os.dup(1)
     os.dup2(2, 1)
     line = None
+    failed = None
     try:
         if world > 1:
             import datetime
             torch.cuda.set_device(local_rank)
-            torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+            torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                                 device_id=torch.device("cuda", local_rank))
         try:
             line = run_ours(args, rank, world, local_rank)
+        except CheckFailed as exc:
+            failed = f"rank {rank}: {exc}"
         finally:
             if world > 1:
                 torch.distributed.destroy_process_group()
@@ -920,6 +1202,9 @@ def main():
         sys.stdout.flush()
         os.dup2(saved_stdout, 1)
         os.close(saved_stdout)
+    if failed:
+        print(json.dumps({"metric": METRIC, "error": failed}), flush=True)
+        sys.exit(3)
     if rank == 0 and line is not None:
         print(json.dumps(line), flush=True)
 

@@ -1,25 +1,31 @@
 """Multi-GPU composition of the path: one process per GPU over torch.distributed.
 
-The per-GPU work is this library's CUDA kernels (the C ABI); this module only
-partitions it and, for scatter_add, runs the one exchange that operation has:
+The per-GPU work is this library's CUDA kernels (the C ABI).  This module partitions
+the work and, where the path has an exchange step, runs it:
 
-* gather: index batches are sharded across ranks and the table is replicated, so every
-  rank gathers its own output rows; no collective.
-* reductions: a non-reduced axis is sharded into slabs, so every rank reduces its own
-  slab to its own outputs; no collective.
+* reductions: a non-reduced axis is sharded into slabs; every rank reduces the slab it
+  holds (any strides: a compact local slab, or a view of a full tensor cut by
+  `shard_view` without a copy) into its own outputs.  No collective.
+* movement / permutation: the destination is sharded along its slowest axis; every
+  rank writes its contiguous output slab from the matching strided view of the source
+  (`movement_slab`).  No collective.
+* gather: index batches are sharded and the table is replicated; every rank gathers
+  its own output rows.  No collective.
 * scatter_add: update batches are sharded.  Every rank adds its updates into a
-  full-size partial destination (rank 0's holds the operand, the others start at zero),
-  and one reduce-scatter (sum) leaves each rank the destination rows it owns.  The
-  floating sums over colliding rows are order-dependent, as in the single-GPU
+  full-size partial destination (rank 0's holds the operand, the others start at
+  zero), and one reduce-scatter (sum) leaves each rank the destination rows it owns.
+  The floating sums over colliding rows are order-dependent, as in the single-GPU
   operation (atomics).
-* RRQR is not sharded: the reference's norm and dot chains fold each lane's rows in
-  order, so splitting rows across GPUs would change the rounding; ranks run
-  independent factorizations.
+* RRQR: rows are sharded; every step exchanges the column norms and the reflector
+  dots (`rrqr_rows_sharded`, NCCL inside the library's C++ driver).
 """
+import ctypes
+
 import torch
 import torch.distributed as dist
 
 import t4a_b200 as _t4
+from t4a_b200 import abi as _abi
 
 
 def shard_range(n, world, rank):
@@ -36,6 +42,13 @@ def _world(group):
     return dist.get_world_size(group), dist.get_rank(group)
 
 
+def shard_view(x, shard_axis, world, rank):
+    """The slab of `x` along NumPy axis `shard_axis` that rank `rank` of `world` owns, as a
+    view (no copy)."""
+    start, stop = shard_range(x.shape[shard_axis], world, rank)
+    return x.narrow(shard_axis, start, stop - start)
+
+
 def gather_rows_sharded(table, indices, group=None, out=None):
     """This rank's share of a gather of whole rows: `indices` holds all index rows;
     the rank gathers rows shard_range(len(indices)) of the output.  No collective."""
@@ -44,15 +57,37 @@ def gather_rows_sharded(table, indices, group=None, out=None):
     return _t4.gather_rows(table, indices.reshape(-1)[start:stop], out=out)
 
 
-def reduce_sharded(x, numpy_axis, op, shard_axis=0, group=None):
-    """This rank's slab of a single-axis reduction: `x` is sharded along `shard_axis`
-    (which must differ from the reduced axis); returns the reduction of this rank's
-    slab.  No collective."""
-    if shard_axis == numpy_axis:
-        raise ValueError("the sharded axis must not be the reduced axis")
-    world, rank = _world(group)
-    start, stop = shard_range(x.shape[shard_axis], world, rank)
-    return _t4.reduce(x.narrow(shard_axis, start, stop - start).contiguous(), numpy_axis, op)
+def reduce_sharded(x_local, numpy_axis, op, out=None, workspace=None, stream=None):
+    """This rank's part of a single-axis reduction whose input is sharded along another
+    axis: reduces the slab `x_local` (any strides, e.g. a `shard_view`) along
+    `numpy_axis` into this rank's outputs.  No collective, no copy of the slab."""
+    return _t4.reduce(x_local, numpy_axis, op, out=out, workspace=workspace, stream=stream)
+
+
+def movement_slab(src_layout, world, rank):
+    """Rank `rank`'s part of a movement whose destination is sharded along its slowest
+    axis (reference axis rank-1 of a t4a layout, NumPy axis 0).  `src_layout` is the
+    source view that the whole destination is materialized from (strides may be
+    negative).  Returns (source slab layout, compact destination slab layout, slab
+    start): the source slab is the same view restricted to destination rows
+    [start, stop) of that axis; the destination slab is the rank's contiguous part of
+    the compact destination."""
+    r = src_layout.rank
+    ext = src_layout.extents_list()
+    strides = src_layout.strides_list()
+    start, stop = shard_range(ext[r - 1], world, rank)
+    slab_ext = ext[:r - 1] + [stop - start]
+    src = _abi.layout(slab_ext, strides, src_layout.offset + start * strides[r - 1])
+    return src, _abi.layout(slab_ext), start
+
+
+def materialize_slab(stream_handle, dtype, dst_ptr, src_ptr, src_layout, src_len, world, rank):
+    """Writes rank `rank`'s destination slab (movement_slab) from the source at
+    `src_ptr` through the strided-copy entry.  Returns the destination slab layout."""
+    src, dst, _ = movement_slab(src_layout, world, rank)
+    n = dst.count()
+    _t4.copy_strided_raw(stream_handle, dtype, dst_ptr, dst, n, src_ptr, src, src_len)
+    return dst
 
 
 def _reduce_scatter_rows(out, partial, group):
@@ -94,3 +129,7 @@ def scatter_add_rows_sharded(partial, indices, updates, group=None, workspace=No
     if out is None:
         out = torch.empty((rows // world, cols), dtype=partial.dtype, device=partial.device)
     return _reduce_scatter_rows(out, partial, group)
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr())

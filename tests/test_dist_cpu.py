@@ -73,3 +73,45 @@ def scatter_worker(rank, world, port):
 
 def test_scatter_add_sharded_exchange_gloo():
     mp.spawn(scatter_worker, args=(2, free_port()), nprocs=2, join=True)
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+def test_movement_slabs_tile_the_destination(world):
+    """The destination slabs of every rank (movement_slab: the slowest destination axis
+    split, each slab read through the strided source view) put together equal the whole
+    materialization, for a permutation and for a reversed axis (negative stride), as
+    computed by the CPU oracle."""
+    import ctypes
+    import numpy as np
+    import oracle
+    from t4a_b200 import abi
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((8, 6, 5, 7)).astype(np.float32)
+    cases = []
+    st = [s // 4 for s in x.strides]
+    perm = (3, 1, 0, 2)
+    cases.append(abi.numpy_layout([x.shape[p] for p in perm], [st[p] for p in perm]))
+    cases.append(abi.numpy_layout(list(x.shape), [st[0], st[1], -st[2], st[3]], (x.shape[2] - 1) * st[2]))
+    for full_l in cases:
+        whole = np.zeros(x.size, np.float32)
+        assert oracle.lib().t4a_oracle_strided_to_strided(abi.F32, oracle.ptr(whole), oracle.ptr(x),
+                                                          ctypes.byref(full_l),
+                                                          ctypes.byref(abi.layout(full_l.extents_list())), 1) == 0
+        parts = []
+        for rank in range(world):
+            src_l, dst_l, start = t4dist.movement_slab(full_l, world, rank)
+            assert start == t4dist.shard_range(full_l.extents[full_l.rank - 1], world, rank)[0]
+            part = np.zeros(dst_l.count(), np.float32)
+            assert oracle.lib().t4a_oracle_strided_to_strided(abi.F32, oracle.ptr(part), oracle.ptr(x),
+                                                              ctypes.byref(src_l), ctypes.byref(dst_l), 1) == 0
+            parts.append(part)
+        assert np.array_equal(np.concatenate(parts), whole)
+
+
+def test_shard_view_is_a_view():
+    x = torch.arange(4 * 6 * 3, dtype=torch.float32).reshape(4, 6, 3)
+    for world in (1, 2, 3):
+        pieces = [t4dist.shard_view(x, 1, world, r) for r in range(world)]
+        assert all(p.data_ptr() >= x.data_ptr() and p.untyped_storage().data_ptr() == x.untyped_storage().data_ptr()
+                   for p in pieces)
+        assert torch.equal(torch.cat(pieces, dim=1), x)

@@ -2,6 +2,7 @@
 single-GPU results bit for bit; the sharded scatter_add (per-rank CUDA scatter into a
 partial destination, then one reduce-scatter) equals the oracle sum of every rank's
 updates within the F64 tolerance (1e-12 relative to max(|x|, 1))."""
+import ctypes
 import datetime
 import socket
 
@@ -64,10 +65,26 @@ def worker(rank, world, port):
         assert torch.equal(torch.cat(outs), table[gidx])
         # reduction: slabs of a non-reduced axis
         x = torch.randn(64, 300, 32, generator=g, dtype=torch.float32).to(dev)
-        slab = t4dist.reduce_sharded(x, 1, abi.SUM, shard_axis=0)
+        slab = t4dist.reduce_sharded(t4dist.shard_view(x, 0, world, rank), 1, abi.SUM)
         full = t4.reduce(x, 1, abi.SUM)
         start, stop = t4dist.shard_range(64, world, rank)
         assert torch.equal(slab.view(torch.int32), full[start:stop].contiguous().view(torch.int32))
+        # the same over a strided slab (axis 1 sharded, axis 0 reduced), no copy of the slab
+        slab0 = t4dist.reduce_sharded(t4dist.shard_view(x, 1, world, rank), 0, abi.MAX)
+        full0 = t4.reduce(x, 0, abi.MAX)
+        s1, e1 = t4dist.shard_range(300, world, rank)
+        assert torch.equal(slab0.view(torch.int32), full0[:, s1:e1].contiguous().view(torch.int32))
+        # movement: destination slabs along the slowest axis from strided source views
+        src = torch.randn(16, 12, 10, 8, generator=g, dtype=torch.float32).to(dev)
+        view = src.permute(3, 1, 0, 2)
+        full_l = t4.tensor_layout(view)
+        want = view.contiguous()
+        dst_l = t4dist.movement_slab(full_l, world, rank)[1]
+        out = torch.empty(dst_l.count(), dtype=torch.float32, device=dev)
+        t4dist.materialize_slab(t4.stream_handle(), abi.F32, ctypes.c_void_p(out.data_ptr()),
+                                ctypes.c_void_p(src.data_ptr()), full_l, src.numel(), world, rank)
+        m0, m1 = t4dist.shard_range(view.shape[0], world, rank)
+        assert torch.equal(out.view(m1 - m0, *view.shape[1:]), want[m0:m1])
         torch.cuda.synchronize()
     finally:
         dist.destroy_process_group()
