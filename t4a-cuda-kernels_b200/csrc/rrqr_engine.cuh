@@ -4,13 +4,15 @@
 // the whole block:
 //   ring_dot      <v, t> * coeff over rows [0, rows) with v_0 = 1 (the reflector's
 //                 implicit leading one), folded by the reference's 32-lane chain (lane l
-//                 visits rows l, l + 32, ...) from segments staged in shared memory;
+//                 visits rows l, l + 32, ...) from segments that bulk copies stage in
+//                 shared memory;
 //   update_direct t = fma(-v, d, t) over the same rows with 16-byte global loads and
 //                 stores by every thread, tracking the largest finite modulus and a
 //                 non-finite flag of rows [1, rows);
 //   peak_direct   the largest modulus of a column read directly by every thread;
-//   ring_norm     the reference's scaled sum of squares: helper warps turn each staged
-//                 segment into |x| / scale in place and the chain warp folds q * q.
+//   scaled_norm   the reference's chain of (|x| / scale)^2: helper warps load x straight
+//                 from global memory, divide, and fill shared-memory buffers that the
+//                 chain warp folds.
 // The chains run in one warp in the reference's visiting order, so every norm, dot and
 // update has the reference's bits; the staging, the direct vector phases and the
 // division of work between warps are this library's.
@@ -20,16 +22,15 @@
 //   warps 1..3   producers: lane 0 of warp 1 + k issues the bulk copies of ring stage k
 //                (a bulk copy costs its issuing warp about the same time whatever its
 //                size, so three warps keep three copies going);
-//   warps 4..11  helpers (scaled magnitudes of the norm phase);
+//   warps 4..11  helpers (the scaled magnitudes of scaled_norm);
 //   every warp   the direct phases.
-// The ring has kColStages stages of kColStageBytes with three mbarriers each: `full`
-// (the stage's copies landed), `ready` (the helpers finished a norm segment), `empty`
-// (the chain warp released the stage).  Ring positions run on across the phases of a
-// block: position p uses stage p % kColStages for the (p / kColStages)-th time, so the
-// parity of every wait is a function of p alone.  A block runs at most one norm phase,
-// whose first position P0 fixes the `ready` parities ((p - P0) / kColStages).  Every wait
-// is bounded; one that runs out stops the block's remaining ring work and sets bit 1 of
-// the status word, and a stopped block writes no result it did not finish.
+// The dot's ring has kColStages stages of kColStageBytes with two mbarriers each: `full`
+// (the stage's copies landed) and `empty` (the chain warp released it).  Ring position p
+// uses stage p % kColStages for the (p / kColStages)-th time, so the parity of every wait
+// is a function of p alone.  scaled_norm views the same bytes as kNormBufs buffers with
+// their own `ready` / `freed` mbarriers; a block runs at most one scaled_norm.  Every
+// wait is bounded; one that runs out stops the block's remaining staged work and sets
+// bit 1 of the status word, and a stopped block writes no result it did not finish.
 //
 // Segment placement: element e of a segment sits at slot sh + e, where sh * sizeof(F) is
 // the operand's address modulo 16 at its first row, so the 16-byte-aligned bytes covering
@@ -52,6 +53,9 @@ constexpr int kColStageBytes = 32768;
 constexpr unsigned kColWaitLimit = 1u << 20;  // try_wait rounds before giving up
 constexpr unsigned kColSuspendNs = 1000;
 
+// scaled_norm's buffers: the ring's bytes viewed as kNormBufs buffers of kNormSeg elements.
+constexpr int kNormBufs = 6;
+
 template <typename F>
 struct ColSmem {
   static constexpr int kPad = 16 / static_cast<int>(sizeof(F));
@@ -59,10 +63,12 @@ struct ColSmem {
   static constexpr int kSeg2 = kSeg1 / 2;                                      // dot: per operand
   static constexpr int kRegion2 = kSeg2 + kPad;                                // dot: slots of one operand
   static constexpr int kStage = kSeg1 + 2 * kPad;
+  static constexpr int kNormSeg = kColStages * kSeg1 / kNormBufs;  // scaled_norm: elements per buffer
   F raw[kColStages][kStage];
   unsigned long long full[kColStages];
   unsigned long long empty[kColStages];
-  unsigned long long ready[kColStages];
+  unsigned long long ready[kNormBufs];  // scaled_norm: buffer b filled by the helpers
+  unsigned long long freed[kNormBufs];  // scaled_norm: buffer b folded by the chain warp
   F red[kColWarps];
   int bad[kColWarps];
   F dot;
@@ -95,7 +101,6 @@ __device__ __forceinline__ void bar_arrive(unsigned long long* bar) {
 
 // Orders this thread's generic-proxy writes before later bulk copies (async proxy).
 __device__ __forceinline__ void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-__device__ __forceinline__ void fence_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 
 __device__ __forceinline__ int stage_of(long long p) { return static_cast<int>(p % kColStages); }
 __device__ __forceinline__ unsigned parity_of(long long p) { return static_cast<unsigned>((p / kColStages) & 1); }
@@ -122,8 +127,11 @@ __device__ __forceinline__ void engine_init(ColSmem<F>& sm) {
     for (int q = 0; q < kColStages; ++q) {
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&sm.full[q])) : "memory");
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&sm.empty[q])) : "memory");
+    }
+    for (int q = 0; q < kNormBufs; ++q) {
       asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(&sm.ready[q])), "n"(kColHelpers / 32)
                    : "memory");
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(&sm.freed[q])) : "memory");
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     sm.abort = 0;
@@ -355,8 +363,7 @@ __device__ __forceinline__ Split16<F> split16(const F* x, long long rows) {
 // 16-byte loads and stores where v and t share their alignment.  The 16-byte groups are
 // taken from the last one down, so the lowest rows, which a following ring phase reads
 // first, are the most recently written.  kTrack: the largest finite modulus and the
-// non-finite flag of the updated rows [1, rows) go to *peak / *flagged.  Ends with the
-// proxy fence that orders the stores before later bulk copies of the same rows.
+// non-finite flag of the updated rows [1, rows) go to *peak / *flagged.
 template <bool kTrack, typename F>
 __device__ __forceinline__ void update_direct(const F* v, F* t, long long rows, F d, F* peak, bool* flagged) {
   using V = typename Vec16<F>::V;
@@ -402,7 +409,6 @@ __device__ __forceinline__ void update_direct(const F* v, F* t, long long rows, 
       tv[q] = xt[u];
     }
   }
-  fence_async_global();
 }
 
 // The largest modulus over rows [0, rows) of x, read by every thread (16-byte loads
@@ -519,44 +525,45 @@ __device__ __forceinline__ bool quotient_safe(const ScaledQuotient<F>& s, F a) {
   return s.fast && (a == F(0) || a >= s.threshold);
 }
 
+// The reference's chain of (|x| / scale)^2 over rows [0, rows) of x (scale > 0), the
+// block's only norm phase.  The helper warps load x straight from global memory (after an
+// update it is L2-hot), turn it into |x| / scale and store it into buffer g %
+// kNormBufs; the chain warp folds each buffer in the reference's lane order and frees
+// it.  A helper issues the loads of its next segment before it waits for a free buffer,
+// so the loads run while the chain folds.  Returns the butterfly-summed chain to every
+// thread (0 in a block that stopped).
+//
+// Measured at config-5 size (65536 rows), this phase takes 20-28 us per block against
+// 10.4 us for the chain alone: the helpers' loads and quotients share the SM with the
+// chain, and the 134 MB matrix, about the size of L2, is streamed by every phase.
+// Staging by bulk copies or by cp.async (64 KB in flight per block) measured the same or
+// slower.
 template <typename F>
-__device__ __forceinline__ long long norm_segments(long long rows) {
-  return (rows + ColSmem<F>::kSeg1 - 1) / ColSmem<F>::kSeg1;
-}
-
-// The reference's chain of (|x| / scale)^2 over rows [0, rows) of x at ring positions
-// [base, base + norm_segments(rows)) -- the block's only norm phase.  Returns, to every
-// thread, the butterfly-summed lanes' partial sums (0 in a stopped block).  scale > 0.
-template <typename F>
-__device__ __forceinline__ F ring_norm(ColSmem<F>& sm, Producer& pr, long long base, const F* x, long long rows,
-                                       F scale, long long* status) {
+__device__ __forceinline__ F scaled_norm(ColSmem<F>& sm, const F* x, long long rows, F scale, long long* status) {
   using S = ColSmem<F>;
+  constexpr int kSeg = S::kNormSeg;
+  constexpr int kPer = kSeg / kColHelpers;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const long long nseg = norm_segments<F>(rows);
-  const Operand<F> op = operand(x, rows, S::kSeg1, 0);
-  if (pr.k >= 0) {
-    if (!produce<F, 1>(sm, pr, &op, base, nseg)) fail(sm, status);
-  } else if (warp >= kColHelperWarp0) {
+  const long long nseg = (rows + kSeg - 1) / kSeg;
+  F* bufs = &sm.raw[0][0];
+  if (warp >= kColHelperWarp0) {
     const ScaledQuotient<F> quo = make_quotient(scale);
     const int h = tid - 32 * kColHelperWarp0;
-    for (long long g = 0; g < nseg; ++g) {
-      const long long p = base + g;
-      const int st = stage_of(p);
-      if (__any_sync(kAllLanes, aborted(sm))) break;
-      if (!__all_sync(kAllLanes, bar_wait(&sm.full[st], parity_of(p)))) {
-        if (lane == 0) fail(sm, status);
-        break;
+    F held[kPer];
+    auto load = [&](long long g) {
+#pragma unroll
+      for (int q = 0; q < kPer; ++q) {
+        const long long i = g * kSeg + h + static_cast<long long>(kColHelpers) * q;
+        held[q] = i < rows ? x[i] : F(0);
       }
-      const long long e0 = g * S::kSeg1;
-      const int len = static_cast<int>(rows - e0 < S::kSeg1 ? rows - e0 : S::kSeg1);
-      F* b = sm.raw[st] + op.sh;
-      constexpr int kPer = S::kSeg1 / kColHelpers;
+    };
+    if (nseg > 0) load(0);
+    for (long long g = 0; g < nseg; ++g) {
       F qv[kPer];
       bool unsafe = false;
 #pragma unroll
       for (int q = 0; q < kPer; ++q) {
-        const int i = h + kColHelpers * q;
-        const F a = i < len ? modulus(b[i]) : F(0);
+        const F a = modulus(held[q]);
         qv[q] = quotient_fast(quo, a);
         unsafe |= !quotient_safe(quo, a);
       }
@@ -564,40 +571,43 @@ __device__ __forceinline__ F ring_norm(ColSmem<F>& sm, Producer& pr, long long b
         // Operands outside the fast quotient's range: IEEE division for those.
 #pragma unroll
         for (int q = 0; q < kPer; ++q) {
-          const int i = h + kColHelpers * q;
-          const F a = i < len ? modulus(b[i]) : F(0);
+          const F a = modulus(held[q]);
           if (!quotient_safe(quo, a)) qv[q] = ieee_quotient(a, quo.b);
         }
       }
-#pragma unroll
-      for (int q = 0; q < kPer; ++q) {
-        const int i = h + kColHelpers * q;
-        if (i < len) b[i] = qv[q];
+      if (g + 1 < nseg) load(g + 1);
+      const int b = static_cast<int>(g % kNormBufs);
+      if (__any_sync(kAllLanes, aborted(sm))) break;
+      if (g >= kNormBufs &&
+          !__all_sync(kAllLanes, bar_wait(&sm.freed[b], static_cast<unsigned>(((g - kNormBufs) / kNormBufs) & 1)))) {
+        if (lane == 0) fail(sm, status);
+        break;
       }
-      fence_async_shared();
+      F* buf = bufs + static_cast<long long>(b) * kSeg;
+#pragma unroll
+      for (int q = 0; q < kPer; ++q) buf[h + kColHelpers * q] = qv[q];
       __syncwarp();
-      if (lane == 0) bar_arrive(&sm.ready[st]);
+      if (lane == 0) bar_arrive(&sm.ready[b]);
     }
   } else if (warp == 0) {
     F acc = F(0);
     for (long long g = 0; g < nseg; ++g) {
-      const long long p = base + g;
-      const int st = stage_of(p);
+      const int b = static_cast<int>(g % kNormBufs);
       if (__any_sync(kAllLanes, aborted(sm))) break;
-      if (!__all_sync(kAllLanes, bar_wait(&sm.ready[st], static_cast<unsigned>((g / kColStages) & 1)))) {
+      if (!__all_sync(kAllLanes, bar_wait(&sm.ready[b], static_cast<unsigned>((g / kNormBufs) & 1)))) {
         if (lane == 0) fail(sm, status);
         break;
       }
-      const F* b = sm.raw[st] + op.sh;
-      const long long e0 = g * S::kSeg1;
-      if (e0 + S::kSeg1 <= rows) {
-        acc = fold_squares<F, S::kSeg1 / 32>(b, lane, acc);
+      const F* buf = bufs + static_cast<long long>(b) * kSeg;
+      const long long e0 = g * kSeg;
+      if (e0 + kSeg <= rows) {
+        acc = fold_squares<F, kSeg / 32>(buf, lane, acc);
       } else {
         const int len = static_cast<int>(rows - e0);
-        for (int i = lane; i < len; i += 32) acc = fma_rn(b[i], b[i], acc);
+        for (int i = lane; i < len; i += 32) acc = fma_rn(buf[i], buf[i], acc);
       }
       __syncwarp();
-      if (lane == 0) bar_arrive(&sm.empty[st]);
+      if (lane == 0) bar_arrive(&sm.freed[b]);
     }
     acc = butterfly(acc, AddOp());
     if (lane == 0) sm.dot = acc;

@@ -13,8 +13,8 @@
 //  swap    flat over rows: column swap, permutation swap, the reflector's scaling of
 //          the new column `step` and its alpha, in one pass;
 //  column  one block per trailing column: ring_dot, update_direct (with the maximum of
-//          the updated rows), then the next step's ring_norm of the updated column.
-// Step 0's norms are a block per column: peak_direct, then ring_norm.
+//          the updated rows), then the next step's scaled_norm of the updated column.
+// Step 0's norms are a block per column: peak_direct, then scaled_norm.
 //
 // Q formation (column_q) applies reflector `step` of the factorized matrix to one
 // column of Q per block with ring_dot and update_direct -- apply_reflector's arithmetic.
@@ -127,8 +127,7 @@ __device__ __forceinline__ void pivot_if_last(const FusedArgs<F>& a, long long p
 // The column_norms result of rows [0, rows) of x (scale from peak_direct<true>): the
 // norm, or -1 when a modulus or the norm is not finite or the block stopped.
 template <typename F>
-__device__ __forceinline__ F engine_column_norm(ColSmem<F>& sm, Producer& pr, long long base, const F* x,
-                                                long long rows, long long* status) {
+__device__ __forceinline__ F engine_column_norm(ColSmem<F>& sm, const F* x, long long rows, long long* status) {
   F peak = F(0);
   bool flagged = false;
   peak_direct<true>(x, rows, &peak, &flagged);
@@ -136,7 +135,7 @@ __device__ __forceinline__ F engine_column_norm(ColSmem<F>& sm, Producer& pr, lo
   bool bad;
   block_peak(sm, peak, flagged, &scale, &bad);
   F total = F(0);
-  if (!bad && scale > F(0)) total = ring_norm(sm, pr, base, x, rows, scale, status);
+  if (!bad && scale > F(0)) total = scaled_norm(sm, x, rows, scale, status);
   const F norm = scale * sqrt(total);
   return (bad || nonfinite(norm) || aborted(sm)) ? F(-1) : norm;
 }
@@ -147,9 +146,7 @@ __device__ __forceinline__ void column_first(const FusedArgs<F>& a, ColSmem<F>& 
   const long long j = blockIdx.x;
   if (j >= a.n) return;
   engine_init(sm);
-  Producer pr = producer_start();
-  const F norm = engine_column_norm(sm, pr, 0, a.w + j * a.ld, a.m, a.status);
-  drain(sm, pr, a.status);
+  const F norm = engine_column_norm(sm, a.w + j * a.ld, a.m, a.status);
   if (threadIdx.x == 0) a.norms[j] = norm;
   pivot_if_last(a, 0, sm);
 }
@@ -174,7 +171,7 @@ __device__ __forceinline__ void column_step(const FusedArgs<F>& a, long long ste
   // the next step's norm of rows [step + 1, m)
   F total = F(0);
   if (next_norm && !aborted(sm) && !bad && scale > F(0))
-    total = ring_norm(sm, pr, dot_segments<F>(rows), t + 1, rows - 1, scale, a.status);
+    total = scaled_norm(sm, t + 1, rows - 1, scale, a.status);
   drain(sm, pr, a.status);
   if (next_norm) {
     const F norm = scale * sqrt(total);
@@ -207,9 +204,7 @@ template <typename F>
 __device__ __forceinline__ void engine_norms_task(const F* x, long long step, long long rows, F* out,
                                                   long long* status, ColSmem<F>& sm) {
   engine_init(sm);
-  Producer pr = producer_start();
-  const F norm = engine_column_norm(sm, pr, 0, x + step, rows - step, status);
-  drain(sm, pr, status);
+  const F norm = engine_column_norm(sm, x + step, rows - step, status);
   if (threadIdx.x == 0) *out = norm;
 }
 
@@ -219,7 +214,6 @@ template <typename F>
 __device__ __forceinline__ void engine_reflect_task(F* x, long long step, long long rows, F* coeff, long long* status,
                                                     ColSmem<F>& sm) {
   engine_init(sm);
-  Producer pr = producer_start();
   F* col = x + step;
   const long long n = rows - step;
   F peak = F(0);
@@ -229,8 +223,7 @@ __device__ __forceinline__ void engine_reflect_task(F* x, long long step, long l
   bool bad;
   block_peak(sm, peak, flagged, &scale, &bad);
   F total = F(0);
-  if (scale > F(0)) total = ring_norm(sm, pr, 0, col, n, scale, status);
-  drain(sm, pr, status);
+  if (scale > F(0)) total = scaled_norm(sm, col, n, scale, status);
   const F norm = scale * sqrt(total);
   const F x0 = col[0];
   __syncthreads();  // x0 is read by every thread before row `step` is written
