@@ -314,6 +314,9 @@ class Config:
     def after_timing(self):
         """Checks of status words after the timed steps (none by default)."""
 
+    def close(self):
+        """Releases what outlives the run (communicators); nothing by default."""
+
 
 class ReduceConfigs(Config):
     """single-axis reductions through t4a_reduce
@@ -711,11 +714,8 @@ class RrqrConfig(Config):
         noise = np.random.default_rng(12).standard_normal((m, n))
         a = torch.from_numpy(np.asfortranarray(u @ v.T + 1e-10 * noise).ravel(order="K").copy())  # column-major
         from t4a_b200 import dist as t4dist
-        # Row sharding needs the library's sharded driver; without it every rank runs the
-        # whole factorization (replicas), which the op's tag says.
-        self.sharded = self.world > 1 and hasattr(t4dist, "RrqrRowsSharded")
-        self.replicated = self.world > 1 and not self.sharded
-        r0, r1 = self.shard(m) if self.sharded else (0, m)
+        self.sharded = self.world > 1
+        r0, r1 = self.shard(m)
         self.rows = r1 - r0
         self.r0 = r0
         local = a.view(n, m)[:, r0:r1].contiguous().view(-1)  # this rank's rows, column-major
@@ -738,10 +738,13 @@ class RrqrConfig(Config):
                                       device=self.device)
         for name in ("perm", "coeff", "pivots"):
             self.host[name] = pinned(torch.empty(n, dtype=torch.float64 if name == "coeff" else torch.int64))
-        tag = "rrqr-f64-65536x256-256steps" + ("-replicated" if self.replicated else "")
-        self.ops = [dict(tag=tag, config=5, bytes=bytes_all,
-                         local_bytes=bytes_all * self.rows // m, inputs=["a"], outputs=["a", "perm", "coeff", "pivots"],
-                         launches=None, e2e_restores=True)]
+        # the factorized block comes back into its own host buffer (the input stays pristine)
+        self.host["a_out"] = pinned(torch.empty_like(local))
+        if not self.host_only:
+            self.dev["a_out"] = self.dev["a"]
+        self.ops = [dict(tag="rrqr-f64-65536x256-256steps", config=5, bytes=bytes_all,
+                         local_bytes=bytes_all * self.rows // m, inputs=["a"],
+                         outputs=["a_out", "perm", "coeff", "pivots"], launches=None, e2e_restores=True)]
         op = self.ops[0]
         op["run"] = self._run
         op["prepare"] = self._prepare
@@ -756,6 +759,10 @@ class RrqrConfig(Config):
         self.checks["rrqr_status"] = status
         if status != 0:
             raise CheckFailed(f"RRQR status {status} after the timed factorizations")
+
+    def close(self):
+        if self.sharded and not self.host_only:
+            self.driver.close()
 
     def _run(self, sh):
         t4, abi, d = self.t4, self.abi, self.dev
@@ -807,8 +814,15 @@ class RrqrConfig(Config):
             self.checks["rrqr_first_pivot_divergence"] = diverge
             if diverge < self.RANK:
                 raise CheckFailed(f"RRQR pivots differ from the single-GPU driver at step {diverge} < {self.RANK}")
-            resid = t4dist.rrqr_residual(work, d["coeff"], d["perm"], self.a_full.to(self.device), m, n)
+            wfull = work.view(n, m).t()
+            q, qst = t4.rrqr_form_q(wfull, d["coeff"][:n])
+            a_dev = self.a_full.to(self.device).view(n, m).t()
+            resid = (torch.linalg.norm(q @ torch.triu(wfull[:n, :]) - a_dev[:, d["perm"]]) /
+                     torch.linalg.norm(a_dev)).item()
+            del q, wfull, a_dev
             self.checks["rrqr_residual_rel"] = resid
+            if int(qst.item()) != 0:
+                raise CheckFailed(f"RRQR Q formation status {int(qst.item())}")
             if not resid <= 1e-8:
                 raise CheckFailed(f"RRQR residual |QR - AP| / |A| = {resid:.3e} > 1e-8")
             tdist.barrier()
@@ -999,6 +1013,9 @@ def run_ours(args, rank, world, local_rank):
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(groups, args)
+    torch.cuda.synchronize()
+    for g in groups:
+        g.close()
     return line
 
 

@@ -465,6 +465,39 @@ int t4a_rrqr(void* stream, int dtype, void* work, const t4a_cuda_layout* work_la
              long long steps, void* permutation, void* coeff, void* pivots, void* status, void* workspace,
              size_t workspace_bytes);
 
+/* ------------------------------------------------------------------------- */
+/* RRQR over GPUs (rows sharded; no counterpart in the reference, which has no */
+/* multi-device code: this is the row-sharded form of the step loop of its     */
+/* bench, examples/bench_kernels.rs:2398-2530)                                 */
+/* ------------------------------------------------------------------------- */
+
+/* NCCL communicator set-up for the sharded driver (NCCL is loaded on first use; without
+ * libnccl.so.2 these return T4A_ERR_CUDA).  t4a_dist_unique_id writes the 128-byte
+ * ncclUniqueId that rank 0 hands to every rank (by the caller's own channel);
+ * t4a_dist_comm_init is collective over the `world` ranks, each with its device
+ * current. */
+int t4a_dist_unique_id(void* id);
+int t4a_dist_comm_init(void** comm, const void* id, int world, int rank);
+int t4a_dist_comm_destroy(void* comm);
+
+/* Workspace of t4a_dist_rrqr: exchange buffers for n columns over `world` ranks. */
+int t4a_dist_rrqr_workspace_bytes(int dtype, long long n, int world, size_t* bytes);
+
+/* `steps` steps of the reference RRQR loop over a [global_rows, n] F32/F64 matrix whose
+ * rows [row0, row0 + local_rows) this rank holds as the column-major `work` (layout
+ * [local_rows, n], row stride 1); every rank of `comm` calls it with its own rows, on
+ * its own stream.  Per step: the pivot from the column norms combined in rank order,
+ * the swap and the reflector on each rank's rows, the dot parts (NCCL all-gather), the
+ * update and the next norm parts (NCCL all-gather).  perm (n), coeff (steps), pivots
+ * (steps) and status (bit 0: a non-finite norm; bit 1: a bounded wait ran out) come out
+ * the same on every rank.  With one rank the results equal t4a_rrqr bit for bit; with
+ * several the norms and dots round differently, so pivots agree where the column norms
+ * are well separated (the rank-revealing prefix).  Nothing is allocated; the caller
+ * synchronizes. */
+int t4a_dist_rrqr(void* comm, void* stream, int dtype, void* work, const t4a_cuda_layout* local_layout,
+                  long long work_len, long long row0, long long global_rows, long long steps, void* permutation,
+                  void* coeff, void* pivots, void* status, void* workspace, size_t workspace_bytes);
+
 #ifdef __cplusplus
 }
 #endif

@@ -70,6 +70,11 @@ def _declare(l):
         "t4a_oracle_identity_shifted": (I, [I, P, L, LL]),
         "t4a_oracle_prefix_rank": (I, [I, P, LP, LP, L, D, D]),
         "t4a_oracle_rrqr_f64": (LL, [P, LL, LL, LL, LP, P, D, D, I]),
+        "t4a_oracle_dist_norm_parts": (I, [P, LL, LL, LL, LL, LL, LL, P]),
+        "t4a_oracle_dist_select_swap": (I, [P, LL, LL, LL, LL, LL, P, I, LP, P, LP, LP]),
+        "t4a_oracle_dist_dot_parts": (I, [P, LL, LL, LL, LL, LL, P]),
+        "t4a_oracle_dist_update": (I, [P, LL, LL, LL, LL, LL, P, I, P]),
+        "t4a_oracle_rrqr_rows_sharded_f64": (LL, [P, LL, LL, LL, I, LP, P, LP]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(l, name)

@@ -1212,3 +1212,252 @@ long long t4a_oracle_rrqr_f64(double* work, long long m, long long n, long long 
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Row-sharded RRQR (the restatement of t4a_dist_rrqr, which has no reference
+// counterpart: the reference has no multi-device code).  A rank holds rows
+// [row0, row0 + mr) of every column, column-major with column stride ld.  Every chain
+// runs the reference's lane order over the rank's own rows (lane l visits the rows
+// first + l + 32 k of the rank's range), every plane sum is the ascending xor tree, and
+// the parts meet in rank order with separately rounded products and sums.  The four
+// functions are one rank's share of a step; t4a_oracle_rrqr_rows_sharded_f64 runs the
+// ranks of one matrix in turn, exchanging their parts as the all-gathers would.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr int kPartElems = 8;  // scale, ssq, rscale, rssq, xrow, bad, own, pad
+
+long long dist_local_from(long long s, long long row0, long long mr) {
+  const long long lo = s - row0;
+  return lo < 0 ? 0 : (lo > mr ? mr : lo);
+}
+
+// Lane chains over rows [lo, mr) of one column: max-scaled parts (flagged or not).
+void dist_scaled_parts(const double* col, long long lo, long long mr, bool flagged, double* scale_out,
+                       double* ssq_out, bool* bad_out) {
+  double lmax[kPlane], lsum[kPlane];
+  bool bad = false;
+  for (int lane = 0; lane < kPlane; ++lane) {
+    double m = 0.0;
+    for (long long r = lo + lane; r < mr; r += kPlane) {
+      const double v = magnitude(col[r]);
+      if (flagged && v - v != 0.0) {
+        bad = true;
+      } else if (v > m) {
+        m = v;
+      }
+    }
+    lmax[lane] = m;
+  }
+  const double scale = tree_max(lmax, kPlane);
+  for (int lane = 0; lane < kPlane; ++lane) {
+    double s = 0.0;
+    if (scale > 0.0 && !(flagged && bad))
+      for (long long r = lo + lane; r < mr; r += kPlane) {
+        const double q = magnitude(col[r]) / scale;
+        s = std::fma(q, q, s);
+      }
+    lsum[lane] = s;
+  }
+  *scale_out = scale;
+  *ssq_out = (flagged && bad) ? 0.0 : tree_sum(lsum, kPlane);
+  if (bad_out) *bad_out = bad;
+}
+
+double dist_combined(const double* parts, int world, long long count, long long idx, bool reflector) {
+  double scale = 0.0;
+  bool bad = false;
+  for (int r = 0; r < world; ++r) {
+    const double* p = parts + (r * count + idx) * kPartElems;
+    const double sc = reflector ? p[2] : p[0];
+    bad = bad || p[5] != 0.0;
+    scale = sc > scale ? sc : scale;
+  }
+  if (!reflector && bad) return -1.0;
+  double ssq = 0.0;
+  for (int r = 0; r < world; ++r) {
+    const double* p = parts + (r * count + idx) * kPartElems;
+    const double sc = reflector ? p[2] : p[0];
+    if (sc > 0.0) {
+      const double ratio = sc == scale ? 1.0 : sc / scale;
+      const double w = ratio * ratio;
+      const double term = w * (reflector ? p[3] : p[1]);
+      ssq = ssq + term;
+    }
+  }
+  const double norm = scale * std::sqrt(ssq);
+  return !reflector && norm - norm != 0.0 ? -1.0 : norm;
+}
+
+}  // namespace
+
+extern "C" {
+
+// Norm parts of columns first_col .. n-1 over this rank's rows at global rows >= s.
+int t4a_oracle_dist_norm_parts(const double* local, long long mr, long long n, long long ld, long long row0,
+                               long long s, long long first_col, double* parts) {
+  const long long lo = dist_local_from(s, row0, mr);
+  const bool holds = s >= row0 && s < row0 + mr;
+  for (long long j = first_col; j < n; ++j) {
+    const double* col = local + j * ld;
+    double* p = parts + (j - first_col) * kPartElems;
+    bool bad = false;
+    dist_scaled_parts(col, lo, mr, true, &p[0], &p[1], &bad);
+    if (bad) {
+      dist_scaled_parts(col, lo, mr, false, &p[2], &p[3], nullptr);
+    } else {
+      p[2] = p[0];
+      p[3] = p[1];
+    }
+    p[4] = holds ? col[s - row0] : 0.0;
+    p[5] = bad ? 1.0 : 0.0;
+    p[6] = holds ? 1.0 : 0.0;
+    p[7] = 0.0;
+  }
+  return 0;
+}
+
+// Step s's pivot, reflector scalars, column swap and scaling of this rank's rows, from
+// every rank's parts of columns s .. n-1 (world blocks of n - s parts).  perm, coeff,
+// pivots and status are this rank's replicated copies.
+int t4a_oracle_dist_select_swap(double* local, long long mr, long long n, long long ld, long long row0, long long s,
+                                const double* parts, int world, long long* perm, double* coeff, long long* pivots,
+                                long long* status) {
+  const long long count = n - s;
+  std::vector<double> norms(n, 0.0);
+  for (long long c = s; c < n; ++c) norms[c] = dist_combined(parts, world, count, c - s, false);
+  t4a_cuda_layout vec{};
+  vec.rank = 1;
+  vec.extents[0] = n;
+  vec.strides[0] = 1;
+  long long pivot = 0;
+  select_pivot_t<double>(norms.data(), perm, &pivot, status, vec, vec, s);
+  double norm = norms[pivot];
+  if (!(norm >= 0.0)) norm = dist_combined(parts, world, count, pivot - s, true);
+  double x0 = 0.0;
+  for (int r = 0; r < world; ++r) {
+    const double* p = parts + (r * count + (pivot - s)) * kPartElems;
+    if (p[6] != 0.0) x0 = p[4];
+  }
+  pivots[s] = pivot;
+  const bool scale = norm != 0.0;
+  double alpha = 0.0, divisor = 1.0;
+  if (scale) {
+    const double phase = x0 < 0.0 ? -1.0 : 1.0;
+    alpha = -phase * norm;
+    divisor = x0 - alpha;
+    coeff[s] = 1.0 + magnitude(x0) / norm;
+  } else {
+    coeff[s] = 0.0;
+  }
+  for (long long i = 0; i < mr; ++i) {
+    const long long g = row0 + i;
+    const double left = local[s * ld + i];
+    double moved = pivot == s ? left : local[pivot * ld + i];
+    if (scale) {
+      if (g == s) {
+        moved = alpha;
+      } else if (g > s) {
+        moved = moved / divisor;
+      }
+    }
+    local[s * ld + i] = moved;
+    if (pivot != s) local[pivot * ld + i] = left;
+  }
+  if (pivot != s) std::swap(perm[s], perm[pivot]);
+  return 0;
+}
+
+// Dot parts of step s: chains of v t over this rank's rows >= s (v_s = 1 on its owner),
+// for columns s+1 .. n-1.
+int t4a_oracle_dist_dot_parts(const double* local, long long mr, long long n, long long ld, long long row0,
+                              long long s, double* dots) {
+  const long long lo = dist_local_from(s, row0, mr);
+  const bool holds = s >= row0 && s < row0 + mr;
+  const double* v = local + s * ld;
+  for (long long j = s + 1; j < n; ++j) {
+    const double* t = local + j * ld;
+    double lanes[kPlane];
+    for (int lane = 0; lane < kPlane; ++lane) {
+      double acc = 0.0;
+      for (long long r = lo + lane; r < mr; r += kPlane) acc = std::fma(r == lo && holds ? 1.0 : v[r], t[r], acc);
+      lanes[lane] = acc;
+    }
+    dots[j - s - 1] = tree_sum(lanes, kPlane);
+  }
+  return 0;
+}
+
+// Update of step s on this rank's rows: d = (rank-ordered sum of every rank's dot part)
+// * coeff[s], t -= v d.
+int t4a_oracle_dist_update(double* local, long long mr, long long n, long long ld, long long row0, long long s,
+                           const double* dots, int world, const double* coeff) {
+  const long long lo = dist_local_from(s, row0, mr);
+  const bool holds = s >= row0 && s < row0 + mr;
+  const long long count = n - s - 1;
+  const double* v = local + s * ld;
+  for (long long j = s + 1; j < n; ++j) {
+    double d = dots[j - s - 1];
+    for (int r = 1; r < world; ++r) d = d + dots[r * count + (j - s - 1)];
+    d = d * coeff[s];
+    double* t = local + j * ld;
+    for (long long r = lo; r < mr; ++r) t[r] = std::fma(-(r == lo && holds ? 1.0 : v[r]), d, t[r]);
+  }
+  return 0;
+}
+
+// The whole row-sharded factorization of one column-major [m, n] matrix, its rows split
+// into `world` balanced blocks (the first m % world hold one row more), the ranks run in
+// turn.  perm (n), coeff (steps), pivots (steps) are the replicated results; returns the
+// status word (bit 0: a non-finite norm).
+long long t4a_oracle_rrqr_rows_sharded_f64(double* work, long long m, long long n, long long steps, int world,
+                                           long long* perm, double* coeff, long long* pivots) {
+  std::vector<long long> row0(world), mr(world);
+  for (int r = 0; r < world; ++r) {
+    const long long base = m / world, extra = m % world;
+    row0[r] = r * base + std::min<long long>(r, extra);
+    mr[r] = base + (r < extra ? 1 : 0);
+  }
+  // Each rank's block as its own column-major buffer.
+  std::vector<std::vector<double>> blocks(world);
+  for (int r = 0; r < world; ++r) {
+    blocks[r].resize(mr[r] * n);
+    for (long long j = 0; j < n; ++j)
+      for (long long i = 0; i < mr[r]; ++i) blocks[r][j * mr[r] + i] = work[j * m + row0[r] + i];
+  }
+  std::vector<std::vector<long long>> perms(world, std::vector<long long>(n));
+  std::vector<std::vector<double>> coeffs(world, std::vector<double>(std::max<long long>(steps, 1)));
+  std::vector<std::vector<long long>> pivs(world, std::vector<long long>(std::max<long long>(steps, 1)));
+  std::vector<long long> status(world, 0);
+  for (int r = 0; r < world; ++r)
+    for (long long c = 0; c < n; ++c) perms[r][c] = c;
+  std::vector<double> parts(world * n * kPartElems), dots(world * n);
+  for (int r = 0; r < world; ++r)
+    t4a_oracle_dist_norm_parts(blocks[r].data(), mr[r], n, mr[r], row0[r], 0, 0, parts.data() + r * n * kPartElems);
+  for (long long s = 0; s < steps; ++s) {
+    for (int r = 0; r < world; ++r)
+      t4a_oracle_dist_select_swap(blocks[r].data(), mr[r], n, mr[r], row0[r], s, parts.data(), world,
+                                  perms[r].data(), coeffs[r].data(), pivs[r].data(), &status[r]);
+    const long long count = n - s - 1;
+    if (count <= 0) continue;
+    for (int r = 0; r < world; ++r)
+      t4a_oracle_dist_dot_parts(blocks[r].data(), mr[r], n, mr[r], row0[r], s, dots.data() + r * count);
+    for (int r = 0; r < world; ++r)
+      t4a_oracle_dist_update(blocks[r].data(), mr[r], n, mr[r], row0[r], s, dots.data(), world, coeffs[r].data());
+    if (s + 1 < steps)
+      for (int r = 0; r < world; ++r)
+        t4a_oracle_dist_norm_parts(blocks[r].data(), mr[r], n, mr[r], row0[r], s + 1, s + 1,
+                                   parts.data() + r * count * kPartElems);
+  }
+  for (int r = 0; r < world; ++r)
+    for (long long j = 0; j < n; ++j)
+      for (long long i = 0; i < mr[r]; ++i) work[j * m + row0[r] + i] = blocks[r][j * mr[r] + i];
+  for (long long c = 0; c < n; ++c) perm[c] = perms[0][c];
+  for (long long s = 0; s < steps; ++s) {
+    coeff[s] = coeffs[0][s];
+    pivots[s] = pivs[0][s];
+  }
+  return status[0];
+}
+
+}  // extern "C"

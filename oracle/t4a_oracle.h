@@ -115,6 +115,22 @@ long long t4a_oracle_rrqr_f64(double* work, long long m, long long n, long long 
                               long long* perm, double* coeff, double rtol, double atol,
                               int threads);
 
+/* Row-sharded RRQR, one rank's share of a step (the restatement of t4a_dist_rrqr): a rank
+ * holds rows [row0, row0 + mr) of every column, column-major with column stride ld.
+ * Parts are 8 doubles per column (scale, ssq, rscale, rssq, xrow, bad, own, pad). */
+int t4a_oracle_dist_norm_parts(const double* local, long long mr, long long n, long long ld, long long row0,
+                               long long s, long long first_col, double* parts);
+int t4a_oracle_dist_select_swap(double* local, long long mr, long long n, long long ld, long long row0, long long s,
+                                const double* parts, int world, long long* perm, double* coeff, long long* pivots,
+                                long long* status);
+int t4a_oracle_dist_dot_parts(const double* local, long long mr, long long n, long long ld, long long row0,
+                              long long s, double* dots);
+int t4a_oracle_dist_update(double* local, long long mr, long long n, long long ld, long long row0, long long s,
+                           const double* dots, int world, const double* coeff);
+/* The ranks of one [m, n] matrix run in turn; returns the status word. */
+long long t4a_oracle_rrqr_rows_sharded_f64(double* work, long long m, long long n, long long steps, int world,
+                                           long long* perm, double* coeff, long long* pivots);
+
 #ifdef __cplusplus
 }
 #endif

@@ -94,7 +94,7 @@ def build(jobs=8, force=False):
         [f.result() for f in cubin_futures]
     lib = os.path.join(LIBDIR, "libt4a_b200.so")
     if force or stale(lib, objs):
-        run([NVCC, "-shared"] + ARCH + ["-o", lib] + objs + ["-lcudart"])
+        run([NVCC, "-shared"] + ARCH + ["-o", lib] + objs + ["-lcudart", "-ldl"])
     return lib
 
 

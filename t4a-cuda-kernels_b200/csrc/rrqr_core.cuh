@@ -156,12 +156,22 @@ __device__ __forceinline__ void lane_chain(Strip<const T> s, long long first, lo
 // elements would otherwise hold 64 registers per lane).
 template <typename T> struct ChainDepth { static constexpr int value = Scalar<T>::kComplex ? 8 : 16; };
 
+// The two halves of a max-scaled norm before they meet: the scale and the butterfly sum
+// of the chain of (|x| / scale)^2 (the norm is scale * sqrt(ssq)).
+template <typename R>
+struct ScaledSum {
+  R scale;
+  R ssq;
+};
+
 // The reference's max-scaled 2-norm of rows [first, rows): scale = the largest finite
 // modulus, then scale * sqrt(sum over the chain of (|x| / scale)^2).  With kFlag, a
 // non-finite modulus is excluded from the scale and reported in *flagged (any lane);
-// without it every modulus competes for the scale, as in the reflector.
+// without it every modulus competes for the scale, as in the reflector.  chain_parts
+// returns the scale and the summed chain, chain_norm the norm.
 template <bool kFlag, int kDepth, typename T>
-__device__ __forceinline__ RealOf<T> chain_norm(Strip<const T> s, long long first, long long rows, bool* flagged) {
+__device__ __forceinline__ ScaledSum<RealOf<T>> chain_parts(Strip<const T> s, long long first, long long rows,
+                                                           bool* flagged) {
   using R = RealOf<T>;
   const int lane = lane_id();
   R peak = R(0);
@@ -183,7 +193,13 @@ __device__ __forceinline__ RealOf<T> chain_norm(Strip<const T> s, long long firs
     });
   }
   if (kFlag) *flagged = __any_sync(kAllLanes, seen);
-  return scale * sqrt(butterfly(ssq, AddOp()));
+  return ScaledSum<R>{scale, butterfly(ssq, AddOp())};
+}
+
+template <bool kFlag, int kDepth, typename T>
+__device__ __forceinline__ RealOf<T> chain_norm(Strip<const T> s, long long first, long long rows, bool* flagged) {
+  const ScaledSum<RealOf<T>> p = chain_parts<kFlag, kDepth>(s, first, rows, flagged);
+  return p.scale * sqrt(p.ssq);
 }
 
 // ---- column_norms ------------------------------------------------------------------

@@ -270,15 +270,17 @@ __device__ __forceinline__ F fold_squares(const F* b, int lane, F acc) {
   return acc;
 }
 
-// <v, t> * coeff over rows [0, rows), v_0 = 1, at ring positions [base, base + nseg)
-// (nseg = dot_segments(rows)); the result goes to every thread (0 in a stopped block).
+// <v, t> * coeff over rows [0, rows), v_0 = 1 (or v_0 as stored when !lead_one: a row
+// block that does not hold the reflector's leading row), at ring positions [base, base +
+// nseg) (nseg = dot_segments(rows)); the result goes to every thread (0 in a stopped
+// block).
 template <typename F>
 __device__ __forceinline__ long long dot_segments(long long rows) {
   return (rows + ColSmem<F>::kSeg2 - 1) / ColSmem<F>::kSeg2;
 }
 template <typename F>
 __device__ __forceinline__ F ring_dot(ColSmem<F>& sm, Producer& pr, long long base, const F* v, const F* t,
-                                      long long rows, F coeff, long long* status) {
+                                      long long rows, F coeff, long long* status, bool lead_one = true) {
   using S = ColSmem<F>;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long nseg = dot_segments<F>(rows);
@@ -300,7 +302,7 @@ __device__ __forceinline__ F ring_dot(ColSmem<F>& sm, Producer& pr, long long ba
       const long long e0 = g * S::kSeg2;
       if (g == 0) {
         const int len = static_cast<int>(rows < S::kSeg2 ? rows : S::kSeg2);
-        for (int i = lane; i < len; i += 32) acc = fma_rn(i == 0 ? F(1) : bv[i], bt[i], acc);
+        for (int i = lane; i < len; i += 32) acc = fma_rn(i == 0 && lead_one ? F(1) : bv[i], bt[i], acc);
       } else if (e0 + S::kSeg2 <= rows) {
         acc = fold_products<F, S::kSeg2 / 32>(bv, bt, lane, acc);
       } else {
@@ -359,13 +361,16 @@ __device__ __forceinline__ Split16<F> split16(const F* x, long long rows) {
   return s;
 }
 
-// t = fma(-v, d, t) over rows [0, rows) (v_0 = 1), by every thread of the block, with
+// t = fma(-v, d, t) over rows [0, rows) (v_0 = 1 unless !lead_one), by every thread, with
 // 16-byte loads and stores where v and t share their alignment.  The 16-byte groups are
 // taken from the last one down, so the lowest rows, which a following ring phase reads
 // first, are the most recently written.  kTrack: the largest finite modulus and the
-// non-finite flag of the updated rows [1, rows) go to *peak / *flagged.
+// non-finite flag of the updated rows other than the implicit-one row go to *peak /
+// *flagged.
 template <bool kTrack, typename F>
-__device__ __forceinline__ void update_direct(const F* v, F* t, long long rows, F d, F* peak, bool* flagged) {
+__device__ __forceinline__ void update_direct(const F* v, F* t, long long rows, F d, F* peak, bool* flagged,
+                                              bool lead_one = true) {
+  const long long one = lead_one ? 0 : -1;  // the row whose v is the implicit 1 (none: -1)
   using V = typename Vec16<F>::V;
   constexpr int kW = Vec16<F>::kW;
   const long long tid = threadIdx.x;
@@ -378,9 +383,9 @@ __device__ __forceinline__ void update_direct(const F* v, F* t, long long rows, 
   const long long edge = sp.lead + (rows - sp.tail0);
   for (long long i = tid; i < edge; i += kColThreads) {
     const long long r = i < sp.lead ? i : sp.tail0 + (i - sp.lead);
-    const F nt = fma_rn(-(r == 0 ? F(1) : v[r]), d, t[r]);
+    const F nt = fma_rn(-(r == one ? F(1) : v[r]), d, t[r]);
     t[r] = nt;
-    if (kTrack && r != 0) track(nt, peak, flagged);
+    if (kTrack && r != one) track(nt, peak, flagged);
   }
   const V* vv = reinterpret_cast<const V*>(v + sp.lead);
   V* tv = reinterpret_cast<V*>(t + sp.lead);
@@ -402,9 +407,9 @@ __device__ __forceinline__ void update_direct(const F* v, F* t, long long rows, 
 #pragma unroll
       for (int e = 0; e < kW; ++e) {
         const long long r = sp.lead + q * kW + e;
-        const F nt = fma_rn(-(r == 0 ? F(1) : elem<F>(xv[u], e)), d, elem<F>(xt[u], e));
+        const F nt = fma_rn(-(r == one ? F(1) : elem<F>(xv[u], e)), d, elem<F>(xt[u], e));
         elem<F>(xt[u], e) = nt;
-        if (kTrack && r != 0) track(nt, peak, flagged);
+        if (kTrack && r != one) track(nt, peak, flagged);
       }
       tv[q] = xt[u];
     }
@@ -488,8 +493,8 @@ struct ScaledQuotient {
   bool fast;
 };
 
-__device__ __noinline__ double ieee_quotient(double a, double b) { return a / b; }
-__device__ __noinline__ float ieee_quotient(float a, float b) { return a / b; }
+static __device__ __noinline__ double ieee_quotient(double a, double b) { return a / b; }
+static __device__ __noinline__ float ieee_quotient(float a, float b) { return a / b; }
 
 __device__ __forceinline__ ScaledQuotient<double> make_quotient(double b) {
   ScaledQuotient<double> q;

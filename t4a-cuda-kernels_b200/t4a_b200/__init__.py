@@ -123,6 +123,11 @@ def _declare(l):
         "t4a_launch_prefix_rank": (I, [ctypes.POINTER(Launch), P, P, P, P, I, LB, ctypes.c_double, ctypes.c_double]),
         "t4a_rrqr_workspace_bytes": (I, [I, LP, ctypes.POINTER(SZ)]),
         "t4a_rrqr_primitive_faults": (I, [ctypes.POINTER(ctypes.c_ulonglong)]),
+        "t4a_dist_unique_id": (I, [P]),
+        "t4a_dist_comm_init": (I, [ctypes.POINTER(P), P, I, I]),
+        "t4a_dist_comm_destroy": (I, [P]),
+        "t4a_dist_rrqr_workspace_bytes": (I, [I, LL, I, ctypes.POINTER(SZ)]),
+        "t4a_dist_rrqr": (I, [P, P, I, P, LP, LL, LL, LL, LL, P, P, P, P, P, SZ]),
         "t4a_rrqr": (I, [P, I, P, LP, LL, LL, P, P, P, P, P, SZ]),
         "t4a_rrqr_form_q": (I, [P, I, P, LP, LL, P, LP, LL, P, LP, LL, P]),
         "t4a_plan_identity_shifted": (I, [I, LP, LL, LL, ctypes.POINTER(Launch)]),

@@ -17,7 +17,7 @@ the work and, where the path has an exchange step, runs it:
   The floating sums over colliding rows are order-dependent, as in the single-GPU
   operation (atomics).
 * RRQR: rows are sharded; every step exchanges the column norms and the reflector
-  dots (`rrqr_rows_sharded`, NCCL inside the library's C++ driver).
+  dots (`RrqrRowsSharded`: NCCL inside the library's C++ driver, t4a_dist_rrqr).
 """
 import ctypes
 
@@ -133,3 +133,85 @@ def scatter_add_rows_sharded(partial, indices, updates, group=None, workspace=No
 
 def _ptr(t):
     return ctypes.c_void_p(t.data_ptr())
+
+
+# ---- RRQR over row blocks ---------------------------------------------------------
+
+class NcclComm:
+    """This library's NCCL communicator over the ranks of a torch.distributed group: rank
+    0's unique id reaches the others through the group (a one-off broadcast), then every
+    rank joins.  Without an initialized process group it is a world of one."""
+
+    def __init__(self, group=None):
+        lib = _t4.lib()
+        if dist.is_available() and dist.is_initialized():
+            world, rank = _world(group)
+        else:
+            world, rank = 1, 0
+        ident = torch.zeros(128, dtype=torch.uint8)
+        if rank == 0:
+            _t4.check(lib.t4a_dist_unique_id(_ptr(ident)), "dist_unique_id")
+        if world > 1:
+            carrier = ident.cuda() if dist.get_backend(group) == "nccl" else ident
+            dist.broadcast(carrier, src=dist.get_global_rank(group, 0) if group is not None else 0, group=group)
+            ident = carrier.cpu()
+        handle = ctypes.c_void_p()
+        _t4.check(lib.t4a_dist_comm_init(ctypes.byref(handle), _ptr(ident), world, rank), "dist_comm_init")
+        self.handle, self.world, self.rank = handle, world, rank
+
+    def close(self):
+        if self.handle is not None and self.handle.value:
+            _t4.check(_t4.lib().t4a_dist_comm_destroy(self.handle), "dist_comm_destroy")
+        self.handle = None
+
+
+class RrqrRowsSharded:
+    """RRQR of a [m, n] F32/F64 matrix whose rows are split across the ranks of `comm`:
+    this rank holds rows [row0, row0 + local_rows) as the column-major block `work`
+    (a flat CUDA tensor of local_rows * n elements, or a 2-D tensor whose transpose is
+    contiguous).  run() does `steps` steps of the reference loop with two NCCL
+    all-gathers per step (t4a_dist_rrqr); perm, coeff, pivots and status come out
+    identical on every rank, and a world of one gives t4a_rrqr's bits."""
+
+    def __init__(self, work, m, n, row0, steps, comm=None, group=None):
+        flat = work.reshape(-1) if work.dim() == 1 else work.t().reshape(-1)
+        self.work = flat
+        self.m, self.n, self.row0, self.steps = m, n, row0, steps
+        self.rows = flat.numel() // n if n else 0
+        self.dtype = _t4.torch_dtype_tag(flat)
+        self.comm = comm if comm is not None else NcclComm(group)
+        self.own_comm = comm is None
+        self.layout = _abi.layout([self.rows, n], [1, max(self.rows, 1)])
+        nbytes = ctypes.c_size_t(0)
+        _t4.check(_t4.lib().t4a_dist_rrqr_workspace_bytes(self.dtype, n, self.comm.world, ctypes.byref(nbytes)),
+                  "dist_rrqr_workspace_bytes")
+        self.workspace = torch.empty(max(nbytes.value, 16), dtype=torch.uint8, device=flat.device)
+        trailing_steps = sum(1 for s in range(steps) if n - s - 1 > 0)
+        self.launches = 2 + steps + 2 * trailing_steps  # kernels; NCCL calls: 1 + 2 per step with trailing columns
+
+    def run(self, stream_handle, perm, coeff, pivots, status):
+        _t4.check(_t4.lib().t4a_dist_rrqr(self.comm.handle, stream_handle, self.dtype, _ptr(self.work),
+                                          ctypes.byref(self.layout), self.work.numel(), self.row0, self.m, self.steps,
+                                          _ptr(perm), _ptr(coeff), _ptr(pivots), _ptr(status),
+                                          _ptr(self.workspace), self.workspace.numel()), "dist_rrqr")
+
+    def close(self):
+        if self.own_comm:
+            self.comm.close()
+
+
+def gather_rows_colmajor(local, m, n, row0, group=None):
+    """The whole [m, n] column-major matrix (flat, m * n elements) on every rank, from each
+    rank's row block (flat column-major, rows shard_range(m) of this rank)."""
+    world, rank = _world(group)
+    sizes = [shard_range(m, world, r) for r in range(world)]
+    most = max(b - a for a, b in sizes)
+    rows = local.numel() // n
+    block = torch.zeros((n, most), dtype=local.dtype, device=local.device)
+    block[:, :rows] = local.view(n, rows)
+    parts = [torch.empty_like(block) for _ in range(world)]
+    dist.all_gather(parts, block, group=group)
+    full = torch.empty((n, m), dtype=local.dtype, device=local.device)
+    for (a, b), part in zip(sizes, parts):
+        full[:, a:b] = part[:, :b - a]
+    return full.reshape(-1)
