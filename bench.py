@@ -29,8 +29,9 @@ cold figure beside the steady one.
 At `--gpus N` (torchrun, one rank per GPU) every op is sharded (strong scaling: the
 global problem stays the same):
   reductions  slabs of a non-reduced axis, one per rank, resident on that rank;
-  movement    destination slabs along its slowest axis, each written from the strided
-              view of the (replicated) source that feeds it;
+  movement    destination parts along the axis slowest in both destination and source
+              (so both sides stream long runs), each written from the strided view of
+              the (replicated) source that feeds it;
   gather      index batches, table replicated;
   scatter_add update batches into per-rank partial destinations, then an NCCL
               reduce-scatter of the partials inside the timed op;
@@ -454,8 +455,9 @@ class ReduceConfigs(Config):
 class MovementConfig(Config):
     """permutations and a reversal through the strided-copy entry.
 
-    Sharding: the destination is split along its slowest axis; every rank writes its
-    contiguous slab from the matching strided view of the source (replicated)."""
+    Sharding: the destination is split along the axis that is slowest in both it and the
+    source view (t4a_b200.dist.movement_shard_axis); every rank writes its part, stored
+    compactly, from the matching strided view of the source (replicated)."""
 
     name = "movement"
 
@@ -482,7 +484,7 @@ class MovementConfig(Config):
         ]
         for i, (tag, dt, src, full_l, es) in enumerate(specs):
             n_full = full_l.count()
-            src_l, dst_l, start = t4dist.movement_slab(full_l, self.world, self.rank)
+            src_l, dst_l, axis, start = t4dist.movement_slab(full_l, self.world, self.rank)
             n_local = dst_l.count()
             name, out = f"src{i}", f"dst{i}"
             self.keep(name, src)
@@ -493,9 +495,12 @@ class MovementConfig(Config):
                 whole = torch.empty_like(self.dev[name])
                 self.t4.copy_strided_raw(self.t4.stream_handle(), dt, vp(whole), abi.layout(full_l.extents_list()),
                                          n_full, vp(self.dev[name]), full_l, flat_len)
-                per_row = n_full // full_l.extents[full_l.rank - 1]
-                lo = start * per_row * es // src.element_size()
-                self.expect[out] = whole[lo:lo + n_local * es // src.element_size()].clone()
+                # the same part of the whole destination (t4a axis `axis` = NumPy axis rank-1-axis)
+                np_shape = list(reversed(full_l.extents_list()))
+                per = es // src.element_size()
+                view = whole.view(np_shape + ([per] if per > 1 else []))
+                part = view.narrow(full_l.rank - 1 - axis, start, dst_l.extents[axis]).contiguous()
+                self.expect[out] = part.view(-1)
             self.host[out] = pinned(torch.empty(n_local * es // src.element_size(), dtype=src.dtype))
             self.ops.append(dict(tag=tag, config=2, bytes=2 * n_full * es, local_bytes=2 * n_local * es, launches=1,
                                  inputs=[name], outputs=[out], dtype=dt, src_l=src_l, dst_l=dst_l, n=n_local,

@@ -6,9 +6,10 @@ the work and, where the path has an exchange step, runs it:
 * reductions: a non-reduced axis is sharded into slabs; every rank reduces the slab it
   holds (any strides: a compact local slab, or a view of a full tensor cut by
   `shard_view` without a copy) into its own outputs.  No collective.
-* movement / permutation: the destination is sharded along its slowest axis; every
-  rank writes its contiguous output slab from the matching strided view of the source
-  (`movement_slab`).  No collective.
+* movement / permutation: the destination is sharded along the axis that is slowest in
+  both it and the source view (`movement_shard_axis`); every rank writes its part,
+  stored compactly, from the matching strided view of the source (`movement_slab`).
+  No collective.
 * gather: index batches are sharded and the table is replicated; every rank gathers
   its own output rows.  No collective.
 * scatter_add: update batches are sharded.  Every rank adds its updates into a
@@ -64,27 +65,46 @@ def reduce_sharded(x_local, numpy_axis, op, out=None, workspace=None, stream=Non
     return _t4.reduce(x_local, numpy_axis, op, out=out, workspace=workspace, stream=stream)
 
 
-def movement_slab(src_layout, world, rank):
-    """Rank `rank`'s part of a movement whose destination is sharded along its slowest
-    axis (reference axis rank-1 of a t4a layout, NumPy axis 0).  `src_layout` is the
-    source view that the whole destination is materialized from (strides may be
-    negative).  Returns (source slab layout, compact destination slab layout, slab
-    start): the source slab is the same view restricted to destination rows
-    [start, stop) of that axis; the destination slab is the rank's contiguous part of
-    the compact destination."""
+def movement_shard_axis(src_layout):
+    """The destination axis (a t4a layout axis: 0 fastest) to shard a movement along: the
+    one whose stride is largest in both the compact destination and the source view
+    (the largest min(|source stride|, destination stride)), so that every rank reads and
+    writes runs as long as the permutation allows; ties go to the slower destination
+    axis."""
+    strides = src_layout.strides_list()
+    ext = src_layout.extents_list()
+    best, best_key = src_layout.rank - 1, None
+    dst_stride = 1
+    for ax in range(src_layout.rank):
+        key = (min(abs(strides[ax]), dst_stride), ax)
+        if ext[ax] > 1 and (best_key is None or key > best_key):
+            best, best_key = ax, key
+        dst_stride *= ext[ax]
+    return best
+
+
+def movement_slab(src_layout, world, rank, axis=None):
+    """Rank `rank`'s part of a movement whose destination is sharded along one of its
+    axes (default movement_shard_axis).  `src_layout` is the source view that the whole
+    destination is materialized from (strides may be negative).  Returns (source layout
+    of the part, compact destination layout of the part, axis, start): the source part is
+    the same view with that axis restricted to [start, stop); the destination part is
+    stored compactly by the rank."""
     r = src_layout.rank
+    axis = movement_shard_axis(src_layout) if axis is None else axis
     ext = src_layout.extents_list()
     strides = src_layout.strides_list()
-    start, stop = shard_range(ext[r - 1], world, rank)
-    slab_ext = ext[:r - 1] + [stop - start]
-    src = _abi.layout(slab_ext, strides, src_layout.offset + start * strides[r - 1])
-    return src, _abi.layout(slab_ext), start
+    start, stop = shard_range(ext[axis], world, rank)
+    part_ext = list(ext)
+    part_ext[axis] = stop - start
+    src = _abi.layout(part_ext, strides, src_layout.offset + start * strides[axis])
+    return src, _abi.layout(part_ext), axis, start
 
 
-def materialize_slab(stream_handle, dtype, dst_ptr, src_ptr, src_layout, src_len, world, rank):
-    """Writes rank `rank`'s destination slab (movement_slab) from the source at
-    `src_ptr` through the strided-copy entry.  Returns the destination slab layout."""
-    src, dst, _ = movement_slab(src_layout, world, rank)
+def materialize_slab(stream_handle, dtype, dst_ptr, src_ptr, src_layout, src_len, world, rank, axis=None):
+    """Writes rank `rank`'s destination part (movement_slab) from the source at
+    `src_ptr` through the strided-copy entry.  Returns the destination part's layout."""
+    src, dst, _, _ = movement_slab(src_layout, world, rank, axis)
     n = dst.count()
     _t4.copy_strided_raw(stream_handle, dtype, dst_ptr, dst, n, src_ptr, src, src_len)
     return dst

@@ -76,11 +76,12 @@ def test_scatter_add_sharded_exchange_gloo():
 
 
 @pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
-def test_movement_slabs_tile_the_destination(world):
-    """The destination slabs of every rank (movement_slab: the slowest destination axis
-    split, each slab read through the strided source view) put together equal the whole
-    materialization, for a permutation and for a reversed axis (negative stride), as
-    computed by the CPU oracle."""
+def test_movement_parts_tile_the_destination(world):
+    """The destination parts of every rank (movement_slab: the destination split along
+    movement_shard_axis, each part read through the strided source view and stored
+    compactly) put together along that axis equal the whole materialization, for a
+    permutation and for a reversed axis (negative stride), as computed by the CPU
+    oracle."""
     import ctypes
     import numpy as np
     import oracle
@@ -97,15 +98,40 @@ def test_movement_slabs_tile_the_destination(world):
         assert oracle.lib().t4a_oracle_strided_to_strided(abi.F32, oracle.ptr(whole), oracle.ptr(x),
                                                           ctypes.byref(full_l),
                                                           ctypes.byref(abi.layout(full_l.extents_list())), 1) == 0
-        parts = []
+        np_shape = list(reversed(full_l.extents_list()))
+        parts, axis0 = [], None
         for rank in range(world):
-            src_l, dst_l, start = t4dist.movement_slab(full_l, world, rank)
-            assert start == t4dist.shard_range(full_l.extents[full_l.rank - 1], world, rank)[0]
+            src_l, dst_l, axis, start = t4dist.movement_slab(full_l, world, rank)
+            axis0 = axis if axis0 is None else axis0
+            assert axis == axis0 == t4dist.movement_shard_axis(full_l)
+            assert start == t4dist.shard_range(full_l.extents[axis], world, rank)[0]
             part = np.zeros(dst_l.count(), np.float32)
             assert oracle.lib().t4a_oracle_strided_to_strided(abi.F32, oracle.ptr(part), oracle.ptr(x),
                                                               ctypes.byref(src_l), ctypes.byref(dst_l), 1) == 0
-            parts.append(part)
-        assert np.array_equal(np.concatenate(parts), whole)
+            parts.append(part.reshape(list(reversed(dst_l.extents_list()))))
+        np_axis = full_l.rank - 1 - axis0
+        assert np.array_equal(np.concatenate(parts, axis=np_axis), whole.reshape(np_shape))
+
+
+def test_movement_shard_axis_keeps_long_runs():
+    """For the BASELINE config-2 permutations the shard axis is slow in both the source
+    view and the destination (runs of 64^2 F32 / 16^4 C64 elements), and for the
+    reversal it is the destination's slowest axis."""
+    from t4a_b200 import abi
+
+    def perm_layout(shape, perm):
+        st, s = [], 1
+        for e in reversed(shape):
+            st.insert(0, s)
+            s *= e
+        return abi.numpy_layout([shape[p] for p in perm], [st[p] for p in perm])
+
+    f32 = perm_layout([64] * 4, (3, 1, 0, 2))
+    c64 = perm_layout([16] * 6, (5, 0, 4, 1, 3, 2))
+    rev = abi.numpy_layout([64] * 4, [64 ** 3, 64 ** 2, -64, 1], 63 * 64)
+    assert t4dist.movement_shard_axis(f32) == 2      # NumPy axis 1 of the destination
+    assert t4dist.movement_shard_axis(c64) == 4      # NumPy axis 1 of the destination
+    assert t4dist.movement_shard_axis(rev) == 3      # NumPy axis 0
 
 
 def test_shard_view_is_a_view():

@@ -79,12 +79,13 @@ def worker(rank, world, port):
         view = src.permute(3, 1, 0, 2)
         full_l = t4.tensor_layout(view)
         want = view.contiguous()
-        dst_l = t4dist.movement_slab(full_l, world, rank)[1]
+        _, dst_l, axis, start = t4dist.movement_slab(full_l, world, rank)
         out = torch.empty(dst_l.count(), dtype=torch.float32, device=dev)
         t4dist.materialize_slab(t4.stream_handle(), abi.F32, ctypes.c_void_p(out.data_ptr()),
                                 ctypes.c_void_p(src.data_ptr()), full_l, src.numel(), world, rank)
-        m0, m1 = t4dist.shard_range(view.shape[0], world, rank)
-        assert torch.equal(out.view(m1 - m0, *view.shape[1:]), want[m0:m1])
+        np_axis = full_l.rank - 1 - axis
+        part = want.narrow(np_axis, start, dst_l.extents[axis])
+        assert torch.equal(out.view(part.shape), part.contiguous())
         torch.cuda.synchronize()
     finally:
         dist.destroy_process_group()
