@@ -198,7 +198,7 @@ void prefer_warp_rows(int dtype, const void* in, int* path, dim3* grid, dim3* bl
 // walking many units, so that its copy ring runs ahead across unit boundaries; smaller
 // passes keep one tile per block.  The staged kernel needs every plane lane to own a
 // row: chunks of at least 32 rows.
-constexpr unsigned kStagedMinTiles = 4;
+constexpr unsigned kStagedMinTiles = 1;
 void prefer_strided_staged(int dtype, int* path, dim3* grid, unsigned* smem, const PassArgs& a) {
   if (*path != kPathStrided || strided_vec_lanes(dtype) == 1) return;
   const long long shortest = a.splits > 1 ? a.chunk : a.in_l.extents[a.axis];
