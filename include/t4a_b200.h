@@ -158,8 +158,9 @@ int t4a_reduce(void* stream, int dtype, int op, void* out, const t4a_cuda_layout
  * T4A_REDUCE_NOALLOC_SCRATCH_BYTES that the library's module holds on every GPU that
  * loads it.  Allocates nothing.  Returns T4A_ERR_WORKSPACE when the partials would
  * not fit that array.  The first call on a device looks the array up (make it before
- * any stream capture); all calls on a device share the array, so calls that may
- * overlap on the GPU race on it. */
+ * any stream capture) and caches its address for the life of the process: after a
+ * cudaDeviceReset of a device, do not call it on that device again.  All calls on a
+ * device share the array, so calls that may overlap on the GPU race on it. */
 int t4a_reduce_noalloc(void* stream, int dtype, int op, void* out, const t4a_cuda_layout* out_layout,
                        long long out_len, const void* in, const t4a_cuda_layout* in_layout, long long in_len,
                        unsigned axis, unsigned plane_width);

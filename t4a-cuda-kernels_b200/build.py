@@ -3,9 +3,10 @@
     python t4a-cuda-kernels_b200/build.py [--jobs N] [--force]
 
 Objects go to <repo>/_build/; the library and the modules to
-t4a-cuda-kernels_b200/t4a_b200/lib/.  The modules are one cubin per kernel family
+t4a-cuda-kernels_b200/t4a_b200/lib/.  The modules are one image per kernel family
 (reduce, movement, gather_scatter, rrqr, linalg_aux), like the reference's per-file modules,
-exporting the reference's `extern "C" __global__` symbols.  A source is rebuilt when it, or any header
+exporting the reference's `extern "C" __global__` symbols, each in three forms: .cubin
+(sm_100a), .fatbin (sm_100a plus compute_100a PTX) and .ptx (compute_100a, for JIT).  A source is rebuilt when it, or any header
 of csrc/ or include/, is newer than its object.
 """
 import argparse
@@ -73,12 +74,44 @@ def compile_one(src, force):
 
 
 def module_one(src, force):
+    """One kernel family as three module images with the same exported symbols:
+    <family>.cubin (sm_100a SASS), <family>.fatbin (sm_100a SASS plus compute_100a PTX,
+    which the driver JIT-compiles where the SASS does not run) and <family>.ptx
+    (compute_100a PTX alone, for callers that load text and JIT it themselves)."""
     name = os.path.basename(src)
-    cubin = os.path.join(LIBDIR, name.replace("_abi.cu", ".cubin"))
-    if force or stale(cubin, [src] + headers(src)):
-        run([NVCC, "-std=c++17", "-O3", "-lineinfo", "-I", os.path.join(ROOT, "include"), "-cubin",
-             "-gencode", "arch=compute_100a,code=sm_100a", src, "-o", cubin])
-    return cubin
+    stem = os.path.join(LIBDIR, name.replace("_abi.cu", ""))
+    base = [NVCC, "-std=c++17", "-O3", "-lineinfo", "-I", os.path.join(ROOT, "include")]
+    deps = [src] + headers(src)
+    if force or stale(stem + ".cubin", deps):
+        run(base + ["-cubin", "-gencode", "arch=compute_100a,code=sm_100a", src, "-o", stem + ".cubin"])
+    if force or stale(stem + ".fatbin", deps):
+        run(base + ["-fatbin", "-gencode", "arch=compute_100a,code=[sm_100a,compute_100a]", src, "-o",
+                    stem + ".fatbin"])
+    if force or stale(stem + ".ptx", deps):
+        run(base + ["-ptx", "-arch=compute_100a", src, "-o", stem + ".ptx"])
+    return stem + ".cubin"
+
+
+# A test build of the kernels that stage data with bulk copies (RRQR, scatter_add), with
+# every staged-data wait limited to zero rounds: the GPU tests drive it to check that a
+# wait that runs out sets the status word and leaves nothing in flight.
+WAITZERO_TUS = ["rrqr_fast.cu", "gather_scatter_fast.cu", "runtime.cu"]
+
+
+def build_waitzero(force=False):
+    out_dir = os.path.join(BUILD, "waitzero")
+    os.makedirs(out_dir, exist_ok=True)
+    objs = []
+    for name in WAITZERO_TUS:
+        src = os.path.join(CSRC, name)
+        obj = os.path.join(out_dir, name + ".o")
+        if force or stale(obj, [src] + headers(src)):
+            run([NVCC] + COMMON + ARCH + ["-DT4A_STAGE_WAIT_LIMIT=0", "-c", src, "-o", obj])
+        objs.append(obj)
+    lib = os.path.join(LIBDIR, "libt4a_waitzero.so")
+    if force or stale(lib, objs):
+        run([NVCC, "-shared"] + ARCH + ["-o", lib] + objs + ["-lcudart"])
+    return lib
 
 
 def build(jobs=8, force=False):
@@ -95,6 +128,7 @@ def build(jobs=8, force=False):
     lib = os.path.join(LIBDIR, "libt4a_b200.so")
     if force or stale(lib, objs):
         run([NVCC, "-shared"] + ARCH + ["-o", lib] + objs + ["-lcudart", "-ldl"])
+    build_waitzero(force)
     return lib
 
 

@@ -764,7 +764,14 @@ __device__ __forceinline__ void scatter_fold_pass(const GroupedPiece* __restrict
 // first.  Per piece the warp executes a few dozen instructions, whatever its size.
 constexpr int kBulkRingBytes = 8192;  // per warp
 constexpr int kBulkMaxSlots = 16;
-constexpr unsigned kBulkWaitLimit = 1u << 20;  // try_wait rounds before giving up
+// try_wait rounds of a staged-data wait before it gives up (a build may lower it: the
+// tests build the library once with 0, so that every such wait runs out at once).
+#ifndef T4A_STAGE_WAIT_LIMIT
+#define T4A_STAGE_WAIT_LIMIT (1u << 20)
+#endif
+constexpr unsigned kBulkWaitLimit = T4A_STAGE_WAIT_LIMIT;
+// Rounds of the drain of loads still in flight when a warp stops: never lowered.
+constexpr unsigned kBulkDrainLimit = 1u << 22;
 
 __host__ __device__ __forceinline__ int bulk_stage_bytes_per_warp() { return kBulkRingBytes + kBulkMaxSlots * 8; }
 
@@ -776,8 +783,8 @@ __device__ __forceinline__ unsigned smem_addr(const void* p) {
 // try may suspend the thread for up to kBulkSuspendNs while the phase is pending,
 // so a waiting warp does not spin on the issue slots.
 constexpr unsigned kBulkSuspendNs = 2000;
-__device__ __forceinline__ bool bar_wait(unsigned bar, unsigned parity) {
-  for (unsigned it = 0; it < kBulkWaitLimit; ++it) {
+__device__ __forceinline__ bool bar_wait(unsigned bar, unsigned parity, unsigned limit = kBulkWaitLimit) {
+  for (unsigned it = 0; it < limit; ++it) {
     unsigned ok;
     asm volatile(
         "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
@@ -923,7 +930,7 @@ __device__ __forceinline__ void scatter_fold_bulk(const GroupedPiece* __restrict
     if (lane == 0) atomicExch(status, 1);
     // Drain the loads still in flight (each wait bounded) before the ring goes away.
     for (int q = 0; q < slots; ++q)
-      if ((pending >> q) & 1u) bar_wait(bars + 8 * q, (phases >> q) & 1u);
+      if ((pending >> q) & 1u) bar_wait(bars + 8 * q, (phases >> q) & 1u, kBulkDrainLimit);
   }
   if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   __syncwarp();

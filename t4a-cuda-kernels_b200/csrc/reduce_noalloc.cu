@@ -12,7 +12,11 @@
 //
 // The first call on a device looks up the array's device address with that device
 // current (cudaGetSymbolAddress; host code cannot use the array's name as a device
-// pointer), so make that first call before any stream capture.  Every call on a device
+// pointer), so make that first call before any stream capture.  The address is cached
+// for the life of the process: after a cudaDeviceReset of a device this library must not
+// be called on that device again (the reset unloads the module and the cached address
+// no longer names the array).  Devices with an ordinal of kMaxDevices or more are looked
+// up on every call.  Every call on a device
 // shares the one array and leaves its partials there: calls whose kernels may overlap
 // on the GPU (different streams without ordering between them) race on it.  Nothing
 // needs to start at zero: pass 1 writes every partial before the combine pass reads it.
@@ -46,7 +50,14 @@ int scratch_of_current_device(void** out) {
     runtime::last_error() = static_cast<int>(e);
     return T4A_ERR_CUDA;
   }
-  if (dev < 0 || dev >= kMaxDevices) return T4A_ERR_CUDA;
+  if (dev < 0 || dev >= kMaxDevices) {
+    const cudaError_t u = cudaGetSymbolAddress(out, t4a_reduce_scratch);
+    if (u != cudaSuccess) {
+      runtime::last_error() = static_cast<int>(u);
+      return T4A_ERR_CUDA;
+    }
+    return T4A_OK;
+  }
   DeviceScratch& s = g_scratch[dev];
   std::call_once(s.once, [&s]() { s.err = cudaGetSymbolAddress(&s.ptr, t4a_reduce_scratch); });
   if (s.err != cudaSuccess) {

@@ -50,7 +50,15 @@ constexpr int kColStages = kColProducers;  // producer k issues every copy of st
 constexpr int kColHelperWarp0 = 1 + kColProducers;
 constexpr int kColHelpers = kColThreads - 32 * kColHelperWarp0;
 constexpr int kColStageBytes = 32768;
-constexpr unsigned kColWaitLimit = 1u << 20;  // try_wait rounds before giving up
+// try_wait rounds of a staged-data wait before it gives up (a build may lower it: the
+// tests build the library once with 0, so that every such wait runs out at once).
+#ifndef T4A_STAGE_WAIT_LIMIT
+#define T4A_STAGE_WAIT_LIMIT (1u << 20)
+#endif
+constexpr unsigned kColWaitLimit = T4A_STAGE_WAIT_LIMIT;
+// Rounds of the exit drain, which waits for the bulk copies still in flight so that none
+// lands in shared memory after the block is gone: separate, and never lowered.
+constexpr unsigned kColDrainLimit = 1u << 22;
 constexpr unsigned kColSuspendNs = 1000;
 
 // scaled_norm's buffers: the ring's bytes viewed as kNormBufs buffers of kNormSeg elements.
@@ -81,9 +89,10 @@ __device__ __forceinline__ unsigned smem_addr(const void* p) {
 }
 
 // Bounded wait for the phase of parity `parity` of an mbarrier; false when it ran out.
-__device__ __forceinline__ bool bar_wait(const unsigned long long* bar, unsigned parity) {
+__device__ __forceinline__ bool bar_wait(const unsigned long long* bar, unsigned parity,
+                                         unsigned limit = kColWaitLimit) {
   const unsigned addr = smem_addr(bar);
-  for (unsigned it = 0; it < kColWaitLimit; ++it) {
+  for (unsigned it = 0; it < limit; ++it) {
     unsigned ok;
     asm volatile(
         "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
@@ -231,7 +240,8 @@ __device__ __forceinline__ bool produce(ColSmem<F>& sm, Producer& pr, const Oper
 template <typename F>
 __device__ __forceinline__ void drain(ColSmem<F>& sm, const Producer& pr, long long* status) {
   if (pr.k < 0 || pr.last < 0) return;
-  if (!bar_wait(&sm.full[pr.k], parity_of(pr.last))) atomicOr(reinterpret_cast<unsigned long long*>(status), 2ull);
+  if (!bar_wait(&sm.full[pr.k], parity_of(pr.last), kColDrainLimit))
+    atomicOr(reinterpret_cast<unsigned long long*>(status), 2ull);
 }
 
 // Chain folds over one full segment (N elements per lane) in shared memory: loads run

@@ -231,6 +231,16 @@ def test_config3_c64_axis1(cuda):
     check_against_oracle(arr, 1, abi.SUM, abi.C64, ftype=np.float64)
 
 
+def test_config3_c64_axis1_full_size(cuda):
+    """The configuration's own C64 case at full size: sum along axis 1 of [8192, 8192]
+    (1 GiB), every output compared bit for bit with the oracle."""
+    rng = np.random.default_rng(6)
+    arr = np.empty((8192, 8192), np.complex128)
+    arr.real = rng.standard_normal((8192, 8192))
+    arr.imag = rng.standard_normal((8192, 8192))
+    check_against_oracle(arr, 1, abi.SUM, abi.C64, ftype=np.float64)
+
+
 @pytest.mark.parametrize("dtype,np_dtype", [(abi.I32, np.int32), (abi.I64, np.int64)])
 @pytest.mark.parametrize("op", [abi.SUM, abi.PROD, abi.MAX, abi.MIN])
 @pytest.mark.parametrize("numpy_axis", [0, 1, 2])

@@ -709,6 +709,49 @@ def test_form_q_matches_the_oracle(cuda, dtype, m, n, k):
     assert np.abs(q64 @ r - ap)[:, :k].max() < eps * m * np.abs(a).max()
 
 
+def unitary_reflectors(m, k, dtype, seed):
+    """Column-major work [m, k] whose column s holds a reflector's tail below row s, and
+    coefficients with I - c v v^H unitary: c = (1 + e^{i theta}) / (v^H v) (real dtypes:
+    theta = 0, c = 2 / (v^H v))."""
+    rng = np.random.default_rng(seed)
+    w = rng.standard_normal((m, k))
+    if dtype in (abi.C32, abi.C64):
+        w = w + 1j * rng.standard_normal((m, k))
+    c = np.zeros(k, np.complex128 if dtype in (abi.C32, abi.C64) else np.float64)
+    for s in range(k):
+        vv = 1.0 + float(np.sum(np.abs(w[s + 1:, s]) ** 2))
+        c[s] = (1 + np.exp(1j * rng.uniform(0, 2 * np.pi))) / vv if np.iscomplexobj(c) else 2.0 / vv
+    return np.asfortranarray(w.astype(NP[dtype])), c.astype(NP[dtype])
+
+
+@pytest.mark.parametrize("dtype,m,k", [(abi.C64, 300, 24), (abi.C64, 3000, 16), (abi.C32, 517, 13),
+                                       (abi.F64, 4096, 16), (abi.F64, 300, 24)])
+def test_form_q_primitive_route_matches_the_oracle(cuda, dtype, m, k):
+    """t4a_rrqr_form_q without a status word (and for complex types, which the column
+    pass does not take) runs identity_shifted and apply_reflector for step = k-1 .. 0 as
+    planned launches.  Against the oracle's loop: F32/F64 bit for bit; C32/C64 within
+    rounding (the oracle's complex sums are not contracted like the device's).  Q is
+    unitary for these coefficients."""
+    import torch
+    w, c = unitary_reflectors(m, k, dtype, seed=m + k + dtype)
+    es = np.dtype(NP[dtype]).itemsize
+    d_w, d_c = dev(w.ravel(order="K")), dev(c)
+    d_q = sentinel_dev(m * k * es)
+    wl, ql, cl = abi.layout([m, k]), abi.layout([m, k]), abi.layout([k])
+    t4.check(t4.lib().t4a_rrqr_form_q(t4.stream_handle(), dtype, vp(d_w), ctypes.byref(wl), m * k, vp(d_c),
+                                      ctypes.byref(cl), k, vp(d_q), ctypes.byref(ql), m * k, None), "form_q")
+    torch.cuda.synchronize()
+    got = host(d_q, m * k * es, NP[dtype]).reshape(k, m).T
+    want = oracle_form_q(w, c, dtype, k)
+    if dtype in (abi.F32, abi.F64):
+        assert np.array_equal(np.ascontiguousarray(got).view(np.uint8), np.ascontiguousarray(want).view(np.uint8))
+    else:
+        tol = 1e-12 if dtype == abi.C64 else 2e-5
+        assert np.abs(got - want).max() <= tol * np.sqrt(m) * k
+    q = got.astype(np.complex128)
+    assert np.abs(q.conj().T @ q - np.eye(k)).max() < (1e-12 if dtype in (abi.F64, abi.C64) else 1e-4) * m
+
+
 def test_form_q_config5_properties(cuda):
     """BASELINE config 5 at full size (m 65536, 256 reflectors): the Q formation's Q is
     orthonormal and Q R equals A P, checked on the GPU in F64."""
