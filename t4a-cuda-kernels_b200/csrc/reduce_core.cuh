@@ -47,7 +47,9 @@ extern __shared__ __align__(16) unsigned char t4a_dyn_smem[];
 template <typename Op, typename T>
 __device__ __forceinline__ T serial_walk(const T* in, long long base, long long stride,
                                          long long start, long long end, int W, int lane, Op op) {
-  constexpr int B = (64 / static_cast<int>(sizeof(T))) < 4 ? 4 : 64 / static_cast<int>(sizeof(T));
+  // Loads per batch: 64 bytes' worth (at least 4), and 8 for 16-byte elements, whose
+  // lane walks over a 256-element chunk are then a single batch.
+  constexpr int B = sizeof(T) >= 16 ? 8 : ((64 / static_cast<int>(sizeof(T))) < 4 ? 4 : 64 / static_cast<int>(sizeof(T)));
   long long i = start + lane;
   if (end > 0x7fffffffffffffffLL - static_cast<long long>(B) * W) {
     T acc = op.seed(in[base + i * stride]);

@@ -16,10 +16,17 @@
 namespace t4a {
 namespace {
 
+// A split reduction's combine pass is launched with programmatic stream serialization
+// after its partials pass (t4a_reduce): it may launch as the partials pass's blocks
+// exit, and this wait holds it until that pass has finished and its partials are
+// visible.  In every other launch the wait returns at once.
+__device__ __forceinline__ void dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 template <typename Op, typename T>
 __global__ void __launch_bounds__(256) k_strided(T* dst, const T* in, t4a_cuda_layout dst_l,
                                                  t4a_cuda_layout in_l, int axis, long long splits,
                                                  long long chunk, bool partials) {
+  dependency_wait();
   constexpr int V = VecOf<T>::kLanes;
   strided_tiles<Op, T, V, 4>(in, dst, in_l, dst_l, strided_ctx(in_l, axis, splits, chunk, V, partials), Op());
 }
@@ -36,6 +43,7 @@ __global__ void __launch_bounds__(256, kStagedBlocksPerSm) k_strided_staged(T* d
                                                                            t4a_cuda_layout in_l, int axis,
                                                                            long long splits, long long chunk,
                                                                            bool partials) {
+  dependency_wait();
   constexpr int V = VecOf<T>::kLanes;
   if constexpr (V * sizeof(T) == 16) {
     strided_warp_staged<Op, T, V, kStagedLanes, kStagedDepth>(
@@ -47,12 +55,14 @@ template <typename Op, typename T>
 __global__ void __launch_bounds__(256) k_cubes(T* dst, const T* in, t4a_cuda_layout dst_l, t4a_cuda_layout in_l,
                                                int axis, long long outputs, long long splits, long long chunk,
                                                bool partials) {
+  dependency_wait();
   plane_cubes<Op, T>(in, dst, in_l, dst_l, axis, outputs, splits, chunk, blockDim.x, partials, partials, Op());
 }
 
 template <typename Op, typename T>
 __global__ void __launch_bounds__(256) k_unit_rows(T* out, const T* in, t4a_cuda_layout out_l, t4a_cuda_layout in_l,
                                                    long long outputs, int rows) {
+  dependency_wait();
   unit_rows<Op, T>(in, out, out_l, in_l, outputs, rows, Op());
 }
 
@@ -63,6 +73,7 @@ template <typename Op, typename T>
 __global__ void __launch_bounds__(kWarpRowsThreads) k_warp_rows(T* out, const T* in, t4a_cuda_layout out_l,
                                                                 t4a_cuda_layout in_l, long long outputs,
                                                                 bool dst_linear) {
+  dependency_wait();
   extern __shared__ __align__(16) unsigned char warp_slices[];
   if constexpr ((kWarpRowsLen * sizeof(T)) % 128 == 0) {
     unit_warp_rows<Op, T, kWarpRowsLen>(in, out, out_l, in_l, outputs, dst_linear,
@@ -73,12 +84,14 @@ __global__ void __launch_bounds__(kWarpRowsThreads) k_warp_rows(T* out, const T*
 template <typename Op, typename T>
 __global__ void __launch_bounds__(256) k_unit(T* out, const T* in, t4a_cuda_layout out_l, t4a_cuda_layout in_l,
                                               int axis, long long outputs) {
+  dependency_wait();
   unit_generic<Op, T>(in, out, out_l, in_l, axis, outputs, Op());
 }
 
 template <typename Op, typename T>
 __global__ void __launch_bounds__(512) k_wide(T* out, const T* in, t4a_cuda_layout out_l, t4a_cuda_layout in_l,
                                               int axis, long long outputs) {
+  dependency_wait();
   wide_plane<Op, T>(in, out, out_l, in_l, axis, outputs, Op());
 }
 
@@ -126,7 +139,24 @@ struct PassArgs {
   long long splits;
   long long chunk;
   bool partials;
+  bool chained = false;  // launched as the link after the partials pass (see dependency_wait)
 };
+
+// Launches a pass kernel, as a chained link when `chained`.
+template <typename... KArgs, typename... Args>
+void go(void (*kernel)(KArgs...), dim3 grid, dim3 block, unsigned smem, cudaStream_t s, bool chained, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = chained ? 1 : 0;
+  cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);  // an error is left for check_launch
+}
 
 template <typename Op, typename T>
 void launch_path(int path, dim3 grid, dim3 block, unsigned smem, cudaStream_t stream, const PassArgs& a) {
@@ -134,39 +164,40 @@ void launch_path(int path, dim3 grid, dim3 block, unsigned smem, cudaStream_t st
   const T* in = static_cast<const T*>(a.in);
   switch (path) {
     case kPathStrided:
-      k_strided<Op, T><<<grid, block, smem, stream>>>(dst, in, a.dst_l, a.in_l, a.axis, a.splits, a.chunk, a.partials);
+      go(k_strided<Op, T>, grid, block, smem, stream, a.chained, dst, in, a.dst_l, a.in_l, a.axis, a.splits, a.chunk,
+         a.partials);
       break;
     case kPathUnitRows: {
       const int rows = unit_rows_per_tile(a.in_l, a.axis, sizeof(T));
-      k_unit_rows<Op, T><<<grid, block, smem, stream>>>(dst, in, a.dst_l, a.in_l, a.outputs, rows);
+      go(k_unit_rows<Op, T>, grid, block, smem, stream, a.chained, dst, in, a.dst_l, a.in_l, a.outputs, rows);
       break;
     }
     case kPathStridedStaged: {
+      auto kernel = k_strided_staged<Op, T>;
       static std::atomic<unsigned long long> raised{0};
       int dev = 0;
       if (cudaGetDevice(&dev) == cudaSuccess) {
         const unsigned long long bit = 1ull << (dev & 63);
         if ((raised.load(std::memory_order_relaxed) & bit) == 0 &&
-            cudaFuncSetAttribute(k_strided_staged<Op, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) ==
-                cudaSuccess)
+            cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) == cudaSuccess)
           raised.fetch_or(bit);
       }
-      k_strided_staged<Op, T><<<grid, block, smem, stream>>>(dst, in, a.dst_l, a.in_l, a.axis, a.splits, a.chunk,
-                                                             a.partials);
+      go(kernel, grid, block, smem, stream, a.chained, dst, in, a.dst_l, a.in_l, a.axis, a.splits, a.chunk, a.partials);
       break;
     }
     case kPathWarpRows:
-      k_warp_rows<Op, T><<<grid, block, smem, stream>>>(dst, in, a.dst_l, a.in_l, a.outputs, dst_linear(a.dst_l));
+      go(k_warp_rows<Op, T>, grid, block, smem, stream, a.chained, dst, in, a.dst_l, a.in_l, a.outputs,
+         dst_linear(a.dst_l));
       break;
     case kPathUnit:
-      k_unit<Op, T><<<grid, block, smem, stream>>>(dst, in, a.dst_l, a.in_l, a.axis, a.outputs);
+      go(k_unit<Op, T>, grid, block, smem, stream, a.chained, dst, in, a.dst_l, a.in_l, a.axis, a.outputs);
       break;
     case kPathWide:
-      k_wide<Op, T><<<grid, block, smem, stream>>>(dst, in, a.dst_l, a.in_l, a.axis, a.outputs);
+      go(k_wide<Op, T>, grid, block, smem, stream, a.chained, dst, in, a.dst_l, a.in_l, a.axis, a.outputs);
       break;
     default:
-      k_cubes<Op, T><<<grid, block, smem, stream>>>(dst, in, a.dst_l, a.in_l, a.axis, a.outputs, a.splits,
-                                                    a.chunk, a.partials);
+      go(k_cubes<Op, T>, grid, block, smem, stream, a.chained, dst, in, a.dst_l, a.in_l, a.axis, a.outputs, a.splits,
+         a.chunk, a.partials);
       break;
   }
 }
@@ -212,6 +243,16 @@ void prefer_strided_staged(int dtype, int* path, dim3* grid, unsigned* smem, con
   *smem = kStagedSmem;
 }
 
+// The per-cube walk is grid-stride: a grid of many short-lived blocks (one cube per
+// plane) runs as eight resident blocks per SM that each take cubes in turn.
+void cap_cube_grid(int path, dim3* grid) {
+  if (path != kPathCubes) return;
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const unsigned cap = static_cast<unsigned>(sms * 8);
+  if (grid->x > cap) grid->x = cap;
+}
+
 // A 16-byte-vector path needs a 16-byte-aligned base; otherwise the same pass runs on
 // the per-cube path, whose geometry is recomputed here.
 bool fix_alignment(int dtype, const void* in, int* path, dim3* grid, dim3* block, unsigned* smem,
@@ -246,6 +287,7 @@ int run_pass(const t4a_launch* launch, void* stream, int dtype, int op, PassArgs
     return T4A_ERR_LAUNCH_LIMIT;
   }
   prefer_strided_staged(dtype, &path, &grid, &smem, a);
+  cap_cube_grid(path, &grid);
 #define T4A_CALL(OP, T) launch_path<OP, T>(path, grid, block, smem, s, a)
   T4A_REDUCE_SWITCH(op, dtype, T4A_CALL)
 #undef T4A_CALL
@@ -378,8 +420,9 @@ int t4a_reduce(void* stream, int dtype, int op, void* out, const t4a_cuda_layout
   if (workspace == nullptr || workspace_bytes < need) return T4A_ERR_WORKSPACE;
   T4A_TRY(t4a_launch_reduce_partials(&plan.pass1, stream, workspace, in, dtype, op, partials, *in_layout,
                                      static_cast<int>(axis), outputs, plan.split.splits, plan.split.chunk_len));
-  return t4a_launch_reduce(&plan.pass2, stream, out, workspace, dtype, plan.combine_op, plan.combine_strategy,
-                           *out_layout, partials, static_cast<int>(axis), outputs);
+  PassArgs a{out, workspace, *out_layout, partials, static_cast<int>(axis), outputs, 1, partials.extents[axis], false,
+             true};
+  return run_pass(&plan.pass2, stream, dtype, plan.combine_op, a);
 }
 
 }  // extern "C"

@@ -247,14 +247,17 @@ __device__ __forceinline__ void drain(ColSmem<F>& sm, const Producer& pr, long l
 // Chain folds over one full segment (N elements per lane) in shared memory: loads run
 // kAhead elements ahead of the dependent fma.
 constexpr int kAhead = 8;
+// lead_one: the segment's element 0 (lane 0's first) takes v = 1, the reflector's
+// implicit leading one, instead of the stored value.
 template <typename F, int N>
-__device__ __forceinline__ F fold_products(const F* bv, const F* bt, int lane, F acc) {
+__device__ __forceinline__ F fold_products(const F* bv, const F* bt, int lane, F acc, bool lead_one = false) {
   F xv[kAhead], xt[kAhead];
 #pragma unroll
   for (int k = 0; k < kAhead; ++k) {
     xv[k] = bv[lane + 32 * k];
     xt[k] = bt[lane + 32 * k];
   }
+  if (lead_one && lane == 0) xv[0] = F(1);
 #pragma unroll
   for (int k = 0; k < N; ++k) {
     const F v = xv[k % kAhead], t = xt[k % kAhead];
@@ -299,10 +302,12 @@ __device__ __forceinline__ F ring_dot(ColSmem<F>& sm, Producer& pr, long long ba
     if (!produce<F, 2>(sm, pr, ops, base, nseg)) fail(sm, status);
   } else if (warp == 0) {
     F acc = F(0);
-    for (long long g = 0; g < nseg; ++g) {
+    // The chain checks the stop flag once: a producer that stops leaves a stage unfilled,
+    // and the chain's bounded wait on it then runs out.
+    const long long count = __any_sync(kAllLanes, aborted(sm)) ? 0 : nseg;
+    for (long long g = 0; g < count; ++g) {
       const long long p = base + g;
       const int st = stage_of(p);
-      if (__any_sync(kAllLanes, aborted(sm))) break;
       if (!__all_sync(kAllLanes, bar_wait(&sm.full[st], parity_of(p)))) {
         if (lane == 0) fail(sm, status);
         break;
@@ -310,11 +315,11 @@ __device__ __forceinline__ F ring_dot(ColSmem<F>& sm, Producer& pr, long long ba
       const F* bv = sm.raw[st] + ops[0].sh;
       const F* bt = sm.raw[st] + S::kRegion2 + ops[1].sh;
       const long long e0 = g * S::kSeg2;
-      if (g == 0) {
-        const int len = static_cast<int>(rows < S::kSeg2 ? rows : S::kSeg2);
+      if (e0 + S::kSeg2 <= rows) {
+        acc = fold_products<F, S::kSeg2 / 32>(bv, bt, lane, acc, g == 0 && lead_one);
+      } else if (g == 0) {
+        const int len = static_cast<int>(rows);
         for (int i = lane; i < len; i += 32) acc = fma_rn(i == 0 && lead_one ? F(1) : bv[i], bt[i], acc);
-      } else if (e0 + S::kSeg2 <= rows) {
-        acc = fold_products<F, S::kSeg2 / 32>(bv, bt, lane, acc);
       } else {
         const int len = static_cast<int>(rows - e0);
         for (int i = lane; i < len; i += 32) acc = fma_rn(bv[i], bt[i], acc);
@@ -606,9 +611,11 @@ __device__ __forceinline__ F scaled_norm(ColSmem<F>& sm, const F* x, long long r
     }
   } else if (warp == 0) {
     F acc = F(0);
-    for (long long g = 0; g < nseg; ++g) {
+    // As in ring_dot: a helper that stops leaves a buffer unfilled, and the chain's
+    // bounded wait on it runs out.
+    const long long count = __any_sync(kAllLanes, aborted(sm)) ? 0 : nseg;
+    for (long long g = 0; g < count; ++g) {
       const int b = static_cast<int>(g % kNormBufs);
-      if (__any_sync(kAllLanes, aborted(sm))) break;
       if (!__all_sync(kAllLanes, bar_wait(&sm.ready[b], static_cast<unsigned>((g / kNormBufs) & 1)))) {
         if (lane == 0) fail(sm, status);
         break;
