@@ -35,7 +35,8 @@ global problem stays the same):
   gather      index batches, table replicated;
   scatter_add update batches into per-rank partial destinations, then an NCCL
               reduce-scatter of the partials inside the timed op;
-  RRQR        row blocks, with the per-step exchange of column norms and reflector dots.
+  RRQR        row blocks, with the per-step exchange of column norms and reflector dots
+              fused into the step kernels (stores into every rank's memory over NVLink).
 Before timing, every rank checks its shard against the single-GPU result of the same
 library (computed on that rank from the full input): bit for bit for reductions,
 movement and gather; for scatter_add (atomic, so its summation order is not fixed)
@@ -694,7 +695,8 @@ class RrqrConfig(Config):
     steps of column_norms -> select_pivot -> swap_columns -> reflector ->
     apply_reflector.  One GPU: the fused driver t4a_rrqr (bit-identical to that loop of
     primitives).  N GPUs: row blocks of m/N rows with the per-step exchange of the
-    column norms and reflector dots (t4a_b200.dist.rrqr_rows_sharded).  Algorithmic
+    column norms and reflector dots fused into the step kernels, as stores into every
+    rank's memory over NVLink (t4a_b200.dist.RrqrRowsSharded, t4a_dist_rrqr_p2p).  Algorithmic
     bytes per factorization: sum over steps s of norms 8(m-s)(n-s) + apply
     16(m-s)(n-s-1) + swap 32m + reflector 16(m-s).  A is restored from a pristine device
     copy before every factorization, outside the op's events; in the end-to-end leg the
@@ -736,7 +738,7 @@ class RrqrConfig(Config):
             d["status"] = torch.zeros(1, dtype=torch.int64, device=self.device)
             if self.sharded:
                 from t4a_b200 import dist as t4dist
-                self.driver = t4dist.RrqrRowsSharded(d["a"], m, n, r0, n)
+                self.driver = t4dist.RrqrRowsSharded(d["a"], m, n, r0, n, exchange="p2p")
             else:
                 self.layout = abi.layout([m, n])
                 self.ws = torch.empty(t4.rrqr_workspace_bytes(abi.F64, self.layout), dtype=torch.uint8,
@@ -896,10 +898,25 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
 
     # Every rank checks its shards against the single-GPU result before timing.
+    # Ranks agree on every group's outcome before the next group runs, so no rank goes on
+    # launching kernels that store into another rank's memory (the sharded RRQR) after
+    # that rank has stopped.
     checks = {}
     if not args.no_check:
         for g in groups:
-            g.check()
+            err = None
+            try:
+                g.check()
+            except CheckFailed as e:
+                err = e
+            torch.cuda.synchronize()
+            if dist_on:
+                flag = torch.tensor([0 if err is None else 1], dtype=torch.int32, device=device)
+                torch.distributed.all_reduce(flag)
+                if int(flag.item()) and err is None:
+                    err = CheckFailed(f"another rank's check of the {g.name} ops failed")
+            if err is not None:
+                raise err
             checks.update(g.checks)
         torch.cuda.synchronize()
     for g in groups:

@@ -499,6 +499,27 @@ int t4a_dist_rrqr(void* comm, void* stream, int dtype, void* work, const t4a_cud
                   long long work_len, long long row0, long long global_rows, long long steps, void* permutation,
                   void* coeff, void* pivots, void* status, void* workspace, size_t workspace_bytes);
 
+/* The same row-sharded RRQR with its exchanges fused into the step kernels: each rank
+ * stores its norm and dot parts into every rank's exchange region over NVLink and
+ * publishes them with a per-rank flag, and the kernel that needs them waits (bounded)
+ * for every rank's flag.  No collective call sits between the step's kernels.
+ *
+ * t4a_p2p_create allocates this GPU's region for matrices of n columns and a world of
+ * `world` ranks, and writes its 64-byte CUDA IPC handle to ipc_handle; the caller
+ * gathers every rank's handle (rank order, world x 64 bytes) and passes them to
+ * t4a_p2p_open, which maps the peers' regions.  t4a_dist_rrqr_p2p takes the arguments
+ * of t4a_dist_rrqr without a workspace, and gives its bits; every rank must make the
+ * same calls in the same order.  Before t4a_p2p_destroy every rank must have finished
+ * its calls (the caller synchronizes and waits for the others), since peers write into
+ * the region.  A wait that ran out sets status bit 1. */
+int t4a_p2p_region_bytes(long long n, int world, size_t* bytes);
+int t4a_p2p_create(long long n, int world, int rank, void** comm, void* ipc_handle);
+int t4a_p2p_open(void* comm, const void* ipc_handles);
+int t4a_p2p_destroy(void* comm);
+int t4a_dist_rrqr_p2p(void* comm, void* stream, int dtype, void* work, const t4a_cuda_layout* local_layout,
+                      long long work_len, long long row0, long long global_rows, long long steps, void* permutation,
+                      void* coeff, void* pivots, void* status);
+
 #ifdef __cplusplus
 }
 #endif

@@ -4,25 +4,9 @@
 // examples/bench_kernels.rs:2398-2530): column_norms, select_pivot, swap_columns,
 // reflector, apply_reflector.
 //
-// Rank r holds rows [row0, row0 + mr) of every column, column-major.  Per step s:
-//   select+swap  every rank combines the gathered norm parts of the trailing columns in
-//                rank order, chooses the pivot (the reference's rule) and the
-//                reflector's scalars, swaps its rows of columns s and pivot and scales
-//                its rows below s of the new column s (the owner of row s writes alpha);
-//   dot          per trailing column, the chain of v t over this rank's rows >= s (the
-//                reference's lane order within the rank's block; v_s = 1 on the owner);
-//   all-gather   the dot parts;
-//   update       d = (sum of the parts in rank order) * coeff; t -= v d on this rank's
-//                rows; then the next step's norm parts of rows >= s + 1: the largest
-//                finite modulus, the chain of (|t| / that)^2, a non-finite flag, the
-//                same pair over every modulus when a value is non-finite (the
-//                reflector's form), and the value at row s + 1 with an owner flag;
-//   all-gather   the norm parts.
-// Norm parts combine as norm = S sqrt(sum_r w_r ssq_r), S = max_r scale_r, w_r = 1 when
-// scale_r == S and (scale_r / S)^2 otherwise.  With one rank every combination is exact,
-// so a world of one reproduces the single-GPU driver bit for bit; with several, norms and
-// dots round differently from the single-GPU order, and pivots agree wherever norms are
-// well separated (the rank-revealing prefix).
+// The step's arithmetic is rrqr_shard.cuh's.  Per step: select+swap (from the gathered
+// norm parts), dot, an all-gather of the dot parts, update with the next step's norm
+// parts, an all-gather of the norm parts.
 //
 // NCCL is loaded on first use (dlopen of libnccl.so.2), so the library loads on hosts
 // without it; the entry points then return T4A_ERR_CUDA.
@@ -34,7 +18,7 @@
 #include <mutex>
 
 #include "plan_common.h"
-#include "rrqr_step.cuh"
+#include "rrqr_shard.cuh"
 #include "runtime.h"
 
 namespace t4a {
@@ -73,103 +57,6 @@ const Nccl& nccl() {
 
 int nccl_status(ncclResult_t r) { return r == ncclSuccess ? T4A_OK : T4A_ERR_CUDA; }
 
-// ---- the exchanged records -----------------------------------------------------------
-
-// One rank's norm parts of one column (eight elements, so a vector of them gathers as F).
-template <typename F>
-struct NormPart {
-  F scale;   // largest finite modulus of the rank's rows
-  F ssq;     // chain of (|x| / scale)^2, butterfly-summed
-  F rscale;  // the reflector's form (every modulus competes): equal to scale / ssq for a
-  F rssq;    // finite column
-  F xrow;    // value at the step's leading row (owner only)
-  F bad;     // 1: a non-finite modulus
-  F own;     // 1: this rank holds the leading row
-  F pad;
-};
-
-template <typename F>
-struct DistRecord {
-  long long pivot;
-  F alpha;
-  F divisor;
-  int scale;  // 0: norm == 0 (no scaling, coefficient 0)
-};
-
-template <typename F>
-struct DistArgs {
-  F* w;              // local rows, column-major
-  long long mr;      // local rows
-  long long n;       // columns
-  long long ld;      // column stride
-  long long row0;    // global index of local row 0
-  int world;
-  long long* perm;   // n (replicated)
-  F* coeff;          // one per step (replicated)
-  long long* pivots;
-  long long* status;
-  NormPart<F>* nsend;  // trailing columns' parts of this rank
-  NormPart<F>* nrecv;  // [world][count]
-  F* dsend;
-  F* drecv;            // [world][count]
-  DistRecord<F>* rec;
-};
-
-// First local row at global row >= s, and whether this rank holds global row s.
-template <typename F>
-__device__ __forceinline__ long long local_from(const DistArgs<F>& a, long long s) {
-  const long long lo = s - a.row0;
-  return lo < 0 ? 0 : (lo > a.mr ? a.mr : lo);
-}
-template <typename F>
-__device__ __forceinline__ bool holds(const DistArgs<F>& a, long long s) {
-  return s >= a.row0 && s < a.row0 + a.mr;
-}
-
-// Separately rounded products and sums (no contraction into fma), so that the combine
-// is the same arithmetic on every rank and in the CPU restatement.
-__device__ __forceinline__ double mul_rn(double a, double b) { return __dmul_rn(a, b); }
-__device__ __forceinline__ float mul_rn(float a, float b) { return __fmul_rn(a, b); }
-__device__ __forceinline__ double add_rn(double a, double b) { return __dadd_rn(a, b); }
-__device__ __forceinline__ float add_rn(float a, float b) { return __fadd_rn(a, b); }
-
-// Combined norm of trailing column c (parts of column c at offset c - first in every
-// rank's block of `count`): the column_norms form (-1 for a non-finite column) or the
-// reflector's form.
-template <typename F, bool kReflector>
-__device__ __forceinline__ F combined_norm(const DistArgs<F>& a, long long count, long long idx) {
-  F scale = F(0);
-  bool bad = false;
-  for (int r = 0; r < a.world; ++r) {
-    const NormPart<F>& p = a.nrecv[r * count + idx];
-    const F sc = kReflector ? p.rscale : p.scale;
-    bad = bad || p.bad != F(0);
-    scale = sc > scale ? sc : scale;
-  }
-  if (!kReflector && bad) return F(-1);
-  F ssq = F(0);
-  for (int r = 0; r < a.world; ++r) {
-    const NormPart<F>& p = a.nrecv[r * count + idx];
-    const F sc = kReflector ? p.rscale : p.scale;
-    if (sc > F(0)) {
-      const F ratio = sc == scale ? F(1) : sc / scale;
-      ssq = add_rn(ssq, mul_rn(mul_rn(ratio, ratio), kReflector ? p.rssq : p.ssq));
-    }
-  }
-  const F norm = mul_rn(scale, sqrt(ssq));
-  return !kReflector && nonfinite(norm) ? F(-1) : norm;
-}
-
-template <typename F>
-__device__ __forceinline__ F leading_value(const DistArgs<F>& a, long long count, long long idx) {
-  F x = F(0);
-  for (int r = 0; r < a.world; ++r) {
-    const NormPart<F>& p = a.nrecv[r * count + idx];
-    if (p.own != F(0)) x = p.xrow;
-  }
-  return x;
-}
-
 // ---- kernels ------------------------------------------------------------------------
 
 template <typename F>
@@ -179,41 +66,6 @@ __global__ void __launch_bounds__(256) k_dist_init(DistArgs<F> a) {
     a.perm[c] = c;
 }
 
-// The norm parts of column j over this rank's rows [lo, mr) (global rows >= s).
-template <typename F>
-__device__ __forceinline__ void norm_parts(const DistArgs<F>& a, ColSmem<F>& sm, const F* col, long long lo, long long s,
-                                           F peak, bool flagged, bool have_peak, NormPart<F>* out) {
-  const long long rows = a.mr - lo;
-  F scale;
-  bool bad;
-  if (!have_peak) {
-    peak = F(0);
-    flagged = false;
-    if (rows > 0) peak_direct<true>(col + lo, rows, &peak, &flagged);
-  }
-  block_peak(sm, peak, flagged, &scale, &bad);
-  F ssq = F(0);
-  if (!bad && scale > F(0) && rows > 0) ssq = scaled_norm(sm, col + lo, rows, scale, a.status);
-  F rscale = scale, rssq = ssq;
-  if (bad && threadIdx.x < 32) {
-    const ScaledSum<F> r = chain_parts<false, 1>(Strip<const F>{col + lo, 1}, 0, rows, nullptr);
-    rscale = r.scale;
-    rssq = r.ssq;
-  }
-  if (threadIdx.x == 0) {
-    NormPart<F> p;
-    p.scale = scale;
-    p.ssq = ssq;
-    p.rscale = rscale;
-    p.rssq = rssq;
-    p.own = holds(a, s) ? F(1) : F(0);
-    p.xrow = holds(a, s) ? col[s - a.row0] : F(0);
-    p.bad = bad ? F(1) : F(0);
-    p.pad = F(0);
-    *out = p;
-  }
-}
-
 // Step 0's norm parts: block per column.
 template <typename F>
 __global__ void __launch_bounds__(kColThreads, 2) k_dist_first(DistArgs<F> a) {
@@ -221,7 +73,8 @@ __global__ void __launch_bounds__(kColThreads, 2) k_dist_first(DistArgs<F> a) {
   ColSmem<F>& sm = *reinterpret_cast<ColSmem<F>*>(smem);
   const long long j = blockIdx.x;
   engine_init(sm);
-  norm_parts(a, sm, a.w + j * a.ld, 0, 0, F(0), false, false, a.nsend + j);
+  NormPart<F>* out = a.nsend + j;
+  norm_parts(a, sm, a.w + j * a.ld, 0, 0, F(0), false, false, [&](const NormPart<F>& p) { *out = p; });
 }
 
 // Pivot of step s from the gathered parts (every block decides the same), then the swap
@@ -231,56 +84,12 @@ __global__ void __launch_bounds__(256) k_dist_select_swap(DistArgs<F> a, long lo
   __shared__ DistRecord<F> rec;
   const long long count = a.n - s;  // gathered parts cover columns s .. n-1
   if (threadIdx.x < 32) {
-    bool flagged = false;
-    const long long pivot = choose_pivot<F>(
-        s, a.n, [&](long long c) { return combined_norm<F, false>(a, count, c - s); },
-        [&](long long c) { return a.perm[c]; }, &flagged);
-    F norm = combined_norm<F, false>(a, count, pivot - s);
-    if (!(norm >= F(0))) norm = combined_norm<F, true>(a, count, pivot - s);
-    const F x0 = leading_value(a, count, pivot - s);
-    if (lane_id() == 0) {
-      DistRecord<F> r;
-      r.pivot = pivot;
-      F c = F(0);
-      if (norm == F(0)) {
-        r.scale = 0;
-        r.alpha = F(0);
-        r.divisor = F(1);
-      } else {
-        const Householder<F> h = householder(x0, norm);
-        r.scale = 1;
-        r.alpha = h.alpha;
-        r.divisor = h.divisor;
-        c = h.coeff;
-      }
-      rec = r;
-      if (blockIdx.x == 0) {
-        *a.rec = r;
-        a.pivots[s] = pivot;
-        a.coeff[s] = c;
-        if (flagged) *a.status |= 1;
-      }
-    }
+    const DistRecord<F> r = shard_pivot(a, s, count, s, blockIdx.x == 0,
+                                        [&](long long c) { return combined_norm<F, false>(a, count, c - s); });
+    if (lane_id() == 0) rec = r;
   }
   __syncthreads();
-  const DistRecord<F> r = rec;
-  F* cs = a.w + s * a.ld;
-  F* cp = a.w + r.pivot * a.ld;
-  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < a.mr;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const long long g = a.row0 + i;
-    const F left = cs[i];
-    F moved = r.pivot == s ? left : cp[i];
-    if (r.scale) {
-      if (g == s) {
-        moved = r.alpha;
-      } else if (g > s) {
-        moved = moved / r.divisor;
-      }
-    }
-    cs[i] = moved;
-    if (r.pivot != s) cp[i] = left;
-  }
+  shard_swap(a, s, rec);
 }
 
 // Dot parts of step s: block per trailing column (and block 0 swaps the permutation).
@@ -289,14 +98,7 @@ __global__ void __launch_bounds__(kColThreads, 2) k_dist_dot(DistArgs<F> a, long
   extern __shared__ __align__(128) unsigned char smem[];
   ColSmem<F>& sm = *reinterpret_cast<ColSmem<F>*>(smem);
   const long long j = s + 1 + blockIdx.x;
-  if (blockIdx.x == 0 && threadIdx.x == 0) {
-    const long long p = a.rec->pivot;
-    if (p != s) {
-      const long long x = a.perm[s];
-      a.perm[s] = a.perm[p];
-      a.perm[p] = x;
-    }
-  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) shard_perm_swap(a, s, a.rec->pivot);
   const long long lo = local_from(a, s);
   const long long rows = a.mr - lo;
   if (rows <= 0) {
@@ -318,12 +120,7 @@ __global__ void __launch_bounds__(kColThreads, 2) k_dist_update(DistArgs<F> a, l
   const long long j = s + 1 + blockIdx.x;
   const long long count = a.n - s - 1;
   engine_init(sm);
-  if (threadIdx.x == 0) {
-    // Rank order, starting from rank 0's part (so one rank's part passes unchanged).
-    F d = a.drecv[blockIdx.x];
-    for (int r = 1; r < a.world; ++r) d = add_rn(d, a.drecv[r * count + blockIdx.x]);
-    sm.dot = mul_rn(d, a.coeff[s]);
-  }
+  if (threadIdx.x == 0) sm.dot = combined_dot(a, count, blockIdx.x, a.coeff[s]);
   __syncthreads();
   const F d = sm.dot;
   const long long lo = local_from(a, s);
@@ -332,7 +129,9 @@ __global__ void __launch_bounds__(kColThreads, 2) k_dist_update(DistArgs<F> a, l
   F peak = F(0);
   bool flagged = false;
   if (rows > 0) update_direct<true>(a.w + s * a.ld + lo, col + lo, rows, d, &peak, &flagged, holds(a, s));
-  if (next_norm) norm_parts(a, sm, col, local_from(a, s + 1), s + 1, peak, flagged, true, a.nsend + blockIdx.x);
+  NormPart<F>* out = a.nsend + blockIdx.x;
+  if (next_norm)
+    norm_parts(a, sm, col, local_from(a, s + 1), s + 1, peak, flagged, true, [&](const NormPart<F>& p) { *out = p; });
 }
 
 template <typename F>

@@ -128,6 +128,11 @@ def _declare(l):
         "t4a_dist_comm_destroy": (I, [P]),
         "t4a_dist_rrqr_workspace_bytes": (I, [I, LL, I, ctypes.POINTER(SZ)]),
         "t4a_dist_rrqr": (I, [P, P, I, P, LP, LL, LL, LL, LL, P, P, P, P, P, SZ]),
+        "t4a_p2p_region_bytes": (I, [LL, I, ctypes.POINTER(SZ)]),
+        "t4a_p2p_create": (I, [LL, I, I, ctypes.POINTER(P), P]),
+        "t4a_p2p_open": (I, [P, P]),
+        "t4a_p2p_destroy": (I, [P]),
+        "t4a_dist_rrqr_p2p": (I, [P, P, I, P, LP, LL, LL, LL, LL, P, P, P, P]),
         "t4a_rrqr": (I, [P, I, P, LP, LL, LL, P, P, P, P, P, SZ]),
         "t4a_rrqr_form_q": (I, [P, I, P, LP, LL, P, LP, LL, P, LP, LL, P]),
         "t4a_plan_identity_shifted": (I, [I, LP, LL, LL, ctypes.POINTER(Launch)]),

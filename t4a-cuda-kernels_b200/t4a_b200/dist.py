@@ -185,31 +185,84 @@ class NcclComm:
         self.handle = None
 
 
+class P2pComm:
+    """This library's NVLink exchange for one rank (t4a_p2p_create / t4a_p2p_open): a
+    region of this GPU's memory that every rank of the group maps through CUDA IPC, for
+    a matrix of n columns.  The 64-byte IPC handles travel through the torch.distributed
+    group once.  Without an initialized process group it is a world of one.  close()
+    waits for every rank (a barrier), so no rank frees its region while another may
+    still write into it."""
+
+    def __init__(self, n, group=None):
+        lib = _t4.lib()
+        if dist.is_available() and dist.is_initialized():
+            world, rank = _world(group)
+        else:
+            world, rank = 1, 0
+        own = (ctypes.c_ubyte * 64)()
+        handle = ctypes.c_void_p()
+        _t4.check(lib.t4a_p2p_create(n, world, rank, ctypes.byref(handle), own), "p2p_create")
+        handles = bytes(own)
+        if world > 1:
+            gathered = [None] * world
+            dist.all_gather_object(gathered, bytes(own), group=group)
+            handles = b"".join(gathered)
+        _t4.check(lib.t4a_p2p_open(handle, ctypes.create_string_buffer(handles, len(handles))), "p2p_open")
+        self.handle, self.world, self.rank, self.n, self.group = handle, world, rank, n, group
+
+    def close(self):
+        if self.handle is not None and self.handle.value:
+            torch.cuda.synchronize()
+            if self.world > 1:
+                dist.barrier(group=self.group)
+            _t4.check(_t4.lib().t4a_p2p_destroy(self.handle), "p2p_destroy")
+        self.handle = None
+
+
 class RrqrRowsSharded:
-    """RRQR of a [m, n] F32/F64 matrix whose rows are split across the ranks of `comm`:
+    """RRQR of a [m, n] F32/F64 matrix whose rows are split across the ranks of a group:
     this rank holds rows [row0, row0 + local_rows) as the column-major block `work`
     (a flat CUDA tensor of local_rows * n elements, or a 2-D tensor whose transpose is
-    contiguous).  run() does `steps` steps of the reference loop with two NCCL
-    all-gathers per step (t4a_dist_rrqr); perm, coeff, pivots and status come out
-    identical on every rank, and a world of one gives t4a_rrqr's bits."""
+    contiguous).  run() does `steps` steps of the reference loop.  exchange="p2p"
+    (t4a_dist_rrqr_p2p): two launches per step, whose column pass stores each column's
+    parts into every rank's memory over NVLink and waits on per-column flags;
+    exchange="nccl" (t4a_dist_rrqr): three launches and two NCCL all-gathers per step.  Both give the same bits; perm, coeff, pivots and status come
+    out identical on every rank, and a world of one gives t4a_rrqr's bits."""
 
-    def __init__(self, work, m, n, row0, steps, comm=None, group=None):
+    def __init__(self, work, m, n, row0, steps, comm=None, group=None, exchange="p2p"):
+        if exchange not in ("p2p", "nccl"):
+            raise ValueError(f"exchange {exchange!r}")
         flat = work.reshape(-1) if work.dim() == 1 else work.t().reshape(-1)
         self.work = flat
         self.m, self.n, self.row0, self.steps = m, n, row0, steps
+        self.exchange = exchange
         self.rows = flat.numel() // n if n else 0
         self.dtype = _t4.torch_dtype_tag(flat)
-        self.comm = comm if comm is not None else NcclComm(group)
-        self.own_comm = comm is None
+        if comm is None:
+            comm = P2pComm(n, group) if exchange == "p2p" else NcclComm(group)
+            self.own_comm = True
+        else:
+            self.own_comm = False
+        self.comm = comm
         self.layout = _abi.layout([self.rows, n], [1, max(self.rows, 1)])
-        nbytes = ctypes.c_size_t(0)
-        _t4.check(_t4.lib().t4a_dist_rrqr_workspace_bytes(self.dtype, n, self.comm.world, ctypes.byref(nbytes)),
-                  "dist_rrqr_workspace_bytes")
-        self.workspace = torch.empty(max(nbytes.value, 16), dtype=torch.uint8, device=flat.device)
         trailing_steps = sum(1 for s in range(steps) if n - s - 1 > 0)
-        self.launches = 2 + steps + 2 * trailing_steps  # kernels; NCCL calls: 1 + 2 per step with trailing columns
+        if exchange == "nccl":
+            nbytes = ctypes.c_size_t(0)
+            _t4.check(_t4.lib().t4a_dist_rrqr_workspace_bytes(self.dtype, n, self.comm.world, ctypes.byref(nbytes)),
+                      "dist_rrqr_workspace_bytes")
+            self.workspace = torch.empty(max(nbytes.value, 16), dtype=torch.uint8, device=flat.device)
+            self.launches = 2 + steps + 2 * trailing_steps  # NCCL calls besides: 1 + 2 per step with trailing columns
+        else:
+            self.workspace = None
+            self.launches = 3 + steps + trailing_steps if steps else 1  # init, first, swap + column per step, leave
 
     def run(self, stream_handle, perm, coeff, pivots, status):
+        if self.exchange == "p2p":
+            _t4.check(_t4.lib().t4a_dist_rrqr_p2p(self.comm.handle, stream_handle, self.dtype, _ptr(self.work),
+                                                  ctypes.byref(self.layout), self.work.numel(), self.row0, self.m,
+                                                  self.steps, _ptr(perm), _ptr(coeff), _ptr(pivots), _ptr(status)),
+                      "dist_rrqr_p2p")
+            return
         _t4.check(_t4.lib().t4a_dist_rrqr(self.comm.handle, stream_handle, self.dtype, _ptr(self.work),
                                           ctypes.byref(self.layout), self.work.numel(), self.row0, self.m, self.steps,
                                           _ptr(perm), _ptr(coeff), _ptr(pivots), _ptr(status),
