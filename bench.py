@@ -33,8 +33,9 @@ global problem stays the same):
               (so both sides stream long runs), each written from the strided view of
               the (replicated) source that feeds it;
   gather      index batches, table replicated;
-  scatter_add update batches into per-rank partial destinations, then an NCCL
-              reduce-scatter of the partials inside the timed op;
+  scatter_add destination rows, cyclic (row r on rank r mod N; owner computes): every
+              rank holds the whole index list and the updates, and applies the updates
+              whose row it owns (t4a_scatter_add_cyclic), so no collective is needed;
   RRQR        row blocks, with the per-step exchange of column norms and reflector dots
               fused into the step kernels (stores into every rank's memory over NVLink).
 Before timing, every rank checks its shard against the single-GPU result of the same
@@ -541,9 +542,13 @@ class GatherScatterConfig(Config):
     output + gathered rows + indices; scatter = updates + indices + destination read
     and write.
 
-    Sharding: index batches (rows shard_range of the 4M); the table is replicated.
-    scatter_add adds each rank's batch into its full-size partial destination, then one
-    NCCL reduce-scatter inside the timed op leaves each rank 1/N of the rows."""
+    Sharding: gather by index batches (rows shard_range of the 4M), the table
+    replicated; scatter_add by destination rows, cyclically (row r on rank r mod N, so
+    the Zipf-hot low rows spread over the ranks; contiguous slabs would give rank 0 about
+    98% of the updates), every rank holding the whole index list and the updates and
+    applying, with t4a_scatter_add_cyclic, only the updates whose row it owns.  Each
+    rank then reads the indices and its rows' update rows, and no collective is
+    needed."""
 
     name = "gather"
     ROWS, COLS, N = 1 << 20, 128, 1 << 22
@@ -561,10 +566,12 @@ class GatherScatterConfig(Config):
         self.keep("table", table)
         gidx_full = gen_rows_uniform(7, N, R, gdev)
         self.keep("gidx", gidx_full[lo:hi].contiguous())
-        upd = gen_normal(8, n * C, torch.float64, gdev, start=lo * C).reshape(n, C)
+        # scatter_add is sharded by destination rows (owner computes): every rank holds the
+        # whole index list and every update row, and applies the updates of its own rows
+        upd = gen_normal(8, N * C, torch.float64, gdev).reshape(N, C)
         sidx_full = gen_rows_zipf(9, N, R, 1.1, gdev)
         self.keep("upd", upd)
-        self.keep("sidx", sidx_full[lo:hi].contiguous())
+        self.keep("sidx", sidx_full)
         self.sharded = self.world > 1
         self.gplan = abi.gather_plan([0], [0], [1], [C, 1], 1, 2)
         self.splan = abi.scatter_plan([0], [0], [1], 1, 2, 2)
@@ -572,12 +579,13 @@ class GatherScatterConfig(Config):
         if not self.host_only:
             d = self.dev
             d["gout"] = torch.empty((n, C), dtype=torch.float32, device=self.device)
-            d["dest"] = torch.zeros((R, C), dtype=torch.float64, device=self.device)  # the partial when sharded
-            self.ws_bytes = t4.scatter_add_workspace_bytes(abi.F64, abi.I64, abi.numpy_layout([R, C]),
-                                                           abi.layout([n, 1]), abi.numpy_layout([n, C]), self.splan)
-            self.ws = torch.empty(max(self.ws_bytes, 16), dtype=torch.uint8, device=self.device)
             if self.sharded:
-                d["shard_out"] = torch.empty((own, C), dtype=torch.float64, device=self.device)
+                d["shard_out"] = torch.zeros((own, C), dtype=torch.float64, device=self.device)
+            else:
+                d["dest"] = torch.zeros((R, C), dtype=torch.float64, device=self.device)
+            self.ws_bytes = t4.scatter_add_workspace_bytes(abi.F64, abi.I64, abi.numpy_layout([R, C]),
+                                                           abi.layout([N, 1]), abi.numpy_layout([N, C]), self.splan)
+            self.ws = torch.empty(max(self.ws_bytes, 16), dtype=torch.uint8, device=self.device)
             # single-GPU results of the whole ops (this rank's rows)
             full_gout = torch.empty((N, C), dtype=torch.float32, device=self.device)
             t4.gather_raw(t4.stream_handle(), abi.F32, abi.I64, vp(full_gout), abi.numpy_layout([N, C]), N * C,
@@ -589,7 +597,7 @@ class GatherScatterConfig(Config):
             full_dest = torch.zeros((R, C), dtype=torch.float64, device=self.device)
             d_sidx = sidx_full.to(self.device)
             t4.scatter_add_rows(full_dest, d_sidx, full_upd)
-            rows = slice(self.rank * own, (self.rank + 1) * own)
+            rows = slice(self.rank, R, self.world)  # this rank's rows (cyclic ownership)
             self.expect["dest"] = full_dest[rows].clone()
             # Two summation orders of the same n terms differ by at most 2 (n - 1) u sum|x|
             # (u = 2^-53, recursive summation): the per-element bound for the check.
@@ -604,8 +612,10 @@ class GatherScatterConfig(Config):
             dict(tag="gather-f32-4Mx128-of-1Mx128", config=4, kind="gather", launches=1,
                  bytes=N * C * 4 * 2 + N * 8, local_bytes=n * C * 4 * 2 + n * 8,
                  inputs=["table", "gidx"], outputs=["gout"]),
-            dict(tag="scatter-add-f64-4Mx128-zipf-into-1Mx128", config=4, kind="scatter", launches=2,
-                 bytes=N * C * 8 + N * 8 + 2 * R * C * 8, local_bytes=n * C * 8 + n * 8 + 2 * R * C * 8,
+            dict(tag="scatter-add-f64-4Mx128-zipf-into-1Mx128", config=4, kind="scatter",
+                 launches=3 if self.sharded else 2,
+                 bytes=N * C * 8 + N * 8 + 2 * R * C * 8,
+                 local_bytes=N * C * 8 // self.world + N * 8 + 2 * own * C * 8,
                  inputs=["sidx", "upd"], outputs=["shard_out" if self.sharded else "dest"]),
         ]
         if self.sharded:
@@ -623,12 +633,18 @@ class GatherScatterConfig(Config):
                 t4.gather_raw(sh, abi.F32, abi.I64, vp(d["gout"]), abi.numpy_layout([n, C]), n * C, vp(d["table"]),
                               abi.numpy_layout([R, C]), R * C, vp(d["gidx"]), abi.layout([n, 1]), n, self.gplan)
                 return
-            t4.scatter_add_raw(sh, abi.F64, abi.I64, vp(d["dest"]), abi.numpy_layout([R, C]), R * C, vp(d["sidx"]),
-                               abi.layout([n, 1]), n, vp(d["upd"]), abi.numpy_layout([n, C]), n * C, self.splan,
-                               vp(self.ws), self.ws_bytes)
+            N = self.N
             if self.sharded:
-                import torch.distributed as tdist
-                tdist.reduce_scatter_tensor(d["shard_out"], d["dest"], op=tdist.ReduceOp.SUM)
+                # this rank's destination rows (r % world == rank), from the whole index list
+                t4.check(t4.lib().t4a_scatter_add_cyclic(
+                    sh, abi.F64, abi.I64, vp(d["shard_out"]), ctypes.byref(abi.numpy_layout([R, C])), R * C, C,
+                    self.world, self.rank, vp(d["sidx"]), ctypes.byref(abi.layout([N, 1])), N, vp(d["upd"]),
+                    ctypes.byref(abi.numpy_layout([N, C])), N * C, self.splan, vp(self.ws), self.ws_bytes),
+                    "scatter_add_cyclic")
+                return
+            t4.scatter_add_raw(sh, abi.F64, abi.I64, vp(d["dest"]), abi.numpy_layout([R, C]), R * C, vp(d["sidx"]),
+                               abi.layout([N, 1]), N, vp(d["upd"]), abi.numpy_layout([N, C]), N * C, self.splan,
+                               vp(self.ws), self.ws_bytes)
         return run
 
     def _cpu(self, op):
@@ -667,8 +683,8 @@ class GatherScatterConfig(Config):
             raise CheckFailed(f"scatter_add status {status}: a bounded wait of the fold ran out")
 
     def reset_scatter(self):
-        """Untimed: the destination (rank 0) or partial (others) back to zeros."""
-        self.dev["dest"].zero_()
+        """Untimed: the destination (or this rank's rows of it) back to zeros."""
+        self.dev["shard_out" if self.sharded else "dest"].zero_()
 
     def check(self):
         import torch

@@ -311,6 +311,37 @@ int t4a_scatter_add(void* stream, int dtype, int index_dtype, void* out, const t
                     long long updates_len, const t4a_cuda_scatter_plan* plan, void* workspace,
                     size_t workspace_bytes);
 
+/* No counterpart in the reference: t4a_scatter_add restricted to the elements
+ * [range_begin, range_end) of the destination, for owner-computes sharding (each GPU
+ * holds a slice of the destination and applies, from the whole index list, only the
+ * updates that land in its slice).  out_layout describes the whole destination, which
+ * must be compact (element e at offset e, layout offset 0); `out` holds elements
+ * [range_begin, range_end) (out[0] is element range_begin).  Elements outside the range
+ * are neither read nor written, and update rows whose destination lies outside it are
+ * not read.  Each contiguous run of an update window must cover whole leading
+ * destination axes and both ends must be multiples of it (e.g. whole rows for a scatter
+ * of rows), otherwise T4A_ERR_SHAPE_MISMATCH.  Two kernels over a caller workspace of
+ * t4a_scatter_add_workspace_bytes (required); its leading status word is 1 when a
+ * bounded wait ran out.  Results equal t4a_scatter_add's on the range up to the order
+ * of floating additions. */
+int t4a_scatter_add_range(void* stream, int dtype, int index_dtype, void* out, const t4a_cuda_layout* out_layout,
+                          long long out_len, long long range_begin, long long range_end, const void* indices,
+                          const t4a_cuda_layout* indices_layout, long long indices_len, const void* updates,
+                          const t4a_cuda_layout* updates_layout, long long updates_len,
+                          const t4a_cuda_scatter_plan* plan, void* workspace, size_t workspace_bytes);
+
+/* The same with block-cyclic ownership: the destination's elements form blocks of
+ * `block` elements, block b belongs to owner b % owners, and `out` holds this owner's
+ * blocks back to back in block order (for a scatter of rows: rows r with
+ * r % owners == owner, out row k = row k * owners + owner).  `block` must be a multiple
+ * of each contiguous run of an update window.  Cyclic ownership spreads skewed (e.g.
+ * Zipf) destination rows evenly across owners, where contiguous slabs would not. */
+int t4a_scatter_add_cyclic(void* stream, int dtype, int index_dtype, void* out, const t4a_cuda_layout* out_layout,
+                           long long out_len, long long block, long long owners, long long owner, const void* indices,
+                           const t4a_cuda_layout* indices_layout, long long indices_len, const void* updates,
+                           const t4a_cuda_layout* updates_layout, long long updates_len,
+                           const t4a_cuda_scatter_plan* plan, void* workspace, size_t workspace_bytes);
+
 /* General-rank gather / scatter_add, the `_any` twins (reference
  * cuda/src/gather_scatter.cu:587, :619; module symbols t4a_cuda_gather_any and
  * t4a_cuda_scatter_add_any in gather_scatter.cubin): element-wise walks over layouts

@@ -580,10 +580,35 @@ constexpr int kGroupPer = kGroupChunk / kGroupThreads;
 // Pass 1: the grouped list of every chunk, in chunk order (one entry per piece).
 // Each thread keeps its kGroupPer pieces in registers and writes them straight to
 // their grouped positions.  Block of kGroupThreads.
-template <typename I, int V>
+//
+// The part of a destination one caller holds, in bytes of the whole destination:
+// block == 0: the span [lo, hi), held from its first byte;
+// block > 0:  the blocks b (bytes [b block, (b + 1) block)) with b % owners == owner,
+//             held back to back in block order (block-cyclic ownership).
+struct OwnedPart {
+  long long lo, hi;
+  long long block, owners, owner;
+};
+
+// Offset within the held part of destination byte `at`, or -1 when another part holds it.
+__host__ __device__ __forceinline__ long long owned_offset(const OwnedPart& o, long long at) {
+  if (o.block == 0) return at >= o.lo && at < o.hi ? at - o.lo : -1;
+  const long long b = at / o.block;
+  if (b % o.owners != o.owner) return -1;
+  return (b / o.owners) * o.block + (at - b * o.block);
+}
+
+// kRange: only pieces whose destination bytes lie in the part `own` holds are listed,
+// with the offset taken within that part; each chunk reserves its slice of the list
+// with one atomic on *reserve (so the list holds the kept pieces only, chunk by chunk, in
+// the order the chunks reserved), and *reserve ends as the list's length.
+template <typename I, int V, bool kRange = false>
 __device__ __forceinline__ void scatter_group_pass(const WindowPlan& p, const I* __restrict__ idx, long long units,
                                                    long long nvec, GroupedPiece* __restrict__ list,
-                                                   GroupTable<kGroupChunk>& t) {
+                                                   GroupTable<kGroupChunk>& t, OwnedPart own = OwnedPart{},
+                                                   unsigned long long* reserve = nullptr) {
+  __shared__ unsigned kept;
+  __shared__ unsigned long long base;
   const ScatterShape sh = scatter_shape(nvec);
   const long long total = units * sh.piece.count;
   const int tid = threadIdx.x;
@@ -591,6 +616,7 @@ __device__ __forceinline__ void scatter_group_pass(const WindowPlan& p, const I*
        c0 += static_cast<long long>(gridDim.x) * kGroupChunk) {
     const int n = total - c0 < kGroupChunk ? static_cast<int>(total - c0) : kGroupChunk;
     clear_table(t, tid, kGroupThreads);
+    if (kRange && tid == 0) kept = 0;
     __syncthreads();
     long long dflag[kGroupPer], src[kGroupPer];
     unsigned long long key[kGroupPer];
@@ -603,6 +629,10 @@ __device__ __forceinline__ void scatter_group_pass(const WindowPlan& p, const I*
       dflag[q] = -1;
       src[q] = 0;
       if (i < n) piece_offsets<I, V>(p, idx, c0 + i, sh, &dflag[q], &src[q]);
+      if (kRange && dflag[q] >= 0) {
+        const long long local = owned_offset(own, dflag[q] & ~1ll);
+        dflag[q] = local >= 0 ? local | (dflag[q] & 1) : -1;
+      }
       key[q] = dflag[q] >= 0 ? key_of(dflag[q], V) : kEmptySlot;
       slot[q] = __umulhi(static_cast<unsigned>((key[q] * 0x9E3779B97F4A7C15ull) >> 32), GroupTable<kGroupChunk>::H);
     }
@@ -613,18 +643,28 @@ __device__ __forceinline__ void scatter_group_pass(const WindowPlan& p, const I*
 #pragma unroll
     for (int q = 0; q < kGroupPer; ++q)
       if (prev[q] != kEmptySlot && prev[q] != key[q]) slot[q] = find_slot(t, key[q]);  // occupied by another key
+    unsigned mine = 0;
 #pragma unroll
     for (int q = 0; q < kGroupPer; ++q)
-      if (key[q] != kEmptySlot) rank[q] = atomicAdd(&t.count[slot[q]], 1u);
+      if (key[q] != kEmptySlot) {
+        rank[q] = atomicAdd(&t.count[slot[q]], 1u);
+        ++mine;
+      }
+    if (kRange && mine) atomicAdd(&kept, mine);
     __syncthreads();
     scan_counts(t, tid, kGroupThreads);
+    if (kRange) {
+      if (tid == 0) base = kept ? atomicAdd(reserve, static_cast<unsigned long long>(kept)) : 0;
+      __syncthreads();
+    }
+    const long long first = kRange ? static_cast<long long>(base) : c0;
 #pragma unroll
     for (int q = 0; q < kGroupPer; ++q) {
       if (dflag[q] >= 0) {
         GroupedPiece g;
         g.dflag = dflag[q];
         g.src = src[q];
-        list[c0 + t.count[slot[q]] + rank[q]] = g;
+        list[first + t.count[slot[q]] + rank[q]] = g;
       }
     }
     __syncthreads();

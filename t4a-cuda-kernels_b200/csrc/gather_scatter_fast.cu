@@ -67,6 +67,37 @@ __global__ void __launch_bounds__(kFoldThreads, kFoldBlocksPerSm) k_scatter_fold
                           static_cast<const unsigned char*>(updates), stage);
 }
 
+// The owned-part scatter (t4a_scatter_add_range, t4a_scatter_add_cyclic): pass 1 lists
+// only the pieces whose destination lies in the part this caller holds (OwnedPart),
+// with offsets within that part, reserving each chunk's slice of the list on the counter
+// at `reserve`; pass 2 folds the list's *count entries into `out`, which holds the part.
+template <typename I, int V>
+__global__ void __launch_bounds__(kGroupThreads, 2) k_scatter_group_range(WindowPlan p, const void* indices,
+                                                                          long long units, long long nvec,
+                                                                          GroupedPiece* list, int* status,
+                                                                          OwnedPart own, unsigned long long* reserve) {
+  __shared__ GroupTable<kGroupChunk> t;
+  if (blockIdx.x == 0 && threadIdx.x == 0) *status = 0;
+  scatter_group_pass<I, V, true>(p, static_cast<const I*>(indices), units, nvec, list, t, own, reserve);
+}
+
+template <typename F>
+__global__ void __launch_bounds__(kFoldThreads, kFoldBlocksPerSm) k_scatter_fold_bulk_counted(
+    const GroupedPiece* list, const unsigned long long* count, long long nvec, void* out, const void* updates,
+    int* status) {
+  extern __shared__ __align__(16) unsigned char stage[];
+  scatter_fold_bulk<F>(list, static_cast<long long>(*count), nvec, static_cast<unsigned char*>(out),
+                       static_cast<const unsigned char*>(updates), stage, status);
+}
+
+template <typename F, int V>
+__global__ void __launch_bounds__(kFoldThreads, kFoldBlocksPerSm) k_scatter_fold_counted(
+    const GroupedPiece* list, const unsigned long long* count, long long nvec, void* out, const void* updates) {
+  extern __shared__ __align__(16) unsigned char stage[];
+  scatter_fold_pass<F, V>(list, static_cast<long long>(*count), nvec, static_cast<unsigned char*>(out),
+                          static_cast<const unsigned char*>(updates), stage);
+}
+
 constexpr int kGatherVariant = 48;
 constexpr int kScatterVariant = 49;
 constexpr unsigned long long kResidentBlocks = 148ull * 8;  // grid cap: a few waves of resident blocks
@@ -301,6 +332,55 @@ void launch_scatter_width(const WindowPlan& p, dim3 grid, cudaStream_t s, void* 
   }
 }
 
+// The range-filtered two-kernel scatter (workspace: the status word and the list
+// counter in its first 16 bytes, then the list).
+template <typename F, typename I, int V>
+int launch_scatter_range_width(const WindowPlan& p, cudaStream_t s, void* out, const void* indices,
+                               const void* updates, long long units, long long nvec, void* workspace,
+                               const OwnedPart& own) {
+  const ScatterShape sh = scatter_shape(nvec);
+  const long long total = units * sh.piece.count;
+  int* status = static_cast<int*>(workspace);
+  auto* count = reinterpret_cast<unsigned long long*>(static_cast<unsigned char*>(workspace) + 8);
+  auto* list = reinterpret_cast<GroupedPiece*>(static_cast<unsigned char*>(workspace) + kScatterStatusBytes);
+  if (cudaMemsetAsync(count, 0, sizeof(*count), s) != cudaSuccess) return runtime::check_launch();
+  unsigned long long gg = plan::ceil_div(static_cast<unsigned long long>(total), kGroupChunk);
+  if (gg > 148ull * 8) gg = 148ull * 8;
+  if (gg == 0) gg = 1;
+  k_scatter_group_range<I, V><<<dim3(static_cast<unsigned>(gg)), dim3(kGroupThreads), 0, s>>>(
+      p, indices, units, nvec, list, status, own, count);
+  const dim3 fgrid(148 * kFoldBlocksPerSm);
+  if constexpr (V == 16) {
+    const unsigned smem = (kFoldThreads / 32) * bulk_stage_bytes_per_warp();
+    static std::atomic<unsigned long long> raised{0};
+    T4A_TRY(allow_dynamic_smem(k_scatter_fold_bulk_counted<F>, smem, raised));
+    k_scatter_fold_bulk_counted<F><<<fgrid, dim3(kFoldThreads), smem, s>>>(list, count, nvec, out, updates, status);
+  } else {
+    const unsigned smem = (kFoldThreads / 32) * fold_stage_bytes_per_warp(V);
+    static std::atomic<unsigned long long> raised{0};
+    T4A_TRY(allow_dynamic_smem(k_scatter_fold_counted<F, V>, smem, raised));
+    k_scatter_fold_counted<F, V><<<fgrid, dim3(kFoldThreads), smem, s>>>(list, count, nvec, out, updates);
+  }
+  return runtime::check_launch();
+}
+
+template <typename F, typename I>
+int launch_scatter_range_typed(const WindowPlan& p, cudaStream_t s, void* out, const void* indices,
+                               const void* updates, void* workspace, const OwnedPart& own) {
+  const long long units = p.batch.len * p.wrest.len;
+  // Vector width from the alignment of the part's base and of its offsets (its start
+  // byte, or its block size) and of the updates.
+  const unsigned long long part = static_cast<unsigned long long>(own.block == 0 ? own.lo : own.block);
+  const int v = window_vec_bytes(p, reinterpret_cast<unsigned long long>(out) | part,
+                                 reinterpret_cast<unsigned long long>(updates));
+  const long long nvec = p.run * p.esize / v;
+  if (v >= 16) return launch_scatter_range_width<F, I, 16>(p, s, out, indices, updates, units, nvec, workspace, own);
+  if (v == 8) return launch_scatter_range_width<F, I, 8>(p, s, out, indices, updates, units, nvec, workspace, own);
+  if constexpr (sizeof(F) == 4)
+    return launch_scatter_range_width<F, I, 4>(p, s, out, indices, updates, units, nvec, workspace, own);
+  return T4A_ERR_UNSUPPORTED_DTYPE;
+}
+
 template <typename F, typename I>
 int launch_scatter_typed(const WindowPlan& p, dim3 grid, cudaStream_t s, void* out, const void* indices,
                          const void* updates, void* workspace) {
@@ -500,6 +580,104 @@ int t4a_scatter_add(void* stream, int dtype, int index_dtype, void* out, const t
   }
   return scatter_launch(&l, stream, out, indices, updates, dtype, index_dtype, out_layout, indices_layout,
                         updates_layout, plan, update_count, workspace);
+}
+
+}  // extern "C"
+
+namespace {
+
+// The owned-part scatter behind t4a_scatter_add_range and t4a_scatter_add_cyclic: `part`
+// in elements of the whole destination (block == 0: [lo, hi); else block-cyclic).
+int scatter_owned(void* stream, int dtype, int index_dtype, void* out, const t4a_cuda_layout* out_layout,
+                  long long out_len, OwnedPart part, const void* indices, const t4a_cuda_layout* indices_layout,
+                  long long indices_len, const void* updates, const t4a_cuda_layout* updates_layout,
+                  long long updates_len, const t4a_cuda_scatter_plan* plan, void* workspace, size_t workspace_bytes) {
+  t4a_launch l;
+  T4A_TRY(t4a_plan_scatter_add(dtype, index_dtype, out_layout, out_len, indices_layout, indices_len, updates_layout,
+                               updates_len, plan, &l));
+  if (workspace == nullptr) return T4A_ERR_WORKSPACE;
+  size_t need = 0;
+  T4A_TRY(scatter_list_bytes(dtype, *out_layout, *indices_layout, *updates_layout, *plan, &need));
+  if (workspace_bytes < need || workspace_bytes < kScatterStatusBytes) return T4A_ERR_WORKSPACE;
+  // The whole destination must be compact (element e at offset e), so that a part is a
+  // set of contiguous spans.
+  long long count = 0;
+  T4A_TRY(element_count(*out_layout, &count));
+  long long expect = 1;
+  for (int d = 0; d < out_layout->rank; ++d) {
+    if (out_layout->extents[d] != 1 && out_layout->strides[d] != expect) return T4A_ERR_INVALID_STRIDE;
+    expect *= out_layout->extents[d];
+  }
+  if (out_layout->offset != 0) return T4A_ERR_INVALID_STRIDE;
+  if (part.block == 0) {
+    if (part.lo < 0 || part.hi < part.lo || part.hi > count) return T4A_ERR_SHAPE_MISMATCH;
+  } else if (part.block < 0 || part.owners < 1 || part.owner < 0 || part.owner >= part.owners) {
+    return T4A_ERR_SHAPE_MISMATCH;
+  }
+  const int es = dtype_size(dtype);
+  if (reinterpret_cast<unsigned long long>(workspace) % 16 != 0) return T4A_ERR_INVALID_STRIDE;
+  if (out == nullptr || indices == nullptr || updates == nullptr) return T4A_ERR_NULL_ARGUMENT;
+  if (reinterpret_cast<unsigned long long>(out) % es != 0) return T4A_ERR_INVALID_STRIDE;
+  if (l.grid[0] == 0 || (part.block == 0 && part.lo == part.hi)) return T4A_OK;
+  if (!scatter_maps_ok(*out_layout, *indices_layout, *updates_layout, *plan)) return T4A_ERR_INVALID_AXIS;
+  const WindowPlan p = make_scatter_plan(*out_layout, *indices_layout, *updates_layout, *plan, es);
+  if (p.run <= 0 || p.batch.len * p.wrest.len <= 0 || !scatter_windows_fit(p)) return T4A_OK;
+  // Every contiguous run of an update window must lie inside one held span: the run
+  // covers whole leading destination axes (so runs start at multiples of it), and the
+  // span ends (or the block size) are multiples of it.
+  long long lead = 1;
+  int d = 0;
+  while (d < out_layout->rank && lead < p.run) lead *= out_layout->extents[d++];
+  if (lead != p.run) return T4A_ERR_SHAPE_MISMATCH;
+  if (part.block == 0 ? (part.lo % p.run != 0 || part.hi % p.run != 0) : part.block % p.run != 0)
+    return T4A_ERR_SHAPE_MISMATCH;
+  OwnedPart own = part;  // in bytes
+  own.lo *= es;
+  own.hi *= es;
+  own.block *= es;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+#define T4A_OWNED_INDEX(F)                                                                                     \
+  switch (index_dtype) {                                                                                       \
+    case T4A_CUDA_F32: return launch_scatter_range_typed<F, float>(p, s, out, indices, updates, workspace, own); \
+    case T4A_CUDA_F64: return launch_scatter_range_typed<F, double>(p, s, out, indices, updates, workspace, own); \
+    case T4A_CUDA_I32: return launch_scatter_range_typed<F, int>(p, s, out, indices, updates, workspace, own);   \
+    case T4A_CUDA_I64:                                                                                         \
+      return launch_scatter_range_typed<F, long long>(p, s, out, indices, updates, workspace, own);            \
+    default: return T4A_ERR_UNSUPPORTED_DTYPE;                                                                 \
+  }
+  switch (dtype) {
+    case T4A_CUDA_F32:
+    case T4A_CUDA_C32: T4A_OWNED_INDEX(float)
+    case T4A_CUDA_F64:
+    case T4A_CUDA_C64: T4A_OWNED_INDEX(double)
+    default: return T4A_ERR_UNSUPPORTED_DTYPE;
+  }
+#undef T4A_OWNED_INDEX
+}
+
+}  // namespace
+
+extern "C" {
+
+int t4a_scatter_add_range(void* stream, int dtype, int index_dtype, void* out, const t4a_cuda_layout* out_layout,
+                          long long out_len, long long range_begin, long long range_end, const void* indices,
+                          const t4a_cuda_layout* indices_layout, long long indices_len, const void* updates,
+                          const t4a_cuda_layout* updates_layout, long long updates_len,
+                          const t4a_cuda_scatter_plan* plan, void* workspace, size_t workspace_bytes) {
+  return scatter_owned(stream, dtype, index_dtype, out, out_layout, out_len, OwnedPart{range_begin, range_end, 0, 1, 0},
+                       indices, indices_layout, indices_len, updates, updates_layout, updates_len, plan, workspace,
+                       workspace_bytes);
+}
+
+int t4a_scatter_add_cyclic(void* stream, int dtype, int index_dtype, void* out, const t4a_cuda_layout* out_layout,
+                           long long out_len, long long block, long long owners, long long owner, const void* indices,
+                           const t4a_cuda_layout* indices_layout, long long indices_len, const void* updates,
+                           const t4a_cuda_layout* updates_layout, long long updates_len,
+                           const t4a_cuda_scatter_plan* plan, void* workspace, size_t workspace_bytes) {
+  if (block <= 0) return T4A_ERR_SHAPE_MISMATCH;
+  return scatter_owned(stream, dtype, index_dtype, out, out_layout, out_len, OwnedPart{0, 0, block, owners, owner},
+                       indices, indices_layout, indices_len, updates, updates_layout, updates_len, plan, workspace,
+                       workspace_bytes);
 }
 
 }  // extern "C"

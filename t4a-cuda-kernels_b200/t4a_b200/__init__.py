@@ -138,6 +138,10 @@ def _declare(l):
         "t4a_plan_identity_shifted": (I, [I, LP, LL, LL, ctypes.POINTER(Launch)]),
         "t4a_launch_identity_shifted": (I, [ctypes.POINTER(Launch), P, P, I, LB, LL]),
         "t4a_scatter_add": (I, [P, I, I, P, LP, LL, P, LP, LL, P, LP, LL, ctypes.POINTER(abi.ScatterPlan), P, SZ]),
+        "t4a_scatter_add_range": (I, [P, I, I, P, LP, LL, LL, LL, P, LP, LL, P, LP, LL,
+                                      ctypes.POINTER(abi.ScatterPlan), P, SZ]),
+        "t4a_scatter_add_cyclic": (I, [P, I, I, P, LP, LL, LL, LL, LL, P, LP, LL, P, LP, LL,
+                                       ctypes.POINTER(abi.ScatterPlan), P, SZ]),
         "t4a_scatter_add_workspace_bytes": (I, [I, I, LP, LP, LP, ctypes.POINTER(abi.ScatterPlan),
                                                 ctypes.POINTER(SZ)]),
     }
@@ -472,6 +476,40 @@ def scatter_add_rows(dest, indices, updates, workspace=None, stream=None):
                     tensor_layout(dest), span(dest), _ptr(indices), abi.layout([n, 1]), n, _ptr(updates),
                     tensor_layout(updates), span(updates), plan, ws, nbytes)
     return dest
+
+
+def scatter_add_rows_range(shard, rows, row0, indices, updates, workspace, stream=None):
+    """Rows [row0, row0 + shard_rows) of a row-major destination [rows, cols] scatter,
+    held by the CUDA tensor `shard` [shard_rows, cols]: shard[clamp(indices[i]) - row0, :]
+    += updates[i, :] for the updates whose clamped row falls in the slice
+    (t4a_scatter_add_range).  `workspace`: scatter_rows_workspace of the whole scatter."""
+    n, cols = updates.shape
+    plan = abi.scatter_plan([0], [0], [1], 1, 2, 2)
+    full = abi.layout([cols, rows], [1, cols])
+    begin = row0 * cols
+    check(lib().t4a_scatter_add_range(stream_handle(stream), torch_dtype_tag(shard), torch_dtype_tag(indices),
+                                      _ptr(shard), ctypes.byref(full), rows * cols, begin,
+                                      begin + shard.shape[0] * cols, _ptr(indices), ctypes.byref(abi.layout([n, 1])),
+                                      n, _ptr(updates), ctypes.byref(tensor_layout(updates)), span(updates), plan,
+                                      _ptr(workspace), workspace.numel()), "scatter_add_range")
+    return shard
+
+
+def scatter_add_rows_cyclic(shard, rows, owners, owner, indices, updates, workspace, stream=None):
+    """Rows r of a row-major destination [rows, cols] with r % owners == owner, held by
+    the CUDA tensor `shard` (its row k is row k * owners + owner):
+    shard[(clamp(indices[i]) - owner) / owners, :] += updates[i, :] for the updates whose
+    clamped row this owner holds (t4a_scatter_add_cyclic).  `workspace`:
+    scatter_rows_workspace of the whole scatter."""
+    n, cols = updates.shape
+    plan = abi.scatter_plan([0], [0], [1], 1, 2, 2)
+    full = abi.layout([cols, rows], [1, cols])
+    check(lib().t4a_scatter_add_cyclic(stream_handle(stream), torch_dtype_tag(shard), torch_dtype_tag(indices),
+                                       _ptr(shard), ctypes.byref(full), rows * cols, cols, owners, owner,
+                                       _ptr(indices), ctypes.byref(abi.layout([n, 1])), n, _ptr(updates),
+                                       ctypes.byref(tensor_layout(updates)), span(updates), plan, _ptr(workspace),
+                                       workspace.numel()), "scatter_add_cyclic")
+    return shard
 
 
 def scatter_rows_workspace(dest, indices, updates):

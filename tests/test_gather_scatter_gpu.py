@@ -749,3 +749,74 @@ def test_any_twins_leave_malformed_maps_untouched(cuda, route):
     torch.cuda.synchronize()
     assert (take(dest, rows * cols * 8).view(np.float64) == 0).all()
     del k1, k2, k3, k4, k5, kg, ks, bad_plans
+
+
+@pytest.mark.parametrize("dtype,cols", [(abi.F64, 128), (abi.F32, 32), (abi.C64, 16), (abi.F64, 3)])
+def test_scatter_range_shards_tile_the_destination(cuda, dtype, cols):
+    """t4a_scatter_add_range (owner-computes sharding): three uneven row slices of a
+    row-major destination, each scattered into its own buffer from the whole index list,
+    together equal t4a_scatter_add over the whole destination within the bound on
+    reordering a sum of k terms, 2 (k - 1) u sum|x| per element (u the unit roundoff).
+    The indices include values below 0 and past the last row, which clamp."""
+    import torch
+    tdt = {abi.F64: torch.float64, abi.F32: torch.float32, abi.C64: torch.complex128}[dtype]
+    u = 2.0 ** -24 if dtype == abi.F32 else 2.0 ** -53
+    rng = np.random.default_rng(77 + dtype + cols)
+    rows, n = 5000, 60000
+    idx_np = zipf_rows(rng, n, rows + 20) - 10
+    idx = torch.from_numpy(idx_np.astype(np.int64)).cuda()
+    g = torch.Generator(device="cpu").manual_seed(5)
+    upd = torch.randn(n, cols, generator=g, dtype=tdt).cuda()
+    dest0 = torch.randn(rows, cols, generator=g, dtype=tdt).cuda()
+    whole = dest0.clone()
+    ws = t4.scatter_rows_workspace(whole, idx, upd)
+    t4.scatter_add_rows(whole, idx, upd, workspace=ws)
+    clamped = idx.clamp(0, rows - 1)
+    comp = (lambda t: torch.view_as_real(t)) if dtype == abi.C64 else (lambda t: t)
+    absum = comp(dest0).abs().clone().index_add_(0, clamped, comp(upd).abs())
+    count = torch.zeros(rows, dtype=torch.float64, device="cuda").index_add_(
+        0, clamped, torch.ones(n, dtype=torch.float64, device="cuda"))
+    shape = (rows,) + (1,) * (absum.dim() - 1)
+    bound = (2.0 * count * u).view(shape) * absum.double()
+    for r0, r1 in [(0, 1700), (1700, 1701), (1701, rows)]:
+        shard = dest0[r0:r1].clone()
+        ws2 = t4.scatter_rows_workspace(whole, idx, upd)
+        t4.scatter_add_rows_range(shard, rows, r0, idx, upd, ws2)
+        torch.cuda.synchronize()
+        assert int(ws2[:4].view(torch.int32).item()) == 0
+        err = (comp(shard) - comp(whole[r0:r1])).abs().double()
+        assert bool((err <= bound[r0:r1]).all()), (r0, r1, float((err - bound[r0:r1]).max()))
+
+
+@pytest.mark.parametrize("dtype,cols", [(abi.F64, 128), (abi.F32, 32), (abi.C64, 16), (abi.F64, 3)])
+def test_scatter_cyclic_owners_tile_the_destination(cuda, dtype, cols):
+    """t4a_scatter_add_cyclic (block-cyclic owner-computes sharding, one row per block):
+    three owners, each scattering the whole index list into its rows r % 3 == owner,
+    together equal t4a_scatter_add over the whole destination within the reordering
+    bound.  The indices include values below 0 and past the last row, which clamp."""
+    import torch
+    tdt = {abi.F64: torch.float64, abi.F32: torch.float32, abi.C64: torch.complex128}[dtype]
+    u = 2.0 ** -24 if dtype == abi.F32 else 2.0 ** -53
+    rng = np.random.default_rng(88 + dtype + cols)
+    rows, n, owners = 5000, 60000, 3
+    idx = torch.from_numpy((zipf_rows(rng, n, rows + 20) - 10).astype(np.int64)).cuda()
+    g = torch.Generator(device="cpu").manual_seed(6)
+    upd = torch.randn(n, cols, generator=g, dtype=tdt).cuda()
+    dest0 = torch.randn(rows, cols, generator=g, dtype=tdt).cuda()
+    whole = dest0.clone()
+    t4.scatter_add_rows(whole, idx, upd, workspace=t4.scatter_rows_workspace(whole, idx, upd))
+    clamped = idx.clamp(0, rows - 1)
+    comp = (lambda t: torch.view_as_real(t)) if dtype == abi.C64 else (lambda t: t)
+    absum = comp(dest0).abs().clone().index_add_(0, clamped, comp(upd).abs())
+    count = torch.zeros(rows, dtype=torch.float64, device="cuda").index_add_(
+        0, clamped, torch.ones(n, dtype=torch.float64, device="cuda"))
+    bound = (2.0 * count * u).view((rows,) + (1,) * (absum.dim() - 1)) * absum.double()
+    for owner in range(owners):
+        shard = dest0[owner::owners].clone()
+        ws = t4.scatter_rows_workspace(whole, idx, upd)
+        t4.scatter_add_rows_cyclic(shard, rows, owners, owner, idx, upd, ws)
+        torch.cuda.synchronize()
+        assert int(ws[:4].view(torch.int32).item()) == 0
+        err = (comp(shard) - comp(whole[owner::owners])).abs().double()
+        assert bool((err <= bound[owner::owners]).all()), (owner, float((err - bound[owner::owners]).max()))
+

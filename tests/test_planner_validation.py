@@ -20,6 +20,8 @@ INVALID_TRANSPOSE_CONFIG = 12
 INVALID_AXIS = 13
 DUPLICATE_AXIS = 14
 SHAPE_MISMATCH = 16
+INVALID_STRIDE = 20
+WORKSPACE = 65
 NEGATIVE_COUNT = 4
 LAUNCH_LIMIT = 11
 
@@ -221,3 +223,27 @@ def test_engine_geometry_for_long_real_columns():
     assert refl.variant == 66 and refl.grid[0] == 1
     app = t4.plan_rrqr("apply_reflector", abi.F64, long_l, 4096 * 8, long_l, 4096 * 8, compact(8), 8, 0, 1, 7)
     assert app.variant == 66 and app.grid[0] == 7
+
+
+def test_scatter_range_refusals():
+    """t4a_scatter_add_range's host checks, before any device access: a range end that
+    cuts an update row, a range outside the destination, a destination that is not
+    compact, and a missing workspace."""
+    import ctypes
+    lib = t4.lib()
+    rows, cols, n = 100, 8, 10
+    plan = abi.scatter_plan([0], [0], [1], 1, 2, 2)
+    full = abi.layout([cols, rows], [1, cols])
+    il, ul = abi.layout([n, 1]), abi.layout([cols, n], [1, cols])
+    fake = ctypes.c_void_p(1 << 20)  # never dereferenced: every case is refused on the host
+
+    def call(layout, begin, end, ws=fake, ws_bytes=1 << 20, out_len=rows * cols):
+        return lib.t4a_scatter_add_range(None, abi.F64, abi.I64, fake, ctypes.byref(layout), out_len, begin, end,
+                                         fake, ctypes.byref(il), n, fake, ctypes.byref(ul), n * cols, plan, ws,
+                                         ws_bytes)
+
+    assert call(full, 8, 12) == SHAPE_MISMATCH  # 12 cuts a row of 8
+    assert call(full, 0, rows * cols + 8) == SHAPE_MISMATCH
+    assert call(full, 16, 8) == SHAPE_MISMATCH
+    assert call(abi.layout([cols, rows], [1, cols + 1]), 0, 8, out_len=rows * (cols + 1)) == INVALID_STRIDE
+    assert call(full, 0, 8, None, 0) == WORKSPACE
