@@ -51,8 +51,16 @@ __global__ void __launch_bounds__(256, kStagedBlocksPerSm) k_strided_staged(T* d
   }
 }
 
+// Resident blocks asked of the per-cube kernel: 16-byte elements (C64) load a whole
+// lane walk of 8 elements at once, so more resident warps keep more bytes in flight.
+template <typename T>
+struct CubesMinBlocks {
+  static constexpr int value = sizeof(T) >= 16 ? 3 : 1;
+};
+
 template <typename Op, typename T>
-__global__ void __launch_bounds__(256) k_cubes(T* dst, const T* in, t4a_cuda_layout dst_l, t4a_cuda_layout in_l,
+__global__ void __launch_bounds__(256, CubesMinBlocks<T>::value) k_cubes(T* dst, const T* in, t4a_cuda_layout dst_l,
+                                                                        t4a_cuda_layout in_l,
                                                int axis, long long outputs, long long splits, long long chunk,
                                                bool partials) {
   dependency_wait();
