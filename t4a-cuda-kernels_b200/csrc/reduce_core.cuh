@@ -478,15 +478,36 @@ __device__ __forceinline__ void strided_warp_staged(const T* __restrict__ in, T*
   for (long long u = gw; u < units; u += nw) {
     const StridedTile t = unit_of(u);
     Vec<T, V> acc[LPT];
-    for (int k = 0; k < t.nk; ++k) {
-      asm volatile("cp.async.wait_group %0;" ::"n"(D - 1) : "memory");
+    // The first stage seeds every accumulator: a tile holds at least 32 rows (the
+    // planner's condition for this pass), so each plane lane owns row lane0 + l.
+    // Peeling it keeps the seed-or-fold select out of the per-element loop.
+    asm volatile("cp.async.wait_group %0;" ::"n"(D - 1) : "memory");
 #pragma unroll
-      for (int l = 0; l < LPT; ++l) {
-        const long long row = t.start + static_cast<long long>(k) * W + lane0 + l;
-        if (row < t.end) {
+    for (int l = 0; l < LPT; ++l) {
+      const Vec<T, V> x = ring[(c_slot * LPT + l) * nthreads + tid];
+#pragma unroll
+      for (int v = 0; v < V; ++v) acc[l].v[v] = op.seed(x.v[v]);
+    }
+    c_slot = c_slot + 1 == D ? 0 : c_slot + 1;
+    issue();
+    for (int k = 1; k < t.nk; ++k) {
+      asm volatile("cp.async.wait_group %0;" ::"n"(D - 1) : "memory");
+      const long long row0 = t.start + static_cast<long long>(k) * W + lane0;
+      if (row0 + LPT <= t.end) {
+#pragma unroll
+        for (int l = 0; l < LPT; ++l) {
           const Vec<T, V> x = ring[(c_slot * LPT + l) * nthreads + tid];
 #pragma unroll
-          for (int v = 0; v < V; ++v) acc[l].v[v] = k == 0 ? op.seed(x.v[v]) : op.fold(acc[l].v[v], x.v[v]);
+          for (int v = 0; v < V; ++v) acc[l].v[v] = op.fold(acc[l].v[v], x.v[v]);
+        }
+      } else {
+#pragma unroll
+        for (int l = 0; l < LPT; ++l) {
+          if (row0 + l < t.end) {
+            const Vec<T, V> x = ring[(c_slot * LPT + l) * nthreads + tid];
+#pragma unroll
+            for (int v = 0; v < V; ++v) acc[l].v[v] = op.fold(acc[l].v[v], x.v[v]);
+          }
         }
       }
       c_slot = c_slot + 1 == D ? 0 : c_slot + 1;

@@ -233,10 +233,13 @@ void prefer_warp_rows(int dtype, const void* in, int* path, dim3* grid, dim3* bl
 }
 
 // A strided pass over 16-byte vectors with at least kStagedMinTiles tiles per resident
-// block runs the staged kernel on a grid of kStagedBlocksPerSm blocks per SM, each warp
-// walking many units, so that its copy ring runs ahead across unit boundaries; smaller
-// passes keep one tile per block.  The staged kernel needs every plane lane to own a
-// row: chunks of at least 32 rows.
+// block runs the staged kernel as a grid-stride walk, each warp walking many units, so
+// that its copy ring runs ahead across unit boundaries; smaller passes keep one tile per
+// block.  The staged kernel needs every plane lane to own a row: chunks of at least 32
+// rows.  The grid is 7/8 of kStagedBlocksPerSm blocks per SM: on config 3's 2.1 GB
+// passes 256-264 blocks ran 1.2-2.9 % faster than 296 (fewer copies queued at the
+// memory controllers, the same bytes), and config 1's 134 MB pass ran the same down to
+// 256 blocks.
 constexpr unsigned kStagedMinTiles = 1;
 void prefer_strided_staged(int dtype, int* path, dim3* grid, unsigned* smem, const PassArgs& a) {
   if (*path != kPathStrided || strided_vec_lanes(dtype) == 1) return;
@@ -244,7 +247,7 @@ void prefer_strided_staged(int dtype, int* path, dim3* grid, unsigned* smem, con
   if (shortest < 32) return;
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const unsigned cap = static_cast<unsigned>(sms * kStagedBlocksPerSm);
+  const unsigned cap = static_cast<unsigned>(sms * kStagedBlocksPerSm * 7 / 8);
   if (grid->x < kStagedMinTiles * cap) return;
   *path = kPathStridedStaged;
   grid->x = cap;
