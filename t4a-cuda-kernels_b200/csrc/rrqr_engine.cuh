@@ -63,6 +63,8 @@ constexpr unsigned kColSuspendNs = 1000;
 
 // scaled_norm's buffers: the ring's bytes viewed as kNormBufs buffers of kNormSeg elements.
 constexpr int kNormBufs = 6;
+// Largest thread-block cluster of the clustered column pass (the portable limit).
+constexpr int kMaxCluster = 8;
 
 template <typename F>
 struct ColSmem {
@@ -79,6 +81,8 @@ struct ColSmem {
   unsigned long long freed[kNormBufs];  // scaled_norm: buffer b folded by the chain warp
   F red[kColWarps];
   int bad[kColWarps];
+  F cpeak[kMaxCluster];  // clustered pass, leader: each rank's block peak and flag
+  int cbad[kMaxCluster];
   F dot;
   int abort;
   int last;  // this block drew the pass's last ticket
@@ -110,6 +114,52 @@ __device__ __forceinline__ void bar_arrive(unsigned long long* bar) {
 
 // Orders this thread's generic-proxy writes before later bulk copies (async proxy).
 __device__ __forceinline__ void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// ---- thread-block clusters (the clustered column pass) -------------------------------
+// This block's rank in its cluster (0 in a launch without clusters).
+__device__ __forceinline__ unsigned cluster_rank() {
+  unsigned r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Every thread of every block of the cluster: the writes before it (shared memory of
+// any block of the cluster, and global memory) are visible to the reads after it.  A
+// hardware barrier: each block of a cluster is resident until it exits, and every thread
+// of the clustered pass reaches each barrier exactly once.
+__device__ __forceinline__ void cluster_barrier() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// The shared::cluster address of `p` (this block's shared memory) in block `rank`.
+__device__ __forceinline__ unsigned cluster_addr(const void* p, unsigned rank) {
+  unsigned a;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_addr(p)), "r"(rank));
+  return a;
+}
+__device__ __forceinline__ double cluster_load(const double* p, unsigned rank) {
+  double v;
+  asm volatile("ld.shared::cluster.f64 %0, [%1];" : "=d"(v) : "r"(cluster_addr(p, rank)) : "memory");
+  return v;
+}
+__device__ __forceinline__ float cluster_load(const float* p, unsigned rank) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_addr(p, rank)) : "memory");
+  return v;
+}
+__device__ __forceinline__ int cluster_load(const int* p, unsigned rank) {
+  int v;
+  asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(cluster_addr(p, rank)) : "memory");
+  return v;
+}
+__device__ __forceinline__ void cluster_store(double* p, unsigned rank, double v) {
+  asm volatile("st.shared::cluster.f64 [%0], %1;" ::"r"(cluster_addr(p, rank)), "d"(v) : "memory");
+}
+__device__ __forceinline__ void cluster_store(float* p, unsigned rank, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(cluster_addr(p, rank)), "f"(v) : "memory");
+}
+__device__ __forceinline__ void cluster_store(int* p, unsigned rank, int v) {
+  asm volatile("st.shared::cluster.s32 [%0], %1;" ::"r"(cluster_addr(p, rank)), "r"(v) : "memory");
+}
 
 __device__ __forceinline__ int stage_of(long long p) { return static_cast<int>(p % kColStages); }
 __device__ __forceinline__ unsigned parity_of(long long p) { return static_cast<unsigned>((p / kColStages) & 1); }
@@ -558,7 +608,10 @@ __device__ __forceinline__ bool quotient_safe(const ScaledQuotient<F>& s, F a) {
 // chain, and the 134 MB matrix, about the size of L2, is streamed by every phase.
 // Staging by bulk copies or by cp.async (64 KB in flight per block) measured the same or
 // slower.
-template <typename F>
+// kFromL2: the helpers read x from L2 (ld.global.cg), bypassing this SM's L1: rows of x
+// written by other blocks of a cluster, whose cache lines this block may hold from its own
+// loads of neighbouring rows.
+template <typename F, bool kFromL2 = false>
 __device__ __forceinline__ F scaled_norm(ColSmem<F>& sm, const F* x, long long rows, F scale, long long* status) {
   using S = ColSmem<F>;
   constexpr int kSeg = S::kNormSeg;
@@ -574,7 +627,7 @@ __device__ __forceinline__ F scaled_norm(ColSmem<F>& sm, const F* x, long long r
 #pragma unroll
       for (int q = 0; q < kPer; ++q) {
         const long long i = g * kSeg + h + static_cast<long long>(kColHelpers) * q;
-        held[q] = i < rows ? x[i] : F(0);
+        held[q] = i < rows ? (kFromL2 ? __ldcg(x + i) : x[i]) : F(0);
       }
     };
     if (nseg > 0) load(0);

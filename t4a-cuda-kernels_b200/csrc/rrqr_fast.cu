@@ -116,6 +116,16 @@ __global__ void __launch_bounds__(kColThreads, 2) k_col_step(FusedArgs<F> a, lon
   column_step<F>(a, step, next_norm != 0, *reinterpret_cast<ColSmem<F>*>(smem));
 }
 
+// The clustered column pass (steps with few trailing columns): `csize` blocks per
+// column, launched with that cluster size.
+template <typename F>
+__global__ void __launch_bounds__(kColThreads, 2) k_col_step_cluster(FusedArgs<F> a, long long step, int next_norm,
+                                                                    unsigned csize) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  chain_enter();
+  column_step_cluster<F>(a, step, next_norm != 0, *reinterpret_cast<ColSmem<F>*>(smem), csize);
+}
+
 // Q formation pass for reflector `step`: one block per column of Q.
 template <typename F>
 __global__ void __launch_bounds__(kColThreads, 2) k_q_step(FusedArgs<F> a, long long step, F* q, long long qld,
@@ -201,25 +211,89 @@ FusedLayout fused_layout(long long n, int fsize) {
   return l;
 }
 
-// Launches `kernel` as the next link of a driver chain (see chain_enter).
+// Launches `kernel` as the next link of a driver chain (see chain_enter); `csize` > 1:
+// with thread-block clusters of that many blocks along x.
 template <typename... KArgs, typename... Args>
-int chain_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, unsigned smem, cudaStream_t s, Args... args) {
+int chain_launch_clustered(void (*kernel)(KArgs...), unsigned csize, dim3 grid, dim3 block, unsigned smem,
+                           cudaStream_t s, Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (csize > 1) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = csize;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
+  }
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
   if (e != cudaSuccess) {
     runtime::last_error() = static_cast<int>(e);
     return T4A_ERR_CUDA;
   }
   return T4A_OK;
+}
+template <typename... KArgs, typename... Args>
+int chain_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, unsigned smem, cudaStream_t s, Args... args) {
+  return chain_launch_clustered(kernel, 1u, grid, block, smem, s, args...);
+}
+
+// The clustered column pass runs one block per SM: its dynamic shared memory is raised
+// above half an SM's, so the cluster scheduler cannot pair two blocks (two leaders' chains
+// and feeds) on one SM.  Measured on config 5 with two blocks per SM allowed: clusters
+// gained 8-11 us per step at 4-19 trailing columns and lost up to 3 us once the pass
+// neared 148 blocks.
+unsigned cluster_smem(unsigned need) {
+  int dev = 0, per_sm = 0, optin = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return need;
+  if (cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
+    return need;
+  const unsigned half = static_cast<unsigned>(per_sm) / 2 + 1024;
+  const unsigned want = half > need ? half : need;
+  return want <= static_cast<unsigned>(optin) ? want : need;
+}
+
+// Cluster size of the column pass over `trailing` columns: the largest of 8, 4, 2 for
+// which every cluster of the pass is resident at once (cudaOccupancyMaxActiveClusters at
+// one block per SM), else 1 (the plain pass).  Capacities are asked once per device.
+template <typename K>
+unsigned column_cluster_size(K kernel, unsigned smem, long long trailing) {
+  static std::atomic<int> cap[64][4];  // [device][log2 size]: resident clusters + 1 (0: not asked)
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return 1;
+  for (int lg = 3; lg >= 1; --lg) {
+    int c = cap[dev][lg].load(std::memory_order_relaxed);
+    if (c == 0) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(1u << lg);
+      cfg.blockDim = dim3(kColThreads);
+      cfg.dynamicSmemBytes = smem;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 1u << lg;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int clusters = 0;
+      if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        clusters = 0;
+      }
+      c = clusters + 1;
+      cap[dev][lg].store(c, std::memory_order_relaxed);
+    }
+    if (trailing <= c - 1) return 1u << lg;
+  }
+  return 1;
 }
 
 template <typename F>
@@ -238,10 +312,12 @@ int run_fused(cudaStream_t s, F* w, long long m, long long n, long long ld, long
   a.norms = reinterpret_cast<F*>(ws + L.norms);
   a.rec = reinterpret_cast<StepRecord<F>*>(ws + L.rec);
   a.done = reinterpret_cast<unsigned*>(ws + L.done);
-  static std::atomic<unsigned long long> raised_first{0}, raised_step{0};
+  static std::atomic<unsigned long long> raised_first{0}, raised_step{0}, raised_cluster{0};
   const unsigned smem = sizeof(ColSmem<F>);
   T4A_TRY(allow_smem(k_col_first<F>, smem, raised_first));
   T4A_TRY(allow_smem(k_col_step<F>, smem, raised_step));
+  const unsigned csmem = cluster_smem(smem);
+  T4A_TRY(allow_smem(k_col_step_cluster<F>, csmem, raised_cluster));
   k_init_perm<<<dim3(static_cast<unsigned>((n + kFlatThreads - 1) / kFlatThreads)), dim3(kFlatThreads), 0, s>>>(
       perm, n, n, a.done);
   if (steps == 0) return runtime::check_launch();
@@ -252,9 +328,15 @@ int run_fused(cudaStream_t s, F* w, long long m, long long n, long long ld, long
   for (long long step = 0; step < steps; ++step) {
     T4A_TRY(chain_launch(k_fused_swap<F>, dim3(swap_grid), dim3(kFlatThreads), 0, s, a, step));
     const long long trailing = n - step - 1;
-    if (trailing > 0)
+    if (trailing <= 0) continue;
+    const int next_norm = step + 1 < steps ? 1 : 0;
+    const unsigned csize = column_cluster_size(k_col_step_cluster<F>, csmem, trailing);
+    if (csize > 1)
+      T4A_TRY(chain_launch_clustered(k_col_step_cluster<F>, csize, dim3(static_cast<unsigned>(trailing) * csize),
+                                     dim3(kColThreads), csmem, s, a, step, next_norm, csize));
+    else
       T4A_TRY(chain_launch(k_col_step<F>, dim3(static_cast<unsigned>(trailing)), dim3(kColThreads), smem, s, a,
-                           step, step + 1 < steps ? 1 : 0));
+                           step, next_norm));
   }
   return runtime::check_launch();
 }

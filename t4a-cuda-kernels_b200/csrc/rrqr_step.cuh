@@ -110,11 +110,14 @@ __device__ __forceinline__ void fused_swap(const FusedArgs<F>& a, long long step
 // After this block's norm is written (by thread 0): publish it and draw a ticket; the
 // block that draws the last one sees every norm of the pass and selects the pivot of
 // `pivot_step` with its warp 0, then rearms the counter for the next pass.
+// `tickets`: the blocks of the pass that draw one (every block; a clustered pass: the
+// leaders).
 template <typename F>
-__device__ __forceinline__ void pivot_if_last(const FusedArgs<F>& a, long long pivot_step, ColSmem<F>& sm) {
+__device__ __forceinline__ void pivot_if_last(const FusedArgs<F>& a, long long pivot_step, ColSmem<F>& sm,
+                                              unsigned tickets) {
   if (threadIdx.x == 0) {
     __threadfence();
-    sm.last = atomicAdd(a.done, 1u) == gridDim.x - 1 ? 1 : 0;
+    sm.last = atomicAdd(a.done, 1u) == tickets - 1 ? 1 : 0;
   }
   __syncthreads();
   if (sm.last) {
@@ -148,7 +151,7 @@ __device__ __forceinline__ void column_first(const FusedArgs<F>& a, ColSmem<F>& 
   engine_init(sm);
   const F norm = engine_column_norm(sm, a.w + j * a.ld, a.m, a.status);
   if (threadIdx.x == 0) a.norms[j] = norm;
-  pivot_if_last(a, 0, sm);
+  pivot_if_last(a, 0, sm, gridDim.x);
 }
 
 // Step pass: trailing column j = step + 1 + blockIdx.x.
@@ -176,7 +179,64 @@ __device__ __forceinline__ void column_step(const FusedArgs<F>& a, long long ste
   if (next_norm) {
     const F norm = scale * sqrt(total);
     if (threadIdx.x == 0) a.norms[j] = (bad || nonfinite(norm) || aborted(sm)) ? F(-1) : norm;
-    pivot_if_last(a, step + 1, sm);
+    pivot_if_last(a, step + 1, sm, gridDim.x);
+  }
+}
+
+// Clustered step pass, for steps with few trailing columns: a cluster of `csize` blocks
+// per trailing column j = step + 1 + blockIdx.x / csize.  The leader (rank 0) runs the
+// dot chain as column_step does; after a cluster barrier every block reads the
+// coefficient from the leader's shared memory and updates its own slice of the rows
+// (slices of a multiple of 32 rows, so every slice starts at the same 16-byte phase),
+// then writes its block peak and flag into the leader's shared memory; after a second
+// barrier the leader takes their maximum and runs the norm and the ticket as
+// column_step does.  The update is elementwise and the maximum exact, so the bits are
+// column_step's.  The leader's norm reads the column from L2: other blocks wrote rows
+// of cache lines that its own update may have brought into its L1.
+template <typename F>
+__device__ __forceinline__ void column_step_cluster(const FusedArgs<F>& a, long long step, bool next_norm,
+                                                    ColSmem<F>& sm, unsigned csize) {
+  const long long j = step + 1 + blockIdx.x / csize;
+  if (j >= a.n) return;  // the same for every block of the cluster
+  const unsigned rank = cluster_rank();
+  engine_init(sm);
+  Producer pr = producer_start();
+  const F* v = a.w + step * a.ld + step;
+  F* t = a.w + j * a.ld + step;
+  const long long rows = a.m - step;
+  if (rank == 0) ring_dot(sm, pr, 0, v, t, rows, a.coeff[step], a.status);
+  cluster_barrier();
+  const F d = cluster_load(&sm.dot, 0);
+  const bool stopped = cluster_load(&sm.abort, 0) != 0;
+  const long long slice = ((rows + csize - 1) / csize + 31) / 32 * 32;
+  const long long lo = static_cast<long long>(rank) * slice < rows ? static_cast<long long>(rank) * slice : rows;
+  const long long hi = lo + slice < rows ? lo + slice : rows;
+  F peak = F(0);
+  bool flagged = false;
+  if (!stopped && hi > lo) update_direct<true>(v + lo, t + lo, hi - lo, d, &peak, &flagged, rank == 0);
+  F scale;
+  bool bad;
+  block_peak(sm, peak, flagged, &scale, &bad);
+  if (threadIdx.x == 0) {
+    cluster_store(&sm.cpeak[rank], 0, scale);
+    cluster_store(&sm.cbad[rank], 0, bad ? 1 : 0);
+  }
+  cluster_barrier();
+  if (rank != 0) return;
+  scale = F(0);
+  bad = false;
+  for (unsigned q = 0; q < csize; ++q) {
+    scale = sm.cpeak[q] > scale ? sm.cpeak[q] : scale;
+    bad = bad || sm.cbad[q] != 0;
+  }
+  F total = F(0);
+  if (next_norm && !aborted(sm) && !bad && scale > F(0))
+    total = scaled_norm<F, true>(sm, t + 1, rows - 1, scale, a.status);
+  drain(sm, pr, a.status);
+  if (next_norm) {
+    const F norm = scale * sqrt(total);
+    if (threadIdx.x == 0) a.norms[j] = (bad || nonfinite(norm) || aborted(sm)) ? F(-1) : norm;
+    pivot_if_last(a, step + 1, sm, gridDim.x / csize);
   }
 }
 
