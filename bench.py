@@ -1,7 +1,7 @@
 """Benchmark of the t4a_b200 hot path on B200 (one JSON line on stdout, rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--op all|movement|reduce|gather|rrqr] [--only TAGS] [--no-cpu-baseline]
+                    [--op all|movement|reduce|gather|rrqr|rrqr-loop] [--only TAGS] [--no-cpu-baseline]
 
 One step runs every operation of the BASELINE configurations once, back to back on one
 stream (the default `--op all`):
@@ -14,6 +14,8 @@ stream (the default `--op all`):
             indices; scatter_add of F64 [4194304,128] updates into [1048576,128] with
             Zipf(1.1) indices;
   config 5  F64 RRQR of [65536,256] = U V^T + 1e-10 N, 256 steps (t4a_rrqr).
+`--op rrqr-loop` (one GPU, not in the default step) times config 5 through the
+reference bench's loop of RRQR primitives, launched one call at a time.
 Inputs are seeded synthetic values (SplitMix64 streams; NumPy generators for config 5);
 no dataset is involved.
 
@@ -861,7 +863,79 @@ class RrqrConfig(Config):
                 raise CheckFailed(f"RRQR prefix rank {int(rank.item())} (status {int(st.item())}), expected 64")
 
 
-CONFIGS = {"reduce": ReduceConfigs, "movement": MovementConfig, "gather": GatherScatterConfig, "rrqr": RrqrConfig}
+class RrqrLoopConfig(RrqrConfig):
+    """Config 5 through the reference bench's loop of primitives instead of the fused
+    driver (not in the default step; `--op rrqr-loop`, one GPU): initialize_permutation,
+    then per step column_norms, select_pivot, swap_columns, reflector and, over the
+    trailing columns, apply_reflector with the reflector column packed into its own
+    buffer (t4a_copy_strided), each planned by this library's planner (plans made
+    before timing) and launched through its launcher on the caller's stream.  This is the speed a caller
+    that ports the reference one call at a time gets; the bits are the fused driver's.
+    Same matrix, bytes, CPU leg and check as `rrqr`."""
+
+    name = "rrqr-loop"
+
+    def setup(self):
+        import torch
+        if self.world > 1:
+            raise SystemExit("--op rrqr-loop runs on one GPU (the sharded RRQR is --op rrqr)")
+        super().setup()
+        t4, abi = self.t4, self.abi
+        m, n = self.M, self.N
+        op = self.ops[0]
+        op["tag"] = "rrqr-loop-f64-65536x256-256steps"
+        op["launches"] = 1 + 4 * n + 2 * (n - 1)
+        if self.host_only:
+            return
+        wl, vl, cl = abi.layout([m, n]), abi.layout([n]), abi.layout([n])
+        packed_l = abi.layout([m, n], [1, 0])
+        self.loop_layouts = (wl, vl, cl, packed_l)
+        span = m * n
+        self.plans = dict(init=t4.plan_rrqr("initialize_permutation", n, n), steps=[])
+        for step in range(n):
+            self.plans["steps"].append(dict(
+                norms=t4.plan_rrqr("column_norms", abi.F64, wl, span, vl, n, step),
+                pivot=t4.plan_rrqr("select_pivot", abi.F64, vl, n, vl, n, 1, 1, step),
+                swap=t4.plan_rrqr("swap_columns", abi.F64, wl, span, vl, n, 1, step),
+                reflector=t4.plan_rrqr("reflector", abi.F64, wl, span, cl, n, step),
+                apply=(t4.plan_rrqr("apply_reflector", abi.F64, packed_l, m, wl, span, cl, n, step, step + 1,
+                                    n - step - 1) if n - step - 1 > 0 else None)))
+        self.dev["norms"] = torch.empty(n, dtype=torch.float64, device=self.device)
+        self.dev["packed"] = torch.empty(m, dtype=torch.float64, device=self.device)
+        self.packed_dst = abi.layout([m])
+        self.packed_src = [abi.layout([m], [1], step * m) for step in range(n)]
+
+    def _run(self, sh):
+        t4, abi, d = self.t4, self.abi, self.dev
+        m, n = self.M, self.N
+        wl, vl, cl, packed_l = self.loop_layouts
+        dt = ctypes.c_int(abi.F64)
+        t4.launch_rrqr("initialize_permutation", self.plans["init"], sh, vp(d["perm"]), ctypes.c_longlong(n),
+                       ctypes.c_longlong(n))
+        for step, p in enumerate(self.plans["steps"]):
+            st = ctypes.c_longlong(step)
+            t4.launch_rrqr("column_norms", p["norms"], sh, vp(d["a"]), vp(d["norms"]), dt, wl, vl, st)
+            t4.launch_rrqr("select_pivot", p["pivot"], sh, vp(d["norms"]), vp(d["perm"]), vp(d["pivots"][step:]),
+                           vp(d["status"]), dt, vl, vl, st)
+            t4.launch_rrqr("swap_columns", p["swap"], sh, vp(d["a"]), vp(d["perm"]), vp(d["pivots"][step:]), dt,
+                           wl, vl, st)
+            t4.launch_rrqr("reflector", p["reflector"], sh, vp(d["a"]), vp(d["coeff"]), dt, wl, cl, st)
+            if p["apply"] is not None:
+                t4.copy_strided_raw(sh, abi.F64, vp(d["packed"]), self.packed_dst, m, vp(d["a"]),
+                                    self.packed_src[step], m * n)
+                t4.launch_rrqr("apply_reflector", p["apply"], sh, vp(d["packed"]), vp(d["a"]), vp(d["coeff"]), dt,
+                               packed_l, wl, cl, st, ctypes.c_longlong(step + 1), ctypes.c_longlong(n - step - 1))
+
+    def after_timing(self):
+        super().after_timing()
+        faults = self.t4.rrqr_primitive_faults()
+        self.checks["rrqr_primitive_faults"] = faults
+        if faults:
+            raise CheckFailed(f"RRQR primitives: a bounded wait ran out (fault word {faults})")
+
+
+CONFIGS = {"reduce": ReduceConfigs, "movement": MovementConfig, "gather": GatherScatterConfig, "rrqr": RrqrConfig,
+           "rrqr-loop": RrqrLoopConfig}
 ORDER = ["reduce", "movement", "gather", "rrqr"]
 
 
@@ -893,7 +967,7 @@ def workload_config(groups, world):
 
 
 def dtype_string(groups):
-    names = {"reduce": "f32,f64,c64", "movement": "f32,c64", "gather": "f32,f64,i64", "rrqr": "f64"}
+    names = {"reduce": "f32,f64,c64", "movement": "f32,c64", "gather": "f32,f64,i64", "rrqr": "f64", "rrqr-loop": "f64"}
     return ";".join(names[g.name] for g in groups)
 
 
@@ -1149,7 +1223,7 @@ def cpu_sample_text(groups):
             parts.append("config 2 whole")
         elif g.name == "gather":
             parts.append(f"config 4 on the first {GatherScatterConfig.SAMPLE} of {GatherScatterConfig.N} index rows")
-        elif g.name == "rrqr":
+        elif g.name in ("rrqr", "rrqr-loop"):
             parts.append(f"config 5's first {RrqrConfig.CPU_STEPS} of {RrqrConfig.N} factorization steps")
     return "; ".join(parts)
 
@@ -1216,7 +1290,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--op", default="all", choices=["all"] + ORDER)
+    ap.add_argument("--op", default="all", choices=["all"] + ORDER + ["rrqr-loop"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-check", action="store_true", help="skip the per-rank check against the single-GPU result")
     ap.add_argument("--only", default=None, help="comma-separated op tags to run (profiling)")
