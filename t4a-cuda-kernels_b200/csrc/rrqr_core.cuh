@@ -259,19 +259,36 @@ __device__ __forceinline__ Candidate<R> best_over_warp(Candidate<R> c) {
 // column's norm and original index.  Negative norms (the non-finite sentinel) are not
 // candidates and set *flagged; NaN norms are skipped.  The empty candidate holds norm 0,
 // so a zero-norm column still beats it; with no candidate the pivot is `step`.
-template <typename R, typename NormAt, typename OriginalAt>
+// Each lane visits its columns in ascending order, kBatch at a time: their norms and
+// original indices are all loaded before any is compared, so the loads overlap (a
+// caller whose norm_at computes rather than loads takes kBatch 1).
+template <typename R, int kBatch = 8, typename NormAt, typename OriginalAt>
 __device__ __forceinline__ long long choose_pivot(long long step, long long columns, NormAt norm_at,
                                                   OriginalAt original_at, bool* flagged) {
   Candidate<R> best{R(0), kNoIndex, kNoIndex};
   bool negative = false;
-  for (long long c = step + lane_id(); c < columns; c += kLanes) {
-    const R norm = norm_at(c);
-    if (norm < R(0)) {
-      negative = true;
-      continue;
+  for (long long c0 = step + lane_id(); c0 < columns; c0 += static_cast<long long>(kLanes) * kBatch) {
+    R norms[kBatch];
+    long long originals[kBatch];
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      const long long c = c0 + static_cast<long long>(k) * kLanes;
+      if (c < columns) {
+        norms[k] = norm_at(c);
+        originals[k] = original_at(c);
+      }
     }
-    const Candidate<R> cand{norm, original_at(c), c};
-    if (cand.norm > best.norm || (cand.norm == best.norm && cand.original < best.original)) best = cand;
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      const long long c = c0 + static_cast<long long>(k) * kLanes;
+      if (c >= columns) continue;
+      if (norms[k] < R(0)) {
+        negative = true;
+        continue;
+      }
+      const Candidate<R> cand{norms[k], originals[k], c};
+      if (cand.norm > best.norm || (cand.norm == best.norm && cand.original < best.original)) best = cand;
+    }
   }
   best = best_over_warp(best);
   *flagged = __any_sync(kAllLanes, negative);

@@ -84,7 +84,7 @@ __global__ void __launch_bounds__(256) k_dist_select_swap(DistArgs<F> a, long lo
   __shared__ DistRecord<F> rec;
   const long long count = a.n - s;  // gathered parts cover columns s .. n-1
   if (threadIdx.x < 32) {
-    const DistRecord<F> r = shard_pivot(a, s, count, s, blockIdx.x == 0,
+    const DistRecord<F> r = shard_pivot<F, 1>(a, s, count, s, blockIdx.x == 0,
                                         [&](long long c) { return combined_norm<F, false>(a, count, c - s); });
     if (lane_id() == 0) rec = r;
   }

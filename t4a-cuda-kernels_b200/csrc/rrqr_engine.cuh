@@ -481,6 +481,40 @@ __device__ __forceinline__ void update_direct(const F* v, F* t, long long rows, 
   }
 }
 
+// x = x / divisor over rows [0, rows), IEEE division per element, by every thread:
+// 16-byte loads and stores, kU groups per thread loaded before any is divided, so the
+// loads of a thread overlap instead of each waiting out its own latency.
+template <typename F>
+__device__ __forceinline__ void divide_direct(F* x, long long rows, F divisor) {
+  using V = typename Vec16<F>::V;
+  constexpr int kW = Vec16<F>::kW;
+  const long long tid = threadIdx.x;
+  const Split16<F> sp = split16(x, rows);
+  const long long edge = sp.lead + (rows - sp.tail0);
+  for (long long i = tid; i < edge; i += kColThreads) {
+    const long long r = i < sp.lead ? i : sp.tail0 + (i - sp.lead);
+    x[r] = x[r] / divisor;
+  }
+  V* xv = reinterpret_cast<V*>(x + sp.lead);
+  constexpr int kU = 4;
+  for (long long q0 = tid; q0 < sp.body; q0 += kU * kColThreads) {
+    V held[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const long long q = q0 + static_cast<long long>(u) * kColThreads;
+      if (q < sp.body) held[u] = xv[q];
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const long long q = q0 + static_cast<long long>(u) * kColThreads;
+      if (q >= sp.body) continue;
+#pragma unroll
+      for (int e = 0; e < kW; ++e) elem<F>(held[u], e) = elem<F>(held[u], e) / divisor;
+      xv[q] = held[u];
+    }
+  }
+}
+
 // The largest modulus over rows [0, rows) of x, read by every thread (16-byte loads
 // where aligned).  kFlag: non-finite moduli are flagged and left out (column_norms);
 // otherwise every modulus competes and NaN never wins (the reflector's norm).

@@ -170,12 +170,13 @@ __device__ __forceinline__ void norm_parts(const DistArgs<F>& a, ColSmem<F>& sm,
 // r's part of column c at nrecv[r * stride + c - first]); with `writer`, lane 0 records
 // the step (record, pivot, coefficient, flag).  Returns the record (the caller shares it
 // through shared memory).
-template <typename F, typename NormOf>
+// kBatch: choose_pivot's batch (1 when norm_of combines the ranks' parts itself).
+template <typename F, int kBatch = 8, typename NormOf>
 __device__ __forceinline__ DistRecord<F> shard_pivot(const DistArgs<F>& a, long long s, long long stride,
                                                      long long first, bool writer, NormOf norm_of) {
   bool flagged = false;
   const long long pivot =
-      choose_pivot<F>(s, a.n, norm_of, [&](long long c) { return a.perm[c]; }, &flagged);
+      choose_pivot<F, kBatch>(s, a.n, norm_of, [&](long long c) { return a.perm[c]; }, &flagged);
   F norm = norm_of(pivot);
   if (!(norm >= F(0))) norm = combined_norm<F, true>(a, stride, pivot - first);
   const F x0 = leading_value(a, stride, pivot - first);

@@ -293,7 +293,7 @@ __device__ __forceinline__ void engine_reflect_task(F* x, long long step, long l
     return;
   }
   const Householder<F> h = householder(x0, norm);
-  for (long long r = 1 + threadIdx.x; r < n; r += kColThreads) col[r] = col[r] / h.divisor;
+  divide_direct(col + 1, n - 1, h.divisor);
   if (threadIdx.x == 0) {
     col[0] = h.alpha;
     *coeff = h.coeff;
